@@ -1,0 +1,350 @@
+"""Benchmark of the semantic-ID-constrained beam path: ms per user and users/sec.
+
+One step = one user request (batch 1, 50 beams): prefill of the user's
+history into the shared prefix, four decode forwards, five step tails
+(double log-softmax over the full vocabulary, trie mask, beam top-k, parent
+gather).  Default workload: the Qwen2.5-1.5B-shaped FP32 model, 3,500-item
+catalog, prompts of 150-350 tokens (synthetic, seeded).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Under torchrun each rank drives one GPU; users are dealt round-robin (weak
+scaling: every rank serves K users) and no collective runs on the per-step
+path - a barrier and max-reduction of the timings bracket the timed region.
+
+* ``value``: users/s over all ranks with the prompts already in HBM, timed
+  with CUDA events on the launching stream (requests queued back to back);
+  median/p95 are per-user device times.
+* ``e2e``: the same through the public host API (``BeamEngine.generate``: pinned
+  H2D of the prompt, D2H of the ranked result, sync-to-sync per user, the
+  reference's timing span ``benchmark_inference.py:230-232``).
+* ``roofline``: the decode projection GEMMs (dominant kernel), algorithmic
+  weight bytes per pass / device time, against the measured HBM copy peak.
+* ``--impl reference``: the reference algorithm on the host cores (the CPU
+  oracle port of HF generate + the reference's processor), rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = 'median/p95 ms per user (batch 1, beam 50) and users/sec at 1/2/4/8 B200'
+
+
+def percentile(values, q):
+    """Linear interpolation at (n-1)*q, as ``benchmark.py:64-68``."""
+    ordered = sorted(values)
+    idx = (len(ordered) - 1) * q
+    lo, hi = int(idx), min(int(idx) + 1, len(ordered) - 1)
+    return ordered[lo] + (ordered[hi] - ordered[lo]) * (idx - lo)
+
+
+def measured_peaks():
+    p = ROOT / 'MEASURED_PEAKS.json'
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d['hbm_gbs'], 'measured'
+    return 6650.0, 'fallback'
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock, throttle reasons)."""
+    FIELDS = ('uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, uuid):
+        self.uuid = uuid
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', f'--query-gpu={self.FIELDS}', '--format=csv,noheader,nounits',
+                                          '-lms', '200'], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, smax, reasons = [], [], set()
+        names = ['hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap']
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(',')]
+            if len(parts) < 9 or (self.uuid and self.uuid not in parts[0]):
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == 'active':
+                    reasons.add(name)
+        if not sm:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled'], 'samples': 0}
+        return {'sm_mhz': statistics.median(sm), 'sm_max_mhz': max(smax), 'reasons': sorted(reasons),
+                'samples': len(sm)}
+
+
+def dist_env():
+    return int(os.environ.get('RANK', 0)), int(os.environ.get('LOCAL_RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
+
+
+def build_workload(name, n_users):
+    from rapidtinyrec_b200 import configs, workload
+    wl = configs.workload(name)
+    items = workload.catalog_items(wl)
+    cons = workload.constraint_dict(wl.model, items)
+    users = workload.users(wl, items, count=min(n_users, wl.users))
+    while len(users) < n_users:  # cycle the cohort if more steps than users are asked
+        users = users + users[:n_users - len(users)]
+    return wl, items, cons, users
+
+
+def gemm_weight_bytes(cfg):
+    b = 4 if cfg.dtype == 'fp32' else 2
+    layer = cfg.qkv_dim * cfg.hidden + cfg.qkv_dim + cfg.hidden * cfg.q_dim + 3 * cfg.hidden * cfg.intermediate
+    return b * (cfg.layers * layer + cfg.vocab * cfg.hidden)
+
+
+def cpu_oracle_time(cfg, weights_cpu, cons, users, budget_s, threads):
+    """Time the CPU port of the reference path on a bounded sample of users."""
+    import torch
+    from oracle.beam_cpu import beam_search
+    from oracle.qwen2_cpu import Qwen2Oracle
+    torch.set_num_threads(threads)
+    model = Qwen2Oracle(cfg, weights_cpu)
+    times = []
+    t_start = time.perf_counter()
+    for u in users:
+        t0 = time.perf_counter()
+        beam_search(model, u.prompt_token_ids, cons, cfg.eos)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() - t_start > budget_s:
+            break
+    return times
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    import torch
+    from rapidtinyrec_b200 import workload as wk
+    threads = os.cpu_count() or 1
+    wl, _, cons, users = build_workload(args.workload, args.warmup + args.steps)
+    cfg = wl.model
+    weights = wk.synth_weights(cfg, seed=wl.weight_seed, device='cpu')
+    warm = cpu_oracle_time(cfg, weights, cons, users[:min(args.warmup, 1)], 0, threads)
+    # bound the run: every step is one full request; cap the count to ~150 s of CPU work
+    per = warm[0] if warm else 1.0
+    k = max(1, min(args.steps, int(150.0 / max(per, 1e-3))))
+    times = cpu_oracle_time(cfg, weights, cons, users[args.warmup:args.warmup + k], 1e9, threads)
+    total = sum(times)
+    value = len(times) / total
+    line = {'metric': METRIC, 'impl': 'reference', 'value': round(value, 4), 'unit': 'users/s',
+            'n_gpus': world, 'steps': len(times), 'warmup': len(warm), 'ms_per_step': round(1000 * total / len(times), 2),
+            'median_ms': round(1000 * statistics.median(times), 2), 'p95_ms': round(1000 * percentile(times, 0.95), 2),
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic', 'config': {'workload': args.workload, 'beams': 50, 'requested_steps': args.steps},
+            'cpu_baseline': {'value': round(value, 4), 'unit': 'users/s', 'cores': threads, 'kind': 'port',
+                             'sample': f'{len(times)} users of {args.workload}, full request each (CPU oracle port of '
+                                       f'HF beam search + GpuSidConstrainedLogitsProcessor + folded SDPA)'},
+            'e2e': {'value': round(value, 4), 'unit': 'users/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from rapidtinyrec_b200 import workload as wk
+    from rapidtinyrec_b200.constraints import GpuSidConstraintTables
+    from rapidtinyrec_b200.engine import BeamEngine
+
+    rank, local, world = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device('cuda', local)
+    if world > 1:
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    per_rank = args.warmup + args.steps
+    wl, items, cons, all_users = build_workload(args.workload, per_rank * world)
+    users = all_users[rank::world]
+    cfg = wl.model
+    max_prefix = max(wl.prompt_max, max(u.prompt_tokens for u in users))
+    weights = wk.synth_weights(cfg, seed=wl.weight_seed, device=f'cuda:{local}')
+    tables = GpuSidConstraintTables(cons, cfg.root, cfg.newline, cfg.eos)
+    engine = BeamEngine(cfg, weights, tables, max_prefix=max_prefix, device=local)
+    weights_cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        weights_cpu = {k: v.cpu() for k, v in weights.items()}
+    del weights
+    torch.cuda.empty_cache()
+    stream = torch.cuda.Stream(device=dev)
+    engine.set_stream(stream)
+
+    ids_dev = [torch.tensor(u.prompt_token_ids, dtype=torch.int32, device=dev) for u in users]
+    ids_host = [torch.tensor(u.prompt_token_ids, dtype=torch.int32).numpy() for u in users]
+    torch.cuda.synchronize(dev)
+
+    # warm-up (graph capture happens on the first request)
+    for i in range(args.warmup):
+        engine.launch_device(ids_dev[i], users[i].prompt_tokens)
+        engine.wait()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+
+    # ---- device-resident timed region
+    timed = range(args.warmup, args.warmup + args.steps)
+    events = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    launches_before = engine.report()['kernel_launches']
+    barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(uuid) as clocks:
+        events[0].record(stream)
+        for j, i in enumerate(timed):
+            engine.launch_device(ids_dev[i], users[i].prompt_tokens)
+            events[j + 1].record(stream)
+        engine.wait()
+        torch.cuda.synchronize(dev)
+    barrier()
+    launches = engine.report()['kernel_launches'] - launches_before
+    per_user = [events[j].elapsed_time(events[j + 1]) for j in range(args.steps)]
+    total_ms = events[0].elapsed_time(events[-1])
+
+    # ---- end-to-end through the host API
+    e2e_lat = []
+    barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    for i in timed:
+        t = time.perf_counter()
+        engine.generate_raw(ids_host[i])
+        e2e_lat.append(time.perf_counter() - t)
+    e2e_total = time.perf_counter() - t0
+    barrier()
+    rep = engine.report()
+
+    # ---- roofline of the dominant kernel: the decode projection GEMMs (M = beams)
+    gemm_ms = engine.profile_gemms(engine.beams, reps=5)
+    gemm_bytes = gemm_weight_bytes(cfg)
+    peak, peak_kind = measured_peaks()
+
+    if world > 1:
+        t = torch.tensor([total_ms, e2e_total], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_total = float(t[0]), float(t[1])
+        lat = torch.tensor(per_user, dtype=torch.float64, device=dev)
+        gathered = [torch.empty_like(lat) for _ in range(world)]
+        dist.all_gather(gathered, lat)
+        per_user = [float(x) for g in gathered for x in g.tolist()]
+        el = torch.tensor(e2e_lat, dtype=torch.float64, device=dev)
+        g2 = [torch.empty_like(el) for _ in range(world)]
+        dist.all_gather(g2, el)
+        e2e_lat = [float(x) for g in g2 for x in g.tolist()]
+
+    cpu = None
+    if weights_cpu is not None:
+        threads = os.cpu_count() or 1
+        times = cpu_oracle_time(cfg, weights_cpu, cons, users[args.warmup:], args.cpu_budget, threads)
+        cpu = {'value': round(len(times) / sum(times), 5), 'unit': 'users/s', 'cores': threads, 'kind': 'port',
+               'sample': f'{len(times)} users of {args.workload} (full request each) through the CPU oracle port '
+                         f'of HF beam search + GpuSidConstrainedLogitsProcessor + folded SDPA, '
+                         f'median {1000 * statistics.median(times):.0f} ms/user'}
+
+    if rank == 0:
+        n_users = args.steps * world
+        value = n_users / (total_ms / 1000.0)
+        achieved = gemm_bytes / (gemm_ms / 1000.0) / 1e9
+        ck = clocks.summary()
+        ffma_peak = 148 * 128 * 2 * (ck['sm_mhz'] or 1965.0) * 1e6 / 1e12
+        gemm_flops = 2.0 * engine.beams * gemm_bytes / (4 if cfg.dtype == 'fp32' else 2)
+        line = {
+            'metric': METRIC, 'value': round(value, 3), 'unit': 'users/s', 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 3),
+            'median_ms': round(statistics.median(per_user), 3), 'p95_ms': round(percentile(per_user, 0.95), 3),
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+            'dtype': 'f32' if cfg.dtype == 'fp32' else 'bf16', 'data': 'synthetic',
+            'config': {'workload': args.workload, 'model': cfg.name, 'beams': engine.beams, 'items': wl.items,
+                       'prompt_tokens': [wl.prompt_min, wl.prompt_max], 'users_per_rank': args.steps,
+                       'parallelism': f'replicas{world}', 'partition': 'users round-robin, no per-step collective',
+                       'l2': 'inputs larger than L2: the 6.2 GB of weights stream from HBM every forward'},
+            'e2e': {'value': round(n_users / e2e_total, 3), 'unit': 'users/s',
+                    'median_ms': round(1000 * statistics.median(e2e_lat), 3),
+                    'p95_ms': round(1000 * percentile(e2e_lat, 0.95), 3),
+                    'h2d_bytes_per_step': rep['h2d_bytes_per_request'],
+                    'd2h_bytes_per_step': rep['d2h_bytes_per_request'],
+                    'timing': 'host wall clock, sync to sync per user'},
+            'roofline': {'bound': 'hbm', 'kernel': 'gemm_f32_kernel (decode projections + LM head, M=50)',
+                         'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
+                         'frac': round(achieved / peak, 4), 'peak_source': peak_kind,
+                         'traffic': None, 'bytes_per_pass': gemm_bytes, 'ms_per_pass': round(gemm_ms, 4),
+                         'ffma_tflops': round(gemm_flops / (gemm_ms / 1000.0) / 1e12, 2),
+                         'ffma_frac': round(gemm_flops / (gemm_ms / 1000.0) / 1e12 / ffma_peak, 4)},
+            'gpu_launches': int(launches),
+            'launches_per_user': rep['launches_per_request'],
+            'clocks': ck,
+        }
+        if cpu is not None:
+            line['cpu_baseline'] = cpu
+        print(json.dumps(line), flush=True)
+    engine.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=40)
+    ap.add_argument('--warmup', type=int, default=3)
+    ap.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    ap.add_argument('--workload', default='qwen1.5b-fp32')
+    ap.add_argument('--cpu-budget', type=float, default=20.0, help='seconds of CPU-baseline work (rank 0, N=1)')
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error('--warmup must be >= 3')
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == '__main__':
+    main()

@@ -1,0 +1,572 @@
+// The fused step tail of the constrained beam search, on device.
+//
+// One beam-search iteration of transformers' GenerationMixin._beam_search
+// (generation/utils.py:3252-3352) with the reference's processor
+// GpuSidConstrainedLogitsProcessor (rapidtinyrec/gpu_constraints.py:90-101):
+//
+//   lp1 = log_softmax(float(logits))            three passes over the vocabulary,
+//   lp2 = log_softmax(lp1)                      split over TAIL_SPLITS CTAs/row
+//   scores = lp2 + mask(lookup(step, ids))      only allowed columns are finite
+//   acc = scores + running_scores               candidates = allowed columns
+//   topk(acc, 2*beams) -> EOS hits -> running topk(beams) -> finished merge
+//   -> parents (cache reorder) -> early-stop heuristic
+//
+// Only the allowed columns can be finite, so the candidate set is
+// beams x width (<= 64 x 256) instead of beams x vocab; a single CTA radix-
+// selects the top 2*beams 64-bit keys (order-preserving score bits, then the
+// complemented flat index, so equal scores rank the lower flat index first).
+// log_softmax keeps torch's CPU form (x - max) - log(sum exp(x - max)); the
+// second pass's max is exactly -log(sum) of the first.
+#include <math.h>
+
+#include "common.cuh"
+#include "engine.h"
+
+namespace rtr {
+
+constexpr int TAIL_THREADS = 256;
+constexpr int SEL_THREADS = 1024;
+constexpr int MAX_CAND = MAX_BEAMS * MAX_WIDTH;
+
+// Deterministic block reductions (fixed shuffle tree, warps summed in order).
+__device__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float r = 0.f;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r += red[i];
+    red[32] = r;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+__device__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = -INFINITY;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
+    red[32] = r;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// ---------------------------------------------------------- SID lookup
+// Row descriptor of GpuSidConstraintTables.lookup (gpu_constraints.py:69-87).
+struct LookupRow {
+  int kind;   // 0: first tokens, 1: one token broadcast, 2: table1 row, 3: table2 row
+  int token;  // kind 1
+  long index; // kinds 2/3
+};
+
+__device__ __forceinline__ bool sid_index(const DevTables& tb, const long* tok, int n, long* index) {
+  bool in_range = true;
+  long idx = 0, stride = 1, limit = 1;
+  for (int j = n - 1; j >= 0; --j) {
+    const long digit = tok[j] - tb.offsets[j];
+    in_range = in_range && digit >= 0 && digit < tb.sizes[j];
+    idx += digit * stride;
+    stride *= tb.sizes[j];
+  }
+  for (int j = 0; j < n; ++j) limit *= tb.sizes[j];
+  idx = idx < 0 ? 0 : (idx > limit - 1 ? limit - 1 : idx);
+  *index = idx;
+  return in_range;
+}
+
+// tok[0..n) are the last n tokens of the row (oldest first); n = 3 at steps 0/3.
+__device__ LookupRow lookup_row(const DevTables& tb, int step, const long* tok) {
+  LookupRow r{1, tb.eos, 0};
+  if (step == 1 || step == 2) {
+    long idx;
+    if (sid_index(tb, tok, step, &idx)) { r.kind = step + 1; r.index = idx; }
+  } else if (step == 0 || step == 3) {
+    long idx;
+    const bool in_range = sid_index(tb, tok, 3, &idx);
+    r.token = (in_range && tb.valid[idx]) ? tb.newline : tb.eos;
+    if (tok[0] == tb.root[0] && tok[1] == tb.root[1] && tok[2] == tb.root[2]) r.kind = 0;
+  }
+  return r;
+}
+
+__device__ __forceinline__ int lookup_col(const DevTables& tb, const LookupRow& r, int j) {
+  switch (r.kind) {
+    case 0: return tb.first_tokens[j];
+    case 2: return tb.table1[r.index * tb.width1 + j];
+    case 3: return tb.table2[r.index * tb.width2 + j];
+    default: return r.token;
+  }
+}
+
+__host__ __device__ int lookup_width_of(const DevTables& tb, int step) {
+  if (step == 0 || step == 3) return tb.n_first;
+  if (step == 1) return tb.width1;
+  if (step == 2) return tb.width2;
+  return 1;
+}
+
+int lookup_width(const DevTables& tb, int step) { return lookup_width_of(tb, step); }
+
+// -------------------------------------------------- vocabulary passes
+__global__ void tail_max_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+  __shared__ float red[33];
+  const int row = blockIdx.x, sp = blockIdx.y;
+  const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
+  const float* x = logits + (long)row * vocab;
+  float m = -INFINITY;
+  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) m = fmaxf(m, x[i]);
+  m = block_max(m, red);
+  if (threadIdx.x == 0) st->part[row][sp][0] = m;
+}
+
+__device__ __forceinline__ float row_max(const BeamState* st, int row) {
+  float m = -INFINITY;
+  for (int s = 0; s < TAIL_SPLITS; ++s) m = fmaxf(m, st->part[row][s][0]);
+  return m;
+}
+
+__global__ void tail_sum1_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+  __shared__ float red[33];
+  const int row = blockIdx.x, sp = blockIdx.y;
+  const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
+  const float* x = logits + (long)row * vocab;
+  const float m = row_max(st, row);
+  float s = 0.f;
+  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) s += expf(x[i] - m);
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) st->part[row][sp][1] = s;
+}
+
+__global__ void tail_sum2_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+  __shared__ float red[33];
+  const int row = blockIdx.x, sp = blockIdx.y;
+  const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
+  const float* x = logits + (long)row * vocab;
+  const float m = row_max(st, row);
+  float s1 = 0.f;
+  for (int k = 0; k < TAIL_SPLITS; ++k) s1 += st->part[row][k][1];
+  const float L1 = logf(s1);
+  const float m2 = (m - m) - L1;  // max of lp1, reached at the arg-max column
+  float s = 0.f;
+  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) s += expf(((x[i] - m) - L1) - m2);
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) {
+    st->part[row][sp][2] = s;
+    if (sp == 0) { st->row_stats[row][0] = m; st->row_stats[row][1] = L1; st->row_stats[row][2] = m2; }
+  }
+}
+
+// ---------------------------------------------------- select + update
+__device__ __forceinline__ uint64_t cand_key(float acc, uint32_t flat) {
+  return ((uint64_t)float_key(acc) << 32) | (uint64_t)(~flat);
+}
+
+struct SelShared {
+  float stats[MAX_BEAMS][4];
+  int32_t o_tok[MAX_BEAMS][NSTEPS], o_par[MAX_BEAMS][NSTEPS], o_anc[MAX_BEAMS][4];
+  float o_score[MAX_BEAMS];
+  int32_t f_tok[MAX_BEAMS][NSTEPS], f_par[MAX_BEAMS][NSTEPS], f_done[MAX_BEAMS];
+  float f_score[MAX_BEAMS];
+  LookupRow rows[MAX_BEAMS];
+  int32_t col0[MAX_BEAMS];
+  uint64_t top[2 * MAX_BEAMS];
+  uint64_t sorted[2 * MAX_BEAMS];
+  float c_score[2 * MAX_BEAMS], c_run[2 * MAX_BEAMS], c_fin[3 * MAX_BEAMS];
+  int32_t c_beam[2 * MAX_BEAMS], c_tok[2 * MAX_BEAMS], c_hit[2 * MAX_BEAMS];
+  int32_t n_run[MAX_BEAMS], n_fin[MAX_BEAMS];
+  unsigned hist[256];
+  uint64_t prefix, mask;
+  int krem, done, counter, finite;
+  float red[33];
+};
+
+__global__ void __launch_bounds__(SEL_THREADS) beam_select_kernel(BeamState* st, const float* __restrict__ logits,
+                                                                 int rows, int vocab, int beams, int step,
+                                                                 DevTables tb, uint32_t* status) {
+  extern __shared__ uint64_t cand[];
+  __shared__ SelShared sh;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const int K = 2 * beams;
+  const int width = lookup_width_of(tb, step);
+  const int nc = beams * width;
+
+  // 1. row statistics and a snapshot of the previous state
+  if (tid < rows) {
+    float s2 = 0.f;
+    for (int k = 0; k < TAIL_SPLITS; ++k) s2 += st->part[tid][k][2];
+    sh.stats[tid][0] = st->row_stats[tid][0];
+    sh.stats[tid][1] = st->row_stats[tid][1];
+    sh.stats[tid][2] = st->row_stats[tid][2];
+    sh.stats[tid][3] = logf(s2);
+    st->row_stats[tid][3] = sh.stats[tid][3];
+  }
+  for (int i = tid; i < beams * NSTEPS; i += nt) {
+    const int b = i / NSTEPS, t = i % NSTEPS;
+    sh.o_tok[b][t] = st->run_tok[b][t]; sh.o_par[b][t] = st->run_par[b][t];
+    sh.f_tok[b][t] = st->fin_tok[b][t]; sh.f_par[b][t] = st->fin_par[b][t];
+  }
+  for (int b = tid; b < beams; b += nt) {
+    sh.o_score[b] = st->run_score[b];
+    sh.f_score[b] = st->fin_score[b];
+    sh.f_done[b] = st->fin_done[b];
+    for (int s = 0; s < 4; ++s) sh.o_anc[b][s] = st->anc[b][s];
+    // lookup prefix: the last tokens of the running sequence
+    long tok[3];
+    if (step == 0) {
+      for (int j = 0; j < 3; ++j) tok[j] = st->prompt_tail[j];
+    } else if (step < 4) {
+      const int n = step == 3 ? 3 : step;
+      for (int j = 0; j < n; ++j) tok[j] = st->run_tok[b][step - n + j];
+    }
+    sh.rows[b] = lookup_row(tb, step, tok);
+    sh.col0[b] = lookup_col(tb, sh.rows[b], 0);
+  }
+  if (tid == 0) { sh.finite = 0; st->width[step] = width; st->same_rows[step] = rows == 1; }
+  __syncthreads();
+
+  // 2. candidates: processed score at every allowed column
+  int finite = 0;
+  for (int i = tid; i < nc; i += nt) {
+    const int b = i / width, j = i - b * width;
+    int col = lookup_col(tb, sh.rows[b], j);
+    if (col < 0 || col >= vocab) { atomicOr(status, RTR_DEV_BAD_TOKEN); col = 0; }
+    const int r = rows == 1 ? 0 : b;
+    const float x = logits[(long)r * vocab + col];
+    const float lp1 = (x - sh.stats[r][0]) - sh.stats[r][1];
+    const float v = (lp1 - sh.stats[r][2]) - sh.stats[r][3];
+    st->cols[step][b][j] = col;
+    st->vals[step][b][j] = v;
+    float acc = v + sh.o_score[b];
+    if (acc != acc) {  // NaN would break the rank permutation below
+      atomicOr(status, RTR_DEV_NAN_SCORE);
+      acc = -INFINITY;
+    }
+    const bool dup = j > 0 && col == sh.col0[b];
+    uint64_t key = 0;
+    if (!dup) {
+      key = cand_key(acc, (uint32_t)(b * vocab + col));
+      if (acc > -INFINITY) ++finite;
+    }
+    cand[i] = key;
+  }
+  finite = (int)block_sum((float)finite, sh.red);
+  const int kk = finite < K ? finite : K;
+  if (tid == 0) {
+    if (finite < beams) atomicOr(status, RTR_DEV_FEW_FINITE);
+    sh.prefix = 0; sh.mask = 0; sh.krem = kk; sh.done = kk == 0; sh.counter = 0;
+  }
+  __syncthreads();
+
+  // 3. radix select of the kk largest keys (8-bit digits, MSB first)
+  for (int pass = 0; pass < 8 && !sh.done; ++pass) {
+    const int shift = 56 - 8 * pass;
+    for (int i = tid; i < 256; i += nt) sh.hist[i] = 0;
+    __syncthreads();
+    const uint64_t pf = sh.prefix, mk = sh.mask;
+    for (int i = tid; i < nc; i += nt) {
+      const uint64_t k = cand[i];
+      if ((k & mk) == pf) atomicAdd(&sh.hist[(k >> shift) & 255], 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      unsigned above = 0;
+      int d = 255;
+      for (; d > 0; --d) {
+        if (above + sh.hist[d] >= (unsigned)sh.krem) break;
+        above += sh.hist[d];
+      }
+      sh.krem -= (int)above;
+      sh.prefix = pf | ((uint64_t)d << shift);
+      sh.mask = mk | (0xFFull << shift);
+      if ((int)sh.hist[d] == sh.krem) sh.done = 1;
+    }
+    __syncthreads();
+  }
+  if (kk > 0) {
+    const uint64_t pf = sh.prefix, mk = sh.mask;
+    for (int i = tid; i < nc; i += nt) {
+      const uint64_t k = cand[i];
+      if (k != 0 && (k & mk) >= pf) {
+        const int pos = atomicAdd(&sh.counter, 1);
+        if (pos < K) sh.top[pos] = k;
+      }
+    }
+  }
+  __syncthreads();
+  // sort the selected keys (descending) by rank; then append -inf fillers
+  if (tid < kk) {
+    const uint64_t k = sh.top[tid];
+    int rank = 0;
+    for (int i = 0; i < kk; ++i) rank += sh.top[i] > k;
+    sh.sorted[rank] = k;
+  }
+  __syncthreads();
+  if (tid == 0 && kk < K) {
+    // -inf entries in ascending flat index: row 0's non-allowed columns
+    int c = 0;
+    for (int pos = kk; pos < K; ++pos) {
+      for (;; ++c) {
+        bool allowed = false;
+        for (int j = 0; j < width && !allowed; ++j) allowed = st->cols[step][0][j] == c;
+        if (!allowed) break;
+      }
+      sh.sorted[pos] = cand_key(-INFINITY, (uint32_t)c);
+      ++c;
+    }
+  }
+  __syncthreads();
+
+  // 4. decode candidates; EOS hits (max_length is never reached in 5 steps)
+  if (tid < K) {
+    const uint64_t k = sh.sorted[tid];
+    const uint32_t flat = ~(uint32_t)(k & 0xffffffffu);
+    const float score = key_float((uint32_t)(k >> 32));
+    int b = (int)(flat / (uint32_t)vocab);
+    if (b >= beams) { atomicOr(status, RTR_DEV_BAD_PARENT); b = 0; }
+    const int tok = (int)(flat % (uint32_t)vocab);
+    const int hit = tok == tb.eos;
+    sh.c_score[tid] = score;
+    sh.c_beam[tid] = b;
+    sh.c_tok[tid] = tok;
+    sh.c_hit[tid] = hit;
+    // _get_running_beams_for_next_iteration: topk_log_probs + hits * -1e9
+    sh.c_run[tid] = score + (hit ? -1.0e9f : -0.0f);
+    // _update_finished_beams (length_penalty 0, early_stopping False)
+    const int unsat = st->unsatisfied;
+    const int did_finish = hit && tid < beams;
+    float f = score / 1.0f + -0.0f;
+    f = f + (unsat ? -0.0f : -1.0e9f);
+    f = f + (did_finish ? -0.0f : -1.0e9f);
+    sh.c_fin[beams + tid] = f;
+  }
+  if (tid < beams) sh.c_fin[tid] = sh.f_score[tid];
+  __syncthreads();
+
+  // 5. running top-beams and finished top-beams (stable: ties keep position order;
+  //    scores are NaN-free, so the ranks form a permutation and fill every slot)
+  if (tid < beams) { sh.n_run[tid] = 0; sh.n_fin[tid] = 0; }
+  __syncthreads();
+  if (tid < K) {
+    const float r = sh.c_run[tid];
+    int rank = 0;
+    for (int i = 0; i < K; ++i) rank += (sh.c_run[i] > r) || (sh.c_run[i] == r && i < tid);
+    if (rank < beams) sh.n_run[rank] = tid;
+  }
+  if (tid < beams + K) {
+    const float f = sh.c_fin[tid];
+    int rank = 0;
+    for (int i = 0; i < beams + K; ++i) rank += (sh.c_fin[i] > f) || (sh.c_fin[i] == f && i < tid);
+    if (rank < beams) sh.n_fin[rank] = tid;
+  }
+  __syncthreads();
+
+  // 6. write the new running and finished sets
+  if (tid < beams) {
+    const int n = tid;
+    const int j = sh.n_run[n];
+    const int p = sh.c_beam[j];
+    for (int t = 0; t < NSTEPS; ++t) {
+      st->run_tok[n][t] = t < step ? sh.o_tok[p][t] : (t == step ? sh.c_tok[j] : tb.eos);
+      st->run_par[n][t] = t < step ? sh.o_par[p][t] : (t == step ? p : -1);
+    }
+    st->run_score[n] = sh.c_run[j];
+    st->next_tok[n] = sh.c_tok[j];
+    for (int s = 0; s < 4; ++s)
+      st->anc[n][s] = (s < step - 1) ? sh.o_anc[p][s] : (s == step - 1 ? p : -1);
+
+    const int m = sh.n_fin[n];
+    if (m < beams) {
+      for (int t = 0; t < NSTEPS; ++t) { st->fin_tok[n][t] = sh.f_tok[m][t]; st->fin_par[n][t] = sh.f_par[m][t]; }
+      st->fin_done[n] = sh.f_done[m];
+    } else {
+      const int c = m - beams, pc = sh.c_beam[c];
+      for (int t = 0; t < NSTEPS; ++t) {
+        st->fin_tok[n][t] = t < step ? sh.o_tok[pc][t] : (t == step ? sh.c_tok[c] : tb.eos);
+        st->fin_par[n][t] = t < step ? sh.o_par[pc][t] : (t == step ? pc : -1);
+      }
+      st->fin_done[n] = sh.c_hit[c] && c < beams;
+    }
+    st->fin_score[n] = sh.c_fin[m];
+  }
+  __syncthreads();
+
+  // 7. early-stop heuristic and the loop condition (utils.py:2876-2943)
+  if (tid == 0) {
+    float worst = INFINITY;
+    for (int b = 0; b < beams; ++b) worst = fminf(worst, st->fin_score[b]);
+    const float best_running = st->run_score[0] / 1.0f;
+    bool improvable = false;
+    for (int b = 0; b < beams; ++b) improvable |= best_running > (st->fin_done[b] ? worst : -1.0e9f);
+    const int unsat = st->unsatisfied && improvable;
+    st->unsatisfied = unsat;
+    bool all_hits = true;
+    for (int i = 0; i < K; ++i) all_hits &= sh.c_hit[i] != 0;
+    const bool running = unsat && !all_hits;
+    if (!running && st->finished_after < 0) st->finished_after = step;
+    if (step < NSTEPS - 1 && !running) atomicOr(status, RTR_DEV_STOPPED_EARLY);
+    if (step == NSTEPS - 1 && running) atomicOr(status, RTR_DEV_NOT_STOPPED);
+  }
+}
+
+cudaError_t beam_init() {
+  return cudaFuncSetAttribute(beam_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)(MAX_CAND * sizeof(uint64_t)));
+}
+
+cudaError_t beam_step(BeamState* st, const float* logits, int rows, int vocab, int beams, int step,
+                      const DevTables& tb, uint32_t* status, cudaStream_t stream) {
+  dim3 grid(rows, TAIL_SPLITS);
+  tail_max_kernel<<<grid, TAIL_THREADS, 0, stream>>>(logits, vocab, st);
+  tail_sum1_kernel<<<grid, TAIL_THREADS, 0, stream>>>(logits, vocab, st);
+  tail_sum2_kernel<<<grid, TAIL_THREADS, 0, stream>>>(logits, vocab, st);
+  const int width = lookup_width_of(tb, step);
+  const size_t need = (size_t)beams * width * sizeof(uint64_t);
+  beam_select_kernel<<<1, SEL_THREADS, need, stream>>>(st, logits, rows, vocab, beams, step, tb, status);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------ reset / output
+__global__ void beam_reset_kernel(BeamState* st, const int32_t* ids, const int32_t* L_dev, int beams) {
+  const int b = threadIdx.x;
+  if (b < beams) {
+    for (int t = 0; t < NSTEPS; ++t) {
+      st->run_tok[b][t] = -1; st->run_par[b][t] = -1;
+      st->fin_tok[b][t] = -1; st->fin_par[b][t] = -1;
+    }
+    st->run_score[b] = b == 0 ? 0.0f : -1.0e9f;
+    st->fin_score[b] = -1.0e9f;
+    st->fin_done[b] = 0;
+    for (int s = 0; s < 4; ++s) st->anc[b][s] = -1;
+  }
+  if (b == 0) {
+    const int L = *L_dev;
+    for (int j = 0; j < 3; ++j) st->prompt_tail[j] = ids[L - 3 + j];
+    st->unsatisfied = 1;
+    st->finished_after = -1;
+  }
+}
+
+cudaError_t beam_reset(BeamState* st, const int32_t* ids_dev, const int32_t* L_dev, int beams,
+                       cudaStream_t stream) {
+  beam_reset_kernel<<<1, MAX_BEAMS, 0, stream>>>(st, ids_dev, L_dev, beams);
+  return cudaGetLastError();
+}
+
+// transition_logp = scores[t][beam_indices[i][t], token[i][t]] (compute_transition_scores)
+__global__ void beam_finalize_kernel(const BeamState* st, int beams, DevResult* res, const uint32_t* status) {
+  const int i = threadIdx.x;
+  if (i < beams) {
+    for (int t = 0; t < NSTEPS; ++t) {
+      const int tok = st->fin_tok[i][t], row = st->fin_par[i][t];
+      res->token_ids[i * NSTEPS + t] = tok;
+      res->beam_indices[i * NSTEPS + t] = row;
+      float v = -INFINITY;
+      if (row >= 0 && row < beams) {
+        const int w = st->width[t];
+        for (int j = 0; j < w; ++j)
+          if (st->cols[t][row][j] == tok) { v = st->vals[t][row][j]; break; }
+      }
+      res->transition_logp[i * NSTEPS + t] = v;
+    }
+    res->sequence_logp[i] = st->fin_score[i];
+  }
+  if (i == 0) {
+    res->status = *status;
+    res->steps = st->finished_after + 1;
+  }
+}
+
+cudaError_t beam_finalize(const BeamState* st, int beams, DevResult* res, const uint32_t* status,
+                          cudaStream_t stream) {
+  beam_finalize_kernel<<<1, MAX_BEAMS, 0, stream>>>(st, beams, res, status);
+  return cudaGetLastError();
+}
+
+__global__ void dense_fill_kernel(float* out, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    out[i] = -INFINITY;
+}
+
+__global__ void dense_scatter_kernel(const BeamState* st, int step, int beams, int vocab, float* out) {
+  const int b = blockIdx.x, w = st->width[step];
+  for (int j = threadIdx.x; j < w; j += blockDim.x) {
+    const int col = st->cols[step][b][j];
+    if (col >= 0 && col < vocab) out[(long)b * vocab + col] = st->vals[step][b][j];
+  }
+}
+
+cudaError_t beam_dense_scores(const BeamState* st, int step, int beams, int vocab, float* out,
+                              cudaStream_t stream) {
+  dense_fill_kernel<<<148 * 4, 256, 0, stream>>>(out, (long)beams * vocab);
+  dense_scatter_kernel<<<beams, 256, 0, stream>>>(st, step, beams, vocab, out);
+  return cudaGetLastError();
+}
+
+// -------------------------------------------- plugin-level entry points
+__global__ void lookup_kernel(DevTables tb, int step, const int64_t* ids, int rows, int cols,
+                              int32_t* out, int width) {
+  const int r = blockIdx.x;
+  __shared__ LookupRow lr;
+  if (threadIdx.x == 0) {
+    long tok[3];
+    const int n = (step == 0 || step == 3) ? 3 : (step < 3 ? step : 0);
+    for (int j = 0; j < n; ++j) tok[j] = ids[(long)r * cols + cols - n + j];
+    lr = lookup_row(tb, step, tok);
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < width; j += blockDim.x) out[(long)r * width + j] = lookup_col(tb, lr, j);
+}
+
+cudaError_t constraint_lookup(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
+                              int32_t* out, cudaStream_t stream) {
+  lookup_kernel<<<rows, 128, 0, stream>>>(tb, step, ids, rows, cols, out, lookup_width_of(tb, step));
+  return cudaGetLastError();
+}
+
+// out = log_softmax(scores) + mask: one CTA per row, two vocabulary passes.
+__global__ void __launch_bounds__(1024) process_kernel(DevTables tb, int step, const int64_t* ids, int cols,
+                                                       const float* scores, float* out, int vocab) {
+  __shared__ float red[33];
+  __shared__ LookupRow lr;
+  const int r = blockIdx.x;
+  const float* x = scores + (long)r * vocab;
+  float* y = out + (long)r * vocab;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, x[i]);
+  m = block_max(m, red);
+  float s = 0.f;
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) s += expf(x[i] - m);
+  s = block_sum(s, red);
+  const float L = logf(s);
+  for (int i = threadIdx.x; i < vocab; i += blockDim.x) y[i] = -INFINITY;
+  if (threadIdx.x == 0) {
+    long tok[3];
+    const int n = (step == 0 || step == 3) ? 3 : (step < 3 ? step : 0);
+    for (int j = 0; j < n; ++j) tok[j] = ids[(long)r * cols + cols - n + j];
+    lr = lookup_row(tb, step, tok);
+  }
+  __syncthreads();
+  const int width = lookup_width_of(tb, step);
+  for (int j = threadIdx.x; j < width; j += blockDim.x) {
+    const int col = lookup_col(tb, lr, j);
+    if (col >= 0 && col < vocab) y[col] = ((x[col] - m) - L) + 0.0f;
+  }
+}
+
+cudaError_t constraint_process(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
+                               const float* scores, float* out, int vocab, float* scratch,
+                               cudaStream_t stream) {
+  (void)scratch;
+  process_kernel<<<rows, 1024, 0, stream>>>(tb, step, ids, cols, scores, out, vocab);
+  return cudaGetLastError();
+}
+
+}  // namespace rtr

@@ -1,0 +1,66 @@
+// Shared device helpers for the sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define RTR_DEVICE __device__ __forceinline__
+
+// Device-side status bits written to the session's status word.  Kernels
+// never trap: a failed bound check records a bit and skips the access.
+enum : uint32_t {
+  RTR_DEV_BAD_TOKEN = 1u << 0,      // token id outside [0, vocab)
+  RTR_DEV_BAD_PARENT = 1u << 1,     // parent index outside [0, beams)
+  RTR_DEV_NOT_STOPPED = 1u << 2,    // beam loop would continue after 5 steps
+  RTR_DEV_STOPPED_EARLY = 1u << 3,  // beam loop would stop before 5 steps
+  RTR_DEV_FEW_FINITE = 1u << 4,     // fewer finite candidates than beams
+  RTR_DEV_BAD_LENGTH = 1u << 5,     // prefix length outside the arena
+  RTR_DEV_TOO_MANY_CAND = 1u << 6,  // candidate buffer overflow
+  RTR_DEV_NAN_SCORE = 1u << 7,      // a NaN score (ranked as -inf)
+};
+
+RTR_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+RTR_DEVICE float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Order-preserving map float -> uint32 (larger float -> larger key; -0 < +0).
+RTR_DEVICE uint32_t float_key(float f) {
+  uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+RTR_DEVICE float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+RTR_DEVICE float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Element load/store for the two activation/weight types.
+template <typename T> RTR_DEVICE float to_f32(T v);
+template <> RTR_DEVICE float to_f32<float>(float v) { return v; }
+template <> RTR_DEVICE float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> RTR_DEVICE T from_f32(float v);
+template <> RTR_DEVICE float from_f32<float>(float v) { return v; }
+template <> RTR_DEVICE __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+RTR_DEVICE void cp_async16(void* smem, const void* gmem, bool pred) {
+  unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  int n = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+RTR_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> RTR_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait for the previous kernel's memory before reading it.
+RTR_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+RTR_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }

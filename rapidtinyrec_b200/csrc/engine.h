@@ -1,0 +1,117 @@
+// Internal declarations shared by the engine's translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace rtr {
+
+enum Epilogue : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3 };
+
+// ---- GEMM (gemm_ffma.cu) ----
+cudaError_t gemm_init();
+size_t gemm_workspace_floats(int max_m, int max_n, int sms);
+int gemm_tile_count(int max_m, int max_n);
+cudaError_t gemm_f32(const float* A, int lda, const float* W, float* C, int ldc, const float* bias,
+                     int M, int N, int K, int epi, float* ws, size_t ws_floats, int* tickets,
+                     int sms, cudaStream_t stream, bool pdl);
+cudaError_t gemv_f32(const float* x, const float* W, float* y, int N, int K, cudaStream_t stream);
+
+// ---- element-wise (elementwise.cu) ----
+cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
+                       int hidden, float* x, uint32_t* status, cudaStream_t stream);
+cudaError_t rms_norm_rows(const float* x, const float* w, float* h, int M, int hidden, float eps,
+                          cudaStream_t stream);
+// RoPE on q and k of a [M, qkv_dim] projection; q -> q_out [M, Hq*D], k/v ->
+// cache rows.  Prefill (slot < 0): row m is position m, K/V go to the prefix
+// arena [Hkv][cap][D] at position m.  Decode (slot >= 0): every row is at
+// position *L_dev + slot, K/V go to suffix slot `slot` [beams][Hkv][D].
+cudaError_t rope_kv(const float* qkv, int M, int heads, int kv_heads, int head_dim,
+                    const float* cos_t, const float* sin_t, int rope_positions,
+                    float* q_out, float* k_dst, float* v_dst, int prefix_cap,
+                    int slot, const int32_t* L_dev, uint32_t* status, cudaStream_t stream);
+cudaError_t synth_fill_device(float* dst, int64_t n, uint64_t seed, uint64_t tid, float scale,
+                              float offset, cudaStream_t stream);
+void synth_fill_host(float* dst, int64_t n, uint64_t seed, uint64_t tid, float scale, float offset);
+cudaError_t f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t stream);
+
+// ---- attention (attention.cu) ----
+cudaError_t attention_prefill(const float* q, const float* k_prefix, const float* v_prefix,
+                              float* out, int L, int prefix_cap, int heads, int kv_heads,
+                              int head_dim, float scale, cudaStream_t stream);
+// Decode attention over the shared prefix (length *L_dev) and `t` suffix
+// slots; suffix slot s of beam b lives in row anc[b*4+s] (slot t-1: row b).
+int attention_decode_chunks(int max_prefix);
+cudaError_t attention_decode(const float* q, const float* k_prefix, const float* v_prefix,
+                             const float* k_suffix, const float* v_suffix, const int32_t* anc,
+                             const int32_t* L_dev, int t, float* part, float* out, int beams,
+                             int prefix_cap, int heads, int kv_heads, int head_dim, float scale,
+                             cudaStream_t stream);
+
+// ---- constraints + beam step (beam.cu) ----
+struct DevTables {
+  int32_t offsets[3], sizes[3];
+  const int32_t* table1; int32_t width1;
+  const int32_t* table2; int32_t width2;
+  const uint8_t* valid;
+  int32_t root[3];
+  const int32_t* first_tokens; int32_t n_first;
+  int32_t newline, eos;
+};
+
+constexpr int MAX_BEAMS = 64;
+constexpr int NSTEPS = 5;
+constexpr int MAX_WIDTH = 256;
+constexpr int TAIL_SPLITS = 16;
+
+// Beam-search state in device memory (HF _beam_search running/finished sets).
+struct BeamState {
+  int32_t run_tok[MAX_BEAMS][NSTEPS];
+  int32_t run_par[MAX_BEAMS][NSTEPS];
+  float run_score[MAX_BEAMS];
+  int32_t fin_tok[MAX_BEAMS][NSTEPS];
+  int32_t fin_par[MAX_BEAMS][NSTEPS];
+  float fin_score[MAX_BEAMS];
+  int32_t fin_done[MAX_BEAMS];
+  int32_t unsatisfied;      // is_early_stop_heuristic_unsatisfied
+  int32_t finished_after;   // step after which the loop stopped (-1: running)
+  int32_t anc[MAX_BEAMS][4];  // physical suffix row of each beam's slot
+  int32_t next_tok[MAX_BEAMS];  // input token of the next forward
+  int32_t prompt_tail[3];   // last three prompt tokens (step-0 lookup)
+  // per step processed scores at the allowed columns (the only finite ones)
+  int32_t cols[NSTEPS][MAX_BEAMS][MAX_WIDTH];
+  float vals[NSTEPS][MAX_BEAMS][MAX_WIDTH];
+  int32_t width[NSTEPS];
+  int32_t same_rows[NSTEPS];  // 1: every beam row holds row 0's logits (step 0)
+  float row_stats[MAX_BEAMS][4];  // max, log-sum, max2, log-sum2
+  float part[MAX_BEAMS][TAIL_SPLITS][3];  // max, sum1, sum2 partials
+};
+
+struct DevResult {
+  int32_t token_ids[MAX_BEAMS * NSTEPS];
+  int32_t beam_indices[MAX_BEAMS * NSTEPS];
+  float sequence_logp[MAX_BEAMS];
+  float transition_logp[MAX_BEAMS * NSTEPS];
+  uint32_t status;
+  int32_t steps;
+};
+
+cudaError_t beam_init();
+cudaError_t beam_reset(BeamState* st, const int32_t* ids_dev, const int32_t* L_dev, int beams,
+                       cudaStream_t stream);
+// Full step tail on logits [rows, V] (rows = 1 at step 0, otherwise beams).
+cudaError_t beam_step(BeamState* st, const float* logits, int rows, int vocab, int beams, int step,
+                      const DevTables& tb, uint32_t* status, cudaStream_t stream);
+cudaError_t beam_finalize(const BeamState* st, int beams, DevResult* res, const uint32_t* status,
+                          cudaStream_t stream);
+cudaError_t beam_dense_scores(const BeamState* st, int step, int beams, int vocab, float* out,
+                              cudaStream_t stream);
+int lookup_width(const DevTables& tb, int step);
+cudaError_t constraint_lookup(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
+                              int32_t* out, cudaStream_t stream);
+cudaError_t constraint_process(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
+                               const float* scores, float* out, int vocab, float* scratch,
+                               cudaStream_t stream);
+
+}  // namespace rtr

@@ -1,0 +1,684 @@
+// Session state and the C ABI (include/rtr_b200.h).
+//
+// Device layout of one session (one replica of the model on one GPU):
+//   weights   embed [V,H]; per layer Wqkv [Hq*D+2*Hkv*D, H] (q, k, v rows),
+//             bias [Hq*D+2*Hkv*D], Wo [H, Hq*D], Wgu [2I, H] (gate/up rows
+//             interleaved in blocks of 16), Wd [H, I], two norms; final norm;
+//             lm_head (aliases embed when tied)
+//   prefix    [layers][K|V][Hkv][max_prefix][D]   one physical copy per request
+//   suffix    [layers][K|V][4 slots][beams][Hkv][D]   written in place per step;
+//             beams find their ancestors' slots through BeamState::anc
+//   logits    [beams, V] fp32 (L2-resident between the LM head and the tail)
+// A request is: prefill (eager launches, M = L rows) -> step-0 tail, then one
+// CUDA graph holding decode steps 1..4 (forward + tail each) and the result
+// copy; the prefix length lives in device memory so the graph serves every L.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/rtr_b200.h"
+#include "common.cuh"
+#include "engine.h"
+
+using namespace rtr;
+
+struct LayerW {
+  float *wqkv, *bqkv, *wo, *wgu, *wd, *n_in, *n_post;
+};
+
+struct rtr_session {
+  rtr_model_config cfg{};
+  int device = 0, sms = 148;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  bool pdl = true;
+  std::string err;
+  // weights
+  float *embed = nullptr, *lm_head = nullptr, *norm_final = nullptr;
+  std::vector<LayerW> layers;
+  std::vector<void*> allocs;
+  bool weights_loaded = false, tables_loaded = false;
+  // rope
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  int rope_positions = 0;
+  // tables
+  DevTables tb{};
+  int32_t *t1 = nullptr, *t2 = nullptr, *tfirst = nullptr;
+  uint8_t* tvalid = nullptr;
+  // KV and activations
+  float *kv_prefix = nullptr, *kv_suffix = nullptr;
+  float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+  float *logits = nullptr, *attn_part = nullptr, *ws = nullptr;
+  size_t ws_floats = 0;
+  int* tickets = nullptr;
+  BeamState* beam = nullptr;
+  DevResult* dres = nullptr;
+  DevResult* hres = nullptr;  // pinned
+  int32_t* d_ids = nullptr;
+  int32_t* d_L = nullptr;
+  int32_t* h_L = nullptr;     // pinned staging
+  int32_t* h_ids = nullptr;   // pinned staging [max_prefix]
+  uint32_t* d_status = nullptr;
+  // request state
+  int L = 0;
+  int steps_done = -1;
+  bool in_flight = false;
+  cudaGraphExec_t graph = nullptr;
+  // counters (rtr_get_report)
+  int64_t requests = 0, launches = 0, graph_kernels = 0;
+  int64_t weight_bytes = 0, device_bytes = 0;
+};
+
+static std::string g_create_error;
+
+static int fail(rtr_session* s, int code, const std::string& msg) {
+  if (s) s->err = msg; else g_create_error = msg;
+  return code;
+}
+
+#define CUDA_TRY(s, expr)                                                                 \
+  do {                                                                                    \
+    cudaError_t _e = (expr);                                                              \
+    if (_e != cudaSuccess)                                                                \
+      return fail((s), RTR_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
+  } while (0)
+
+template <typename T>
+static cudaError_t dev_alloc(rtr_session* s, T** p, size_t count) {
+  void* raw = nullptr;
+  cudaError_t e = cudaMalloc(&raw, count * sizeof(T) + 256);
+  if (e != cudaSuccess) return e;
+  s->allocs.push_back(raw);
+  s->device_bytes += (int64_t)(count * sizeof(T) + 256);
+  *p = static_cast<T*>(raw);
+  return cudaSuccess;
+}
+
+static int beams_of(const rtr_session* s) { return s->cfg.num_beams; }
+static int qkv_dim(const rtr_model_config& c) { return (c.heads + 2 * c.kv_heads) * c.head_dim; }
+
+static void default_rope(const rtr_model_config& c, int n, std::vector<float>& cs, std::vector<float>& sn) {
+  const int half = c.head_dim / 2;
+  cs.resize((size_t)n * half);
+  sn.resize((size_t)n * half);
+  for (int i = 0; i < half; ++i) {
+    const float expo = (float)(2 * i) / (float)c.head_dim;
+    const float inv = (float)(1.0 / std::pow((double)c.rope_theta, (double)expo));
+    for (int p = 0; p < n; ++p) {
+      const float ang = inv * (float)p;
+      cs[(size_t)p * half + i] = (float)std::cos((double)ang);
+      sn[(size_t)p * half + i] = (float)std::sin((double)ang);
+    }
+  }
+}
+
+extern "C" {
+
+const char* rtr_last_error(const rtr_session* s) { return s ? s->err.c_str() : g_create_error.c_str(); }
+
+int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** out) {
+  if (!cfg || !out) return fail(nullptr, RTR_ERR_ARG, "null config or output pointer");
+  const rtr_model_config& c = *cfg;
+  if (c.layers < 1 || c.hidden < 16 || c.heads < 1 || c.kv_heads < 1 || c.vocab < 16)
+    return fail(nullptr, RTR_ERR_ARG, "non-positive model dimension");
+  if (c.heads % c.kv_heads) return fail(nullptr, RTR_ERR_ARG, "heads must be a multiple of kv_heads");
+  if (c.head_dim != 64 && c.head_dim != 128) return fail(nullptr, RTR_ERR_ARG, "head_dim must be 64 or 128");
+  if (c.hidden % 16 || c.intermediate % 16 || (c.heads * c.head_dim) % 16)
+    return fail(nullptr, RTR_ERR_ARG, "hidden, intermediate and heads*head_dim must be multiples of 16");
+  if (c.num_beams < 1 || c.num_beams > MAX_BEAMS) return fail(nullptr, RTR_ERR_ARG, "num_beams must be in [1, 64]");
+  if (c.max_prefix < 3 || c.max_prefix > 32768) return fail(nullptr, RTR_ERR_ARG, "max_prefix must be in [3, 32768]");
+  if ((long)c.num_beams * c.vocab >= (1L << 32)) return fail(nullptr, RTR_ERR_ARG, "beams*vocab must fit 32 bits");
+  if (c.dtype != RTR_DTYPE_F32) return fail(nullptr, RTR_ERR_ARG, "this build serves dtype RTR_DTYPE_F32 only");
+
+  auto* s = new rtr_session();
+  s->cfg = c;
+  s->device = device;
+  auto bail = [&](int code) {
+    g_create_error = s->err;
+    rtr_session_destroy(s);
+    return code;
+  };
+#define CREATE_TRY(expr)                                                              \
+  do {                                                                                \
+    cudaError_t _e = (expr);                                                          \
+    if (_e != cudaSuccess) {                                                          \
+      s->err = std::string(#expr) + ": " + cudaGetErrorString(_e);                    \
+      return bail(RTR_ERR_CUDA);                                                      \
+    }                                                                                 \
+  } while (0)
+  CREATE_TRY(cudaSetDevice(device));
+  CREATE_TRY(cudaDeviceGetAttribute(&s->sms, cudaDevAttrMultiProcessorCount, device));
+  CREATE_TRY(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+  s->own_stream = true;
+  CREATE_TRY(gemm_init());
+  CREATE_TRY(beam_init());
+
+  const long H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
+  const long qd = (long)c.heads * D, kvd = (long)c.kv_heads * D, qkvd = qkv_dim(c);
+  const long B = c.num_beams, cap = c.max_prefix;
+  const long M = cap > B ? cap : B;
+  CREATE_TRY(dev_alloc(s, &s->embed, V * H));
+  s->layers.resize(c.layers);
+  for (auto& l : s->layers) {
+    CREATE_TRY(dev_alloc(s, &l.wqkv, qkvd * H));
+    CREATE_TRY(dev_alloc(s, &l.bqkv, qkvd));
+    CREATE_TRY(dev_alloc(s, &l.wo, H * qd));
+    CREATE_TRY(dev_alloc(s, &l.wgu, 2 * I * H));
+    CREATE_TRY(dev_alloc(s, &l.wd, H * I));
+    CREATE_TRY(dev_alloc(s, &l.n_in, H));
+    CREATE_TRY(dev_alloc(s, &l.n_post, H));
+  }
+  CREATE_TRY(dev_alloc(s, &s->norm_final, H));
+  if (c.tied_embeddings) s->lm_head = s->embed;
+  else CREATE_TRY(dev_alloc(s, &s->lm_head, V * H));
+  s->weight_bytes = s->device_bytes;
+
+  CREATE_TRY(dev_alloc(s, &s->kv_prefix, (size_t)c.layers * 2 * kvd * cap));
+  CREATE_TRY(dev_alloc(s, &s->kv_suffix, (size_t)c.layers * 2 * 4 * B * kvd));
+  CREATE_TRY(dev_alloc(s, &s->x, M * H));
+  CREATE_TRY(dev_alloc(s, &s->h, M * H));
+  CREATE_TRY(dev_alloc(s, &s->qkv, M * qkvd));
+  CREATE_TRY(dev_alloc(s, &s->q, M * qd));
+  CREATE_TRY(dev_alloc(s, &s->attn, M * qd));
+  CREATE_TRY(dev_alloc(s, &s->act, M * I));
+  CREATE_TRY(dev_alloc(s, &s->logits, B * V));
+  CREATE_TRY(dev_alloc(s, &s->attn_part, (size_t)B * c.heads * attention_decode_chunks(cap) * (D + 2)));
+  long max_n = qkvd;
+  if (H > max_n) max_n = H;
+  if (2 * I > max_n) max_n = 2 * I;
+  s->ws_floats = gemm_workspace_floats(64, (int)max_n, s->sms);
+  CREATE_TRY(dev_alloc(s, &s->ws, s->ws_floats));
+  CREATE_TRY(dev_alloc(s, &s->tickets, 4096));
+  CREATE_TRY(cudaMemset(s->tickets, 0, 4096 * sizeof(int)));
+  CREATE_TRY(dev_alloc(s, &s->beam, 1));
+  CREATE_TRY(cudaMemset(s->beam, 0, sizeof(BeamState)));
+  CREATE_TRY(dev_alloc(s, &s->dres, 1));
+  CREATE_TRY(dev_alloc(s, &s->d_ids, cap));
+  CREATE_TRY(dev_alloc(s, &s->d_L, 1));
+  CREATE_TRY(dev_alloc(s, &s->d_status, 1));
+  CREATE_TRY(cudaMemset(s->d_status, 0, sizeof(uint32_t)));
+  CREATE_TRY(cudaMallocHost(&s->hres, sizeof(DevResult)));
+  CREATE_TRY(cudaMallocHost(&s->h_L, sizeof(int32_t)));
+  CREATE_TRY(cudaMallocHost(&s->h_ids, cap * sizeof(int32_t)));
+
+  s->rope_positions = (int)cap + 8;
+  CREATE_TRY(dev_alloc(s, &s->rope_cos, (size_t)s->rope_positions * D / 2));
+  CREATE_TRY(dev_alloc(s, &s->rope_sin, (size_t)s->rope_positions * D / 2));
+  std::vector<float> cs, sn;
+  default_rope(c, s->rope_positions, cs, sn);
+  CREATE_TRY(cudaMemcpy(s->rope_cos, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
+  CREATE_TRY(cudaMemcpy(s->rope_sin, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+#undef CREATE_TRY
+  *out = s;
+  return RTR_OK;
+}
+
+int rtr_session_destroy(rtr_session* s) {
+  if (!s) return RTR_OK;
+  cudaSetDevice(s->device);
+  if (s->graph) cudaGraphExecDestroy(s->graph);
+  for (void* p : s->allocs) cudaFree(p);
+  if (s->tvalid) cudaFree(s->tvalid);
+  if (s->t1) cudaFree(s->t1);
+  if (s->t2) cudaFree(s->t2);
+  if (s->tfirst) cudaFree(s->tfirst);
+  if (s->hres) cudaFreeHost(s->hres);
+  if (s->h_L) cudaFreeHost(s->h_L);
+  if (s->h_ids) cudaFreeHost(s->h_ids);
+  if (s->own_stream && s->stream) cudaStreamDestroy(s->stream);
+  delete s;
+  return RTR_OK;
+}
+
+int rtr_set_stream(rtr_session* s, void* stream) {
+  if (!s) return RTR_ERR_ARG;
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+  if (s->own_stream) { cudaStreamDestroy(s->stream); s->own_stream = false; }
+  if (stream) {
+    s->stream = static_cast<cudaStream_t>(stream);
+  } else {
+    CUDA_TRY(s, cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+    s->own_stream = true;
+  }
+  return RTR_OK;
+}
+
+int rtr_load_rope(rtr_session* s, const float* cos_host, const float* sin_host, int32_t n_positions) {
+  if (!s || !cos_host || !sin_host) return RTR_ERR_ARG;
+  if (n_positions < s->rope_positions)
+    return fail(s, RTR_ERR_ARG, "rope table must cover max_prefix + 8 positions");
+  const size_t bytes = (size_t)s->rope_positions * s->cfg.head_dim / 2 * sizeof(float);
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  CUDA_TRY(s, cudaMemcpy(s->rope_cos, cos_host, bytes, cudaMemcpyHostToDevice));
+  CUDA_TRY(s, cudaMemcpy(s->rope_sin, sin_host, bytes, cudaMemcpyHostToDevice));
+  return RTR_OK;
+}
+
+int rtr_load_weights(rtr_session* s, const void* const* tensors, int32_t n_tensors, int32_t src_dtype,
+                     int32_t src_on_device) {
+  if (!s || !tensors) return RTR_ERR_ARG;
+  const auto& c = s->cfg;
+  const int expect = 1 + 12 * c.layers + 1 + (c.tied_embeddings ? 0 : 1);
+  if (n_tensors != expect) return fail(s, RTR_ERR_ARG, "expected " + std::to_string(expect) + " weight tensors");
+  if (src_dtype != RTR_DTYPE_F32) return fail(s, RTR_ERR_ARG, "weights must be float32 for this build");
+  for (int i = 0; i < n_tensors; ++i)
+    if (!tensors[i]) return fail(s, RTR_ERR_ARG, "null weight tensor " + std::to_string(i));
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  const size_t H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
+  const size_t qd = c.heads * D, kvd = c.kv_heads * D;
+  const size_t f = sizeof(float);
+  auto cp = [&](void* dst, const void* src, size_t n) { return cudaMemcpy(dst, src, n * f, kind); };
+  CUDA_TRY(s, cp(s->embed, tensors[0], V * H));
+  for (int l = 0; l < c.layers; ++l) {
+    const void* const* t = tensors + 1 + 12 * l;
+    LayerW& w = s->layers[l];
+    CUDA_TRY(s, cp(w.wqkv, t[0], qd * H));
+    CUDA_TRY(s, cp(w.bqkv, t[1], qd));
+    CUDA_TRY(s, cp(w.wqkv + qd * H, t[2], kvd * H));
+    CUDA_TRY(s, cp(w.bqkv + qd, t[3], kvd));
+    CUDA_TRY(s, cp(w.wqkv + (qd + kvd) * H, t[4], kvd * H));
+    CUDA_TRY(s, cp(w.bqkv + qd + kvd, t[5], kvd));
+    CUDA_TRY(s, cp(w.wo, t[6], H * qd));
+    // gate/up interleaved in blocks of 16 rows
+    CUDA_TRY(s, cudaMemcpy2D(w.wgu, 32 * H * f, t[7], 16 * H * f, 16 * H * f, I / 16, kind));
+    CUDA_TRY(s, cudaMemcpy2D(w.wgu + 16 * H, 32 * H * f, t[8], 16 * H * f, 16 * H * f, I / 16, kind));
+    CUDA_TRY(s, cp(w.wd, t[9], H * I));
+    CUDA_TRY(s, cp(w.n_in, t[10], H));
+    CUDA_TRY(s, cp(w.n_post, t[11], H));
+  }
+  CUDA_TRY(s, cp(s->norm_final, tensors[1 + 12 * c.layers], H));
+  if (!c.tied_embeddings) CUDA_TRY(s, cp(s->lm_head, tensors[2 + 12 * c.layers], V * H));
+  CUDA_TRY(s, cudaDeviceSynchronize());
+  s->weights_loaded = true;
+  return RTR_OK;
+}
+
+int rtr_load_constraints(rtr_session* s, const rtr_constraint_tables* t) {
+  if (!s || !t) return RTR_ERR_ARG;
+  const auto& c = s->cfg;
+  long prod = 1;
+  for (int i = 0; i < 3; ++i) {
+    if (t->sizes[i] < 1) return fail(s, RTR_ERR_ARG, "SID level sizes must be positive");
+    prod *= t->sizes[i];
+  }
+  if (prod > 100000000L) return fail(s, RTR_ERR_ARG, "Dense SID-validity table too large for this implementation");
+  if (t->width1 < 1 || t->width1 > MAX_WIDTH || t->width2 < 1 || t->width2 > MAX_WIDTH ||
+      t->n_first < 1 || t->n_first > MAX_WIDTH)
+    return fail(s, RTR_ERR_ARG, "lookup widths must be in [1, 256]");
+  if (!t->table1 || !t->table2 || !t->valid || !t->first_tokens) return fail(s, RTR_ERR_ARG, "null table");
+  auto in_vocab = [&](int v) { return v >= 0 && v < c.vocab; };
+  if (!in_vocab(t->newline) || !in_vocab(t->eos)) return fail(s, RTR_ERR_ARG, "newline/eos outside the vocabulary");
+  // every row: sorted unique tokens, then repeats of its first token (gpu_constraints.py:51-54)
+  auto check_rows = [&](const int32_t* tab, long rows, int w) -> bool {
+    for (long r = 0; r < rows; ++r) {
+      const int32_t* row = tab + r * w;
+      bool pad = false;
+      for (int j = 0; j < w; ++j) {
+        if (!in_vocab(row[j])) return false;
+        if (j == 0) continue;
+        if (row[j] == row[0]) pad = true;
+        else if (pad || row[j] <= row[j - 1]) return false;
+      }
+    }
+    return true;
+  };
+  const long rows1 = t->sizes[0], rows2 = (long)t->sizes[0] * t->sizes[1];
+  if (!check_rows(t->table1, rows1, t->width1) || !check_rows(t->table2, rows2, t->width2) ||
+      !check_rows(t->first_tokens, 1, t->n_first))
+    return fail(s, RTR_ERR_ARG, "table rows must be sorted unique tokens padded with their first token");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  if (s->t1) { cudaFree(s->t1); cudaFree(s->t2); cudaFree(s->tfirst); cudaFree(s->tvalid); }
+  CUDA_TRY(s, cudaMalloc(&s->t1, rows1 * t->width1 * sizeof(int32_t)));
+  CUDA_TRY(s, cudaMalloc(&s->t2, rows2 * t->width2 * sizeof(int32_t)));
+  CUDA_TRY(s, cudaMalloc(&s->tfirst, t->n_first * sizeof(int32_t)));
+  CUDA_TRY(s, cudaMalloc(&s->tvalid, prod));
+  CUDA_TRY(s, cudaMemcpy(s->t1, t->table1, rows1 * t->width1 * sizeof(int32_t), cudaMemcpyHostToDevice));
+  CUDA_TRY(s, cudaMemcpy(s->t2, t->table2, rows2 * t->width2 * sizeof(int32_t), cudaMemcpyHostToDevice));
+  CUDA_TRY(s, cudaMemcpy(s->tfirst, t->first_tokens, t->n_first * sizeof(int32_t), cudaMemcpyHostToDevice));
+  CUDA_TRY(s, cudaMemcpy(s->tvalid, t->valid, prod, cudaMemcpyHostToDevice));
+  DevTables& d = s->tb;
+  for (int i = 0; i < 3; ++i) { d.offsets[i] = t->offsets[i]; d.sizes[i] = t->sizes[i]; d.root[i] = t->root[i]; }
+  d.table1 = s->t1; d.width1 = t->width1;
+  d.table2 = s->t2; d.width2 = t->width2;
+  d.valid = s->tvalid;
+  d.first_tokens = s->tfirst; d.n_first = t->n_first;
+  d.newline = t->newline; d.eos = t->eos;
+  if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+  s->tables_loaded = true;
+  return RTR_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ forward
+static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W, float* C, int ldc,
+                        const float* bias, int M, int N, int K, int epi) {
+  return gemm_f32(A, lda, W, C, ldc, bias, M, N, K, epi, s->ws, s->ws_floats, s->tickets, s->sms,
+                  s->stream, s->pdl);
+}
+
+#define FWD_TRY(expr)                      \
+  do {                                     \
+    cudaError_t _e = (expr);               \
+    if (_e != cudaSuccess) return _e;      \
+  } while (0)
+
+// t = 0: prefill of L rows (host L); t >= 1: decode step with beams rows.
+static cudaError_t forward(rtr_session* s, int t) {
+  const auto& c = s->cfg;
+  const int H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
+  const int qd = c.heads * D, kvd = c.kv_heads * D, qkvd = qkv_dim(c);
+  const int B = beams_of(s), cap = c.max_prefix;
+  const int M = t == 0 ? s->L : B;
+  const float scale = (float)std::pow((double)D, -0.5);
+  cudaStream_t st = s->stream;
+  const int32_t* ids = t == 0 ? s->d_ids : &s->beam->next_tok[0];
+  FWD_TRY(embed_rows(ids, 1, M, s->embed, V, H, s->x, s->d_status, st));
+  for (int l = 0; l < c.layers; ++l) {
+    const LayerW& w = s->layers[l];
+    float* kp = s->kv_prefix + (size_t)l * 2 * kvd * cap;
+    float* vp = kp + (size_t)kvd * cap;
+    float* ks = s->kv_suffix + (size_t)l * 2 * 4 * B * kvd;
+    float* vs = ks + (size_t)4 * B * kvd;
+    FWD_TRY(rms_norm_rows(s->x, w.n_in, s->h, M, H, c.rms_eps, st));
+    FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));
+    if (t == 0) {
+      FWD_TRY(rope_kv(s->qkv, M, c.heads, c.kv_heads, D, s->rope_cos, s->rope_sin, s->rope_positions,
+                      s->q, kp, vp, cap, -1, s->d_L, s->d_status, st));
+      FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, M, cap, c.heads, c.kv_heads, D, scale, st));
+    } else {
+      const size_t slot = (size_t)(t - 1) * B * kvd;
+      FWD_TRY(rope_kv(s->qkv, M, c.heads, c.kv_heads, D, s->rope_cos, s->rope_sin, s->rope_positions,
+                      s->q, ks + slot, vs + slot, cap, t - 1, s->d_L, s->d_status, st));
+      FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn_part,
+                               s->attn, B, cap, c.heads, c.kv_heads, D, scale, st));
+    }
+    FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID));
+    FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, M, H, c.rms_eps, st));
+    FWD_TRY(gemm(s, s->h, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
+    FWD_TRY(gemm(s, s->act, I, w.wd, s->x, H, nullptr, M, H, I, EPI_RESID));
+  }
+  if (t == 0) {
+    FWD_TRY(rms_norm_rows(s->x + (size_t)(M - 1) * H, s->norm_final, s->h, 1, H, c.rms_eps, st));
+    FWD_TRY(gemv_f32(s->h, s->lm_head, s->logits, V, H, st));
+  } else {
+    FWD_TRY(rms_norm_rows(s->x, s->norm_final, s->h, B, H, c.rms_eps, st));
+    FWD_TRY(gemm(s, s->h, H, s->lm_head, s->logits, V, nullptr, B, V, H, EPI_STORE));
+  }
+  return cudaSuccess;
+}
+
+static cudaError_t decode_and_tail(rtr_session* s, int t) {
+  FWD_TRY(forward(s, t));
+  return beam_step(s->beam, s->logits, beams_of(s), s->cfg.vocab, beams_of(s), t, s->tb, s->d_status, s->stream);
+}
+
+static cudaError_t finalize_and_copy(rtr_session* s) {
+  FWD_TRY(beam_finalize(s->beam, beams_of(s), s->dres, s->d_status, s->stream));
+  return cudaMemcpyAsync(s->hres, s->dres, sizeof(DevResult), cudaMemcpyDeviceToHost, s->stream);
+}
+
+static int ready(rtr_session* s) {
+  if (!s->weights_loaded) return fail(s, RTR_ERR_STATE, "weights not loaded");
+  if (!s->tables_loaded) return fail(s, RTR_ERR_STATE, "constraint tables not loaded");
+  return RTR_OK;
+}
+
+static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t on_device) {
+  if (!ids) return fail(s, RTR_ERR_ARG, "null ids");
+  if (L < 3 || L > s->cfg.max_prefix)
+    return fail(s, RTR_ERR_ARG, "Expected one complete history within prefix capacity (3 <= L <= max_prefix)");
+  if (int r = ready(s)) return r;
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  s->L = L;
+  *s->h_L = L;
+  CUDA_TRY(s, cudaMemcpyAsync(s->d_L, s->h_L, sizeof(int32_t), cudaMemcpyHostToDevice, s->stream));
+  CUDA_TRY(s, cudaMemcpyAsync(s->d_ids, ids, (size_t)L * sizeof(int32_t),
+                              on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s->stream));
+  CUDA_TRY(s, cudaMemsetAsync(s->d_status, 0, sizeof(uint32_t), s->stream));
+  CUDA_TRY(s, beam_reset(s->beam, s->d_ids, s->d_L, beams_of(s), s->stream));
+  CUDA_TRY(s, forward(s, 0));
+  CUDA_TRY(s, beam_step(s->beam, s->logits, 1, s->cfg.vocab, beams_of(s), 0, s->tb, s->d_status, s->stream));
+  s->launches += 1 + (1 + 8 * (int64_t)s->cfg.layers + 2) + 4;
+  s->steps_done = 0;
+  s->in_flight = false;
+  return RTR_OK;
+}
+
+static int check_result(rtr_session* s, const rtr_result* out) {
+  const DevResult& r = *s->hres;
+  const uint32_t st = r.status;
+  if (st & (RTR_DEV_BAD_TOKEN | RTR_DEV_BAD_PARENT | RTR_DEV_BAD_LENGTH | RTR_DEV_TOO_MANY_CAND | RTR_DEV_NAN_SCORE))
+    return fail(s, RTR_ERR_DEVICE, "device bound check failed (status 0x" + std::to_string(st) + ")");
+  if (st & RTR_DEV_NOT_STOPPED)
+    return fail(s, RTR_ERR_DEVICE, "beam search would continue after 5 steps (catalog grammar is not 3 SID tokens + newline + EOS)");
+  if (st & RTR_DEV_STOPPED_EARLY)
+    return fail(s, RTR_ERR_DEVICE, "beam search stopped before 5 steps");
+  const int B = beams_of(s);
+  if (out) {
+    if (out->token_ids) memcpy(out->token_ids, r.token_ids, sizeof(int32_t) * B * NSTEPS);
+    if (out->beam_indices) memcpy(out->beam_indices, r.beam_indices, sizeof(int32_t) * B * NSTEPS);
+    if (out->sequence_logp) memcpy(out->sequence_logp, r.sequence_logp, sizeof(float) * B);
+    if (out->transition_logp) memcpy(out->transition_logp, r.transition_logp, sizeof(float) * B * NSTEPS);
+  }
+  s->err = (st & RTR_DEV_FEW_FINITE) ? "warning: fewer finite candidates than beams at some step" : "";
+  return RTR_OK;
+}
+
+extern "C" {
+
+int rtr_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t ids_on_device) {
+  if (!s) return RTR_ERR_ARG;
+  return stage_prefill(s, ids, L, ids_on_device);
+}
+
+int rtr_decode_step(rtr_session* s, int32_t t) {
+  if (!s) return RTR_ERR_ARG;
+  if (t < 1 || t >= NSTEPS) return fail(s, RTR_ERR_ARG, "decode step must be in 1..4");
+  if (s->steps_done != t - 1) return fail(s, RTR_ERR_STATE, "decode steps must follow prefill in order");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  CUDA_TRY(s, decode_and_tail(s, t));
+  s->launches += (1 + 9 * (int64_t)s->cfg.layers + 2) + 4;
+  s->steps_done = t;
+  return RTR_OK;
+}
+
+int rtr_read_results(rtr_session* s, const rtr_result* out) {
+  if (!s) return RTR_ERR_ARG;
+  if (s->steps_done != NSTEPS - 1) return fail(s, RTR_ERR_STATE, "all four decode steps must run first");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  CUDA_TRY(s, finalize_and_copy(s));
+  s->launches += 1;
+  CUDA_TRY(s, cudaStreamSynchronize(s->stream));
+  return check_result(s, out);
+}
+
+int rtr_launch(rtr_session* s, const int32_t* ids, int32_t L, int32_t ids_on_device) {
+  if (!s) return RTR_ERR_ARG;
+  if (!ids) return fail(s, RTR_ERR_ARG, "null ids");
+  if (L < 3 || L > s->cfg.max_prefix)
+    return fail(s, RTR_ERR_ARG, "Expected one complete history within prefix capacity (3 <= L <= max_prefix)");
+  if (int r = ready(s)) return r;
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  if (!s->graph) {
+    cudaGraph_t g = nullptr;
+    CUDA_TRY(s, cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+    cudaError_t e = cudaSuccess;
+    for (int t = 1; t < NSTEPS && e == cudaSuccess; ++t) e = decode_and_tail(s, t);
+    if (e == cudaSuccess) e = finalize_and_copy(s);
+    cudaError_t e2 = cudaStreamEndCapture(s->stream, &g);
+    if (e != cudaSuccess || e2 != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return fail(s, RTR_ERR_CUDA, std::string("decode graph capture: ") +
+                                       cudaGetErrorString(e != cudaSuccess ? e : e2));
+    }
+    size_t n = 0;
+    cudaGraphGetNodes(g, nullptr, &n);
+    std::vector<cudaGraphNode_t> nodes(n);
+    cudaGraphGetNodes(g, nodes.data(), &n);
+    s->graph_kernels = 0;
+    for (auto node : nodes) {
+      cudaGraphNodeType ty;
+      if (cudaGraphNodeGetType(node, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++s->graph_kernels;
+    }
+    e = cudaGraphInstantiate(&s->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { s->graph = nullptr; return fail(s, RTR_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e)); }
+  }
+  // Device ids may be queued behind a request in flight (stream order keeps
+  // them apart); host ids reuse the pinned staging buffer, so wait first.
+  if (s->in_flight && !ids_on_device) CUDA_TRY(s, cudaStreamSynchronize(s->stream));
+  const int32_t* src = ids;
+  if (!ids_on_device) {
+    // stage the prompt through pinned memory so the copy is asynchronous
+    memcpy(s->h_ids, ids, (size_t)L * sizeof(int32_t));
+    src = s->h_ids;
+  }
+  if (int r = stage_prefill(s, src, L, ids_on_device)) return r;
+  CUDA_TRY(s, cudaGraphLaunch(s->graph, s->stream));
+  s->launches += s->graph_kernels;
+  s->requests += 1;
+  s->steps_done = NSTEPS - 1;
+  s->in_flight = true;
+  return RTR_OK;
+}
+
+int rtr_wait(rtr_session* s, const rtr_result* out) {
+  if (!s) return RTR_ERR_ARG;
+  if (!s->in_flight) return fail(s, RTR_ERR_STATE, "no request in flight");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  s->in_flight = false;
+  CUDA_TRY(s, cudaStreamSynchronize(s->stream));
+  return check_result(s, out);
+}
+
+int rtr_generate(rtr_session* s, const int32_t* ids_host, int32_t L, const rtr_result* out) {
+  if (int r = rtr_launch(s, ids_host, L, 0)) return r;
+  return rtr_wait(s, out);
+}
+
+int rtr_get_report(const rtr_session* s, rtr_report* out) {
+  if (!s || !out) return RTR_ERR_ARG;
+  const auto& c = s->cfg;
+  const int64_t kvd = (int64_t)c.kv_heads * c.head_dim, B = c.num_beams;
+  const int64_t per_layer_prefill = 8, per_layer_decode = 9, tail = 4;
+  memset(out, 0, sizeof(*out));
+  out->requests = s->requests;
+  out->kernel_launches = s->launches;
+  out->launches_per_request = 1 + (1 + per_layer_prefill * c.layers + 2) + tail +
+                              (NSTEPS - 1) * ((1 + per_layer_decode * c.layers + 2) + tail) + 1;
+  out->graph_kernel_nodes = s->graph_kernels;
+  out->prefix_bytes_written = (int64_t)c.layers * 2 * kvd * s->L * (int64_t)sizeof(float);
+  out->prefix_bytes_reordered = 0;
+  out->suffix_bytes_written = (int64_t)c.layers * 2 * kvd * B * (NSTEPS - 1) * (int64_t)sizeof(float);
+  out->suffix_bytes_gathered = 0;
+  out->weight_bytes = s->weight_bytes;
+  out->device_bytes = s->device_bytes;
+  out->h2d_bytes_per_request = (int64_t)s->L * 4 + 4;
+  out->d2h_bytes_per_request = (int64_t)sizeof(DevResult);
+  return RTR_OK;
+}
+
+int rtr_profile_gemms(rtr_session* s, int32_t M, int32_t reps, float* ms_per_pass) {
+  if (!s || !ms_per_pass || reps < 1) return RTR_ERR_ARG;
+  if (M < 1 || M > (s->cfg.max_prefix > s->cfg.num_beams ? s->cfg.max_prefix : s->cfg.num_beams))
+    return fail(s, RTR_ERR_ARG, "M outside the activation buffers");
+  if (s->in_flight) return fail(s, RTR_ERR_STATE, "request in flight");
+  if (!s->weights_loaded) return fail(s, RTR_ERR_STATE, "weights not loaded");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  const auto& c = s->cfg;
+  const int H = c.hidden, I = c.intermediate, qd = c.heads * c.head_dim, qkvd = qkv_dim(c);
+  cudaEvent_t a, b;
+  CUDA_TRY(s, cudaEventCreate(&a));
+  CUDA_TRY(s, cudaEventCreate(&b));
+  auto pass = [&]() -> cudaError_t {
+    for (int l = 0; l < c.layers; ++l) {
+      const LayerW& w = s->layers[l];
+      FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));
+      FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_STORE));
+      FWD_TRY(gemm(s, s->h, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
+      FWD_TRY(gemm(s, s->act, I, w.wd, s->x, H, nullptr, M, H, I, EPI_STORE));
+    }
+    return gemm(s, s->h, H, s->lm_head, s->logits, c.vocab, nullptr, M < c.num_beams ? M : c.num_beams,
+                c.vocab, H, EPI_STORE);
+  };
+  cudaError_t e = pass();  // warm-up
+  if (e == cudaSuccess) e = cudaEventRecord(a, s->stream);
+  for (int r = 0; r < reps && e == cudaSuccess; ++r) e = pass();
+  if (e == cudaSuccess) e = cudaEventRecord(b, s->stream);
+  if (e == cudaSuccess) e = cudaEventSynchronize(b);
+  float ms = 0.f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (e != cudaSuccess) return fail(s, RTR_ERR_CUDA, std::string("profile: ") + cudaGetErrorString(e));
+  *ms_per_pass = ms / reps;
+  return RTR_OK;
+}
+
+int rtr_step_scores(rtr_session* s, int32_t t, float* out_dev) {
+  if (!s || !out_dev) return RTR_ERR_ARG;
+  if (t < 0 || t >= NSTEPS) return fail(s, RTR_ERR_ARG, "step must be in 0..4");
+  if (s->steps_done < t) return fail(s, RTR_ERR_STATE, "step has not run");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  CUDA_TRY(s, beam_dense_scores(s->beam, t, beams_of(s), s->cfg.vocab, out_dev, s->stream));
+  CUDA_TRY(s, cudaStreamSynchronize(s->stream));
+  return RTR_OK;
+}
+
+int rtr_lookup_width(const rtr_session* s, int32_t step, int32_t* width) {
+  if (!s || !width || !s->tables_loaded || step < 0) return RTR_ERR_ARG;
+  *width = lookup_width(s->tb, step);
+  return RTR_OK;
+}
+
+int rtr_constraint_lookup(rtr_session* s, int32_t step, const int64_t* input_ids_dev, int32_t rows,
+                          int32_t cols, int32_t* out_dev) {
+  if (!s || !input_ids_dev || !out_dev || rows < 1) return RTR_ERR_ARG;
+  if (!s->tables_loaded) return fail(s, RTR_ERR_STATE, "constraint tables not loaded");
+  if (step < 0) return fail(s, RTR_ERR_ARG, "negative step");
+  const int need = (step == 0 || step == 3) ? 3 : (step < 3 ? step : 0);
+  if (cols < need) return fail(s, RTR_ERR_ARG, "input_ids shorter than the step's prefix");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  CUDA_TRY(s, constraint_lookup(s->tb, step, input_ids_dev, rows, cols, out_dev, s->stream));
+  CUDA_TRY(s, cudaStreamSynchronize(s->stream));
+  return RTR_OK;
+}
+
+int rtr_constraint_process(rtr_session* s, int32_t step, const int64_t* input_ids_dev, int32_t rows,
+                           int32_t cols, const float* scores_dev, float* out_dev) {
+  if (!s || !input_ids_dev || !scores_dev || !out_dev || rows < 1) return RTR_ERR_ARG;
+  if (!s->tables_loaded) return fail(s, RTR_ERR_STATE, "constraint tables not loaded");
+  if (scores_dev == out_dev) return fail(s, RTR_ERR_ARG, "output aliases the scores");
+  if (step < 0) return fail(s, RTR_ERR_ARG, "negative step");
+  const int need = (step == 0 || step == 3) ? 3 : (step < 3 ? step : 0);
+  if (cols < need) return fail(s, RTR_ERR_ARG, "input_ids shorter than the step's prefix");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  CUDA_TRY(s, constraint_process(s->tb, step, input_ids_dev, rows, cols, scores_dev, out_dev, s->cfg.vocab,
+                                 nullptr, s->stream));
+  CUDA_TRY(s, cudaStreamSynchronize(s->stream));
+  return RTR_OK;
+}
+
+int rtr_synth_fill_host(float* dst, int64_t n, uint64_t seed, uint64_t tid, float scale, float offset) {
+  if (!dst || n < 0) return RTR_ERR_ARG;
+  synth_fill_host(dst, n, seed, tid, scale, offset);
+  return RTR_OK;
+}
+
+int rtr_synth_fill_device(float* dst_dev, int64_t n, uint64_t seed, uint64_t tid, float scale, float offset,
+                          void* stream) {
+  if (!dst_dev || n < 0) return RTR_ERR_ARG;
+  cudaError_t e = synth_fill_device(dst_dev, n, seed, tid, scale, offset, static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(nullptr, RTR_ERR_CUDA, cudaGetErrorString(e));
+  return RTR_OK;
+}
+
+}  // extern "C"

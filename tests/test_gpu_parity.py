@@ -1,0 +1,231 @@
+"""CUDA path vs the oracle / the reference's golden vectors, through the C ABI.
+
+Bars (from the reference's own acceptance rules):
+* trie lookups, constraint masks, generated tokens and beam parents: bit-exact;
+* FP32 scores: |delta| <= 1e-4 (sequence and transition log-probabilities);
+* every emitted SID is a catalog item, 50 distinct per request, the sequence
+  score equals the sequential FP32 sum of the five transitions.
+"""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, load_generate_fixture
+
+pytestmark = pytest.mark.gpu
+
+SCORE_TOL = 1e-4
+
+
+@pytest.fixture(scope='module')
+def cuda():
+    if not torch.cuda.is_available():
+        pytest.fail('CUDA device required for -m gpu tests')
+    from rapidtinyrec_b200 import _native
+    _native.load()
+    return torch.device('cuda:0')
+
+
+def make_engine(cfg, weights, constraints, max_prefix):
+    from rapidtinyrec_b200.constraints import GpuSidConstraintTables
+    from rapidtinyrec_b200.engine import BeamEngine
+    tables = GpuSidConstraintTables(constraints, cfg.root, cfg.newline, cfg.eos)
+    return BeamEngine(cfg, weights, tables, max_prefix=max_prefix)
+
+
+def compare_records(got, ref, tol=SCORE_TOL):
+    assert got['token_ids'] == ref['token_ids']
+    assert got['beam_indices'] == ref['beam_indices']
+    ds = np.abs(np.array(got['sequence_logp']) - np.array(ref['sequence_logp'])).max()
+    dt = np.abs(np.array(got['transition_logp']) - np.array(ref['transition_logp'])).max()
+    assert ds <= tol and dt <= tol, (ds, dt)
+    return max(ds, dt)
+
+
+def check_invariants(rec, cfg, items):
+    toks = [tuple(t) for t in rec['token_ids']]
+    assert len(set(toks)) == len(toks)
+    for t, seq, trans in zip(toks, rec['sequence_logp'], rec['transition_logp']):
+        assert t[:3] in items and t[3] == cfg.newline and t[4] == cfg.eos
+        assert all(np.isfinite(trans))
+        acc = np.float32(0)
+        for v in trans:
+            acc = np.float32(acc + np.float32(v))
+        assert acc == np.float32(seq)
+    assert rec['sequence_logp'] == sorted(rec['sequence_logp'], reverse=True)
+
+
+# ------------------------------------------------------------- workload
+def test_device_filler_matches_numpy(cuda):
+    from rapidtinyrec_b200 import _native, workload
+    t = torch.empty(300007, device=cuda)
+    _native.synth_fill(t, 0, 11, 0.0346, 0.0)
+    assert np.array_equal(t.cpu().numpy(), workload.synth_values_numpy(0, 11, 300007, 0.0346, 0.0))
+
+
+# ------------------------------------------------------------ constraints
+def grammar_engine(name, tiny):
+    from rapidtinyrec_b200 import configs
+    from tests.golden.make_golden import catalog_5x5x4, grammar_444
+    if name == 'test_catalog':
+        cons, root, nl, eos, vocab = catalog_5x5x4(), (1, 2, 3), 510, 511, 512
+    elif name == 'grammar_444':
+        cons, root, nl, eos, vocab = grammar_444(), (1, 2, 3), 4, 5, 512
+    else:
+        c = tiny['cfg']
+        cons, root, nl, eos, vocab = tiny['constraints'], c.root, c.newline, c.eos, c.vocab
+    cfg = configs.ModelConfig('tables', layers=1, hidden=64, heads=1, kv_heads=1, head_dim=64,
+                              intermediate=64, vocab=vocab, tied=True, dtype='fp32', newline=nl, eos=eos, root=root)
+    return make_engine(cfg, None, cons, max_prefix=16), cons, eos
+
+
+@pytest.mark.parametrize('name', ['test_catalog', 'grammar_444', 'tiny'])
+def test_lookup_bit_exact_vs_reference(cuda, tiny, name):
+    eng, _, _ = grammar_engine(name, tiny)
+    z = np.load(GOLDEN / f'constraints_{name}.npz')
+    for step in range(6):
+        cases = torch.from_numpy(z[f'cases_{step}'].astype(np.int64))
+        got = eng.constraint_lookup(step, cases).cpu().numpy()
+        assert np.array_equal(got, z[f'lookup_{step}']), step
+
+
+@pytest.mark.parametrize('name', ['test_catalog', 'grammar_444', 'tiny'])
+def test_processor_mask_exact_values_close(cuda, tiny, name):
+    eng, _, _ = grammar_engine(name, tiny)
+    vocab = eng.cfg.vocab
+    z = np.load(GOLDEN / f'processor_{name}.npz')
+    scores = torch.randn((50, vocab), dtype=torch.float32, generator=torch.Generator().manual_seed(142)).to(cuda)
+    for step in range(6):
+        ids = torch.from_numpy(z[f'input_{step}'].astype(np.int64)).to(cuda)
+        out = torch.empty_like(scores)
+        eng.constraint_process(step, ids, scores, out)
+        r, c = torch.nonzero(torch.isfinite(out), as_tuple=True)
+        assert np.array_equal(r.cpu().numpy(), z[f'rows_{step}'])
+        assert np.array_equal(c.cpu().numpy(), z[f'cols_{step}'])
+        vals = out[r, c].cpu().numpy()
+        assert np.abs(vals - z[f'vals_{step}']).max() <= 4e-6, step
+
+
+def test_processor_rejects_aliasing(cuda, tiny):
+    from rapidtinyrec_b200._native import NativeError
+    eng, _, _ = grammar_engine('test_catalog', tiny)
+    x = torch.zeros((50, 512), device=cuda)
+    ids = torch.ones((50, 3), dtype=torch.int64, device=cuda)
+    with pytest.raises(NativeError, match='alias'):
+        eng.constraint_process(0, ids, x, x)
+
+
+# ------------------------------------------------------------ end to end
+@pytest.fixture(scope='module')
+def tiny_engine(cuda, tiny):
+    return make_engine(tiny['cfg'], tiny['weights'], tiny['constraints'], max_prefix=128)
+
+
+def test_tiny_generate_matches_reference_golden(tiny_engine, tiny):
+    meta, _ = load_generate_fixture('tiny_fp32')
+    worst = 0.0
+    items = set(tiny['items'])
+    for rec in meta['records']:
+        got = tiny_engine.generate(rec['prompt_token_ids'])
+        worst = max(worst, compare_records(got, rec))
+        check_invariants(got, tiny['cfg'], items)
+    print(f'tiny: max |delta score| vs reference = {worst:.3e}')
+
+
+def test_tiny_step_scores_match_reference(tiny_engine):
+    meta, arrays = load_generate_fixture('tiny_fp32')
+    for u, rec in enumerate(meta['records'][:3]):
+        tiny_engine.prefill(rec['prompt_token_ids'])
+        for t in range(1, 5):
+            tiny_engine.decode_step(t)
+        got = tiny_engine.read_results()
+        compare_records(got, rec)
+        for t in range(5):
+            s = tiny_engine.step_scores(t)
+            r, c = torch.nonzero(torch.isfinite(s), as_tuple=True)
+            assert np.array_equal(r.cpu().numpy(), arrays[f'u{u}_rows_{t}'])
+            assert np.array_equal(c.cpu().numpy(), arrays[f'u{u}_cols_{t}'])
+            assert np.abs(s[r, c].cpu().numpy() - arrays[f'u{u}_vals_{t}']).max() <= SCORE_TOL
+
+
+def test_graph_and_eager_steps_bit_identical_and_repeatable(tiny_engine, tiny):
+    ids = tiny['users'][3].prompt_token_ids
+    a = tiny_engine.generate(ids)
+    tiny_engine.prefill(ids)
+    for t in range(1, 5):
+        tiny_engine.decode_step(t)
+    b = tiny_engine.read_results()
+    c = tiny_engine.generate(tiny['users'][5].prompt_token_ids)
+    d = tiny_engine.generate(ids)
+    assert a == b == d
+    assert c != a
+
+
+def test_contract_violations_raise(tiny_engine, tiny):
+    from rapidtinyrec_b200._native import RTR_ERR_ARG, RTR_ERR_STATE, NativeError
+    with pytest.raises(NativeError) as e:
+        tiny_engine.generate(list(range(1000, 1000 + 200)))
+    assert e.value.code == RTR_ERR_ARG and 'capacity' in str(e.value)
+    with pytest.raises(NativeError) as e:
+        tiny_engine.generate([1, 2])
+    assert e.value.code == RTR_ERR_ARG
+    tiny_engine.prefill(tiny['users'][0].prompt_token_ids)
+    with pytest.raises(NativeError) as e:
+        tiny_engine.decode_step(2)
+    assert e.value.code == RTR_ERR_STATE
+    with pytest.raises(NativeError) as e:
+        tiny_engine.read_results()
+    assert e.value.code == RTR_ERR_STATE
+
+
+def test_out_of_vocab_prompt_token_reported(tiny_engine, tiny):
+    from rapidtinyrec_b200._native import RTR_ERR_DEVICE, NativeError
+    ids = list(tiny['users'][0].prompt_token_ids)
+    ids[5] = tiny['cfg'].vocab + 7
+    with pytest.raises(NativeError) as e:
+        tiny_engine.generate(ids)
+    assert e.value.code == RTR_ERR_DEVICE
+    # the session stays usable after a rejected request
+    rec = tiny_engine.generate(tiny['users'][0].prompt_token_ids)
+    assert len(rec['token_ids']) == 50
+
+
+# --------------------------------------------------- full-size parity
+def full_size_case(name, n_oracle, n_props, cuda):
+    from oracle.beam_cpu import beam_search
+    from oracle.qwen2_cpu import Qwen2Oracle
+    from rapidtinyrec_b200 import configs, workload
+    wl = configs.workload(name)
+    cfg = wl.model
+    items = workload.catalog_items(wl)
+    cons = workload.constraint_dict(cfg, items)
+    users = workload.users(wl, items, count=max(n_oracle, n_props))
+    weights = workload.synth_weights(cfg, seed=wl.weight_seed, device='cuda')
+    eng = make_engine(cfg, weights, cons, max_prefix=wl.prompt_max)
+    cpu_w = {k: v.cpu() for k, v in weights.items()}
+    del weights
+    torch.cuda.empty_cache()
+    model = Qwen2Oracle(cfg, cpu_w)
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    worst = 0.0
+    iset = set(items)
+    for u in users[:n_props]:
+        got = eng.generate(u.prompt_token_ids)
+        check_invariants(got, cfg, iset)
+        if u.cohort_index < n_oracle:
+            ref = beam_search(model, u.prompt_token_ids, cons, cfg.eos)
+            worst = max(worst, compare_records(got, ref))
+    eng.close()
+    return worst
+
+
+def test_primary_1p5b_fp32_matches_oracle(cuda):
+    worst = full_size_case('qwen1.5b-fp32', n_oracle=2, n_props=6, cuda=cuda)
+    print(f'qwen1.5b-fp32: max |delta score| vs oracle = {worst:.3e}')
+
+
+def test_0p5b_fp32_head_dim_64_matches_oracle(cuda):
+    worst = full_size_case('qwen0.5b-fp32', n_oracle=1, n_props=4, cuda=cuda)
+    print(f'qwen0.5b-fp32: max |delta score| vs oracle = {worst:.3e}')
