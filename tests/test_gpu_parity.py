@@ -35,13 +35,32 @@ def make_engine(cfg, weights, constraints, max_prefix):
     return BeamEngine(cfg, weights, tables, max_prefix=max_prefix)
 
 
-def compare_records(got, ref, tol=SCORE_TOL):
-    assert got['token_ids'] == ref['token_ids']
-    assert got['beam_indices'] == ref['beam_indices']
-    ds = np.abs(np.array(got['sequence_logp']) - np.array(ref['sequence_logp'])).max()
-    dt = np.abs(np.array(got['transition_logp']) - np.array(ref['transition_logp'])).max()
-    assert ds <= tol and dt <= tol, (ds, dt)
-    return max(ds, dt)
+TIE_TOL = 2e-5  # reference scores closer than this are a tie under FP32 reordering
+
+
+def compare_records(got, ref, tol=SCORE_TOL, tie_tol=TIE_TOL):
+    """Same ranked SIDs, same beam paths, scores within ``tol``.
+
+    Beams are matched by their SID.  Two ranks may appear swapped only when the
+    reference itself scores them within ``tie_tol`` (e.g. a bit-exact FP32 tie,
+    whose order torch.topk leaves unspecified); every other position must be
+    identical.  Returns the largest score difference.
+    """
+    g = {tuple(t): i for i, t in enumerate(got['token_ids'])}
+    r = {tuple(t): i for i, t in enumerate(ref['token_ids'])}
+    assert set(g) == set(r), 'different top-50 SID sets'
+    worst = 0.0
+    for sid, ri in r.items():
+        gi = g[sid]
+        assert got['beam_indices'][gi] == ref['beam_indices'][ri], ('beam path', sid)
+        worst = max(worst, abs(got['sequence_logp'][gi] - ref['sequence_logp'][ri]),
+                    *(abs(a - b) for a, b in zip(got['transition_logp'][gi], ref['transition_logp'][ri])))
+        if gi != ri:
+            # the reference score at the got position must tie with this SID's reference score
+            tie = abs(ref['sequence_logp'][gi] - ref['sequence_logp'][ri])
+            assert tie <= tie_tol, (f'rank {ri} -> {gi} moved without a tie', tie)
+    assert worst <= tol, worst
+    return worst
 
 
 def check_invariants(rec, cfg, items):
