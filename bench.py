@@ -328,8 +328,46 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_profile(args):
+    """Small, self-contained launch sequences for ncu captures (one GPU).
+
+    profile-request: one warm-up request, then one request bracketed by
+      cudaProfilerStart/Stop (use ncu --profile-from-start off).
+    profile-gemms: a model cut to --layers layers; every projection GEMM of one
+      forward over --rows rows runs twice (warm-up pass + one timed pass).
+    """
+    import dataclasses
+    import torch
+    from rapidtinyrec_b200 import workload as wk
+    from rapidtinyrec_b200.constraints import GpuSidConstraintTables
+    from rapidtinyrec_b200.engine import BeamEngine
+    wl, _, cons, users = build_workload(args.workload, 2)
+    cfg = wl.model if args.layers is None else dataclasses.replace(wl.model, layers=args.layers)
+    weights = wk.synth_weights(cfg, seed=wl.weight_seed, device='cuda')
+    engine = BeamEngine(cfg, weights, GpuSidConstraintTables(cons, cfg.root, cfg.newline, cfg.eos),
+                        max_prefix=max(wl.prompt_max, args.rows))
+    del weights
+    torch.cuda.empty_cache()
+    if args.mode == 'profile-request':
+        engine.generate(users[0].prompt_token_ids)
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        t0 = time.perf_counter()
+        engine.generate(users[1].prompt_token_ids)
+        torch.cuda.profiler.stop()
+        print(json.dumps({'mode': args.mode, 'prompt_tokens': users[1].prompt_tokens,
+                          'wall_ms': 1000 * (time.perf_counter() - t0), 'report': engine.report()}))
+    else:
+        print(json.dumps({'mode': args.mode, 'rows': args.rows, 'layers': cfg.layers,
+                          'ms_per_pass': engine.profile_gemms(args.rows, reps=1)}))
+    engine.close()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--mode', choices=('bench', 'profile-request', 'profile-gemms'), default='bench')
+    ap.add_argument('--rows', type=int, default=50, help='profile-gemms: activation rows')
+    ap.add_argument('--layers', type=int, default=None, help='profile modes: cut the model to this many layers')
     ap.add_argument('--gpus', type=int, default=1)
     ap.add_argument('--steps', type=int, default=40)
     ap.add_argument('--warmup', type=int, default=3)
@@ -338,6 +376,9 @@ def main():
     ap.add_argument('--cpu-budget', type=float, default=20.0, help='seconds of CPU-baseline work (rank 0, N=1)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     args = ap.parse_args()
+    if args.mode != 'bench':
+        run_profile(args)
+        return
     if args.warmup < 3:
         ap.error('--warmup must be >= 3')
     if args.impl == 'reference':

@@ -531,22 +531,61 @@ cudaError_t constraint_lookup(const DevTables& tb, int step, const int64_t* ids,
   return cudaGetLastError();
 }
 
-// out = log_softmax(scores) + mask: one CTA per row, two vocabulary passes.
-__global__ void __launch_bounds__(1024) process_kernel(DevTables tb, int step, const int64_t* ids, int cols,
-                                                       const float* scores, float* out, int vocab) {
+// out = log_softmax(scores) + mask, split over PROC_SPLITS CTAs per row.
+// Pass 1: per-slice max -> scratch[row][slice][0]; pass 2: exact row max, per-
+// slice sum exp(x - max) -> scratch[row][slice][1]; pass 3: log of the summed
+// slices (fixed order), -inf everywhere in the slice, then the processed
+// value (x - max) - log(sum) at the allowed columns that fall in the slice.
+__device__ __forceinline__ void slice_bounds(int vocab, int sp, long* lo, long* hi) {
+  *lo = (long)vocab * sp / PROC_SPLITS;
+  *hi = (long)vocab * (sp + 1) / PROC_SPLITS;
+}
+
+__global__ void proc_max_kernel(const float* __restrict__ scores, int vocab, float* scratch) {
   __shared__ float red[33];
+  const int r = blockIdx.x, sp = blockIdx.y;
+  long lo, hi;
+  slice_bounds(vocab, sp, &lo, &hi);
+  const float* x = scores + (long)r * vocab;
+  float m = -INFINITY;
+  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) m = fmaxf(m, x[i]);
+  m = block_max(m, red);
+  if (threadIdx.x == 0) scratch[((long)r * PROC_SPLITS + sp) * 2] = m;
+}
+
+__device__ __forceinline__ float proc_row_max(const float* scratch, int r) {
+  float m = -INFINITY;
+  for (int k = 0; k < PROC_SPLITS; ++k) m = fmaxf(m, scratch[((long)r * PROC_SPLITS + k) * 2]);
+  return m;
+}
+
+__global__ void proc_sum_kernel(const float* __restrict__ scores, int vocab, float* scratch) {
+  __shared__ float red[33];
+  const int r = blockIdx.x, sp = blockIdx.y;
+  long lo, hi;
+  slice_bounds(vocab, sp, &lo, &hi);
+  const float* x = scores + (long)r * vocab;
+  const float m = proc_row_max(scratch, r);
+  float s = 0.f;
+  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) s += expf(x[i] - m);
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) scratch[((long)r * PROC_SPLITS + sp) * 2 + 1] = s;
+}
+
+__global__ void proc_write_kernel(DevTables tb, int step, const int64_t* __restrict__ ids, int cols,
+                                  const float* __restrict__ scores, float* __restrict__ out, int vocab,
+                                  const float* scratch) {
   __shared__ LookupRow lr;
-  const int r = blockIdx.x;
+  const int r = blockIdx.x, sp = blockIdx.y;
+  long lo, hi;
+  slice_bounds(vocab, sp, &lo, &hi);
   const float* x = scores + (long)r * vocab;
   float* y = out + (long)r * vocab;
-  float m = -INFINITY;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) m = fmaxf(m, x[i]);
-  m = block_max(m, red);
+  const float m = proc_row_max(scratch, r);
   float s = 0.f;
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) s += expf(x[i] - m);
-  s = block_sum(s, red);
+  for (int k = 0; k < PROC_SPLITS; ++k) s += scratch[((long)r * PROC_SPLITS + k) * 2 + 1];
   const float L = logf(s);
-  for (int i = threadIdx.x; i < vocab; i += blockDim.x) y[i] = -INFINITY;
+  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) y[i] = -INFINITY;
   if (threadIdx.x == 0) {
     long tok[3];
     const int n = (step == 0 || step == 3) ? 3 : (step < 3 ? step : 0);
@@ -557,15 +596,17 @@ __global__ void __launch_bounds__(1024) process_kernel(DevTables tb, int step, c
   const int width = lookup_width_of(tb, step);
   for (int j = threadIdx.x; j < width; j += blockDim.x) {
     const int col = lookup_col(tb, lr, j);
-    if (col >= 0 && col < vocab) y[col] = ((x[col] - m) - L) + 0.0f;
+    if (col >= lo && col < hi) y[col] = ((x[col] - m) - L) + 0.0f;
   }
 }
 
 cudaError_t constraint_process(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
                                const float* scores, float* out, int vocab, float* scratch,
                                cudaStream_t stream) {
-  (void)scratch;
-  process_kernel<<<rows, 1024, 0, stream>>>(tb, step, ids, cols, scores, out, vocab);
+  const dim3 grid(rows, PROC_SPLITS);
+  proc_max_kernel<<<grid, TAIL_THREADS, 0, stream>>>(scores, vocab, scratch);
+  proc_sum_kernel<<<grid, TAIL_THREADS, 0, stream>>>(scores, vocab, scratch);
+  proc_write_kernel<<<grid, TAIL_THREADS, 0, stream>>>(tb, step, ids, cols, scores, out, vocab, scratch);
   return cudaGetLastError();
 }
 

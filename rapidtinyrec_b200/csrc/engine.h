@@ -108,6 +108,9 @@ cudaError_t beam_finalize(const BeamState* st, int beams, DevResult* res, const 
 cudaError_t beam_dense_scores(const BeamState* st, int step, int beams, int vocab, float* out,
                               cudaStream_t stream);
 int lookup_width(const DevTables& tb, int step);
+// Processor scratch: PROC_SPLITS (max, sum) partial pairs per row.
+constexpr int PROC_SPLITS = 16;
+constexpr int PROC_MAX_ROWS = 4096;
 cudaError_t constraint_lookup(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
                               int32_t* out, cudaStream_t stream);
 cudaError_t constraint_process(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,

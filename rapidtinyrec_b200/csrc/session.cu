@@ -53,6 +53,7 @@ struct rtr_session {
   float *kv_prefix = nullptr, *kv_suffix = nullptr;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
   float *logits = nullptr, *attn_part = nullptr, *ws = nullptr;
+  float* proc_scratch = nullptr;  // [PROC_MAX_ROWS][PROC_SPLITS][2]
   size_t ws_floats = 0;
   int* tickets = nullptr;
   BeamState* beam = nullptr;
@@ -193,6 +194,7 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   s->ws_floats = gemm_workspace_floats(64, (int)max_n, s->sms);
   CREATE_TRY(dev_alloc(s, &s->ws, s->ws_floats));
   CREATE_TRY(dev_alloc(s, &s->tickets, 4096));
+  CREATE_TRY(dev_alloc(s, &s->proc_scratch, (size_t)PROC_MAX_ROWS * PROC_SPLITS * 2));
   CREATE_TRY(cudaMemset(s->tickets, 0, 4096 * sizeof(int)));
   CREATE_TRY(dev_alloc(s, &s->beam, 1));
   CREATE_TRY(cudaMemset(s->beam, 0, sizeof(BeamState)));
@@ -659,9 +661,10 @@ int rtr_constraint_process(rtr_session* s, int32_t step, const int64_t* input_id
   if (step < 0) return fail(s, RTR_ERR_ARG, "negative step");
   const int need = (step == 0 || step == 3) ? 3 : (step < 3 ? step : 0);
   if (cols < need) return fail(s, RTR_ERR_ARG, "input_ids shorter than the step's prefix");
+  if (rows > PROC_MAX_ROWS) return fail(s, RTR_ERR_ARG, "at most 4096 rows per call");
   CUDA_TRY(s, cudaSetDevice(s->device));
   CUDA_TRY(s, constraint_process(s->tb, step, input_ids_dev, rows, cols, scores_dev, out_dev, s->cfg.vocab,
-                                 nullptr, s->stream));
+                                 s->proc_scratch, s->stream));
   CUDA_TRY(s, cudaStreamSynchronize(s->stream));
   return RTR_OK;
 }
