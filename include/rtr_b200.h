@@ -208,6 +208,26 @@ int rtr_constraint_lookup(rtr_session* s, int32_t step, const int64_t* input_ids
 int rtr_constraint_process(rtr_session* s, int32_t step, const int64_t* input_ids_dev,
                            int32_t rows, int32_t cols, const float* scores_dev, float* out_dev);
 
+/* Allocation-free rtr_constraint_process.  No counterpart in the reference.
+ * For callers that must not allocate device memory per call - a plugin whose
+ * host framework owns the GPU allocator, or code that runs while a stream is
+ * being captured into a graph, where cudaMalloc is not permitted.  It computes
+ * the same scores with the same kernels, but keeps the per-row reduction
+ * scratch in a fixed static device array of the library instead of session
+ * memory, and it calls no cudaMalloc, cudaFree or allocating routine.
+ * Limits and caveats:
+ *   - rows <= 256 (the array's size: 256 rows x 16 slices x 2 floats = 32 KiB,
+ *     held by every GPU that loads the library until the process exits);
+ *     larger requests fail with RTR_ERR_ARG;
+ *   - the first call on a device looks the array's device address up once;
+ *     make that first call before any stream capture;
+ *   - all calls share the one array, so calls whose work overlaps on the GPU
+ *     (other streams, other sessions on the same device) race on it; nothing
+ *     needs clearing between calls, because each call writes every slot it
+ *     reads before reading it. */
+int rtr_constraint_process_static(rtr_session* s, int32_t step, const int64_t* input_ids_dev,
+                                  int32_t rows, int32_t cols, const float* scores_dev, float* out_dev);
+
 /* ---- synthetic workload --------------------------------------------------- */
 
 /* Deterministic synthetic tensor values: element i of stream (seed, tid) is

@@ -22,7 +22,7 @@ EXPORTS = (
     'rtr_decode_step', 'rtr_read_results', 'rtr_generate', 'rtr_step_scores',
     'rtr_lookup_width', 'rtr_constraint_lookup', 'rtr_constraint_process',
     'rtr_synth_fill_host', 'rtr_synth_fill_device', 'rtr_launch', 'rtr_wait', 'rtr_get_report',
-    'rtr_profile_gemms',
+    'rtr_profile_gemms', 'rtr_constraint_process_static',
 )
 
 
@@ -104,6 +104,7 @@ def load():
         'rtr_wait': (P, ctypes.POINTER(ResultC)),
         'rtr_get_report': (P, ctypes.POINTER(ReportC)),
         'rtr_profile_gemms': (P, I32, I32, ctypes.POINTER(F)),
+        'rtr_constraint_process_static': (P, I32, P, I32, I32, P, P),
     }
     for name, args in sig.items():
         fn = getattr(lib, name)

@@ -19,6 +19,8 @@
 // second pass's max is exactly -log(sum) of the first.
 #include <math.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "engine.h"
 
@@ -608,6 +610,42 @@ cudaError_t constraint_process(const DevTables& tb, int step, const int64_t* ids
   proc_sum_kernel<<<grid, TAIL_THREADS, 0, stream>>>(scores, vocab, scratch);
   proc_write_kernel<<<grid, TAIL_THREADS, 0, stream>>>(tb, step, ids, cols, scores, out, vocab, scratch);
   return cudaGetLastError();
+}
+
+// ------------------------------------------- allocation-free processor
+// Scratch for rtr_constraint_process_static: the per-(row, slice) max/sum
+// partials live in this file-scope device array (32 KiB on every GPU that
+// loads the library, for the life of the process) instead of memory the
+// session allocated.  Host code must not pass `g_static_proc_scratch`
+// itself to a kernel - on the host that name is only a stand-in - so its
+// device address is looked up once per device with cudaGetSymbolAddress.
+static __device__ __align__(256) float g_static_proc_scratch[STATIC_PROC_MAX_ROWS * PROC_SPLITS * 2];
+
+static std::mutex g_static_proc_mutex;
+static float* g_static_proc_ptr[STATIC_PROC_MAX_DEVICES] = {};
+
+cudaError_t constraint_process_static(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
+                                      const float* scores, float* out, int vocab, cudaStream_t stream) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= STATIC_PROC_MAX_DEVICES || rows < 1 || rows > STATIC_PROC_MAX_ROWS)
+    return cudaErrorInvalidValue;
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_static_proc_mutex);
+    if (!g_static_proc_ptr[dev]) {
+      // first call on this device (the current one): resolve the array's address
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, g_static_proc_scratch);
+      if (e != cudaSuccess) return e;
+      g_static_proc_ptr[dev] = static_cast<float*>(p);
+    }
+    scratch = g_static_proc_ptr[dev];
+  }
+  // every slot a launch reads is written earlier in the same launch sequence,
+  // so nothing left by a previous call needs clearing
+  return constraint_process(tb, step, ids, rows, cols, scores, out, vocab, scratch, stream);
 }
 
 }  // namespace rtr

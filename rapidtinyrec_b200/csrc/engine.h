@@ -111,6 +111,11 @@ int lookup_width(const DevTables& tb, int step);
 // Processor scratch: PROC_SPLITS (max, sum) partial pairs per row.
 constexpr int PROC_SPLITS = 16;
 constexpr int PROC_MAX_ROWS = 4096;
+// Allocation-free variant: partials in a static device array of 256 rows.
+constexpr int STATIC_PROC_MAX_ROWS = 256;
+constexpr int STATIC_PROC_MAX_DEVICES = 64;
+cudaError_t constraint_process_static(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
+                                      const float* scores, float* out, int vocab, cudaStream_t stream);
 cudaError_t constraint_lookup(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,
                               int32_t* out, cudaStream_t stream);
 cudaError_t constraint_process(const DevTables& tb, int step, const int64_t* ids, int rows, int cols,

@@ -669,6 +669,23 @@ int rtr_constraint_process(rtr_session* s, int32_t step, const int64_t* input_id
   return RTR_OK;
 }
 
+int rtr_constraint_process_static(rtr_session* s, int32_t step, const int64_t* input_ids_dev, int32_t rows,
+                                  int32_t cols, const float* scores_dev, float* out_dev) {
+  if (!s || !input_ids_dev || !scores_dev || !out_dev || rows < 1) return RTR_ERR_ARG;
+  if (!s->tables_loaded) return fail(s, RTR_ERR_STATE, "constraint tables not loaded");
+  if (scores_dev == out_dev) return fail(s, RTR_ERR_ARG, "output aliases the scores");
+  if (step < 0) return fail(s, RTR_ERR_ARG, "negative step");
+  const int need = (step == 0 || step == 3) ? 3 : (step < 3 ? step : 0);
+  if (cols < need) return fail(s, RTR_ERR_ARG, "input_ids shorter than the step's prefix");
+  if (rows > STATIC_PROC_MAX_ROWS)
+    return fail(s, RTR_ERR_ARG, "rtr_constraint_process_static serves at most 256 rows (its static scratch size)");
+  CUDA_TRY(s, cudaSetDevice(s->device));
+  CUDA_TRY(s, constraint_process_static(s->tb, step, input_ids_dev, rows, cols, scores_dev, out_dev, s->cfg.vocab,
+                                        s->stream));
+  CUDA_TRY(s, cudaStreamSynchronize(s->stream));
+  return RTR_OK;
+}
+
 int rtr_synth_fill_host(float* dst, int64_t n, uint64_t seed, uint64_t tid, float scale, float offset) {
   if (!dst || n < 0) return RTR_ERR_ARG;
   synth_fill_host(dst, n, seed, tid, scale, offset);
