@@ -28,7 +28,8 @@ constexpr int ATT_THREADS = 256;
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS) prefill_attn_kernel(
     const float* __restrict__ q, const float* __restrict__ kp, const float* __restrict__ vp,
-    float* __restrict__ out, int L, int cap, int heads, int kv_heads, float scale) {
+    float* __restrict__ out, float* __restrict__ out_big, float* __restrict__ out_small, int L, int cap, int heads,
+    int kv_heads, float scale) {
   constexpr int PER = HD / 32;
   __shared__ float qs[QB][HD];
   __shared__ float ks[HD][KC + 1];
@@ -94,18 +95,21 @@ __global__ void __launch_bounds__(ATT_THREADS) prefill_attn_kernel(
     if (qpos >= L) continue;
     const float inv = 1.0f / l_run[r];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) out[((long)qpos * heads + h) * HD + lane + 32 * i] = acc[r][i] * inv;
+    for (int i = 0; i < PER; ++i)
+      store_split(out, out_big, out_small, ((long)qpos * heads + h) * HD + lane + 32 * i, acc[r][i] * inv);
   }
 }
 
 cudaError_t attention_prefill(const float* q, const float* k_prefix, const float* v_prefix,
-                              float* out, int L, int prefix_cap, int heads, int kv_heads,
-                              int head_dim, float scale, cudaStream_t stream) {
+                              float* out, float* out_big, float* out_small, int L, int prefix_cap, int heads,
+                              int kv_heads, int head_dim, float scale, cudaStream_t stream) {
   dim3 grid((L + QB - 1) / QB, heads);
   if (head_dim == 128)
-    prefill_attn_kernel<128><<<grid, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, out, L, prefix_cap, heads, kv_heads, scale);
+    prefill_attn_kernel<128><<<grid, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, out, out_big, out_small, L,
+                                                               prefix_cap, heads, kv_heads, scale);
   else if (head_dim == 64)
-    prefill_attn_kernel<64><<<grid, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, out, L, prefix_cap, heads, kv_heads, scale);
+    prefill_attn_kernel<64><<<grid, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, out, out_big, out_small, L,
+                                                              prefix_cap, heads, kv_heads, scale);
   else
     return cudaErrorInvalidValue;
   return cudaGetLastError();
@@ -176,7 +180,8 @@ template <int HD>
 __global__ void decode_combine_kernel(const float* __restrict__ q, const float* __restrict__ ks,
                                       const float* __restrict__ vsuf, const int32_t* __restrict__ anc,
                                       const int32_t* __restrict__ L_dev, const float* __restrict__ part,
-                                      float* __restrict__ out, int beams, int heads, int kv_heads,
+                                      float* __restrict__ out, float* __restrict__ out_big,
+                                      float* __restrict__ out_small, int beams, int heads, int kv_heads,
                                       int nc_max, int t, float scale) {
   constexpr int PER = HD / 32;
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -226,23 +231,24 @@ __global__ void decode_combine_kernel(const float* __restrict__ q, const float* 
   }
   const float inv = 1.0f / l;
 #pragma unroll
-  for (int i = 0; i < PER; ++i) out[((long)b * heads + h) * HD + lane + 32 * i] = acc[i] * inv;
+  for (int i = 0; i < PER; ++i)
+    store_split(out, out_big, out_small, ((long)b * heads + h) * HD + lane + 32 * i, acc[i] * inv);
 }
 
 cudaError_t attention_decode(const float* q, const float* k_prefix, const float* v_prefix,
                              const float* k_suffix, const float* v_suffix, const int32_t* anc,
-                             const int32_t* L_dev, int t, float* part, float* out, int beams,
-                             int prefix_cap, int heads, int kv_heads, int head_dim, float scale,
-                             cudaStream_t stream) {
+                             const int32_t* L_dev, int t, float* part, float* out, float* out_big,
+                             float* out_small, int beams, int prefix_cap, int heads, int kv_heads, int head_dim,
+                             float scale, cudaStream_t stream) {
   const int nc_max = attention_decode_chunks(prefix_cap);
   dim3 g1(nc_max, kv_heads, heads / kv_heads);
   const int warps = beams * heads, cb = (warps + 3) / 4;
   if (head_dim == 128) {
     decode_prefix_kernel<128><<<g1, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, L_dev, part, beams, prefix_cap, heads, kv_heads, nc_max, scale);
-    decode_combine_kernel<128><<<cb, 128, 0, stream>>>(q, k_suffix, v_suffix, anc, L_dev, part, out, beams, heads, kv_heads, nc_max, t, scale);
+    decode_combine_kernel<128><<<cb, 128, 0, stream>>>(q, k_suffix, v_suffix, anc, L_dev, part, out, out_big, out_small, beams, heads, kv_heads, nc_max, t, scale);
   } else if (head_dim == 64) {
     decode_prefix_kernel<64><<<g1, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, L_dev, part, beams, prefix_cap, heads, kv_heads, nc_max, scale);
-    decode_combine_kernel<64><<<cb, 128, 0, stream>>>(q, k_suffix, v_suffix, anc, L_dev, part, out, beams, heads, kv_heads, nc_max, t, scale);
+    decode_combine_kernel<64><<<cb, 128, 0, stream>>>(q, k_suffix, v_suffix, anc, L_dev, part, out, out_big, out_small, beams, heads, kv_heads, nc_max, t, scale);
   } else {
     return cudaErrorInvalidValue;
   }

@@ -18,6 +18,7 @@ enum : uint32_t {
   RTR_DEV_BAD_LENGTH = 1u << 5,     // prefix length outside the arena
   RTR_DEV_TOO_MANY_CAND = 1u << 6,  // candidate buffer overflow
   RTR_DEV_NAN_SCORE = 1u << 7,      // a NaN score (ranked as -inf)
+  RTR_DEV_TIMEOUT = 1u << 8,        // a bounded pipeline wait expired (kernel gave up)
 };
 
 RTR_DEVICE float warp_sum(float v) {
@@ -43,6 +44,25 @@ RTR_DEVICE float key_float(uint32_t k) {
 }
 
 RTR_DEVICE float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Round to the nearest tf32 value (ties away from zero): the low 13 mantissa
+// bits are clear, so a tensor core reads it exactly.
+RTR_DEVICE float tf32_round(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Store x and its tf32 split (big = tf32(x), small = x - big, exact) when the
+// split outputs are present; the tensor-core GEMMs consume the split pair.
+RTR_DEVICE void store_split(float* out, float* big, float* small, long i, float x) {
+  out[i] = x;
+  if (big) {
+    const float b = tf32_round(x);
+    big[i] = b;
+    small[i] = x - b;
+  }
+}
 
 // Element load/store for the two activation/weight types.
 template <typename T> RTR_DEVICE float to_f32(T v);

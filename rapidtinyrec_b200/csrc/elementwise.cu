@@ -30,7 +30,8 @@ cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* t
 
 // ------------------------------------------------------------------ RMSNorm
 // Qwen2RMSNorm.forward (modeling_qwen2.py:258-263): w * (x * rsqrt(mean(x^2) + eps)).
-__global__ void rms_norm_kernel(const float* x, const float* w, float* h, int hidden, float eps) {
+__global__ void rms_norm_kernel(const float* x, const float* w, float* h, float* h_big, float* h_small, int hidden,
+                                float eps) {
   const int m = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + (long)m * hidden);
   float ss = 0.f;
@@ -51,17 +52,19 @@ __global__ void rms_norm_kernel(const float* x, const float* w, float* h, int hi
   __syncthreads();
   const float r = 1.0f / sqrtf(red[0] / (float)hidden + eps);
   const float4* wr = reinterpret_cast<const float4*>(w);
-  float4* hr = reinterpret_cast<float4*>(h + (long)m * hidden);
+  const long row = (long)m * hidden;
   for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) {
-    float4 v = xr[i], g = wr[i], o;
-    o.x = g.x * (v.x * r); o.y = g.y * (v.y * r); o.z = g.z * (v.z * r); o.w = g.w * (v.w * r);
-    hr[i] = o;
+    const float4 v = xr[i], g = wr[i];
+    store_split(h, h_big, h_small, row + 4 * i, g.x * (v.x * r));
+    store_split(h, h_big, h_small, row + 4 * i + 1, g.y * (v.y * r));
+    store_split(h, h_big, h_small, row + 4 * i + 2, g.z * (v.z * r));
+    store_split(h, h_big, h_small, row + 4 * i + 3, g.w * (v.w * r));
   }
 }
 
-cudaError_t rms_norm_rows(const float* x, const float* w, float* h, int M, int hidden, float eps,
-                          cudaStream_t stream) {
-  rms_norm_kernel<<<M, 256, 0, stream>>>(x, w, h, hidden, eps);
+cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big, float* h_small, int M, int hidden,
+                          float eps, cudaStream_t stream) {
+  rms_norm_kernel<<<M, 256, 0, stream>>>(x, w, h, h_big, h_small, hidden, eps);
   return cudaGetLastError();
 }
 

@@ -18,11 +18,27 @@ cudaError_t gemm_f32(const float* A, int lda, const float* W, float* C, int ldc,
                      int sms, cudaStream_t stream, bool pdl);
 cudaError_t gemv_f32(const float* x, const float* W, float* y, int N, int K, cudaStream_t stream);
 
+// ---- tensor-core GEMM (gemm_tc.cu): 3xTF32 on tcgen05 ----
+struct alignas(64) TensorMap { unsigned char bytes[128]; };  // a CUtensorMap
+// fp32 row-major [rows][cols], row stride ld floats; TMA box [box_rows][32]
+bool make_tmap_f32(TensorMap* out, const float* base, long rows, long cols, long ld, int box_rows);
+cudaError_t gemm_tc_init();
+// Weights are packed once into tile-contiguous blocks for the tensor-core GEMM.
+size_t packed_weight_floats(int N, int K);
+cudaError_t pack_weight_tiles(const float* src, int N, int K, float* dst, cudaStream_t stream);
+bool make_tmap_packed(TensorMap* out, const float* packed, int N, int K);
+// Activations are consumed as a (big, small) pair: big = tf32(x), small = x - big.
+cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
+                    float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
+                    size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
+                    bool pdl);
+
 // ---- element-wise (elementwise.cu) ----
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
                        int hidden, float* x, uint32_t* status, cudaStream_t stream);
-cudaError_t rms_norm_rows(const float* x, const float* w, float* h, int M, int hidden, float eps,
-                          cudaStream_t stream);
+// h = w * (x * rsqrt(mean(x^2) + eps)); h_big/h_small (optional) get the tf32 split of h.
+cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big, float* h_small, int M, int hidden,
+                          float eps, cudaStream_t stream);
 // RoPE on q and k of a [M, qkv_dim] projection; q -> q_out [M, Hq*D], k/v ->
 // cache rows.  Prefill (slot < 0): row m is position m, K/V go to the prefix
 // arena [Hkv][cap][D] at position m.  Decode (slot >= 0): every row is at
@@ -37,15 +53,17 @@ void synth_fill_host(float* dst, int64_t n, uint64_t seed, uint64_t tid, float s
 cudaError_t f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t stream);
 
 // ---- attention (attention.cu) ----
+// out_big/out_small (optional) receive the tf32 split of out.
 cudaError_t attention_prefill(const float* q, const float* k_prefix, const float* v_prefix,
-                              float* out, int L, int prefix_cap, int heads, int kv_heads,
-                              int head_dim, float scale, cudaStream_t stream);
+                              float* out, float* out_big, float* out_small, int L, int prefix_cap, int heads,
+                              int kv_heads, int head_dim, float scale, cudaStream_t stream);
 // Decode attention over the shared prefix (length *L_dev) and `t` suffix
 // slots; suffix slot s of beam b lives in row anc[b*4+s] (slot t-1: row b).
 int attention_decode_chunks(int max_prefix);
 cudaError_t attention_decode(const float* q, const float* k_prefix, const float* v_prefix,
                              const float* k_suffix, const float* v_suffix, const int32_t* anc,
-                             const int32_t* L_dev, int t, float* part, float* out, int beams,
+                             const int32_t* L_dev, int t, float* part, float* out, float* out_big,
+                             float* out_small, int beams,
                              int prefix_cap, int heads, int kv_heads, int head_dim, float scale,
                              cudaStream_t stream);
 

@@ -132,15 +132,18 @@ __global__ void __launch_bounds__(THREADS, 2) gemm_f32_kernel(GemmParams p) {
     if (!last) return;
     __threadfence();
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int m = m0 + tm + 16 * i;
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int n = n0 + tn + 16 * j;
-        float v = 0.f;
-        if (n < p.N)
-          for (int z = 0; z < p.splits; ++z) v += __ldcg(p.ws + ((long)z * mpad + m) * p.N + n);
-        acc[i][j] = v;
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int z = 0; z < p.splits; ++z) {  // split order; 32 independent loads per split
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int m = m0 + tm + 16 * i;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int n = n0 + tn + 16 * j;
+          if (n < p.N) acc[i][j] += __ldcg(p.ws + ((long)z * mpad + m) * p.N + n);
+        }
       }
     }
   }

@@ -1,0 +1,561 @@
+// FP32 projection GEMM on the 5th-generation tensor cores: error-compensated
+// 3xTF32 with tcgen05.mma, TMA-staged operands, A operand and accumulators in
+// tensor memory.
+//
+//   C[m, n] (+ epilogue) = sum_k X[m, k] * W[n, k]        X: activations, W: nn.Linear weight
+//
+// A CTA owns 128 weight rows (the MMA M side) x 64 activation rows (the MMA
+// N side) for a range of K, walked in 32-wide chunks (one 128-byte row):
+//   warp 0     TMA of the W tile [128 x 32] into a 6-deep shared ring (128B swizzle)
+//   warp 10    TMA of the activation tile (its own warp, so a wait on the
+//              MMA-paced activation ring never stalls the weight stream): the
+//              big and small halves of X, which the
+//              producing kernels already split (X_b = tf32(X), X_s = X - X_b), are
+//              stacked into one [128 x 32] operand [X_b ; X_s]
+//   warps 2..5 (one TMEM lane quarter each, thread = weight row) read their row
+//              of W, split it in registers (W_b = tf32(W), W_s = W - W_b), store
+//              both into tensor memory and free the W stage at once
+//   warp 1     MMA (A from TMEM, B from shared memory):
+//                D[:, 0:128] += W_b . [X_b ; X_s]     D[:, 0:64] += W_s . X_b
+//              so D[:, 0:64] + D[:, 64:128] = W.X up to W_s.X_s (~2^-22 relative)
+//   warps 6..9 promote: the tensor core's fp32 accumulation drifts over long K,
+//              so every 4 chunks the accumulator (double-buffered in TMEM) is
+//              added into IEEE fp32 registers; they also run the epilogue.
+// Every role has its own ring, so loading, splitting, MMA and promotion of
+// different chunks overlap.  Small GEMMs split K over CTAs; the
+// last CTA to arrive sums the partial tiles in split order (deterministic).
+// Every mbarrier wait is bounded (~1 s): on expiry the CTA records
+// RTR_DEV_TIMEOUT, stops issuing work, drains what it issued and frees TMEM.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "common.cuh"
+#include "engine.h"
+
+namespace rtr {
+
+constexpr int TC_THREADS = 352;          // 11 warps
+constexpr int TC_KC = 32;                // fp32 per 128-byte row
+constexpr int TC_WROWS = 128;            // MMA M
+constexpr int TC_NTOK = 64;              // activation rows per CTA
+constexpr int TC_WSTAGES = 6;            // W ring depth
+constexpr int TC_XSTAGES = 4;            // activation ring depth
+constexpr int TC_ASTAGES = 4;            // TMEM A-operand stages
+constexpr int TC_PROMOTE = 4;            // chunks accumulated in TMEM per promotion
+constexpr int TC_W_BYTES = TC_WROWS * 128;
+constexpr int TC_X_BYTES = 2 * TC_NTOK * 128;  // [X_b ; X_s]
+constexpr int TC_D_COLS = 2 * TC_NTOK;         // one accumulator buffer
+constexpr int TC_A_COLS = 2 * TC_KC;           // W_b and W_s of one chunk
+constexpr int TC_TMEM_COLS = 512;              // 2 accumulators + 4 A stages
+constexpr int TC_NBARS = 2 * TC_WSTAGES + 2 * TC_XSTAGES + 2 * TC_ASTAGES + 4;
+constexpr int TC_SMEM_BYTES = TC_WSTAGES * TC_W_BYTES + TC_XSTAGES * TC_X_BYTES + 1024 + 8 * TC_NBARS + 16;
+constexpr long long TC_WAIT_CYCLES = 2000000000LL;
+
+// ------------------------------------------------------------- PTX helpers
+RTR_DEVICE uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+
+RTR_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+RTR_DEVICE void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+RTR_DEVICE void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+RTR_DEVICE bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false when the CTA aborted or ~1 s passed (then abort is set).
+RTR_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > TC_WAIT_CYCLES) { *abort_flag = 1; return false; }
+  }
+  return true;
+}
+RTR_DEVICE void mbar_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity) && clock64() - t0 < TC_WAIT_CYCLES) {}
+}
+
+RTR_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+RTR_DEVICE void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+RTR_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+RTR_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+RTR_DEVICE void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+RTR_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[tmem] . B[smem]
+RTR_DEVICE void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+RTR_DEVICE void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+#define RTR_R32(r)                                                                                       \
+  "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),   \
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),   \
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),   \
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+#define RTR_W32(r)                                                                                       \
+  "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),       \
+      "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),          \
+      "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),        \
+      "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),        \
+      "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+#define RTR_OPS32                                                                                        \
+  "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, " \
+  "%22, %23, %24, %25, %26, %27, %28, %29, %30, %31}"
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i <-> lane (base lane + i).
+RTR_DEVICE void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 " RTR_OPS32 ", [%32];" : RTR_W32(r) : "r"(taddr) : "memory");
+}
+RTR_DEVICE void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+RTR_DEVICE void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+               "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+               :
+               : "r"(taddr), RTR_R32(r)
+               : "memory");
+}
+RTR_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major operand, rows of 128 bytes in the
+// TMA 128-byte swizzle, 8-row core groups 1024 bytes apart.
+RTR_DEVICE uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;               // leading byte offset (unused with swizzle)
+  d |= (uint64_t)(1024 >> 4) << 32;     // stride byte offset
+  d |= (uint64_t)1 << 46;               // descriptor version
+  d |= (uint64_t)2 << 61;               // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::tf32: D f32, A/B tf32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+RTR_DEVICE float silu_f(float g) { return g / (1.0f + expf(-g)); }
+
+struct TcParams {
+  float* C;
+  float* C_big;     // SWIGLU: also write the split halves of the activation
+  float* C_small;
+  const float* bias;
+  int M, N, K, ldc, epi, splits;
+  float* ws;
+  int* tickets;
+  uint32_t* status;
+};
+
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
+                   const __grid_constant__ CUtensorMap tmXs, TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* wring = smem;
+  uint8_t* xring = smem + TC_WSTAGES * TC_W_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + TC_XSTAGES * TC_X_BYTES);
+  uint64_t* w_full = bars;
+  uint64_t* w_empty = w_full + TC_WSTAGES;
+  uint64_t* x_full = w_empty + TC_WSTAGES;
+  uint64_t* x_empty = x_full + TC_XSTAGES;
+  uint64_t* a_full = x_empty + TC_XSTAGES;
+  uint64_t* a_empty = a_full + TC_ASTAGES;
+  uint64_t* d_full = a_empty + TC_ASTAGES;  // [2]
+  uint64_t* d_empty = d_full + 2;           // [2]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2) + 1;
+  __shared__ int last_cta;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok0 = blockIdx.x * TC_NTOK;
+  const int n0 = blockIdx.y * TC_WROWS;
+  const int nchunks = (p.K + TC_KC - 1) / TC_KC;
+  const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
+  const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
+  const int nloc = c1 - c0;
+  const int ngroups = (nloc + TC_PROMOTE - 1) / TC_PROMOTE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_WSTAGES; ++s) { mbar_init(smem_addr(&w_full[s]), 1); mbar_init(smem_addr(&w_empty[s]), 4); }
+    for (int s = 0; s < TC_XSTAGES; ++s) { mbar_init(smem_addr(&x_full[s]), 1); mbar_init(smem_addr(&x_empty[s]), 1); }
+    for (int s = 0; s < TC_ASTAGES; ++s) { mbar_init(smem_addr(&a_full[s]), 4); mbar_init(smem_addr(&a_empty[s]), 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(smem_addr(&d_full[b]), 1); mbar_init(smem_addr(&d_empty[b]), 4); }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmXb);
+    tma_prefetch_desc(&tmXs);
+  }
+  if (warp == 1) tmem_alloc(smem_addr(tmem_slot), TC_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_a = tmem + 2 * TC_D_COLS;  // A stages after the two accumulators
+
+  int w_issued = 0, x_issued = 0, mma_groups = 0;
+  float acc[TC_NTOK];  // live only in the promoter warps (set there)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------- W producer (TMA)
+      // weights do not depend on the previous kernel: no griddepcontrol.wait
+      for (int i = 0; i < nloc; ++i) {
+        const int s = i % TC_WSTAGES;
+        if (!mbar_wait(smem_addr(&w_empty[s]), ((i / TC_WSTAGES) & 1) ^ 1, abort_flag)) break;
+        const uint32_t fb = smem_addr(&w_full[s]);
+        mbar_expect_tx(fb, TC_W_BYTES);
+        // packed weights: the [128 x 32] block of (tile, chunk) is 16 KB contiguous
+        tma_load_2d(smem_addr(wring + s * TC_W_BYTES), &tmW, 0, (blockIdx.y * nchunks + c0 + i) * TC_WROWS, fb);
+        w_issued = i + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_cat = idesc_tf32(TC_WROWS, 2 * TC_NTOK);
+      constexpr uint32_t id_x = idesc_tf32(TC_WROWS, TC_NTOK);
+      for (int i = 0; i < nloc; ++i) {
+        const int g = i / TC_PROMOTE, b = g & 1;
+        if (i % TC_PROMOTE == 0 && g >= 2 &&
+            !mbar_wait(smem_addr(&d_empty[b]), ((g >> 1) - 1) & 1, abort_flag))
+          break;
+        const int as = i % TC_ASTAGES, xs = i % TC_XSTAGES;
+        if (!mbar_wait(smem_addr(&a_full[as]), (i / TC_ASTAGES) & 1, abort_flag)) break;
+        if (!mbar_wait(smem_addr(&x_full[xs]), (i / TC_XSTAGES) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * TC_D_COLS;
+        const uint32_t ab = tmem_a + as * TC_A_COLS, asml = ab + TC_KC;
+        const uint64_t bx = sw128_desc(smem_addr(xring + xs * TC_X_BYTES));
+#pragma unroll
+        for (int kk = 0; kk < TC_KC / 8; ++kk) {
+          const uint64_t adv = (uint64_t)(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
+          mma_tf32_ts(d, ab + kk * 8, bx + adv, id_cat, (i % TC_PROMOTE != 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_ts(d, asml + kk * 8, bx + adv, id_x, 1u);
+        }
+        mma_commit(smem_addr(&a_empty[as]));
+        mma_commit(smem_addr(&x_empty[xs]));
+        if (i % TC_PROMOTE == TC_PROMOTE - 1 || i == nloc - 1) {
+          mma_commit(smem_addr(&d_full[b]));
+          mma_groups = g + 1;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 10) {
+    // --------------------------------------- activation producer (TMA)
+    pdl_wait();
+    if (lane == 0) {
+      for (int i = 0; i < nloc; ++i) {
+        const int s = i % TC_XSTAGES;
+        if (!mbar_wait(smem_addr(&x_empty[s]), ((i / TC_XSTAGES) & 1) ^ 1, abort_flag)) break;
+        const uint32_t fb = smem_addr(&x_full[s]);
+        uint8_t* st = xring + s * TC_X_BYTES;
+        mbar_expect_tx(fb, TC_X_BYTES);
+        tma_load_2d(smem_addr(st), &tmXb, (c0 + i) * TC_KC, tok0, fb);
+        tma_load_2d(smem_addr(st + TC_X_BYTES / 2), &tmXs, (c0 + i) * TC_KC, tok0, fb);
+        x_issued = i + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp <= 5) {
+    // ------------------------------- warps 2..5: split W rows into TMEM
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // TMEM lane = weight row of the tile
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    for (int i = 0; i < nloc; ++i) {
+      const int ws = i % TC_WSTAGES, as = i % TC_ASTAGES;
+      if (!mbar_wait(smem_addr(&w_full[ws]), (i / TC_WSTAGES) & 1, abort_flag)) break;
+      const uint8_t* tile = wring + ws * TC_W_BYTES + row * 128;
+      uint32_t big[TC_KC], small[TC_KC];
+#pragma unroll
+      for (int c = 0; c < TC_KC / 4; ++c) {  // undo the 128B swizzle: chunk c lives at c ^ (row % 8)
+        const float4 v = *reinterpret_cast<const float4*>(tile + ((c ^ (row & 7)) << 4));
+        big[4 * c] = __float_as_uint(v.x); big[4 * c + 1] = __float_as_uint(v.y);
+        big[4 * c + 2] = __float_as_uint(v.z); big[4 * c + 3] = __float_as_uint(v.w);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&w_empty[ws]));  // the row is in registers
+#pragma unroll
+      for (int k = 0; k < TC_KC; ++k) {
+        const float w = __uint_as_float(big[k]);
+        const float bv = tf32_round(w);
+        big[k] = __float_as_uint(bv);
+        small[k] = __float_as_uint(w - bv);
+      }
+      if (!mbar_wait(smem_addr(&a_empty[as]), ((i / TC_ASTAGES) & 1) ^ 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t a = tmem_a + lane_base + as * TC_A_COLS;
+      tmem_st32(a, big);
+      tmem_st32(a + TC_KC, small);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&a_full[as]));
+    }
+  } else {
+    // ------------------------- warps 6..9: promote accumulators, epilogue
+    pdl_wait();
+#pragma unroll
+    for (int j = 0; j < TC_NTOK; ++j) acc[j] = 0.f;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    for (int g = 0; g < ngroups; ++g) {
+      const int b = g & 1;
+      if (!mbar_wait(smem_addr(&d_full[b]), (g >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + lane_base + b * TC_D_COLS;
+#pragma unroll
+      for (int cb = 0; cb < TC_NTOK; cb += 32) {
+        uint32_t r[32];
+        float part[32];
+        tmem_ld32(d + cb, r);             // W_b.X_b + W_s.X_b
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) part[j] = __uint_as_float(r[j]);
+        tmem_ld32(d + TC_NTOK + cb, r);   // W_b.X_s
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[cb + j] += part[j] + __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&d_empty[b]));
+    }
+  }
+  pdl_launch_dependents();
+
+  // drain on abort: issued copies and MMAs must land before smem/TMEM go away
+  if (*abort_flag) {
+    if (threadIdx.x == 0) atomicOr(p.status, RTR_DEV_TIMEOUT);
+    if (warp == 0 && lane == 0)
+      for (int i = 0; i < w_issued; ++i) mbar_drain(smem_addr(&w_full[i % TC_WSTAGES]), (i / TC_WSTAGES) & 1);
+    if (warp == 10 && lane == 0)
+      for (int i = 0; i < x_issued; ++i) mbar_drain(smem_addr(&x_full[i % TC_XSTAGES]), (i / TC_XSTAGES) & 1);
+    if (warp == 1 && lane == 0 && mma_groups > 0) {
+      const int g = mma_groups - 1;
+      mbar_drain(smem_addr(&d_full[g & 1]), (g >> 1) & 1);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TC_TMEM_COLS);
+  }
+  if (*abort_flag) return;
+
+  const bool have = warp >= 6 && warp <= 9;
+  const int quarter = warp & 3;
+  const int n = n0 + quarter * 32 + lane;  // weight row of this thread
+  if (p.splits > 1) {
+    const long mpad = (long)gridDim.x * TC_NTOK;
+    if (have && n < p.N) {
+      float* w = p.ws + ((long)blockIdx.z * mpad + tok0) * p.N + n;
+#pragma unroll
+      for (int j = 0; j < TC_NTOK; ++j) {
+        __stcg(w, acc[j]);
+        w += p.N;
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int* tk = p.tickets + blockIdx.y * gridDim.x + blockIdx.x;
+      last_cta = atomicAdd(tk, 1) == p.splits - 1;
+      if (last_cta) *tk = 0;  // re-arm for the next launch / graph replay
+    }
+    __syncthreads();
+    if (!last_cta) return;
+    __threadfence();
+    if (have && n < p.N) {
+#pragma unroll
+      for (int j = 0; j < TC_NTOK; ++j) acc[j] = 0.f;
+      for (int z = 0; z < p.splits; ++z) {  // split order; 16 independent loads at a time
+        const float* w = p.ws + ((long)z * mpad + tok0) * p.N + n;
+#pragma unroll
+        for (int jb = 0; jb < TC_NTOK; jb += 16) {
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __ldcg(w + (long)j * p.N);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) acc[jb + j] += v[j];
+          w += 16L * p.N;
+        }
+      }
+    }
+  }
+  if (!have) return;
+
+  if (p.epi == EPI_SWIGLU) {
+    // packed rows: 32 q + [0,16) gate, 32 q + [16,32) up of intermediate 16 q + [0,16)
+    const int inter = ((n0 + quarter * 32) >> 5) * 16 + (lane & 15);
+#pragma unroll
+    for (int j = 0; j < TC_NTOK; ++j) {
+      const float up = __shfl_down_sync(0xffffffffu, acc[j], 16);
+      const int m = tok0 + j;
+      if (lane < 16 && n < p.N && m < p.M) {
+        const float a = silu_f(acc[j]) * up;
+        const long o = (long)m * p.ldc + inter;
+        p.C[o] = a;
+        const float ab = tf32_round(a);
+        p.C_big[o] = ab;
+        p.C_small[o] = a - ab;
+      }
+    }
+    return;
+  }
+  if (n >= p.N) return;
+  const float bv = p.epi == EPI_BIAS ? p.bias[n] : 0.f;
+#pragma unroll
+  for (int j = 0; j < TC_NTOK; ++j) {
+    const int m = tok0 + j;
+    if (m < p.M) {
+      float* c = p.C + (long)m * p.ldc + n;
+      if (p.epi == EPI_STORE) *c = acc[j];
+      else if (p.epi == EPI_BIAS) *c = acc[j] + bv;
+      else *c = *c + acc[j];
+    }
+  }
+}
+
+// ---------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D fp32 row-major [rows][cols] (row stride ld floats), box [box_rows][32].
+bool make_tmap_f32(TensorMap* out, const float* base, long rows, long cols, long ld, int box_rows) {
+  static_assert(sizeof(TensorMap) == sizeof(CUtensorMap), "TensorMap size");
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (ld * 4) % 16 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {(cuuint32_t)TC_KC, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base),
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Weight layout for the tensor-core GEMM: W [N, K] becomes blocks
+// [N/128 tiles][K/32 chunks][128 rows][32 floats] (zero padded), so every TMA
+// load of a (tile, chunk) reads 16 KB of contiguous memory.
+__global__ void pack_tiles_kernel(const float* __restrict__ src, int N, int K, int nchunks, float* __restrict__ dst,
+                                  long total) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int k = (int)(i & 31);
+    const int r = (int)((i >> 5) & 127);
+    const long blk = i >> 12;
+    const int c = (int)(blk % nchunks);
+    const long t = blk / nchunks;
+    const long row = t * TC_WROWS + r, col = (long)c * TC_KC + k;
+    dst[i] = (row < N && col < K) ? src[row * K + col] : 0.f;
+  }
+}
+
+size_t packed_weight_floats(int N, int K) {
+  return (size_t)((N + TC_WROWS - 1) / TC_WROWS) * ((K + TC_KC - 1) / TC_KC) * TC_WROWS * TC_KC;
+}
+
+cudaError_t pack_weight_tiles(const float* src, int N, int K, float* dst, cudaStream_t stream) {
+  const long total = (long)packed_weight_floats(N, K);
+  pack_tiles_kernel<<<148 * 8, 256, 0, stream>>>(src, N, K, (K + TC_KC - 1) / TC_KC, dst, total);
+  return cudaGetLastError();
+}
+
+bool make_tmap_packed(TensorMap* out, const float* packed, int N, int K) {
+  const long rows = (long)packed_weight_floats(N, K) / TC_KC;
+  return make_tmap_f32(out, packed, rows, TC_KC, TC_KC, TC_WROWS);
+}
+
+cudaError_t gemm_tc_init() {
+  return cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES);
+}
+
+static int tc_splits(int tiles, int nchunks, int sms) {
+  if (tiles >= sms) return 1;
+  int s = sms / tiles;
+  if (s > nchunks / 2) s = nchunks / 2;  // keep at least two chunks per split
+  if (s > 16) s = 16;
+  return s < 1 ? 1 : s;
+}
+
+cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
+                    float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
+                    size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
+                    bool pdl) {
+  if (epi == EPI_SWIGLU && (!C_big || !C_small)) return cudaErrorInvalidValue;
+  const int tt = (M + TC_NTOK - 1) / TC_NTOK, wt = (N + TC_WROWS - 1) / TC_WROWS;
+  const int nchunks = (K + TC_KC - 1) / TC_KC;
+  int splits = tc_splits(tt * wt, nchunks, sms);
+  while (splits > 1 && ((size_t)splits * tt * TC_NTOK * N > ws_floats || tt * wt > max_tickets)) --splits;
+  TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tt, wt, splits);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = TC_SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, *reinterpret_cast<const CUtensorMap*>(&tmW),
+                            *reinterpret_cast<const CUtensorMap*>(&tmXb), *reinterpret_cast<const CUtensorMap*>(&tmXs),
+                            p);
+}
+
+}  // namespace rtr

@@ -18,6 +18,9 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <cstdlib>
+#include <map>
+#include <utility>
 #include <vector>
 
 #include "../../include/rtr_b200.h"
@@ -36,6 +39,11 @@ struct rtr_session {
   cudaStream_t stream = nullptr;
   bool own_stream = false;
   bool pdl = true;
+  bool use_tc = true;  // tcgen05 GEMMs (RTR_GEMM=ffma selects the FFMA kernel)
+  // TMA descriptors keyed by (buffer, box rows): activations at 64/128 rows,
+  // weights at 128 rows
+  std::map<std::pair<const void*, int>, TensorMap> tmaps;
+  std::map<const void*, float*> packed;  // tile-packed copy of each weight matrix
   std::string err;
   // weights
   float *embed = nullptr, *lm_head = nullptr, *norm_final = nullptr;
@@ -52,6 +60,10 @@ struct rtr_session {
   // KV and activations
   float *kv_prefix = nullptr, *kv_suffix = nullptr;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
+  // tf32 split (big = tf32(v), small = v - big) of the GEMM activation operands
+  float *h_big = nullptr, *h_small = nullptr, *attn_big = nullptr, *attn_small = nullptr;
+  float *act_big = nullptr, *act_small = nullptr;
+  std::map<const void*, std::pair<float*, float*>> split_of;
   float *logits = nullptr, *attn_part = nullptr, *ws = nullptr;
   float* proc_scratch = nullptr;  // [PROC_MAX_ROWS][PROC_SPLITS][2]
   size_t ws_floats = 0;
@@ -98,6 +110,8 @@ static cudaError_t dev_alloc(rtr_session* s, T** p, size_t count) {
   *p = static_cast<T*>(raw);
   return cudaSuccess;
 }
+
+static constexpr int kTickets = 4096;  // split-K tickets: one per output tile
 
 static int beams_of(const rtr_session* s) { return s->cfg.num_beams; }
 static int qkv_dim(const rtr_model_config& c) { return (c.heads + 2 * c.kv_heads) * c.head_dim; }
@@ -157,6 +171,8 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   s->own_stream = true;
   CREATE_TRY(gemm_init());
   CREATE_TRY(beam_init());
+  CREATE_TRY(gemm_tc_init());
+  if (const char* g = std::getenv("RTR_GEMM")) s->use_tc = std::strcmp(g, "ffma") != 0;
 
   const long H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
   const long qd = (long)c.heads * D, kvd = (long)c.kv_heads * D, qkvd = qkv_dim(c);
@@ -186,6 +202,12 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(dev_alloc(s, &s->q, M * qd));
   CREATE_TRY(dev_alloc(s, &s->attn, M * qd));
   CREATE_TRY(dev_alloc(s, &s->act, M * I));
+  CREATE_TRY(dev_alloc(s, &s->h_big, M * H));
+  CREATE_TRY(dev_alloc(s, &s->h_small, M * H));
+  CREATE_TRY(dev_alloc(s, &s->attn_big, M * qd));
+  CREATE_TRY(dev_alloc(s, &s->attn_small, M * qd));
+  CREATE_TRY(dev_alloc(s, &s->act_big, M * I));
+  CREATE_TRY(dev_alloc(s, &s->act_small, M * I));
   CREATE_TRY(dev_alloc(s, &s->logits, B * V));
   CREATE_TRY(dev_alloc(s, &s->attn_part, (size_t)B * c.heads * attention_decode_chunks(cap) * (D + 2)));
   long max_n = qkvd;
@@ -193,9 +215,9 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   if (2 * I > max_n) max_n = 2 * I;
   s->ws_floats = gemm_workspace_floats(64, (int)max_n, s->sms);
   CREATE_TRY(dev_alloc(s, &s->ws, s->ws_floats));
-  CREATE_TRY(dev_alloc(s, &s->tickets, 4096));
+  CREATE_TRY(dev_alloc(s, &s->tickets, kTickets));
   CREATE_TRY(dev_alloc(s, &s->proc_scratch, (size_t)PROC_MAX_ROWS * PROC_SPLITS * 2));
-  CREATE_TRY(cudaMemset(s->tickets, 0, 4096 * sizeof(int)));
+  CREATE_TRY(cudaMemset(s->tickets, 0, kTickets * sizeof(int)));
   CREATE_TRY(dev_alloc(s, &s->beam, 1));
   CREATE_TRY(cudaMemset(s->beam, 0, sizeof(BeamState)));
   CREATE_TRY(dev_alloc(s, &s->dres, 1));
@@ -214,6 +236,22 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   default_rope(c, s->rope_positions, cs, sn);
   CREATE_TRY(cudaMemcpy(s->rope_cos, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
   CREATE_TRY(cudaMemcpy(s->rope_sin, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+
+  // TMA descriptors of the GEMM activation operands: the big and small halves
+  struct Act { const float* v; float* big; float* small; long width; };
+  const Act acts[3] = {{s->h, s->h_big, s->h_small, H}, {s->attn, s->attn_big, s->attn_small, qd},
+                       {s->act, s->act_big, s->act_small, I}};
+  for (const auto& a : acts) {
+    s->split_of[a.v] = {a.big, a.small};
+    for (const float* half : {a.big, a.small}) {
+      TensorMap m;
+      if (!make_tmap_f32(&m, half, M, a.width, a.width, 64)) {
+        s->err = "cuTensorMapEncodeTiled failed for an activation buffer";
+        return bail(RTR_ERR_CUDA);
+      }
+      s->tmaps[{half, 64}] = m;
+    }
+  }
 #undef CREATE_TRY
   *out = s;
   return RTR_OK;
@@ -297,6 +335,36 @@ int rtr_load_weights(rtr_session* s, const void* const* tensors, int32_t n_tenso
   CUDA_TRY(s, cp(s->norm_final, tensors[1 + 12 * c.layers], H));
   if (!c.tied_embeddings) CUDA_TRY(s, cp(s->lm_head, tensors[2 + 12 * c.layers], V * H));
   CUDA_TRY(s, cudaDeviceSynchronize());
+  // Tensor-core GEMM operands: every weight matrix packed into tile-contiguous
+  // blocks (allocated once), with its TMA descriptor keyed by the original matrix
+  if (s->use_tc) {
+    auto wmap = [&](const float* w, long rows, long cols) -> cudaError_t {
+      float* packed = nullptr;
+      auto it = s->packed.find(w);
+      if (it == s->packed.end()) {
+        cudaError_t e = dev_alloc(s, &packed, packed_weight_floats((int)rows, (int)cols));
+        if (e != cudaSuccess) return e;
+        s->packed[w] = packed;
+      } else {
+        packed = it->second;
+      }
+      cudaError_t e = pack_weight_tiles(w, (int)rows, (int)cols, packed, 0);
+      if (e != cudaSuccess) return e;
+      TensorMap m;
+      if (!make_tmap_packed(&m, packed, (int)rows, (int)cols)) return cudaErrorInvalidValue;
+      s->tmaps[{w, 128}] = m;
+      return cudaSuccess;
+    };
+    CUDA_TRY(s, wmap(s->lm_head, V, H));
+    for (int l = 0; l < c.layers; ++l) {
+      const LayerW& w = s->layers[l];
+      CUDA_TRY(s, wmap(w.wqkv, qd + 2 * kvd, H));
+      CUDA_TRY(s, wmap(w.wo, H, qd));
+      CUDA_TRY(s, wmap(w.wgu, 2 * I, H));
+      CUDA_TRY(s, wmap(w.wd, H, I));
+    }
+    CUDA_TRY(s, cudaDeviceSynchronize());
+  }
   s->weights_loaded = true;
   return RTR_OK;
 }
@@ -359,8 +427,28 @@ int rtr_load_constraints(rtr_session* s, const rtr_constraint_tables* t) {
 }  // extern "C"
 
 // ------------------------------------------------------------------ forward
+// Projection GEMM: the tcgen05 3xTF32 kernel on the tf32 split of activation
+// buffer A and the weight matrix W (the FFMA kernel when RTR_GEMM=ffma).
 static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W, float* C, int ldc,
                         const float* bias, int M, int N, int K, int epi) {
+  if (s->use_tc) {
+    auto sp = s->split_of.find(A);
+    if (sp == s->split_of.end()) return cudaErrorInvalidValue;
+    auto xb = s->tmaps.find({sp->second.first, 64});
+    auto xs = s->tmaps.find({sp->second.second, 64});
+    auto w = s->tmaps.find({W, 128});
+    if (xb == s->tmaps.end() || xs == s->tmaps.end() || w == s->tmaps.end()) return cudaErrorInvalidValue;
+    float* cb = nullptr;
+    float* cs = nullptr;
+    if (epi == EPI_SWIGLU) {
+      auto out = s->split_of.find(C);
+      if (out == s->split_of.end()) return cudaErrorInvalidValue;
+      cb = out->second.first;
+      cs = out->second.second;
+    }
+    return gemm_tc(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws, s->ws_floats,
+                   s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl);
+  }
   return gemm_f32(A, lda, W, C, ldc, bias, M, N, K, epi, s->ws, s->ws_floats, s->tickets, s->sms,
                   s->stream, s->pdl);
 }
@@ -388,29 +476,30 @@ static cudaError_t forward(rtr_session* s, int t) {
     float* vp = kp + (size_t)kvd * cap;
     float* ks = s->kv_suffix + (size_t)l * 2 * 4 * B * kvd;
     float* vs = ks + (size_t)4 * B * kvd;
-    FWD_TRY(rms_norm_rows(s->x, w.n_in, s->h, M, H, c.rms_eps, st));
+    FWD_TRY(rms_norm_rows(s->x, w.n_in, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
     FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));
     if (t == 0) {
       FWD_TRY(rope_kv(s->qkv, M, c.heads, c.kv_heads, D, s->rope_cos, s->rope_sin, s->rope_positions,
                       s->q, kp, vp, cap, -1, s->d_L, s->d_status, st));
-      FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, M, cap, c.heads, c.kv_heads, D, scale, st));
+      FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
+                                scale, st));
     } else {
       const size_t slot = (size_t)(t - 1) * B * kvd;
       FWD_TRY(rope_kv(s->qkv, M, c.heads, c.kv_heads, D, s->rope_cos, s->rope_sin, s->rope_positions,
                       s->q, ks + slot, vs + slot, cap, t - 1, s->d_L, s->d_status, st));
-      FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn_part,
-                               s->attn, B, cap, c.heads, c.kv_heads, D, scale, st));
+      FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn_part, s->attn,
+                               s->attn_big, s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, st));
     }
     FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID));
-    FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, M, H, c.rms_eps, st));
+    FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
     FWD_TRY(gemm(s, s->h, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
     FWD_TRY(gemm(s, s->act, I, w.wd, s->x, H, nullptr, M, H, I, EPI_RESID));
   }
   if (t == 0) {
-    FWD_TRY(rms_norm_rows(s->x + (size_t)(M - 1) * H, s->norm_final, s->h, 1, H, c.rms_eps, st));
+    FWD_TRY(rms_norm_rows(s->x + (size_t)(M - 1) * H, s->norm_final, s->h, nullptr, nullptr, 1, H, c.rms_eps, st));
     FWD_TRY(gemv_f32(s->h, s->lm_head, s->logits, V, H, st));
   } else {
-    FWD_TRY(rms_norm_rows(s->x, s->norm_final, s->h, B, H, c.rms_eps, st));
+    FWD_TRY(rms_norm_rows(s->x, s->norm_final, s->h, s->h_big, s->h_small, B, H, c.rms_eps, st));
     FWD_TRY(gemm(s, s->h, H, s->lm_head, s->logits, V, nullptr, B, V, H, EPI_STORE));
   }
   return cudaSuccess;
@@ -456,7 +545,8 @@ static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t 
 static int check_result(rtr_session* s, const rtr_result* out) {
   const DevResult& r = *s->hres;
   const uint32_t st = r.status;
-  if (st & (RTR_DEV_BAD_TOKEN | RTR_DEV_BAD_PARENT | RTR_DEV_BAD_LENGTH | RTR_DEV_TOO_MANY_CAND | RTR_DEV_NAN_SCORE))
+  if (st & (RTR_DEV_BAD_TOKEN | RTR_DEV_BAD_PARENT | RTR_DEV_BAD_LENGTH | RTR_DEV_TOO_MANY_CAND | RTR_DEV_NAN_SCORE |
+            RTR_DEV_TIMEOUT))
     return fail(s, RTR_ERR_DEVICE, "device bound check failed (status 0x" + std::to_string(st) + ")");
   if (st & RTR_DEV_NOT_STOPPED)
     return fail(s, RTR_ERR_DEVICE, "beam search would continue after 5 steps (catalog grammar is not 3 SID tokens + newline + EOS)");
