@@ -185,6 +185,76 @@ struct TcParams {
   uint32_t* status;
 };
 
+RTR_DEVICE float4 f4add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
+
+// Split-K finish, run by every thread of the last CTA to arrive on a tile:
+// (1) sum the partial tiles in split order into a [64][128] shared tile
+//     (float4 slots, four splits of loads in flight per slot);
+// (2) apply the epilogue from shared memory with float4 stores.
+// Requires N % 4 == 0 and ldc % 4 == 0 (checked by the host).
+RTR_DEVICE void splitk_reduce_epilogue(const TcParams& p, float* red, int tok0, int n0, int rows, int tile,
+                                       long tstride) {
+  constexpr int SLOTS = (TC_NTOK * TC_WROWS / 4 + TC_THREADS - 1) / TC_THREADS;
+  const int cols4 = (p.N - n0 < TC_WROWS ? p.N - n0 : TC_WROWS) >> 2;
+  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (TC_NTOK * TC_WROWS));
+  const long zs = tstride >> 2;
+  const int nslots = rows * (TC_WROWS / 4);
+  float4 s[SLOTS];
+#pragma unroll
+  for (int u = 0; u < SLOTS; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int z = 0; z < p.splits; z += 4) {
+    float4 v[4][SLOTS];
+#pragma unroll
+    for (int dz = 0; dz < 4; ++dz)
+#pragma unroll
+      for (int u = 0; u < SLOTS; ++u) {
+        const int q = threadIdx.x + u * TC_THREADS;
+        const bool ok = z + dz < p.splits && q < nslots && (q & 31) < cols4;
+        v[dz][u] = ok ? __ldcg(base + (z + dz) * zs + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int dz = 0; dz < 4; ++dz)
+#pragma unroll
+      for (int u = 0; u < SLOTS; ++u) s[u] = f4add(s[u], v[dz][u]);  // split order (zero adds are exact)
+  }
+  float4* red4 = reinterpret_cast<float4*>(red);
+#pragma unroll
+  for (int u = 0; u < SLOTS; ++u) {
+    const int q = threadIdx.x + u * TC_THREADS;
+    if (q < nslots) red4[q] = s[u];
+  }
+  __syncthreads();
+
+  if (p.epi == EPI_SWIGLU) {
+    // packed rows: 32 q + [0,16) gate, 32 q + [16,32) up of intermediate 16 q + [0,16)
+    for (int q = threadIdx.x; q < rows * 16; q += TC_THREADS) {
+      const int j = q >> 4, blk = (q >> 2) & 3, g4 = q & 3;
+      const int c4 = blk * 8 + g4;
+      if (c4 + 4 >= cols4) continue;  // the up half lies past N
+      const float4 g = red4[j * 32 + c4], u = red4[j * 32 + c4 + 4];
+      float a[4] = {silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w};
+      float b[4], sm[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { b[e] = tf32_round(a[e]); sm[e] = a[e] - b[e]; }
+      const long o = (long)(tok0 + j) * p.ldc + ((n0 + blk * 32) >> 5) * 16 + g4 * 4;
+      *reinterpret_cast<float4*>(p.C + o) = make_float4(a[0], a[1], a[2], a[3]);
+      *reinterpret_cast<float4*>(p.C_big + o) = make_float4(b[0], b[1], b[2], b[3]);
+      *reinterpret_cast<float4*>(p.C_small + o) = make_float4(sm[0], sm[1], sm[2], sm[3]);
+    }
+    return;
+  }
+  for (int q = threadIdx.x; q < nslots; q += TC_THREADS) {
+    const int j = q >> 5, c4 = q & 31;
+    if (c4 >= cols4) continue;
+    float4 v = red4[q];
+    const int col = n0 + c4 * 4;
+    float4* c = reinterpret_cast<float4*>(p.C + (long)(tok0 + j) * p.ldc + col);
+    if (p.epi == EPI_BIAS) v = f4add(v, *reinterpret_cast<const float4*>(p.bias + col));
+    else if (p.epi == EPI_RESID) v = f4add(*c, v);
+    *c = v;
+  }
+}
+
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
                    const __grid_constant__ CUtensorMap tmXs, TcParams p) {
@@ -387,42 +457,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const bool have = warp >= 6 && warp <= 9;
   const int quarter = warp & 3;
   const int n = n0 + quarter * 32 + lane;  // weight row of this thread
+  const int rows = p.M - tok0 < TC_NTOK ? p.M - tok0 : TC_NTOK;  // real activation rows of the tile
   if (p.splits > 1) {
-    const long mpad = (long)gridDim.x * TC_NTOK;
+    // Partial tiles are tile-contiguous: ws[(split * tiles + tile)][row][128].
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    const long tstride = (long)gridDim.x * gridDim.y * (TC_NTOK * TC_WROWS);
     if (have && n < p.N) {
-      float* w = p.ws + ((long)blockIdx.z * mpad + tok0) * p.N + n;
+      float* w = p.ws + blockIdx.z * tstride + (long)tile * (TC_NTOK * TC_WROWS) + quarter * 32 + lane;
 #pragma unroll
-      for (int j = 0; j < TC_NTOK; ++j) {
-        __stcg(w, acc[j]);
-        w += p.N;
-      }
+      for (int j = 0; j < TC_NTOK; ++j)
+        if (j < rows) __stcg(w + j * TC_WROWS, acc[j]);
     }
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-      int* tk = p.tickets + blockIdx.y * gridDim.x + blockIdx.x;
+      int* tk = p.tickets + tile;
       last_cta = atomicAdd(tk, 1) == p.splits - 1;
       if (last_cta) *tk = 0;  // re-arm for the next launch / graph replay
     }
     __syncthreads();
     if (!last_cta) return;
     __threadfence();
-    if (have && n < p.N) {
-#pragma unroll
-      for (int j = 0; j < TC_NTOK; ++j) acc[j] = 0.f;
-      for (int z = 0; z < p.splits; ++z) {  // split order; 16 independent loads at a time
-        const float* w = p.ws + ((long)z * mpad + tok0) * p.N + n;
-#pragma unroll
-        for (int jb = 0; jb < TC_NTOK; jb += 16) {
-          float v[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __ldcg(w + (long)j * p.N);
-#pragma unroll
-          for (int j = 0; j < 16; ++j) acc[jb + j] += v[j];
-          w += 16L * p.N;
-        }
-      }
-    }
+    splitk_reduce_epilogue(p, reinterpret_cast<float*>(smem), tok0, n0, rows, tile, tstride);
+    return;
   }
   if (!have) return;
 
@@ -541,7 +598,8 @@ cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap
   const int tt = (M + TC_NTOK - 1) / TC_NTOK, wt = (N + TC_WROWS - 1) / TC_WROWS;
   const int nchunks = (K + TC_KC - 1) / TC_KC;
   int splits = tc_splits(tt * wt, nchunks, sms);
-  while (splits > 1 && ((size_t)splits * tt * TC_NTOK * N > ws_floats || tt * wt > max_tickets)) --splits;
+  if (splits > 1 && (N % 4 || ldc % 4 || (reinterpret_cast<uintptr_t>(C) & 15))) return cudaErrorInvalidValue;
+  while (splits > 1 && ((size_t)splits * tt * wt * TC_NTOK * TC_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
   TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tt, wt, splits);

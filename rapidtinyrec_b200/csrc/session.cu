@@ -674,6 +674,7 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   out->device_bytes = s->device_bytes;
   out->h2d_bytes_per_request = (int64_t)s->L * 4 + 4;
   out->d2h_bytes_per_request = (int64_t)sizeof(DevResult);
+  out->tensor_core_gemm = s->use_tc ? 1 : 0;
   return RTR_OK;
 }
 
