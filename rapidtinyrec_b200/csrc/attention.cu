@@ -2,18 +2,22 @@
 //
 // Prefill: causal GQA attention of one request (sdpa_attention_forward with
 // is_causal=True, transformers integrations/sdpa_attention.py:40-104).  A CTA
-// owns 16 query positions of one query head; key/value chunks of 32 rows are
-// staged in shared memory (keys transposed so lane j scores key j
-// conflict-free) and every warp runs an online softmax for its two rows.
+// owns 16 query positions of one query head, two per warp.
 //
 // Decode: the reference's folded_sdpa (rapidtinyrec/folded_attention.py:16-31)
 // maps query head h to KV head h / (Hq/Hkv) and attends over
 // cat(prefix.expand(50), suffix) (shared_prefix.py:22-29).  Here the prefix is
-// read in place: phase 1 streams each 32-key prefix chunk of a KV head into
-// shared memory once and scores it against all 50 beams of one query head,
-// writing (max, sum, weighted V) partials; phase 2 merges the partials with the
-// beam's own suffix keys, found through the ancestry table instead of a
-// physical reorder (the direct_reorder parent gather, prefix_replay.py:95-117).
+// read in place and never expanded: a CTA owns one query head and 8 beams (one
+// warp each); after the prefix, every warp walks its beam's own suffix keys,
+// found through the ancestry table instead of a physical reorder (the
+// direct_reorder parent gather, prefix_replay.py:95-117).
+//
+// Both stream the prefix K/V rows of the head's KV group through a
+// double-buffered shared ring of 64-key chunks with cp.async (K rows padded by
+// four floats so the float4 score reads of 8 consecutive keys hit distinct
+// banks), and every warp runs an online softmax over its query rows: lane j
+// scores keys j and j + 32 of the chunk, then accumulates P.V over its own
+// HD/32 output dimensions.
 #include <math.h>
 
 #include "common.cuh"
@@ -21,238 +25,273 @@
 
 namespace rtr {
 
-constexpr int KC = 32;     // keys per chunk
-constexpr int QB = 16;     // prefill query positions per CTA
-constexpr int ATT_THREADS = 256;
+constexpr int AK = 64;         // keys per chunk
+constexpr int AWARPS = 8;      // warps per CTA
+constexpr int ATHREADS = AWARPS * 32;
+constexpr int PQ = 16;         // prefill query positions per CTA (2 per warp)
+constexpr int DBEAMS = AWARPS; // decode beams per CTA (1 per warp)
 
+template <int HD> constexpr int kld() { return HD + 4; }
+template <int HD> constexpr size_t attn_smem_bytes(int qrows) {
+  return (size_t)(2 * AK * kld<HD>() + 2 * AK * HD + qrows * HD) * sizeof(float);
+}
+
+// Stage keys [k0, k0 + AK) of one KV group into ring slot `buf` (zero rows
+// past `kend`); one cp.async group.
 template <int HD>
-__global__ void __launch_bounds__(ATT_THREADS) prefill_attn_kernel(
+RTR_DEVICE void load_kv_chunk(float* kbuf, float* vbuf, const float* kbase, const float* vbase, int k0, int kend,
+                              int buf) {
+  constexpr int V4 = HD / 4;
+  float* kd = kbuf + (size_t)buf * AK * kld<HD>();
+  float* vd = vbuf + (size_t)buf * AK * HD;
+  for (int i = threadIdx.x; i < AK * V4; i += ATHREADS) {
+    const int j = i / V4, d = (i % V4) * 4;
+    const bool ok = k0 + j < kend;
+    const long row = ok ? k0 + j : 0;
+    cp_async16(kd + j * kld<HD>() + d, kbase + row * HD + d, ok);
+    cp_async16(vd + j * HD + d, vbase + row * HD + d, ok);
+  }
+  cp_async_commit();
+}
+
+// VEC consecutive floats from shared memory as one vector access.
+template <int VEC> RTR_DEVICE void load_vec(const float* src, float (&x)[VEC]);
+template <> RTR_DEVICE void load_vec<4>(const float* src, float (&x)[4]) {
+  const float4 v = *reinterpret_cast<const float4*>(src);
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+template <> RTR_DEVICE void load_vec<2>(const float* src, float (&x)[2]) {
+  const float2 v = *reinterpret_cast<const float2*>(src);
+  x[0] = v.x; x[1] = v.y;
+}
+
+// One warp, one query row (q in shared memory), one staged chunk of keys
+// [k0, k0 + AK): online-softmax update of (m, l, acc) over keys < kend.
+template <int HD>
+RTR_DEVICE void chunk_update(const float* qrow, const float* kc, const float* vc, int k0, int kend, float scale,
+                             float& m, float& l, float (&acc)[HD / 32]) {
+  constexpr int VEC = HD / 32;
+  const int lane = threadIdx.x & 31;
+  const float4* q4 = reinterpret_cast<const float4*>(qrow);
+  const float4* ka = reinterpret_cast<const float4*>(kc + lane * kld<HD>());
+  const float4* kb = reinterpret_cast<const float4*>(kc + (lane + 32) * kld<HD>());
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll 8
+  for (int d = 0; d < HD / 4; ++d) {
+    const float4 qq = q4[d], a = ka[d], b = kb[d];
+    s0 = fmaf(qq.x, a.x, s0); s0 = fmaf(qq.y, a.y, s0); s0 = fmaf(qq.z, a.z, s0); s0 = fmaf(qq.w, a.w, s0);
+    s1 = fmaf(qq.x, b.x, s1); s1 = fmaf(qq.y, b.y, s1); s1 = fmaf(qq.z, b.z, s1); s1 = fmaf(qq.w, b.w, s1);
+  }
+  s0 = k0 + lane < kend ? s0 * scale : -INFINITY;
+  s1 = k0 + lane + 32 < kend ? s1 * scale : -INFINITY;
+  const float mn = fmaxf(m, warp_max(fmaxf(s0, s1)));  // finite: key k0 is always valid
+  const float corr = expf(m - mn);
+  const float p0 = expf(s0 - mn), p1 = expf(s1 - mn);
+  l = l * corr + warp_sum(p0 + p1);
+  m = mn;
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) acc[i] *= corr;
+  const float* va = vc + lane * VEC;
+#pragma unroll 4
+  for (int j = 0; j < 32; ++j) {
+    const float pa = __shfl_sync(0xffffffffu, p0, j), pb = __shfl_sync(0xffffffffu, p1, j);
+    float x[VEC], y[VEC];
+    load_vec<VEC>(va + j * HD, x);
+    load_vec<VEC>(va + (j + 32) * HD, y);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] = fmaf(pa, x[i], acc[i]);
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[i] = fmaf(pb, y[i], acc[i]);
+  }
+}
+
+// ------------------------------------------------------------------ prefill
+template <int HD>
+__global__ void __launch_bounds__(ATHREADS) prefill_attn_kernel(
     const float* __restrict__ q, const float* __restrict__ kp, const float* __restrict__ vp,
     float* __restrict__ out, float* __restrict__ out_big, float* __restrict__ out_small, int L, int cap, int heads,
     int kv_heads, float scale) {
-  constexpr int PER = HD / 32;
-  __shared__ float qs[QB][HD];
-  __shared__ float ks[HD][KC + 1];
-  __shared__ float vs[KC][HD];
+  constexpr int VEC = HD / 32, ROWS = PQ / AWARPS;
+  extern __shared__ __align__(16) float asmem[];
+  float* kbuf = asmem;
+  float* vbuf = kbuf + 2 * AK * kld<HD>();
+  float* qs = vbuf + 2 * AK * HD;  // [PQ][HD]
   const int h = blockIdx.y, g = h / (heads / kv_heads);
-  const int q0 = blockIdx.x * QB;
+  const int q0 = blockIdx.x * PQ;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* kbase = kp + (long)g * cap * HD;
   const float* vbase = vp + (long)g * cap * HD;
+  const int kend = min(L, q0 + PQ);  // keys any row of the block may see
+  const int nchunks = (kend + AK - 1) / AK;
 
-  for (int i = threadIdx.x; i < QB * HD; i += ATT_THREADS) {
-    const int r = i / HD, d = i % HD;
-    qs[r][d] = (q0 + r < L) ? q[((long)(q0 + r) * heads + h) * HD + d] : 0.f;
+  load_kv_chunk<HD>(kbuf, vbuf, kbase, vbase, 0, kend, 0);
+  for (int i = threadIdx.x; i < PQ * HD / 4; i += ATHREADS) {
+    const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + r < L) v = *reinterpret_cast<const float4*>(q + ((long)(q0 + r) * heads + h) * HD + d);
+    *reinterpret_cast<float4*>(qs + r * HD + d) = v;
   }
-  constexpr int ROWS = QB / (ATT_THREADS / 32);  // 2 rows per warp
-  float m_run[ROWS], l_run[ROWS], acc[ROWS][PER];
+  float m[ROWS], l[ROWS], acc[ROWS][VEC];
 #pragma unroll
   for (int r = 0; r < ROWS; ++r) {
-    m_run[r] = -INFINITY; l_run[r] = 0.f;
+    m[r] = -INFINITY; l[r] = 0.f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) acc[r][i] = 0.f;
+    for (int i = 0; i < VEC; ++i) acc[r][i] = 0.f;
   }
-  const int last = min(L, q0 + QB) - 1;  // highest query position in the block
-  for (int c0 = 0; c0 <= last; c0 += KC) {
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + 1 < nchunks) load_kv_chunk<HD>(kbuf, vbuf, kbase, vbase, (c + 1) * AK, kend, (c + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
-    for (int i = threadIdx.x; i < KC * HD; i += ATT_THREADS) {
-      const int j = i / HD, d = i % HD;
-      const bool ok = c0 + j < L;
-      ks[d][j] = ok ? kbase[(long)(c0 + j) * HD + d] : 0.f;
-      vs[j][d] = ok ? vbase[(long)(c0 + j) * HD + d] : 0.f;
-    }
-    __syncthreads();
+    const float* kc = kbuf + (c & 1) * AK * kld<HD>();
+    const float* vc = vbuf + (c & 1) * AK * HD;
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
-      const int row = warp * ROWS + r;
-      const int qpos = q0 + row;
-      if (qpos >= L || c0 > qpos) continue;
-      float s = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < HD; ++d) s = fmaf(qs[row][d], ks[d][lane], s);
-      s *= scale;
-      const int kpos = c0 + lane;
-      if (kpos > qpos) s = -INFINITY;
-      const float mc = warp_max(s);
-      const float mn = fmaxf(m_run[r], mc);
-      const float corr = expf(m_run[r] - mn);
-      const float p = expf(s - mn);
-      l_run[r] = l_run[r] * corr + warp_sum(p);
-      m_run[r] = mn;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) acc[r][i] *= corr;
-#pragma unroll 8
-      for (int j = 0; j < KC; ++j) {
-        const float pj = __shfl_sync(0xffffffffu, p, j);
-#pragma unroll
-        for (int i = 0; i < PER; ++i) acc[r][i] = fmaf(pj, vs[j][lane + 32 * i], acc[r][i]);
-      }
+      const int row = warp * ROWS + r, qpos = q0 + row;
+      if (qpos < L && c * AK <= qpos)
+        chunk_update<HD>(qs + row * HD, kc, vc, c * AK, qpos + 1, scale, m[r], l[r], acc[r]);
     }
+    __syncthreads();  // the slot is refilled by the next iteration's load
   }
 #pragma unroll
   for (int r = 0; r < ROWS; ++r) {
     const int qpos = q0 + warp * ROWS + r;
     if (qpos >= L) continue;
-    const float inv = 1.0f / l_run[r];
+    const float inv = 1.0f / l[r];
 #pragma unroll
-    for (int i = 0; i < PER; ++i)
-      store_split(out, out_big, out_small, ((long)qpos * heads + h) * HD + lane + 32 * i, acc[r][i] * inv);
+    for (int i = 0; i < VEC; ++i)
+      store_split(out, out_big, out_small, ((long)qpos * heads + h) * HD + lane * VEC + i, acc[r][i] * inv);
   }
 }
 
 cudaError_t attention_prefill(const float* q, const float* k_prefix, const float* v_prefix,
                               float* out, float* out_big, float* out_small, int L, int prefix_cap, int heads,
                               int kv_heads, int head_dim, float scale, cudaStream_t stream) {
-  dim3 grid((L + QB - 1) / QB, heads);
+  if (L <= 0 || L > prefix_cap) return cudaErrorInvalidValue;
+  dim3 grid((L + PQ - 1) / PQ, heads);
   if (head_dim == 128)
-    prefill_attn_kernel<128><<<grid, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, out, out_big, out_small, L,
-                                                               prefix_cap, heads, kv_heads, scale);
+    prefill_attn_kernel<128><<<grid, ATHREADS, attn_smem_bytes<128>(PQ), stream>>>(
+        q, k_prefix, v_prefix, out, out_big, out_small, L, prefix_cap, heads, kv_heads, scale);
   else if (head_dim == 64)
-    prefill_attn_kernel<64><<<grid, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, out, out_big, out_small, L,
-                                                              prefix_cap, heads, kv_heads, scale);
+    prefill_attn_kernel<64><<<grid, ATHREADS, attn_smem_bytes<64>(PQ), stream>>>(
+        q, k_prefix, v_prefix, out, out_big, out_small, L, prefix_cap, heads, kv_heads, scale);
   else
     return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------- decode
-int attention_decode_chunks(int max_prefix) { return (max_prefix + KC - 1) / KC; }
-
-// Phase 1: grid (chunks, kv_heads, heads_per_group); one query head of the
-// group against one prefix chunk, all beams.
 template <int HD>
-__global__ void __launch_bounds__(ATT_THREADS) decode_prefix_kernel(
+__global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     const float* __restrict__ q, const float* __restrict__ kp, const float* __restrict__ vp,
-    const int32_t* __restrict__ L_dev, float* __restrict__ part, int beams, int cap, int heads,
-    int kv_heads, int nc_max, float scale) {
-  constexpr int PER = HD / 32;
-  __shared__ float ks[HD][KC + 1];
-  __shared__ float vs[KC][HD];
-  __shared__ float qrow[ATT_THREADS / 32][HD];
-  const int L = *L_dev;
-  const int c = blockIdx.x, g = blockIdx.y;
-  const int h = g * (heads / kv_heads) + blockIdx.z;
-  const int c0 = c * KC;
-  if (c0 >= L || L > cap) return;
-  const int nkeys = min(KC, L - c0);
-  const float* kbase = kp + ((long)g * cap + c0) * HD;
-  const float* vbase = vp + ((long)g * cap + c0) * HD;
-  for (int i = threadIdx.x; i < KC * HD; i += ATT_THREADS) {
-    const int j = i / HD, d = i % HD;
-    const bool ok = j < nkeys;
-    ks[d][j] = ok ? kbase[(long)j * HD + d] : 0.f;
-    vs[j][d] = ok ? vbase[(long)j * HD + d] : 0.f;
-  }
-  __syncthreads();
+    const float* __restrict__ ksuf, const float* __restrict__ vsuf, const int32_t* __restrict__ anc,
+    const int32_t* __restrict__ L_dev, float* __restrict__ out, float* __restrict__ out_big,
+    float* __restrict__ out_small, int beams, int cap, int heads, int kv_heads, int t, float scale,
+    uint32_t* __restrict__ status) {
+  constexpr int VEC = HD / 32;
+  extern __shared__ __align__(16) float asmem[];
+  float* kbuf = asmem;
+  float* vbuf = kbuf + 2 * AK * kld<HD>();
+  float* qs = vbuf + 2 * AK * HD;  // [DBEAMS][HD]
+  const int h = blockIdx.x, g = h / (heads / kv_heads);
+  const int b0 = blockIdx.y * DBEAMS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int b = warp; b < beams; b += ATT_THREADS / 32) {
-    const float* qr = q + ((long)b * heads + h) * HD;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) qrow[warp][lane + 32 * i] = qr[lane + 32 * i];
-    __syncwarp();
-    float s = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < HD; ++d) s = fmaf(qrow[warp][d], ks[d][lane], s);
-    s = lane < nkeys ? s * scale : -INFINITY;
-    const float m = warp_max(s);
-    const float p = expf(s - m);
-    const float l = warp_sum(p);
-    float acc[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) acc[i] = 0.f;
-#pragma unroll 8
-    for (int j = 0; j < KC; ++j) {
-      const float pj = __shfl_sync(0xffffffffu, p, j);
-#pragma unroll
-      for (int i = 0; i < PER; ++i) acc[i] = fmaf(pj, vs[j][lane + 32 * i], acc[i]);
-    }
-    float* dst = part + (((long)b * heads + h) * nc_max + c) * (HD + 2);
-    if (lane == 0) { dst[0] = m; dst[1] = l; }
-#pragma unroll
-    for (int i = 0; i < PER; ++i) dst[2 + lane + 32 * i] = acc[i];
-    __syncwarp();
+  const int b = b0 + warp;
+  int L = *L_dev;
+  if (L < 1 || L > cap) {  // the prefill recorded no valid prefix: attend to the suffix only
+    if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
+    L = 0;
   }
-}
+  const float* kbase = kp + (long)g * cap * HD;
+  const float* vbase = vp + (long)g * cap * HD;
+  const int nchunks = (L + AK - 1) / AK;
 
-// Phase 2: one warp per (beam, query head): merge prefix partials and the
-// beam's suffix keys (slots 0..t-1).
-template <int HD>
-__global__ void decode_combine_kernel(const float* __restrict__ q, const float* __restrict__ ks,
-                                      const float* __restrict__ vsuf, const int32_t* __restrict__ anc,
-                                      const int32_t* __restrict__ L_dev, const float* __restrict__ part,
-                                      float* __restrict__ out, float* __restrict__ out_big,
-                                      float* __restrict__ out_small, int beams, int heads, int kv_heads,
-                                      int nc_max, int t, float scale) {
-  constexpr int PER = HD / 32;
-  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (warp_global >= beams * heads) return;
-  const int b = warp_global / heads, h = warp_global % heads;
-  const int g = h / (heads / kv_heads);
-  const int L = *L_dev;
-  const int nc = min((L + KC - 1) / KC, nc_max);
-  float qv[PER];
+  if (nchunks > 0) load_kv_chunk<HD>(kbuf, vbuf, kbase, vbase, 0, L, 0);
+  for (int i = threadIdx.x; i < DBEAMS * HD / 4; i += ATHREADS) {
+    const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (b0 + r < beams) v = *reinterpret_cast<const float4*>(q + ((long)(b0 + r) * heads + h) * HD + d);
+    *reinterpret_cast<float4*>(qs + r * HD + d) = v;
+  }
+  float m = -INFINITY, l = 0.f, acc[VEC];
 #pragma unroll
-  for (int i = 0; i < PER; ++i) qv[i] = q[((long)b * heads + h) * HD + lane + 32 * i];
-  // suffix scores
-  float ss[4];
-  int rows[4];
-  float M = -INFINITY;
+  for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + 1 < nchunks) load_kv_chunk<HD>(kbuf, vbuf, kbase, vbase, (c + 1) * AK, L, (c + 1) & 1);
+    else cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    if (b < beams)
+      chunk_update<HD>(qs + warp * HD, kbuf + (c & 1) * AK * kld<HD>(), vbuf + (c & 1) * AK * HD, c * AK, L, scale,
+                       m, l, acc);
+    __syncthreads();  // the slot is refilled by the next iteration's load
+  }
+  if (nchunks == 0) __syncthreads();  // q rows staged
+  if (b >= beams) return;
+
+  // the beam's suffix: slot s < t - 1 lives in row anc[b][s], slot t - 1 in row b
+  const float* qrow = qs + warp * HD + lane * VEC;
+  float qv[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) qv[i] = qrow[i];
   for (int s = 0; s < t; ++s) {
     int row = (s == t - 1) ? b : anc[b * 4 + s];
-    if (row < 0 || row >= beams) row = b;
-    rows[s] = row;
-    const float* key = ks + (((long)s * beams + row) * kv_heads + g) * HD;
+    if (row < 0 || row >= beams) {
+      if (lane == 0) atomicOr(status, RTR_DEV_BAD_PARENT);
+      row = b;
+    }
+    const long off = (((long)s * beams + row) * kv_heads + g) * HD + lane * VEC;
     float d = 0.f;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) d = fmaf(qv[i], key[lane + 32 * i], d);
-    d = warp_sum(d) * scale;
-    ss[s] = d;
-    M = fmaxf(M, d);
-  }
-  const float* pb = part + ((long)b * heads + h) * nc_max * (HD + 2);
-  for (int c = 0; c < nc; ++c) M = fmaxf(M, pb[c * (HD + 2)]);
-  float l = 0.f, acc[PER];
+    for (int i = 0; i < VEC; ++i) d = fmaf(qv[i], ksuf[off + i], d);
+    const float sc = warp_sum(d) * scale;
+    const float mn = fmaxf(m, sc);
+    const float corr = expf(m - mn);
+    const float p = expf(sc - mn);
+    l = l * corr + p;
+    m = mn;
 #pragma unroll
-  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
-  for (int c = 0; c < nc; ++c) {
-    const float* pc = pb + c * (HD + 2);
-    const float w = expf(pc[0] - M);
-    l = fmaf(pc[1], w, l);
-#pragma unroll
-    for (int i = 0; i < PER; ++i) acc[i] = fmaf(pc[2 + lane + 32 * i], w, acc[i]);
-  }
-  for (int s = 0; s < t; ++s) {
-    const float w = expf(ss[s] - M);
-    l += w;
-    const float* val = vsuf + (((long)s * beams + rows[s]) * kv_heads + g) * HD;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) acc[i] = fmaf(w, val[lane + 32 * i], acc[i]);
+    for (int i = 0; i < VEC; ++i) acc[i] = fmaf(p, vsuf[off + i], acc[i] * corr);
   }
   const float inv = 1.0f / l;
 #pragma unroll
-  for (int i = 0; i < PER; ++i)
-    store_split(out, out_big, out_small, ((long)b * heads + h) * HD + lane + 32 * i, acc[i] * inv);
+  for (int i = 0; i < VEC; ++i)
+    store_split(out, out_big, out_small, ((long)b * heads + h) * HD + lane * VEC + i, acc[i] * inv);
 }
 
 cudaError_t attention_decode(const float* q, const float* k_prefix, const float* v_prefix,
                              const float* k_suffix, const float* v_suffix, const int32_t* anc,
-                             const int32_t* L_dev, int t, float* part, float* out, float* out_big,
-                             float* out_small, int beams, int prefix_cap, int heads, int kv_heads, int head_dim,
-                             float scale, cudaStream_t stream) {
-  const int nc_max = attention_decode_chunks(prefix_cap);
-  dim3 g1(nc_max, kv_heads, heads / kv_heads);
-  const int warps = beams * heads, cb = (warps + 3) / 4;
-  if (head_dim == 128) {
-    decode_prefix_kernel<128><<<g1, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, L_dev, part, beams, prefix_cap, heads, kv_heads, nc_max, scale);
-    decode_combine_kernel<128><<<cb, 128, 0, stream>>>(q, k_suffix, v_suffix, anc, L_dev, part, out, out_big, out_small, beams, heads, kv_heads, nc_max, t, scale);
-  } else if (head_dim == 64) {
-    decode_prefix_kernel<64><<<g1, ATT_THREADS, 0, stream>>>(q, k_prefix, v_prefix, L_dev, part, beams, prefix_cap, heads, kv_heads, nc_max, scale);
-    decode_combine_kernel<64><<<cb, 128, 0, stream>>>(q, k_suffix, v_suffix, anc, L_dev, part, out, out_big, out_small, beams, heads, kv_heads, nc_max, t, scale);
-  } else {
+                             const int32_t* L_dev, int t, float* out, float* out_big, float* out_small, int beams,
+                             int prefix_cap, int heads, int kv_heads, int head_dim, float scale, uint32_t* status,
+                             cudaStream_t stream) {
+  if (t < 1 || t > 4 || beams > MAX_BEAMS) return cudaErrorInvalidValue;
+  dim3 grid(heads, (beams + DBEAMS - 1) / DBEAMS);
+  if (head_dim == 128)
+    decode_attn_kernel<128><<<grid, ATHREADS, attn_smem_bytes<128>(DBEAMS), stream>>>(
+        q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, out, out_big, out_small, beams, prefix_cap, heads,
+        kv_heads, t, scale, status);
+  else if (head_dim == 64)
+    decode_attn_kernel<64><<<grid, ATHREADS, attn_smem_bytes<64>(DBEAMS), stream>>>(
+        q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, out, out_big, out_small, beams, prefix_cap, heads,
+        kv_heads, t, scale, status);
+  else
     return cudaErrorInvalidValue;
-  }
   return cudaGetLastError();
+}
+
+cudaError_t attention_init() {
+  cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)attn_smem_bytes<128>(PQ));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn_smem_bytes<64>(PQ));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn_smem_bytes<128>(DBEAMS));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn_smem_bytes<64>(DBEAMS));
+  return e;
 }
 
 }  // namespace rtr

@@ -59,13 +59,12 @@ cudaError_t attention_prefill(const float* q, const float* k_prefix, const float
                               int kv_heads, int head_dim, float scale, cudaStream_t stream);
 // Decode attention over the shared prefix (length *L_dev) and `t` suffix
 // slots; suffix slot s of beam b lives in row anc[b*4+s] (slot t-1: row b).
-int attention_decode_chunks(int max_prefix);
 cudaError_t attention_decode(const float* q, const float* k_prefix, const float* v_prefix,
                              const float* k_suffix, const float* v_suffix, const int32_t* anc,
-                             const int32_t* L_dev, int t, float* part, float* out, float* out_big,
-                             float* out_small, int beams,
-                             int prefix_cap, int heads, int kv_heads, int head_dim, float scale,
+                             const int32_t* L_dev, int t, float* out, float* out_big, float* out_small, int beams,
+                             int prefix_cap, int heads, int kv_heads, int head_dim, float scale, uint32_t* status,
                              cudaStream_t stream);
+cudaError_t attention_init();
 
 // ---- constraints + beam step (beam.cu) ----
 struct DevTables {

@@ -64,7 +64,7 @@ struct rtr_session {
   float *h_big = nullptr, *h_small = nullptr, *attn_big = nullptr, *attn_small = nullptr;
   float *act_big = nullptr, *act_small = nullptr;
   std::map<const void*, std::pair<float*, float*>> split_of;
-  float *logits = nullptr, *attn_part = nullptr, *ws = nullptr;
+  float *logits = nullptr, *ws = nullptr;
   float* proc_scratch = nullptr;  // [PROC_MAX_ROWS][PROC_SPLITS][2]
   size_t ws_floats = 0;
   int* tickets = nullptr;
@@ -172,6 +172,7 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(gemm_init());
   CREATE_TRY(beam_init());
   CREATE_TRY(gemm_tc_init());
+  CREATE_TRY(attention_init());
   if (const char* g = std::getenv("RTR_GEMM")) s->use_tc = std::strcmp(g, "ffma") != 0;
 
   const long H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
@@ -209,7 +210,6 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(dev_alloc(s, &s->act_big, M * I));
   CREATE_TRY(dev_alloc(s, &s->act_small, M * I));
   CREATE_TRY(dev_alloc(s, &s->logits, B * V));
-  CREATE_TRY(dev_alloc(s, &s->attn_part, (size_t)B * c.heads * attention_decode_chunks(cap) * (D + 2)));
   long max_n = qkvd;
   if (H > max_n) max_n = H;
   if (2 * I > max_n) max_n = 2 * I;
@@ -487,8 +487,8 @@ static cudaError_t forward(rtr_session* s, int t) {
       const size_t slot = (size_t)(t - 1) * B * kvd;
       FWD_TRY(rope_kv(s->qkv, M, c.heads, c.kv_heads, D, s->rope_cos, s->rope_sin, s->rope_positions,
                       s->q, ks + slot, vs + slot, cap, t - 1, s->d_L, s->d_status, st));
-      FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn_part, s->attn,
-                               s->attn_big, s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, st));
+      FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
+                               s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, st));
     }
     FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID));
     FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
