@@ -521,6 +521,14 @@ static int ready(rtr_session* s) {
   return RTR_OK;
 }
 
+
+// Kernels one forward pass launches: embedding, 8 per layer (RMSNorm, q/k/v
+// GEMM, RoPE + cache write, attention, o GEMM, RMSNorm, gate/up GEMM, down
+// GEMM), final RMSNorm and the LM head.  The step tail is 4 (max, two sums,
+// beam selection).
+static int64_t forward_kernels(const rtr_session* s) { return 1 + 8 * (int64_t)s->cfg.layers + 2; }
+static constexpr int64_t kTailKernels = 4;
+
 static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t on_device) {
   if (!ids) return fail(s, RTR_ERR_ARG, "null ids");
   if (L < 3 || L > s->cfg.max_prefix)
@@ -536,7 +544,7 @@ static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t 
   CUDA_TRY(s, beam_reset(s->beam, s->d_ids, s->d_L, beams_of(s), s->stream));
   CUDA_TRY(s, forward(s, 0));
   CUDA_TRY(s, beam_step(s->beam, s->logits, 1, s->cfg.vocab, beams_of(s), 0, s->tb, s->d_status, s->stream));
-  s->launches += 1 + (1 + 8 * (int64_t)s->cfg.layers + 2) + 4;
+  s->launches += 1 + forward_kernels(s) + kTailKernels;  // beam_reset, forward, step tail
   s->steps_done = 0;
   s->in_flight = false;
   return RTR_OK;
@@ -576,7 +584,7 @@ int rtr_decode_step(rtr_session* s, int32_t t) {
   if (s->steps_done != t - 1) return fail(s, RTR_ERR_STATE, "decode steps must follow prefill in order");
   CUDA_TRY(s, cudaSetDevice(s->device));
   CUDA_TRY(s, decode_and_tail(s, t));
-  s->launches += (1 + 9 * (int64_t)s->cfg.layers + 2) + 4;
+  s->launches += forward_kernels(s) + kTailKernels;
   s->steps_done = t;
   return RTR_OK;
 }
@@ -659,12 +667,11 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   if (!s || !out) return RTR_ERR_ARG;
   const auto& c = s->cfg;
   const int64_t kvd = (int64_t)c.kv_heads * c.head_dim, B = c.num_beams;
-  const int64_t per_layer_prefill = 8, per_layer_decode = 9, tail = 4;
   memset(out, 0, sizeof(*out));
   out->requests = s->requests;
   out->kernel_launches = s->launches;
-  out->launches_per_request = 1 + (1 + per_layer_prefill * c.layers + 2) + tail +
-                              (NSTEPS - 1) * ((1 + per_layer_decode * c.layers + 2) + tail) + 1;
+  // beam_reset + NSTEPS x (forward + step tail) + beam_finalize
+  out->launches_per_request = 1 + NSTEPS * (forward_kernels(s) + kTailKernels) + 1;
   out->graph_kernel_nodes = s->graph_kernels;
   out->prefix_bytes_written = (int64_t)c.layers * 2 * kvd * s->L * (int64_t)sizeof(float);
   out->prefix_bytes_reordered = 0;

@@ -182,6 +182,19 @@ def test_graph_and_eager_steps_bit_identical_and_repeatable(tiny_engine, tiny):
     assert c != a
 
 
+def test_report_counts_match_the_captured_graph(tiny_engine, tiny):
+    """The per-request launch count the bench reports equals what runs: the
+    decode graph's kernel nodes plus the eager prefill kernels."""
+    tiny_engine.generate(tiny['users'][0].prompt_token_ids)
+    rep = tiny_engine.report()
+    cfg = tiny['cfg']
+    forward = 1 + 8 * cfg.layers + 2          # embed, 8 per layer, final norm, LM head
+    tail = 4                                  # max, two sums, beam selection
+    assert rep['graph_kernel_nodes'] == 4 * (forward + tail) + 1   # decode steps 1-4, finalize
+    assert rep['launches_per_request'] == 1 + forward + tail + rep['graph_kernel_nodes']
+    assert rep['tensor_core_gemm'] == 1
+
+
 def test_contract_violations_raise(tiny_engine, tiny):
     from rapidtinyrec_b200._native import RTR_ERR_ARG, RTR_ERR_STATE, NativeError
     with pytest.raises(NativeError) as e:
