@@ -112,6 +112,8 @@ __global__ void __launch_bounds__(ATHREADS) prefill_attn_kernel(
     float* __restrict__ out, float* __restrict__ out_big, float* __restrict__ out_small, int L, int cap, int heads,
     int kv_heads, float scale) {
   constexpr int VEC = HD / 32, ROWS = PQ / AWARPS;
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) float asmem[];
   float* kbuf = asmem;
   float* vbuf = kbuf + 2 * AK * kld<HD>();
@@ -170,14 +172,12 @@ cudaError_t attention_prefill(const float* q, const float* k_prefix, const float
   if (L <= 0 || L > prefix_cap) return cudaErrorInvalidValue;
   dim3 grid((L + PQ - 1) / PQ, heads);
   if (head_dim == 128)
-    prefill_attn_kernel<128><<<grid, ATHREADS, attn_smem_bytes<128>(PQ), stream>>>(
-        q, k_prefix, v_prefix, out, out_big, out_small, L, prefix_cap, heads, kv_heads, scale);
+    return launch_pdl(PDL_ATTN, prefill_attn_kernel<128>, grid, dim3(ATHREADS), attn_smem_bytes<128>(PQ), stream, q, k_prefix,
+                      v_prefix, out, out_big, out_small, L, prefix_cap, heads, kv_heads, scale);
   else if (head_dim == 64)
-    prefill_attn_kernel<64><<<grid, ATHREADS, attn_smem_bytes<64>(PQ), stream>>>(
-        q, k_prefix, v_prefix, out, out_big, out_small, L, prefix_cap, heads, kv_heads, scale);
-  else
-    return cudaErrorInvalidValue;
-  return cudaGetLastError();
+    return launch_pdl(PDL_ATTN, prefill_attn_kernel<64>, grid, dim3(ATHREADS), attn_smem_bytes<64>(PQ), stream, q, k_prefix,
+                      v_prefix, out, out_big, out_small, L, prefix_cap, heads, kv_heads, scale);
+  return cudaErrorInvalidValue;
 }
 
 // ------------------------------------------------------------------- decode
@@ -189,6 +189,8 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     float* __restrict__ out_small, int beams, int cap, int heads, int kv_heads, int t, float scale,
     uint32_t* __restrict__ status) {
   constexpr int VEC = HD / 32;
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) float asmem[];
   float* kbuf = asmem;
   float* vbuf = kbuf + 2 * AK * kld<HD>();
@@ -267,16 +269,14 @@ cudaError_t attention_decode(const float* q, const float* k_prefix, const float*
   if (t < 1 || t > 4 || beams > MAX_BEAMS) return cudaErrorInvalidValue;
   dim3 grid(heads, (beams + DBEAMS - 1) / DBEAMS);
   if (head_dim == 128)
-    decode_attn_kernel<128><<<grid, ATHREADS, attn_smem_bytes<128>(DBEAMS), stream>>>(
-        q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, out, out_big, out_small, beams, prefix_cap, heads,
-        kv_heads, t, scale, status);
+    return launch_pdl(PDL_ATTN, decode_attn_kernel<128>, grid, dim3(ATHREADS), attn_smem_bytes<128>(DBEAMS), stream, q,
+                      k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, out, out_big, out_small, beams, prefix_cap,
+                      heads, kv_heads, t, scale, status);
   else if (head_dim == 64)
-    decode_attn_kernel<64><<<grid, ATHREADS, attn_smem_bytes<64>(DBEAMS), stream>>>(
-        q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, out, out_big, out_small, beams, prefix_cap, heads,
-        kv_heads, t, scale, status);
-  else
-    return cudaErrorInvalidValue;
-  return cudaGetLastError();
+    return launch_pdl(PDL_ATTN, decode_attn_kernel<64>, grid, dim3(ATHREADS), attn_smem_bytes<64>(DBEAMS), stream, q,
+                      k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, out, out_big, out_small, beams, prefix_cap,
+                      heads, kv_heads, t, scale, status);
+  return cudaErrorInvalidValue;
 }
 
 cudaError_t attention_init() {

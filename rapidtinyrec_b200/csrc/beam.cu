@@ -119,6 +119,8 @@ int lookup_width(const DevTables& tb, int step) { return lookup_width_of(tb, ste
 
 // -------------------------------------------------- vocabulary passes
 __global__ void tail_max_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[33];
   const int row = blockIdx.x, sp = blockIdx.y;
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
@@ -136,6 +138,8 @@ __device__ __forceinline__ float row_max(const BeamState* st, int row) {
 }
 
 __global__ void tail_sum1_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[33];
   const int row = blockIdx.x, sp = blockIdx.y;
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
@@ -148,6 +152,8 @@ __global__ void tail_sum1_kernel(const float* __restrict__ logits, int vocab, Be
 }
 
 __global__ void tail_sum2_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[33];
   const int row = blockIdx.x, sp = blockIdx.y;
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
@@ -193,6 +199,8 @@ struct SelShared {
 __global__ void __launch_bounds__(SEL_THREADS) beam_select_kernel(BeamState* st, const float* __restrict__ logits,
                                                                  int rows, int vocab, int beams, int step,
                                                                  DevTables tb, uint32_t* status) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ uint64_t cand[];
   __shared__ SelShared sh;
   const int tid = threadIdx.x, nt = blockDim.x;
@@ -426,13 +434,15 @@ cudaError_t beam_init() {
 cudaError_t beam_step(BeamState* st, const float* logits, int rows, int vocab, int beams, int step,
                       const DevTables& tb, uint32_t* status, cudaStream_t stream) {
   dim3 grid(rows, TAIL_SPLITS);
-  tail_max_kernel<<<grid, TAIL_THREADS, 0, stream>>>(logits, vocab, st);
-  tail_sum1_kernel<<<grid, TAIL_THREADS, 0, stream>>>(logits, vocab, st);
-  tail_sum2_kernel<<<grid, TAIL_THREADS, 0, stream>>>(logits, vocab, st);
+  cudaError_t e = launch_pdl(PDL_TAIL, tail_max_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st);
+  if (e == cudaSuccess) e = launch_pdl(PDL_TAIL, tail_sum1_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st);
+  if (e == cudaSuccess) e = launch_pdl(PDL_TAIL, tail_sum2_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st);
   const int width = lookup_width_of(tb, step);
   const size_t need = (size_t)beams * width * sizeof(uint64_t);
-  beam_select_kernel<<<1, SEL_THREADS, need, stream>>>(st, logits, rows, vocab, beams, step, tb, status);
-  return cudaGetLastError();
+  if (e == cudaSuccess)
+    e = launch_pdl(PDL_TAIL, beam_select_kernel, dim3(1), dim3(SEL_THREADS), need, stream, st, logits, rows, vocab, beams, step,
+                   tb, status);
+  return e;
 }
 
 // ------------------------------------------------------------ reset / output

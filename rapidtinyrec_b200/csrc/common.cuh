@@ -4,6 +4,10 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <utility>
 
 #define RTR_DEVICE __device__ __forceinline__
 
@@ -84,3 +88,55 @@ template <int N> RTR_DEVICE void cp_async_wait() { asm volatile("cp.async.wait_g
 // prologue, and wait for the previous kernel's memory before reading it.
 RTR_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 RTR_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }
+
+// Programmatic dependent launch (PDL) policy per kernel class.  RTR_PDL is a
+// comma-separated list of classes launched with PDL ("gemm", "norm", "rope",
+// "attn", "embed", "gemv", "tail"), "0" for none, "all" for every class.
+// Read once per process.  The default leaves RMSNorm and RoPE on plain
+// launches: a tensor-core GEMM CTA (352 threads x 168 registers) cannot share
+// an SM with their CTAs, so placing them early (waiting on the previous GEMM)
+// splits the next GEMM's single-wave grid; measured on the 1.5B decode, PDL on
+// RMSNorm cost 1.9 ms per request, on RoPE 0.2 ms, while the GEMM, attention,
+// embedding, GEMV and beam-tail launches each gained.
+enum PdlClass : unsigned {
+  PDL_GEMM = 1u, PDL_NORM = 2u, PDL_ROPE = 4u, PDL_ATTN = 8u, PDL_EMBED = 16u, PDL_GEMV = 32u, PDL_TAIL = 64u,
+  PDL_ALL = 127u
+};
+constexpr unsigned kPdlDefault = PDL_GEMM | PDL_ATTN | PDL_EMBED | PDL_GEMV | PDL_TAIL;
+inline unsigned pdl_mask() {
+  static const unsigned mask = [] {
+    const char* e = getenv("RTR_PDL");
+    if (!e) return kPdlDefault;
+    if (strcmp(e, "all") == 0) return (unsigned)PDL_ALL;
+    static const struct { const char* name; unsigned bit; } names[] = {
+        {"gemm", PDL_GEMM}, {"norm", PDL_NORM}, {"rope", PDL_ROPE}, {"attn", PDL_ATTN},
+        {"embed", PDL_EMBED}, {"gemv", PDL_GEMV}, {"tail", PDL_TAIL}};
+    unsigned m = 0;
+    for (const auto& n : names)
+      if (strstr(e, n.name)) m |= n.bit;
+    return m;
+  }();
+  return mask;
+}
+inline bool pdl_on(unsigned cls) { return (pdl_mask() & cls) != 0; }
+
+// Launch with programmatic stream serialization: the kernel may be scheduled
+// while its predecessor in the stream is still running.  Kernels launched this
+// way call pdl_launch_dependents() and then pdl_wait() before touching memory
+// (the tensor-core GEMM streams its constant weights before the wait), so
+// memory order stays stream order and only launch latency and prologues overlap.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(unsigned cls, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_on(cls) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}

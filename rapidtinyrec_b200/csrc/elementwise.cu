@@ -11,6 +11,8 @@ namespace rtr {
 // ---------------------------------------------------------------- embedding
 __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* table, int vocab,
                              int hidden, float* x, uint32_t* status) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int m = blockIdx.x;
   int tok = ids[(long)m * ids_stride];
   if (tok < 0 || tok >= vocab) {
@@ -24,14 +26,15 @@ __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* ta
 
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
                        int hidden, float* x, uint32_t* status, cudaStream_t stream) {
-  embed_kernel<<<M, 128, 0, stream>>>(ids, ids_stride, table, vocab, hidden, x, status);
-  return cudaGetLastError();
+  return launch_pdl(PDL_EMBED, embed_kernel, dim3(M), dim3(128), 0, stream, ids, ids_stride, table, vocab, hidden, x, status);
 }
 
 // ------------------------------------------------------------------ RMSNorm
 // Qwen2RMSNorm.forward (modeling_qwen2.py:258-263): w * (x * rsqrt(mean(x^2) + eps)).
 __global__ void rms_norm_kernel(const float* x, const float* w, float* h, float* h_big, float* h_small, int hidden,
                                 float eps) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int m = blockIdx.x;
   const float4* xr = reinterpret_cast<const float4*>(x + (long)m * hidden);
   float ss = 0.f;
@@ -64,8 +67,7 @@ __global__ void rms_norm_kernel(const float* x, const float* w, float* h, float*
 
 cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big, float* h_small, int M, int hidden,
                           float eps, cudaStream_t stream) {
-  rms_norm_kernel<<<M, 256, 0, stream>>>(x, w, h, h_big, h_small, hidden, eps);
-  return cudaGetLastError();
+  return launch_pdl(PDL_NORM, rms_norm_kernel, dim3(M), dim3(256), 0, stream, x, w, h, h_big, h_small, hidden, eps);
 }
 
 // --------------------------------------------------------------------- RoPE
@@ -75,6 +77,8 @@ __global__ void rope_kv_kernel(const float* qkv, int heads, int kv_heads, int he
                                const float* cos_t, const float* sin_t, int rope_positions,
                                float* q_out, float* k_dst, float* v_dst, int prefix_cap, int slot,
                                const int32_t* L_dev, uint32_t* status) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int m = blockIdx.x;
   const int half = head_dim / 2;
   const int qkv_dim = (heads + 2 * kv_heads) * head_dim;
@@ -118,14 +122,15 @@ cudaError_t rope_kv(const float* qkv, int M, int heads, int kv_heads, int head_d
                     const float* cos_t, const float* sin_t, int rope_positions,
                     float* q_out, float* k_dst, float* v_dst, int prefix_cap,
                     int slot, const int32_t* L_dev, uint32_t* status, cudaStream_t stream) {
-  rope_kv_kernel<<<M, 256, 0, stream>>>(qkv, heads, kv_heads, head_dim, cos_t, sin_t, rope_positions,
-                                        q_out, k_dst, v_dst, prefix_cap, slot, L_dev, status);
-  return cudaGetLastError();
+  return launch_pdl(PDL_ROPE, rope_kv_kernel, dim3(M), dim3(256), 0, stream, qkv, heads, kv_heads, head_dim, cos_t, sin_t,
+                    rope_positions, q_out, k_dst, v_dst, prefix_cap, slot, L_dev, status);
 }
 
 // --------------------------------------------------------------------- GEMV
 // y[n] = dot(x, W[n]) for the last-token LM head of the prefill (M = 1).
 __global__ void gemv_kernel(const float* x, const float* W, float* y, int N, int K) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ float xs[];
   for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = x[i];
   __syncthreads();
@@ -152,8 +157,8 @@ __global__ void gemv_kernel(const float* x, const float* W, float* y, int N, int
 
 cudaError_t gemv_f32(const float* x, const float* W, float* y, int N, int K, cudaStream_t stream) {
   const int threads = 256, rows_per_block = (threads / 32) * 4;
-  gemv_kernel<<<(N + rows_per_block - 1) / rows_per_block, threads, K * sizeof(float), stream>>>(x, W, y, N, K);
-  return cudaGetLastError();
+  return launch_pdl(PDL_GEMV, gemv_kernel, dim3((N + rows_per_block - 1) / rows_per_block), dim3(threads), K * sizeof(float),
+                    stream, x, W, y, N, K);
 }
 
 // ------------------------------------------------------- synthetic weights

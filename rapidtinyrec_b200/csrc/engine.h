@@ -7,7 +7,23 @@
 
 namespace rtr {
 
-enum Epilogue : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3 };
+enum Epilogue : int { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ROPE = 4 };
+
+// EPI_ROPE (tensor-core GEMM only): the q/k/v projection's epilogue adds the
+// bias, applies RoPE to q and k and writes q to q_out [M][heads*D] and k/v to
+// the cache, exactly as rope_kv() below does from a stored projection.
+struct RopeArgs {
+  const float* cos_t;
+  const float* sin_t;
+  int positions;           // rows of the cos/sin tables
+  int heads, kv_heads, head_dim;
+  float* q_out;
+  float* k_dst;
+  float* v_dst;
+  int prefix_cap;
+  int slot;                // < 0: prefill (row m at position m); else decode suffix slot
+  const int32_t* L_dev;    // decode: prefix length (position = *L_dev + slot)
+};
 
 // ---- GEMM (gemm_ffma.cu) ----
 cudaError_t gemm_init();
@@ -31,7 +47,7 @@ bool make_tmap_packed(TensorMap* out, const float* packed, int N, int K);
 cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
                     float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                     size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
-                    bool pdl);
+                    bool pdl, const RopeArgs* rope = nullptr);
 
 // ---- element-wise (elementwise.cu) ----
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,

@@ -183,19 +183,16 @@ struct TcParams {
   float* ws;
   int* tickets;
   uint32_t* status;
+  RopeArgs rope;    // EPI_ROPE only
 };
 
 RTR_DEVICE float4 f4add(float4 a, float4 b) { return make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w); }
 
-// Split-K finish, run by every thread of the last CTA to arrive on a tile:
-// (1) sum the partial tiles in split order into a [64][128] shared tile
-//     (float4 slots, four splits of loads in flight per slot);
-// (2) apply the epilogue from shared memory with float4 stores.
-// Requires N % 4 == 0 and ldc % 4 == 0 (checked by the host).
-RTR_DEVICE void splitk_reduce_epilogue(const TcParams& p, float* red, int tok0, int n0, int rows, int tile,
-                                       long tstride) {
+// Split-K finish, part 1, run by every thread of the last CTA to arrive on a
+// tile: sum the partial tiles in split order into a [64][128] shared tile
+// (float4 slots, four splits of loads in flight per slot).
+RTR_DEVICE void splitk_sum(const TcParams& p, float4* red4, int rows, int cols4, int tile, long tstride) {
   constexpr int SLOTS = (TC_NTOK * TC_WROWS / 4 + TC_THREADS - 1) / TC_THREADS;
-  const int cols4 = (p.N - n0 < TC_WROWS ? p.N - n0 : TC_WROWS) >> 2;
   const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (TC_NTOK * TC_WROWS));
   const long zs = tstride >> 2;
   const int nslots = rows * (TC_WROWS / 4);
@@ -217,21 +214,33 @@ RTR_DEVICE void splitk_reduce_epilogue(const TcParams& p, float* red, int tok0, 
 #pragma unroll
       for (int u = 0; u < SLOTS; ++u) s[u] = f4add(s[u], v[dz][u]);  // split order (zero adds are exact)
   }
-  float4* red4 = reinterpret_cast<float4*>(red);
 #pragma unroll
   for (int u = 0; u < SLOTS; ++u) {
     const int q = threadIdx.x + u * TC_THREADS;
     if (q < nslots) red4[q] = s[u];
   }
   __syncthreads();
+}
 
+RTR_DEVICE float4 f4mul(float4 a, float4 b) {
+  return make_float4(__fmul_rn(a.x, b.x), __fmul_rn(a.y, b.y), __fmul_rn(a.z, b.z), __fmul_rn(a.w, b.w));
+}
+RTR_DEVICE float4 f4add_rn(float4 a, float4 b) {
+  return make_float4(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y), __fadd_rn(a.z, b.z), __fadd_rn(a.w, b.w));
+}
+RTR_DEVICE float4 f4neg(float4 a) { return make_float4(-a.x, -a.y, -a.z, -a.w); }
+
+// Epilogue from a [rows][ld4 float4] shared tile of finished sums, run by
+// every thread of the CTA with float4 loads and stores (N, ldc and the head
+// dimension are multiples of 4; checked by the host).
+RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, int tok0, int n0, int rows, int cols4) {
   if (p.epi == EPI_SWIGLU) {
     // packed rows: 32 q + [0,16) gate, 32 q + [16,32) up of intermediate 16 q + [0,16)
     for (int q = threadIdx.x; q < rows * 16; q += TC_THREADS) {
       const int j = q >> 4, blk = (q >> 2) & 3, g4 = q & 3;
       const int c4 = blk * 8 + g4;
       if (c4 + 4 >= cols4) continue;  // the up half lies past N
-      const float4 g = red4[j * 32 + c4], u = red4[j * 32 + c4 + 4];
+      const float4 g = red4[j * ld4 + c4], u = red4[j * ld4 + c4 + 4];
       float a[4] = {silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w};
       float b[4], sm[4];
 #pragma unroll
@@ -243,10 +252,49 @@ RTR_DEVICE void splitk_reduce_epilogue(const TcParams& p, float* red, int tok0, 
     }
     return;
   }
-  for (int q = threadIdx.x; q < nslots; q += TC_THREADS) {
+  if (p.epi == EPI_ROPE) {
+    // q/k/v projection + bias, then apply_rotary_pos_emb (modeling_qwen2.py:116-146)
+    // on q and k with separately rounded products, as rope_kv() does.  A
+    // 128-column tile holds whole heads, so each rotary partner is in the tile.
+    const RopeArgs& r = p.rope;
+    const int D = r.head_dim, half = D >> 1;
+    const int base_pos = r.slot < 0 ? 0 : *r.L_dev + r.slot;
+    for (int q = threadIdx.x; q < rows * 32; q += TC_THREADS) {
+      const int j = q >> 5, c4 = q & 31;
+      if (c4 >= cols4) continue;
+      const int col = n0 + c4 * 4, m = tok0 + j;
+      const int h = col / D, d = col % D;
+      float4 v = f4add(red4[j * ld4 + c4], *reinterpret_cast<const float4*>(p.bias + col));
+      if (h < r.heads + r.kv_heads) {
+        const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
+        const float4 pv = f4add(red4[j * ld4 + pc4], *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4));
+        int pos = r.slot < 0 ? m : base_pos;
+        if (pos < 0 || pos >= r.positions) {
+          atomicOr(p.status, RTR_DEV_BAD_LENGTH);
+          pos = 0;
+        }
+        const float4 cs = *reinterpret_cast<const float4*>(r.cos_t + (long)pos * half + (d % half));
+        const float4 sn = *reinterpret_cast<const float4*>(r.sin_t + (long)pos * half + (d % half));
+        v = d < half ? f4add_rn(f4mul(v, cs), f4mul(f4neg(pv), sn))   // x1 cos - x2 sin
+                     : f4add_rn(f4mul(v, cs), f4mul(pv, sn));          // x2 cos + x1 sin
+      }
+      float* dst;
+      if (h < r.heads) {
+        dst = r.q_out + ((long)m * r.heads + h) * D + d;
+      } else {
+        const bool is_k = h < r.heads + r.kv_heads;
+        const int g = is_k ? h - r.heads : h - r.heads - r.kv_heads;
+        float* cache = is_k ? r.k_dst : r.v_dst;
+        dst = r.slot < 0 ? cache + ((long)g * r.prefix_cap + m) * D + d : cache + ((long)m * r.kv_heads + g) * D + d;
+      }
+      *reinterpret_cast<float4*>(dst) = v;
+    }
+    return;
+  }
+  for (int q = threadIdx.x; q < rows * 32; q += TC_THREADS) {
     const int j = q >> 5, c4 = q & 31;
     if (c4 >= cols4) continue;
-    float4 v = red4[q];
+    float4 v = red4[j * ld4 + c4];
     const int col = n0 + c4 * 4;
     float4* c = reinterpret_cast<float4*>(p.C + (long)(tok0 + j) * p.ldc + col);
     if (p.epi == EPI_BIAS) v = f4add(v, *reinterpret_cast<const float4*>(p.bias + col));
@@ -458,6 +506,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int quarter = warp & 3;
   const int n = n0 + quarter * 32 + lane;  // weight row of this thread
   const int rows = p.M - tok0 < TC_NTOK ? p.M - tok0 : TC_NTOK;  // real activation rows of the tile
+  const int cols4 = (p.N - n0 < TC_WROWS ? p.N - n0 : TC_WROWS) >> 2;
+  float4* red4 = reinterpret_cast<float4*>(smem);  // the rings are free now
   if (p.splits > 1) {
     // Partial tiles are tile-contiguous: ws[(split * tiles + tile)][row][128].
     const int tile = blockIdx.y * gridDim.x + blockIdx.x;
@@ -478,41 +528,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     if (!last_cta) return;
     __threadfence();
-    splitk_reduce_epilogue(p, reinterpret_cast<float*>(smem), tok0, n0, rows, tile, tstride);
+    splitk_sum(p, red4, rows, cols4, tile, tstride);
+    tile_epilogue(p, red4, TC_WROWS / 4, tok0, n0, rows, cols4);
     return;
   }
-  if (!have) return;
-
-  if (p.epi == EPI_SWIGLU) {
-    // packed rows: 32 q + [0,16) gate, 32 q + [16,32) up of intermediate 16 q + [0,16)
-    const int inter = ((n0 + quarter * 32) >> 5) * 16 + (lane & 15);
+  // Stage the finished tile in shared memory ([64][TC_WROWS + 4], padded so
+  // the float4 reads of consecutive rows spread over the banks); then every
+  // thread of the CTA stores float4s.
+  constexpr int RLD = TC_WROWS + 4;
+  if (have && n < p.N) {
+    float* red = reinterpret_cast<float*>(smem) + quarter * 32 + lane;
 #pragma unroll
-    for (int j = 0; j < TC_NTOK; ++j) {
-      const float up = __shfl_down_sync(0xffffffffu, acc[j], 16);
-      const int m = tok0 + j;
-      if (lane < 16 && n < p.N && m < p.M) {
-        const float a = silu_f(acc[j]) * up;
-        const long o = (long)m * p.ldc + inter;
-        p.C[o] = a;
-        const float ab = tf32_round(a);
-        p.C_big[o] = ab;
-        p.C_small[o] = a - ab;
-      }
-    }
-    return;
+    for (int j = 0; j < TC_NTOK; ++j)
+      if (j < rows) red[j * RLD] = acc[j];
   }
-  if (n >= p.N) return;
-  const float bv = p.epi == EPI_BIAS ? p.bias[n] : 0.f;
-#pragma unroll
-  for (int j = 0; j < TC_NTOK; ++j) {
-    const int m = tok0 + j;
-    if (m < p.M) {
-      float* c = p.C + (long)m * p.ldc + n;
-      if (p.epi == EPI_STORE) *c = acc[j];
-      else if (p.epi == EPI_BIAS) *c = acc[j] + bv;
-      else *c = *c + acc[j];
-    }
-  }
+  __syncthreads();
+  tile_epilogue(p, red4, RLD / 4, tok0, n0, rows, cols4);
 }
 
 // ---------------------------------------------------------------- host side
@@ -593,14 +624,22 @@ static int tc_splits(int tiles, int nchunks, int sms) {
 cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
                     float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                     size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
-                    bool pdl) {
+                    bool pdl, const RopeArgs* rope) {
   if (epi == EPI_SWIGLU && (!C_big || !C_small)) return cudaErrorInvalidValue;
+  if (epi == EPI_ROPE) {
+    // whole heads per 128-row tile, float4 pairs, q/k/v row layout
+    if (!rope || !bias || (rope->head_dim != 64 && rope->head_dim != 128) ||
+        N != (rope->heads + 2 * rope->kv_heads) * rope->head_dim || (reinterpret_cast<uintptr_t>(bias) & 15))
+      return cudaErrorInvalidValue;
+  }
+  // float4 epilogue: column counts, row strides and bases in 16-byte units
+  if (epi != EPI_ROPE && (N % 4 || ldc % 4 || (reinterpret_cast<uintptr_t>(C) & 15))) return cudaErrorInvalidValue;
   const int tt = (M + TC_NTOK - 1) / TC_NTOK, wt = (N + TC_WROWS - 1) / TC_WROWS;
   const int nchunks = (K + TC_KC - 1) / TC_KC;
   int splits = tc_splits(tt * wt, nchunks, sms);
-  if (splits > 1 && (N % 4 || ldc % 4 || (reinterpret_cast<uintptr_t>(C) & 15))) return cudaErrorInvalidValue;
   while (splits > 1 && ((size_t)splits * tt * wt * TC_NTOK * TC_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
-  TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status};
+  TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
+  if (rope) p.rope = *rope;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tt, wt, splits);
   cfg.blockDim = dim3(TC_THREADS);

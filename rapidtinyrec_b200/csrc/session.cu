@@ -174,6 +174,7 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(gemm_tc_init());
   CREATE_TRY(attention_init());
   if (const char* g = std::getenv("RTR_GEMM")) s->use_tc = std::strcmp(g, "ffma") != 0;
+  s->pdl = pdl_on(PDL_GEMM);
 
   const long H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
   const long qd = (long)c.heads * D, kvd = (long)c.kv_heads * D, qkvd = qkv_dim(c);
@@ -430,7 +431,7 @@ int rtr_load_constraints(rtr_session* s, const rtr_constraint_tables* t) {
 // Projection GEMM: the tcgen05 3xTF32 kernel on the tf32 split of activation
 // buffer A and the weight matrix W (the FFMA kernel when RTR_GEMM=ffma).
 static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W, float* C, int ldc,
-                        const float* bias, int M, int N, int K, int epi) {
+                        const float* bias, int M, int N, int K, int epi, const RopeArgs* rope = nullptr) {
   if (s->use_tc) {
     auto sp = s->split_of.find(A);
     if (sp == s->split_of.end()) return cudaErrorInvalidValue;
@@ -447,7 +448,7 @@ static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W,
       cs = out->second.second;
     }
     return gemm_tc(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws, s->ws_floats,
-                   s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl);
+                   s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope);
   }
   return gemm_f32(A, lda, W, C, ldc, bias, M, N, K, epi, s->ws, s->ws_floats, s->tickets, s->sms,
                   s->stream, s->pdl);
@@ -477,16 +478,22 @@ static cudaError_t forward(rtr_session* s, int t) {
     float* ks = s->kv_suffix + (size_t)l * 2 * 4 * B * kvd;
     float* vs = ks + (size_t)4 * B * kvd;
     FWD_TRY(rms_norm_rows(s->x, w.n_in, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
-    FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));
+    const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * kvd;
+    if (s->use_tc) {
+      // q/k/v projection with RoPE and the cache write fused into its epilogue
+      const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
+                        t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L};
+      FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra));
+    } else {
+      FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));
+      FWD_TRY(rope_kv(s->qkv, M, c.heads, c.kv_heads, D, s->rope_cos, s->rope_sin, s->rope_positions, s->q,
+                      t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L,
+                      s->d_status, st));
+    }
     if (t == 0) {
-      FWD_TRY(rope_kv(s->qkv, M, c.heads, c.kv_heads, D, s->rope_cos, s->rope_sin, s->rope_positions,
-                      s->q, kp, vp, cap, -1, s->d_L, s->d_status, st));
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
                                 scale, st));
     } else {
-      const size_t slot = (size_t)(t - 1) * B * kvd;
-      FWD_TRY(rope_kv(s->qkv, M, c.heads, c.kv_heads, D, s->rope_cos, s->rope_sin, s->rope_positions,
-                      s->q, ks + slot, vs + slot, cap, t - 1, s->d_L, s->d_status, st));
       FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
                                s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, st));
     }
@@ -522,11 +529,13 @@ static int ready(rtr_session* s) {
 }
 
 
-// Kernels one forward pass launches: embedding, 8 per layer (RMSNorm, q/k/v
-// GEMM, RoPE + cache write, attention, o GEMM, RMSNorm, gate/up GEMM, down
-// GEMM), final RMSNorm and the LM head.  The step tail is 4 (max, two sums,
-// beam selection).
-static int64_t forward_kernels(const rtr_session* s) { return 1 + 8 * (int64_t)s->cfg.layers + 2; }
+// Kernels one forward pass launches: embedding, per layer RMSNorm, q/k/v GEMM,
+// RoPE + cache write (fused into the q/k/v GEMM on the tensor-core path),
+// attention, o GEMM, RMSNorm, gate/up GEMM, down GEMM; then the final RMSNorm
+// and the LM head.  The step tail is 4 (max, two sums, beam selection).
+static int64_t forward_kernels(const rtr_session* s) {
+  return 1 + (s->use_tc ? 7 : 8) * (int64_t)s->cfg.layers + 2;
+}
 static constexpr int64_t kTailKernels = 4;
 
 static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t on_device) {

@@ -188,7 +188,7 @@ def test_report_counts_match_the_captured_graph(tiny_engine, tiny):
     tiny_engine.generate(tiny['users'][0].prompt_token_ids)
     rep = tiny_engine.report()
     cfg = tiny['cfg']
-    forward = 1 + 8 * cfg.layers + 2          # embed, 8 per layer, final norm, LM head
+    forward = 1 + 7 * cfg.layers + 2          # embed, 7 per layer (RoPE fused), final norm, LM head
     tail = 4                                  # max, two sums, beam selection
     assert rep['graph_kernel_nodes'] == 4 * (forward + tail) + 1   # decode steps 1-4, finalize
     assert rep['launches_per_request'] == 1 + forward + tail + rep['graph_kernel_nodes']
