@@ -93,10 +93,9 @@ RTR_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_de
 // comma-separated list of classes launched with PDL ("gemm", "norm", "rope",
 // "attn", "embed", "gemv", "tail"), "0" for none, "all" for every class.
 // Read once per process.  The default leaves RMSNorm and RoPE on plain
-// launches: a tensor-core GEMM CTA (352 threads x 168 registers) cannot share
-// an SM with their CTAs, so placing them early (waiting on the previous GEMM)
-// splits the next GEMM's single-wave grid; measured on the 1.5B decode, PDL on
-// RMSNorm cost 1.9 ms per request, on RoPE 0.2 ms, while the GEMM, attention,
+// launches: measured on the 1.5B decode, PDL on RMSNorm cost 1.9 ms per
+// request (4 ms with 64-thread norm CTAs that fit beside a GEMM CTA, so SM
+// co-residency is not the cause), on RoPE 0.2 ms, while the GEMM, attention,
 // embedding, GEMV and beam-tail launches each gained.
 enum PdlClass : unsigned {
   PDL_GEMM = 1u, PDL_NORM = 2u, PDL_ROPE = 4u, PDL_ATTN = 8u, PDL_EMBED = 16u, PDL_GEMV = 32u, PDL_TAIL = 64u,
