@@ -62,6 +62,12 @@ class GpuSidConstraintTables:
                          'unknown_prefix_behavior': 'EOS fallback on device',
                          'runtime_cpu_token_transfers': 0}
 
+    def host_arrays(self):
+        """Every table as a host array (for the runner's unchanged-input audit)."""
+        return {'offsets': np.array(self.offsets, np.int64), 'sizes': np.array(self.sizes, np.int64),
+                'tables.1': self.tables[1], 'tables.2': self.tables[2], 'valid_sids': self.valid_sids,
+                'first_tokens': self.first_tokens, 'root_prefix': np.array(self.root_prefix, np.int64)}
+
     def as_c(self):
         """The ``rtr_constraint_tables`` struct (host pointers kept alive by ``self``)."""
         self._keep = [np.ascontiguousarray(self.tables[1]), np.ascontiguousarray(self.tables[2]),
