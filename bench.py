@@ -139,7 +139,7 @@ def cpu_oracle_time(cfg, weights_cpu, cons, users, budget_s, threads):
     from oracle.beam_cpu import beam_search
     from oracle.qwen2_cpu import Qwen2Oracle
     torch.set_num_threads(threads)
-    model = Qwen2Oracle(cfg, weights_cpu)
+    model = Qwen2Oracle(cfg, weights_cpu, dtype=torch.bfloat16 if cfg.dtype == 'bf16' else torch.float32)
     times = []
     t_start = time.perf_counter()
     for u in users:
@@ -171,7 +171,8 @@ def run_reference(args):
     line = {'metric': METRIC, 'impl': 'reference', 'value': round(value, 4), 'unit': 'users/s',
             'n_gpus': world, 'steps': len(times), 'warmup': len(warm), 'ms_per_step': round(1000 * total / len(times), 2),
             'median_ms': round(1000 * statistics.median(times), 2), 'p95_ms': round(1000 * percentile(times, 0.95), 2),
-            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
+            'dtype': 'f32' if cfg.dtype == 'fp32' else 'bf16',
             'data': 'synthetic', 'config': {'workload': args.workload, 'beams': 50, 'requested_steps': args.steps},
             'cpu_baseline': {'value': round(value, 4), 'unit': 'users/s', 'cores': threads, 'kind': 'port',
                              'sample': f'{len(times)} users of {args.workload}, full request each (CPU oracle port of '
@@ -292,8 +293,11 @@ def run_ours(args):
         achieved = gemm_bytes / (gemm_ms / 1000.0) / 1e9
         ck = clocks.summary()
         gemm_flops = 2.0 * engine.beams * gemm_bytes / (4 if cfg.dtype == 'fp32' else 2)
-        gemm_kernel = ('gemm_tc_kernel (tcgen05 3xTF32' if rep['tensor_core_gemm'] else 'gemm_f32_kernel (FFMA') + \
-            f', decode projections + LM head, M={engine.beams})'
+        if cfg.dtype == 'bf16':
+            gemm_kernel = 'gemm_bf16_kernel (tcgen05 kind::f16'
+        else:
+            gemm_kernel = 'gemm_tc_kernel (tcgen05 3xTF32' if rep['tensor_core_gemm'] else 'gemm_f32_kernel (FFMA'
+        gemm_kernel += f', decode projections + LM head, M={engine.beams})'
         line = {
             'metric': METRIC, 'value': round(value, 3), 'unit': 'users/s', 'n_gpus': world, 'steps': args.steps,
             'warmup': args.warmup, 'ms_per_step': round(total_ms / args.steps, 3),
@@ -303,7 +307,8 @@ def run_ours(args):
             'config': {'workload': args.workload, 'model': cfg.name, 'beams': engine.beams, 'items': wl.items,
                        'prompt_tokens': [wl.prompt_min, wl.prompt_max], 'users_per_rank': args.steps,
                        'parallelism': f'replicas{world}', 'partition': 'users round-robin, no per-step collective',
-                       'l2': 'inputs larger than L2: the 6.2 GB of weights stream from HBM every forward'},
+                       'l2': f'inputs larger than L2: the {gemm_bytes / 1e9:.1f} GB of weights stream from HBM '
+                             f'every forward'},
             'e2e': {'value': round(n_users / e2e_total, 3), 'unit': 'users/s',
                     'median_ms': round(1000 * statistics.median(e2e_lat), 3),
                     'p95_ms': round(1000 * percentile(e2e_lat, 0.95), 3),

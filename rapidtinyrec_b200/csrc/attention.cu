@@ -31,54 +31,77 @@ constexpr int ATHREADS = AWARPS * 32;
 constexpr int PQ = 16;         // prefill query positions per CTA (2 per warp)
 constexpr int DBEAMS = AWARPS; // decode beams per CTA (1 per warp)
 
-template <int HD> constexpr int kld() { return HD + 4; }
-template <int HD> constexpr size_t attn_smem_bytes(int qrows) {
-  return (size_t)(2 * AK * kld<HD>() + 2 * AK * HD + qrows * HD) * sizeof(float);
+// Prefix K/V rows are staged in their storage type T (fp32, or bf16 in the
+// bf16 mode); K rows are padded so 16-byte copies stay aligned and the score
+// reads of consecutive keys spread over the banks.  q lives in fp32.
+template <int HD, typename T> __host__ __device__ constexpr int kld() { return HD + 16 / (int)sizeof(T); }
+template <int HD, typename T> constexpr size_t attn_smem_bytes(int qrows) {
+  return (size_t)(2 * AK * kld<HD, T>() + 2 * AK * HD) * sizeof(T) + (size_t)qrows * HD * sizeof(float);
 }
+
+// Four consecutive elements as floats.
+RTR_DEVICE float4 ld4f(const float* p) { return *reinterpret_cast<const float4*>(p); }
+RTR_DEVICE float4 ld4f(const __nv_bfloat16* p) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+// Output element i of a row: fp32 rows also get their tf32 split (the 3xTF32
+// GEMM operands); bf16 rows are rounded once.
+RTR_DEVICE void store_out(float* out, float* big, float* small, long i, float v) { store_split(out, big, small, i, v); }
+RTR_DEVICE void store_out(__nv_bfloat16* out, float*, float*, long i, float v) { out[i] = __float2bfloat16_rn(v); }
 
 // Stage keys [k0, k0 + AK) of one KV group into ring slot `buf` (zero rows
 // past `kend`); one cp.async group.
-template <int HD>
-RTR_DEVICE void load_kv_chunk(float* kbuf, float* vbuf, const float* kbase, const float* vbase, int k0, int kend,
-                              int buf) {
-  constexpr int V4 = HD / 4;
-  float* kd = kbuf + (size_t)buf * AK * kld<HD>();
-  float* vd = vbuf + (size_t)buf * AK * HD;
+template <int HD, typename T>
+RTR_DEVICE void load_kv_chunk(T* kbuf, T* vbuf, const T* kbase, const T* vbase, int k0, int kend, int buf) {
+  constexpr int E = 16 / (int)sizeof(T);  // elements per 16-byte copy
+  constexpr int V4 = HD / E;
+  T* kd = kbuf + (size_t)buf * AK * kld<HD, T>();
+  T* vd = vbuf + (size_t)buf * AK * HD;
   for (int i = threadIdx.x; i < AK * V4; i += ATHREADS) {
-    const int j = i / V4, d = (i % V4) * 4;
+    const int j = i / V4, d = (i % V4) * E;
     const bool ok = k0 + j < kend;
     const long row = ok ? k0 + j : 0;
-    cp_async16(kd + j * kld<HD>() + d, kbase + row * HD + d, ok);
+    cp_async16(kd + j * kld<HD, T>() + d, kbase + row * HD + d, ok);
     cp_async16(vd + j * HD + d, vbase + row * HD + d, ok);
   }
   cp_async_commit();
 }
 
-// VEC consecutive floats from shared memory as one vector access.
-template <int VEC> RTR_DEVICE void load_vec(const float* src, float (&x)[VEC]);
-template <> RTR_DEVICE void load_vec<4>(const float* src, float (&x)[4]) {
+// VEC consecutive elements from shared memory as one vector access.
+RTR_DEVICE void load_vec(const float* src, float (&x)[4]) {
   const float4 v = *reinterpret_cast<const float4*>(src);
   x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
 }
-template <> RTR_DEVICE void load_vec<2>(const float* src, float (&x)[2]) {
+RTR_DEVICE void load_vec(const float* src, float (&x)[2]) {
   const float2 v = *reinterpret_cast<const float2*>(src);
+  x[0] = v.x; x[1] = v.y;
+}
+RTR_DEVICE void load_vec(const __nv_bfloat16* src, float (&x)[4]) {
+  const float4 v = ld4f(src);
+  x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+}
+RTR_DEVICE void load_vec(const __nv_bfloat16* src, float (&x)[2]) {
+  const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(src));
   x[0] = v.x; x[1] = v.y;
 }
 
 // One warp, one query row (q in shared memory), one staged chunk of keys
 // [k0, k0 + AK): online-softmax update of (m, l, acc) over keys < kend.
-template <int HD>
-RTR_DEVICE void chunk_update(const float* qrow, const float* kc, const float* vc, int k0, int kend, float scale,
+template <int HD, typename T>
+RTR_DEVICE void chunk_update(const float* qrow, const T* kc, const T* vc, int k0, int kend, float scale,
                              float& m, float& l, float (&acc)[HD / 32]) {
   constexpr int VEC = HD / 32;
   const int lane = threadIdx.x & 31;
   const float4* q4 = reinterpret_cast<const float4*>(qrow);
-  const float4* ka = reinterpret_cast<const float4*>(kc + lane * kld<HD>());
-  const float4* kb = reinterpret_cast<const float4*>(kc + (lane + 32) * kld<HD>());
+  const T* ka = kc + lane * kld<HD, T>();
+  const T* kb = kc + (lane + 32) * kld<HD, T>();
   float s0 = 0.f, s1 = 0.f;
 #pragma unroll 8
   for (int d = 0; d < HD / 4; ++d) {
-    const float4 qq = q4[d], a = ka[d], b = kb[d];
+    const float4 qq = q4[d], a = ld4f(ka + 4 * d), b = ld4f(kb + 4 * d);
     s0 = fmaf(qq.x, a.x, s0); s0 = fmaf(qq.y, a.y, s0); s0 = fmaf(qq.z, a.z, s0); s0 = fmaf(qq.w, a.w, s0);
     s1 = fmaf(qq.x, b.x, s1); s1 = fmaf(qq.y, b.y, s1); s1 = fmaf(qq.z, b.z, s1); s1 = fmaf(qq.w, b.w, s1);
   }
@@ -91,13 +114,13 @@ RTR_DEVICE void chunk_update(const float* qrow, const float* kc, const float* vc
   m = mn;
 #pragma unroll
   for (int i = 0; i < VEC; ++i) acc[i] *= corr;
-  const float* va = vc + lane * VEC;
+  const T* va = vc + lane * VEC;
 #pragma unroll 4
   for (int j = 0; j < 32; ++j) {
     const float pa = __shfl_sync(0xffffffffu, p0, j), pb = __shfl_sync(0xffffffffu, p1, j);
     float x[VEC], y[VEC];
-    load_vec<VEC>(va + j * HD, x);
-    load_vec<VEC>(va + (j + 32) * HD, y);
+    load_vec(va + j * HD, x);
+    load_vec(va + (j + 32) * HD, y);
 #pragma unroll
     for (int i = 0; i < VEC; ++i) acc[i] = fmaf(pa, x[i], acc[i]);
 #pragma unroll
@@ -106,31 +129,31 @@ RTR_DEVICE void chunk_update(const float* qrow, const float* kc, const float* vc
 }
 
 // ------------------------------------------------------------------ prefill
-template <int HD>
+template <int HD, typename T>
 __global__ void __launch_bounds__(ATHREADS) prefill_attn_kernel(
-    const float* __restrict__ q, const float* __restrict__ kp, const float* __restrict__ vp,
-    float* __restrict__ out, float* __restrict__ out_big, float* __restrict__ out_small, int L, int cap, int heads,
+    const T* __restrict__ q, const T* __restrict__ kp, const T* __restrict__ vp,
+    T* __restrict__ out, float* __restrict__ out_big, float* __restrict__ out_small, int L, int cap, int heads,
     int kv_heads, float scale) {
   constexpr int VEC = HD / 32, ROWS = PQ / AWARPS;
   pdl_launch_dependents();
   pdl_wait();
-  extern __shared__ __align__(16) float asmem[];
-  float* kbuf = asmem;
-  float* vbuf = kbuf + 2 * AK * kld<HD>();
-  float* qs = vbuf + 2 * AK * HD;  // [PQ][HD]
+  extern __shared__ __align__(16) unsigned char asmem[];
+  T* kbuf = reinterpret_cast<T*>(asmem);
+  T* vbuf = kbuf + 2 * AK * kld<HD, T>();
+  float* qs = reinterpret_cast<float*>(vbuf + 2 * AK * HD);  // [PQ][HD]
   const int h = blockIdx.y, g = h / (heads / kv_heads);
   const int q0 = blockIdx.x * PQ;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const float* kbase = kp + (long)g * cap * HD;
-  const float* vbase = vp + (long)g * cap * HD;
+  const T* kbase = kp + (long)g * cap * HD;
+  const T* vbase = vp + (long)g * cap * HD;
   const int kend = min(L, q0 + PQ);  // keys any row of the block may see
   const int nchunks = (kend + AK - 1) / AK;
 
-  load_kv_chunk<HD>(kbuf, vbuf, kbase, vbase, 0, kend, 0);
+  load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, 0, kend, 0);
   for (int i = threadIdx.x; i < PQ * HD / 4; i += ATHREADS) {
     const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q0 + r < L) v = *reinterpret_cast<const float4*>(q + ((long)(q0 + r) * heads + h) * HD + d);
+    if (q0 + r < L) v = ld4f(q + ((long)(q0 + r) * heads + h) * HD + d);
     *reinterpret_cast<float4*>(qs + r * HD + d) = v;
   }
   float m[ROWS], l[ROWS], acc[ROWS][VEC];
@@ -141,17 +164,17 @@ __global__ void __launch_bounds__(ATHREADS) prefill_attn_kernel(
     for (int i = 0; i < VEC; ++i) acc[r][i] = 0.f;
   }
   for (int c = 0; c < nchunks; ++c) {
-    if (c + 1 < nchunks) load_kv_chunk<HD>(kbuf, vbuf, kbase, vbase, (c + 1) * AK, kend, (c + 1) & 1);
+    if (c + 1 < nchunks) load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, (c + 1) * AK, kend, (c + 1) & 1);
     else cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const float* kc = kbuf + (c & 1) * AK * kld<HD>();
-    const float* vc = vbuf + (c & 1) * AK * HD;
+    const T* kc = kbuf + (c & 1) * AK * kld<HD, T>();
+    const T* vc = vbuf + (c & 1) * AK * HD;
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
       const int row = warp * ROWS + r, qpos = q0 + row;
       if (qpos < L && c * AK <= qpos)
-        chunk_update<HD>(qs + row * HD, kc, vc, c * AK, qpos + 1, scale, m[r], l[r], acc[r]);
+        chunk_update<HD, T>(qs + row * HD, kc, vc, c * AK, qpos + 1, scale, m[r], l[r], acc[r]);
     }
     __syncthreads();  // the slot is refilled by the next iteration's load
   }
@@ -162,39 +185,51 @@ __global__ void __launch_bounds__(ATHREADS) prefill_attn_kernel(
     const float inv = 1.0f / l[r];
 #pragma unroll
     for (int i = 0; i < VEC; ++i)
-      store_split(out, out_big, out_small, ((long)qpos * heads + h) * HD + lane * VEC + i, acc[r][i] * inv);
+      store_out(out, out_big, out_small, ((long)qpos * heads + h) * HD + lane * VEC + i, acc[r][i] * inv);
   }
 }
 
-cudaError_t attention_prefill(const float* q, const float* k_prefix, const float* v_prefix,
-                              float* out, float* out_big, float* out_small, int L, int prefix_cap, int heads,
-                              int kv_heads, int head_dim, float scale, cudaStream_t stream) {
-  if (L <= 0 || L > prefix_cap) return cudaErrorInvalidValue;
+template <int HD, typename T>
+static cudaError_t launch_prefill(const void* q, const void* kp, const void* vp, void* out, float* ob, float* os, int L,
+                                  int cap, int heads, int kv_heads, float scale, cudaStream_t stream) {
   dim3 grid((L + PQ - 1) / PQ, heads);
+  return launch_pdl(PDL_ATTN, prefill_attn_kernel<HD, T>, grid, dim3(ATHREADS), attn_smem_bytes<HD, T>(PQ), stream,
+                    static_cast<const T*>(q), static_cast<const T*>(kp), static_cast<const T*>(vp), static_cast<T*>(out),
+                    ob, os, L, cap, heads, kv_heads, scale);
+}
+
+cudaError_t attention_prefill(const void* q, const void* k_prefix, const void* v_prefix, void* out, float* out_big,
+                              float* out_small, int L, int prefix_cap, int heads, int kv_heads, int head_dim,
+                              float scale, bool bf16, cudaStream_t stream) {
+  if (L <= 0 || L > prefix_cap) return cudaErrorInvalidValue;
   if (head_dim == 128)
-    return launch_pdl(PDL_ATTN, prefill_attn_kernel<128>, grid, dim3(ATHREADS), attn_smem_bytes<128>(PQ), stream, q, k_prefix,
-                      v_prefix, out, out_big, out_small, L, prefix_cap, heads, kv_heads, scale);
-  else if (head_dim == 64)
-    return launch_pdl(PDL_ATTN, prefill_attn_kernel<64>, grid, dim3(ATHREADS), attn_smem_bytes<64>(PQ), stream, q, k_prefix,
-                      v_prefix, out, out_big, out_small, L, prefix_cap, heads, kv_heads, scale);
+    return bf16 ? launch_prefill<128, __nv_bfloat16>(q, k_prefix, v_prefix, out, nullptr, nullptr, L, prefix_cap, heads,
+                                                     kv_heads, scale, stream)
+                : launch_prefill<128, float>(q, k_prefix, v_prefix, out, out_big, out_small, L, prefix_cap, heads,
+                                             kv_heads, scale, stream);
+  if (head_dim == 64)
+    return bf16 ? launch_prefill<64, __nv_bfloat16>(q, k_prefix, v_prefix, out, nullptr, nullptr, L, prefix_cap, heads,
+                                                    kv_heads, scale, stream)
+                : launch_prefill<64, float>(q, k_prefix, v_prefix, out, out_big, out_small, L, prefix_cap, heads,
+                                            kv_heads, scale, stream);
   return cudaErrorInvalidValue;
 }
 
 // ------------------------------------------------------------------- decode
-template <int HD>
+template <int HD, typename T>
 __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
-    const float* __restrict__ q, const float* __restrict__ kp, const float* __restrict__ vp,
-    const float* __restrict__ ksuf, const float* __restrict__ vsuf, const int32_t* __restrict__ anc,
-    const int32_t* __restrict__ L_dev, float* __restrict__ out, float* __restrict__ out_big,
+    const T* __restrict__ q, const T* __restrict__ kp, const T* __restrict__ vp,
+    const T* __restrict__ ksuf, const T* __restrict__ vsuf, const int32_t* __restrict__ anc,
+    const int32_t* __restrict__ L_dev, T* __restrict__ out, float* __restrict__ out_big,
     float* __restrict__ out_small, int beams, int cap, int heads, int kv_heads, int t, float scale,
     uint32_t* __restrict__ status) {
   constexpr int VEC = HD / 32;
   pdl_launch_dependents();
   pdl_wait();
-  extern __shared__ __align__(16) float asmem[];
-  float* kbuf = asmem;
-  float* vbuf = kbuf + 2 * AK * kld<HD>();
-  float* qs = vbuf + 2 * AK * HD;  // [DBEAMS][HD]
+  extern __shared__ __align__(16) unsigned char asmem[];
+  T* kbuf = reinterpret_cast<T*>(asmem);
+  T* vbuf = kbuf + 2 * AK * kld<HD, T>();
+  float* qs = reinterpret_cast<float*>(vbuf + 2 * AK * HD);  // [DBEAMS][HD]
   const int h = blockIdx.x, g = h / (heads / kv_heads);
   const int b0 = blockIdx.y * DBEAMS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -204,27 +239,27 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
     L = 0;
   }
-  const float* kbase = kp + (long)g * cap * HD;
-  const float* vbase = vp + (long)g * cap * HD;
+  const T* kbase = kp + (long)g * cap * HD;
+  const T* vbase = vp + (long)g * cap * HD;
   const int nchunks = (L + AK - 1) / AK;
 
-  if (nchunks > 0) load_kv_chunk<HD>(kbuf, vbuf, kbase, vbase, 0, L, 0);
+  if (nchunks > 0) load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, 0, L, 0);
   for (int i = threadIdx.x; i < DBEAMS * HD / 4; i += ATHREADS) {
     const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (b0 + r < beams) v = *reinterpret_cast<const float4*>(q + ((long)(b0 + r) * heads + h) * HD + d);
+    if (b0 + r < beams) v = ld4f(q + ((long)(b0 + r) * heads + h) * HD + d);
     *reinterpret_cast<float4*>(qs + r * HD + d) = v;
   }
   float m = -INFINITY, l = 0.f, acc[VEC];
 #pragma unroll
   for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
   for (int c = 0; c < nchunks; ++c) {
-    if (c + 1 < nchunks) load_kv_chunk<HD>(kbuf, vbuf, kbase, vbase, (c + 1) * AK, L, (c + 1) & 1);
+    if (c + 1 < nchunks) load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, (c + 1) * AK, L, (c + 1) & 1);
     else cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
     if (b < beams)
-      chunk_update<HD>(qs + warp * HD, kbuf + (c & 1) * AK * kld<HD>(), vbuf + (c & 1) * AK * HD, c * AK, L, scale,
+      chunk_update<HD, T>(qs + warp * HD, kbuf + (c & 1) * AK * kld<HD, T>(), vbuf + (c & 1) * AK * HD, c * AK, L, scale,
                        m, l, acc);
     __syncthreads();  // the slot is refilled by the next iteration's load
   }
@@ -245,7 +280,7 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     const long off = (((long)s * beams + row) * kv_heads + g) * HD + lane * VEC;
     float d = 0.f;
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) d = fmaf(qv[i], ksuf[off + i], d);
+    for (int i = 0; i < VEC; ++i) d = fmaf(qv[i], to_f32(ksuf[off + i]), d);
     const float sc = warp_sum(d) * scale;
     const float mn = fmaxf(m, sc);
     const float corr = expf(m - mn);
@@ -253,44 +288,61 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     l = l * corr + p;
     m = mn;
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] = fmaf(p, vsuf[off + i], acc[i] * corr);
+    for (int i = 0; i < VEC; ++i) acc[i] = fmaf(p, to_f32(vsuf[off + i]), acc[i] * corr);
   }
   const float inv = 1.0f / l;
 #pragma unroll
   for (int i = 0; i < VEC; ++i)
-    store_split(out, out_big, out_small, ((long)b * heads + h) * HD + lane * VEC + i, acc[i] * inv);
+    store_out(out, out_big, out_small, ((long)b * heads + h) * HD + lane * VEC + i, acc[i] * inv);
 }
 
-cudaError_t attention_decode(const float* q, const float* k_prefix, const float* v_prefix,
-                             const float* k_suffix, const float* v_suffix, const int32_t* anc,
-                             const int32_t* L_dev, int t, float* out, float* out_big, float* out_small, int beams,
-                             int prefix_cap, int heads, int kv_heads, int head_dim, float scale, uint32_t* status,
-                             cudaStream_t stream) {
-  if (t < 1 || t > 4 || beams > MAX_BEAMS) return cudaErrorInvalidValue;
+template <int HD, typename T>
+static cudaError_t launch_decode(const void* q, const void* kp, const void* vp, const void* ks, const void* vs,
+                                 const int32_t* anc, const int32_t* L_dev, int t, void* out, float* ob, float* os,
+                                 int beams, int cap, int heads, int kv_heads, float scale, uint32_t* status,
+                                 cudaStream_t stream) {
   dim3 grid(heads, (beams + DBEAMS - 1) / DBEAMS);
+  return launch_pdl(PDL_ATTN, decode_attn_kernel<HD, T>, grid, dim3(ATHREADS), attn_smem_bytes<HD, T>(DBEAMS), stream,
+                    static_cast<const T*>(q), static_cast<const T*>(kp), static_cast<const T*>(vp),
+                    static_cast<const T*>(ks), static_cast<const T*>(vs), anc, L_dev, static_cast<T*>(out), ob, os,
+                    beams, cap, heads, kv_heads, t, scale, status);
+}
+
+cudaError_t attention_decode(const void* q, const void* k_prefix, const void* v_prefix, const void* k_suffix,
+                             const void* v_suffix, const int32_t* anc, const int32_t* L_dev, int t, void* out,
+                             float* out_big, float* out_small, int beams, int prefix_cap, int heads, int kv_heads,
+                             int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream) {
+  if (t < 1 || t > 4 || beams > MAX_BEAMS) return cudaErrorInvalidValue;
   if (head_dim == 128)
-    return launch_pdl(PDL_ATTN, decode_attn_kernel<128>, grid, dim3(ATHREADS), attn_smem_bytes<128>(DBEAMS), stream, q,
-                      k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, out, out_big, out_small, beams, prefix_cap,
-                      heads, kv_heads, t, scale, status);
-  else if (head_dim == 64)
-    return launch_pdl(PDL_ATTN, decode_attn_kernel<64>, grid, dim3(ATHREADS), attn_smem_bytes<64>(DBEAMS), stream, q,
-                      k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, out, out_big, out_small, beams, prefix_cap,
-                      heads, kv_heads, t, scale, status);
+    return bf16 ? launch_decode<128, __nv_bfloat16>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out,
+                                                    nullptr, nullptr, beams, prefix_cap, heads, kv_heads, scale, status,
+                                                    stream)
+                : launch_decode<128, float>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out, out_big,
+                                            out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream);
+  if (head_dim == 64)
+    return bf16 ? launch_decode<64, __nv_bfloat16>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out,
+                                                   nullptr, nullptr, beams, prefix_cap, heads, kv_heads, scale, status,
+                                                   stream)
+                : launch_decode<64, float>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out, out_big,
+                                           out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream);
   return cudaErrorInvalidValue;
 }
 
+template <int HD, typename T>
+static cudaError_t attn_set_smem() {
+  cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<HD, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)attn_smem_bytes<HD, T>(PQ));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_kernel<HD, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)attn_smem_bytes<HD, T>(DBEAMS));
+  return e;
+}
+
 cudaError_t attention_init() {
-  cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)attn_smem_bytes<128>(PQ));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(prefill_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)attn_smem_bytes<64>(PQ));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(decode_attn_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)attn_smem_bytes<128>(DBEAMS));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(decode_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)attn_smem_bytes<64>(DBEAMS));
+  cudaError_t e = attn_set_smem<128, float>();
+  if (e == cudaSuccess) e = attn_set_smem<64, float>();
+  if (e == cudaSuccess) e = attn_set_smem<128, __nv_bfloat16>();
+  if (e == cudaSuccess) e = attn_set_smem<64, __nv_bfloat16>();
   return e;
 }
 

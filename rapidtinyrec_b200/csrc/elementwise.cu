@@ -70,6 +70,117 @@ cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big
   return launch_pdl(PDL_NORM, rms_norm_kernel, dim3(M), dim3(256), 0, stream, x, w, h, h_big, h_small, hidden, eps);
 }
 
+// ------------------------------------------------------------- bf16 mode
+// The bf16 model of the reference's bf16-experimental opt-in: embeddings,
+// residual stream and norms in bf16, reductions in fp32.
+__global__ void embed_bf16_kernel(const int32_t* ids, int ids_stride, const __nv_bfloat16* table, int vocab,
+                                  int hidden, __nv_bfloat16* x, uint32_t* status) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int m = blockIdx.x;
+  int tok = ids[(long)m * ids_stride];
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_TOKEN);
+    tok = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(table + (long)tok * hidden);
+  uint4* dst = reinterpret_cast<uint4*>(x + (long)m * hidden);
+  for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+cudaError_t embed_rows_bf16(const int32_t* ids, int ids_stride, int M, const void* table, int vocab, int hidden,
+                            void* x, uint32_t* status, cudaStream_t stream) {
+  return launch_pdl(PDL_EMBED, embed_bf16_kernel, dim3(M), dim3(128), 0, stream, ids, ids_stride,
+                    static_cast<const __nv_bfloat16*>(table), vocab, hidden, static_cast<__nv_bfloat16*>(x), status);
+}
+
+// Qwen2RMSNorm on a bf16 model (modeling_qwen2.py:258-263): the variance in
+// fp32, then weight * bf16(x * rsqrt(var + eps)) rounded to bf16; w holds the
+// bf16 norm weights as fp32.
+__global__ void rms_norm_bf16_kernel(const __nv_bfloat16* x, const float* w, __nv_bfloat16* h, int hidden, float eps) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int m = blockIdx.x;
+  const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + (long)m * hidden);
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < hidden / 2; i += blockDim.x) {
+    const float2 v = __bfloat1622float2(xr[i]);
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+  }
+  __shared__ float red[32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float r = 1.0f / sqrtf(red[0] / (float)hidden + eps);
+  __nv_bfloat162* hr = reinterpret_cast<__nv_bfloat162*>(h + (long)m * hidden);
+  for (int i = threadIdx.x; i < hidden / 2; i += blockDim.x) {
+    const float2 v = __bfloat1622float2(xr[i]);
+    const float a = bf16_round(v.x * r), b = bf16_round(v.y * r);
+    hr[i] = __floats2bfloat162_rn(w[2 * i] * a, w[2 * i + 1] * b);
+  }
+}
+
+cudaError_t rms_norm_rows_bf16(const void* x, const float* w, void* h, int M, int hidden, float eps,
+                               cudaStream_t stream) {
+  return launch_pdl(PDL_NORM, rms_norm_bf16_kernel, dim3(M), dim3(256), 0, stream,
+                    static_cast<const __nv_bfloat16*>(x), w, static_cast<__nv_bfloat16*>(h), hidden, eps);
+}
+
+// y[n] = float(bf16(dot(x, W[n]))) for the prefill's last-row LM head: bf16
+// weights and activations, fp32 accumulation, logits rounded like a bf16 model's.
+__global__ void gemv_bf16_kernel(const __nv_bfloat16* x, const __nv_bfloat16* W, float* y, int N, int K) {
+  pdl_launch_dependents();
+  pdl_wait();
+  extern __shared__ float xs[];
+  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[i] = __bfloat162float(x[i]);
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rows_per_warp = 4;
+  const int n0 = (blockIdx.x * (blockDim.x >> 5) + warp) * rows_per_warp;
+#pragma unroll
+  for (int r = 0; r < rows_per_warp; ++r) {
+    const int n = n0 + r;
+    if (n >= N) return;
+    const __nv_bfloat162* w = reinterpret_cast<const __nv_bfloat162*>(W + (long)n * K);
+    float acc = 0.f;
+    for (int k = lane; k < K / 2; k += 32) {
+      const float2 a = __bfloat1622float2(w[k]);
+      acc = fmaf(a.x, xs[2 * k], acc);
+      acc = fmaf(a.y, xs[2 * k + 1], acc);
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) y[n] = bf16_round(acc);
+  }
+}
+
+cudaError_t gemv_bf16(const void* x, const void* W, float* y, int N, int K, cudaStream_t stream) {
+  const int threads = 256, rows_per_block = (threads / 32) * 4;
+  return launch_pdl(PDL_GEMV, gemv_bf16_kernel, dim3((N + rows_per_block - 1) / rows_per_block), dim3(threads),
+                    K * sizeof(float), stream, static_cast<const __nv_bfloat16*>(x),
+                    static_cast<const __nv_bfloat16*>(W), y, N, K);
+}
+
+// fp32 -> bf16-rounded fp32 (biases and norm weights of the bf16 mode)
+__global__ void round_bf16_kernel(float* v, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    v[i] = bf16_round(v[i]);
+}
+
+cudaError_t round_to_bf16(float* v, int64_t n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  round_bf16_kernel<<<blocks, 256, 0, stream>>>(v, n);
+  return cudaGetLastError();
+}
+
 // --------------------------------------------------------------------- RoPE
 // apply_rotary_pos_emb (modeling_qwen2.py:116-146): out = x*cos + rotate_half(x)*sin
 // with separately rounded products, as the CPU reference evaluates it.

@@ -49,6 +49,19 @@ cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap
                     size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
                     bool pdl, const RopeArgs* rope = nullptr);
 
+// ---- bf16 tensor-core GEMM (gemm_bf16.cu): the bf16 mode ----
+// X: bf16 activations [rows][K]; weights packed once into bf16 tile blocks.
+// C is bf16 except EPI_STORE (fp32 copies of the bf16 logits); bias holds bf16
+// values in fp32; EPI_ROPE writes bf16 q and cache rows.
+bool make_tmap_bf16(TensorMap* out, const void* base, long rows, long cols, long ld, int box_rows);
+cudaError_t gemm_bf16_init();
+size_t packed_weight_elems_bf16(int N, int K);
+cudaError_t pack_weight_tiles_bf16(const float* src, int N, int K, void* dst, cudaStream_t stream);
+bool make_tmap_packed_bf16(TensorMap* out, const void* packed, int N, int K);
+cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int ldc, const float* bias, int M, int N,
+                      int K, int epi, float* ws, size_t ws_floats, int* tickets, int max_tickets, uint32_t* status,
+                      int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr);
+
 // ---- element-wise (elementwise.cu) ----
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
                        int hidden, float* x, uint32_t* status, cudaStream_t stream);
@@ -67,19 +80,26 @@ cudaError_t synth_fill_device(float* dst, int64_t n, uint64_t seed, uint64_t tid
                               float offset, cudaStream_t stream);
 void synth_fill_host(float* dst, int64_t n, uint64_t seed, uint64_t tid, float scale, float offset);
 cudaError_t f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t stream);
+// bf16 mode (bf16 activations; norm weights and biases as bf16 values in fp32)
+cudaError_t embed_rows_bf16(const int32_t* ids, int ids_stride, int M, const void* table, int vocab, int hidden,
+                            void* x, uint32_t* status, cudaStream_t stream);
+cudaError_t rms_norm_rows_bf16(const void* x, const float* w, void* h, int M, int hidden, float eps,
+                               cudaStream_t stream);
+cudaError_t gemv_bf16(const void* x, const void* W, float* y, int N, int K, cudaStream_t stream);
+cudaError_t round_to_bf16(float* v, int64_t n, cudaStream_t stream);
 
 // ---- attention (attention.cu) ----
-// out_big/out_small (optional) receive the tf32 split of out.
-cudaError_t attention_prefill(const float* q, const float* k_prefix, const float* v_prefix,
-                              float* out, float* out_big, float* out_small, int L, int prefix_cap, int heads,
-                              int kv_heads, int head_dim, float scale, cudaStream_t stream);
+// out_big/out_small (optional, fp32 only) receive the tf32 split of out.
+// bf16: q, K/V and out are bf16 (the bf16 mode); otherwise fp32.
+cudaError_t attention_prefill(const void* q, const void* k_prefix, const void* v_prefix, void* out, float* out_big,
+                              float* out_small, int L, int prefix_cap, int heads, int kv_heads, int head_dim,
+                              float scale, bool bf16, cudaStream_t stream);
 // Decode attention over the shared prefix (length *L_dev) and `t` suffix
 // slots; suffix slot s of beam b lives in row anc[b*4+s] (slot t-1: row b).
-cudaError_t attention_decode(const float* q, const float* k_prefix, const float* v_prefix,
-                             const float* k_suffix, const float* v_suffix, const int32_t* anc,
-                             const int32_t* L_dev, int t, float* out, float* out_big, float* out_small, int beams,
-                             int prefix_cap, int heads, int kv_heads, int head_dim, float scale, uint32_t* status,
-                             cudaStream_t stream);
+cudaError_t attention_decode(const void* q, const void* k_prefix, const void* v_prefix, const void* k_suffix,
+                             const void* v_suffix, const int32_t* anc, const int32_t* L_dev, int t, void* out,
+                             float* out_big, float* out_small, int beams, int prefix_cap, int heads, int kv_heads,
+                             int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream);
 cudaError_t attention_init();
 
 // ---- constraints + beam step (beam.cu) ----

@@ -1,0 +1,453 @@
+// BF16 projection GEMM on the 5th-generation tensor cores (the bf16 mode of
+// the engine: weights, activations and KV in bf16, fp32 accumulation).
+//
+//   C[m, n] (+ epilogue) = sum_k X[m, k] * W[n, k]        X: bf16 activations, W: bf16 weight
+//
+// A CTA owns 128 weight rows (MMA M) x 64 activation rows (MMA N) for a range
+// of K, walked in 64-element chunks (one 128-byte row of bf16):
+//   warp 0     TMA of the packed W tile [128 x 64] into an 8-deep ring (128B swizzle)
+//   warp 1     MMA issuer: tcgen05.mma kind::f16, A = W, B = X, both from shared
+//              memory, 4 instructions (K = 16 each) per chunk
+//   warp 2     TMA of the activation tile [64 x 64] into a 4-deep ring
+//   warps 4..7 promote the TMEM accumulator (double-buffered) into fp32
+//              registers every 4 chunks, as the 3xTF32 kernel does
+// Epilogues round where a bf16 torch model rounds (the reference's
+// bf16-experimental mode casts the whole model, benchmark_inference.py:93-98):
+// every linear output is rounded to bf16 once (bias included), the residual
+// add, SiLU, the SwiGLU product and each RoPE product and sum are rounded
+// again; the LM head writes fp32 copies of its bf16 logits (HF upcasts the
+// logits before the log-softmax).  Split-K and the shared-memory epilogue are
+// the 3xTF32 kernel's.  Every mbarrier wait is bounded.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "engine.h"
+#include "tcgen05.cuh"
+
+namespace rtr {
+
+constexpr int BF_THREADS = 256;          // 8 warps
+constexpr int BF_KC = 64;                // bf16 per 128-byte row
+constexpr int BF_WROWS = 128;            // MMA M
+constexpr int BF_NTOK = 64;              // activation rows per CTA (MMA N)
+constexpr int BF_WSTAGES = 8;
+constexpr int BF_XSTAGES = 4;
+constexpr int BF_PROMOTE = 4;
+constexpr int BF_W_BYTES = BF_WROWS * 128;
+constexpr int BF_X_BYTES = BF_NTOK * 128;
+constexpr int BF_D_COLS = BF_NTOK;
+constexpr int BF_TMEM_COLS = 2 * BF_D_COLS;   // 128: double-buffered accumulator
+constexpr int BF_NBARS = 2 * BF_WSTAGES + 2 * BF_XSTAGES + 4;
+constexpr int BF_RING_BYTES = BF_WSTAGES * BF_W_BYTES + BF_XSTAGES * BF_X_BYTES;
+constexpr int BF_SMEM_BYTES = BF_RING_BYTES + 1024 + 8 * BF_NBARS + 16;
+constexpr int BF_RLD = BF_WROWS + 4;          // epilogue tile row stride (floats)
+static_assert(BF_NTOK * BF_RLD * 4 <= BF_RING_BYTES, "epilogue tile fits in the rings");
+
+struct BfParams {
+  void* C;                 // bf16 [M][ldc]; fp32 for EPI_STORE (logits)
+  const float* bias;       // bf16 values held in fp32
+  int M, N, K, ldc, epi, splits;
+  float* ws;
+  int* tickets;
+  uint32_t* status;
+  RopeArgs rope;           // EPI_ROPE: q_out / k_dst / v_dst are bf16
+};
+
+RTR_DEVICE float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+RTR_DEVICE __nv_bfloat16* bfp(void* p) { return static_cast<__nv_bfloat16*>(p); }
+RTR_DEVICE float4 rbf4(float4 v) { return make_float4(rbf(v.x), rbf(v.y), rbf(v.z), rbf(v.w)); }
+RTR_DEVICE void st_bf4(__nv_bfloat16* dst, float4 v) {  // 8-byte store of 4 bf16
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+RTR_DEVICE float4 ld_bf4(const __nv_bfloat16* src) {
+  const uint2 u = *reinterpret_cast<const uint2*>(src);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+RTR_DEVICE float4 bf_mul4(float4 a, float4 b) { return rbf4(make_float4(a.x * b.x, a.y * b.y, a.z * b.z, a.w * b.w)); }
+RTR_DEVICE float4 bf_add4(float4 a, float4 b) { return rbf4(make_float4(a.x + b.x, a.y + b.y, a.z + b.z, a.w + b.w)); }
+
+// Epilogue from a [rows][ld4 float4] shared tile of fp32 sums, every thread of
+// the CTA, 4 columns at a time.
+RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4, int tok0, int n0, int rows,
+                                 int cols4) {
+  if (p.epi == EPI_SWIGLU) {
+    // packed rows: 32 q + [0,16) gate, 32 q + [16,32) up of intermediate 16 q + [0,16)
+    for (int q = threadIdx.x; q < rows * 16; q += BF_THREADS) {
+      const int j = q >> 4, blk = (q >> 2) & 3, g4 = q & 3;
+      const int c4 = blk * 8 + g4;
+      if (c4 + 4 >= cols4) continue;
+      const float4 g = rbf4(red4[j * ld4 + c4]), u = rbf4(red4[j * ld4 + c4 + 4]);
+      const float4 sg = rbf4(make_float4(silu_f(g.x), silu_f(g.y), silu_f(g.z), silu_f(g.w)));
+      const long o = (long)(tok0 + j) * p.ldc + ((n0 + blk * 32) >> 5) * 16 + g4 * 4;
+      st_bf4(bfp(p.C) + o, bf_mul4(sg, u));
+    }
+    return;
+  }
+  if (p.epi == EPI_ROPE) {
+    const RopeArgs& r = p.rope;
+    const int D = r.head_dim, half = D >> 1;
+    const int base_pos = r.slot < 0 ? 0 : *r.L_dev + r.slot;
+    for (int q = threadIdx.x; q < rows * 32; q += BF_THREADS) {
+      const int j = q >> 5, c4 = q & 31;
+      if (c4 >= cols4) continue;
+      const int col = n0 + c4 * 4, m = tok0 + j;
+      const int h = col / D, d = col % D;
+      float4 v = rbf4(f4add(red4[j * ld4 + c4], *reinterpret_cast<const float4*>(p.bias + col)));
+      if (h < r.heads + r.kv_heads) {
+        const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
+        const float4 pv = rbf4(f4add(red4[j * ld4 + pc4], *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4)));
+        int pos = r.slot < 0 ? m : base_pos;
+        if (pos < 0 || pos >= r.positions) {
+          atomicOr(p.status, RTR_DEV_BAD_LENGTH);
+          pos = 0;
+        }
+        const float4 cs = *reinterpret_cast<const float4*>(r.cos_t + (long)pos * half + (d % half));
+        const float4 sn = *reinterpret_cast<const float4*>(r.sin_t + (long)pos * half + (d % half));
+        // q * cos + rotate_half(q) * sin, each product and the sum rounded to bf16
+        v = d < half ? bf_add4(bf_mul4(v, cs), bf_mul4(f4neg(pv), sn)) : bf_add4(bf_mul4(v, cs), bf_mul4(pv, sn));
+      }
+      __nv_bfloat16* dst;
+      if (h < r.heads) {
+        dst = bfp(r.q_out) + ((long)m * r.heads + h) * D + d;
+      } else {
+        const bool is_k = h < r.heads + r.kv_heads;
+        const int g = is_k ? h - r.heads : h - r.heads - r.kv_heads;
+        __nv_bfloat16* cache = bfp(is_k ? r.k_dst : r.v_dst);
+        dst = r.slot < 0 ? cache + ((long)g * r.prefix_cap + m) * D + d : cache + ((long)m * r.kv_heads + g) * D + d;
+      }
+      st_bf4(dst, v);
+    }
+    return;
+  }
+  for (int q = threadIdx.x; q < rows * 32; q += BF_THREADS) {
+    const int j = q >> 5, c4 = q & 31;
+    if (c4 >= cols4) continue;
+    const int col = n0 + c4 * 4;
+    const long o = (long)(tok0 + j) * p.ldc + col;
+    float4 v = red4[j * ld4 + c4];
+    if (p.epi == EPI_STORE) {  // logits: fp32 copies of the bf16 values
+      *reinterpret_cast<float4*>(static_cast<float*>(p.C) + o) = rbf4(v);
+    } else if (p.epi == EPI_BIAS) {
+      st_bf4(bfp(p.C) + o, f4add(v, *reinterpret_cast<const float4*>(p.bias + col)));
+    } else {  // EPI_RESID: x = bf16(x + bf16(y))
+      st_bf4(bfp(p.C) + o, f4add(ld_bf4(bfp(p.C) + o), rbf4(v)));
+    }
+  }
+}
+
+// Split-K part 1 (last CTA of a tile): partials summed in split order into a
+// [64][128] shared tile.
+RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int rows, int cols4, int tile, long tstride) {
+  constexpr int SLOTS = (BF_NTOK * BF_WROWS / 4 + BF_THREADS - 1) / BF_THREADS;
+  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (BF_NTOK * BF_WROWS));
+  const long zs = tstride >> 2;
+  const int nslots = rows * (BF_WROWS / 4);
+  float4 s[SLOTS];
+#pragma unroll
+  for (int u = 0; u < SLOTS; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int z = 0; z < p.splits; z += 2) {
+    float4 v[2][SLOTS];
+#pragma unroll
+    for (int dz = 0; dz < 2; ++dz)
+#pragma unroll
+      for (int u = 0; u < SLOTS; ++u) {
+        const int q = threadIdx.x + u * BF_THREADS;
+        const bool ok = z + dz < p.splits && q < nslots && (q & 31) < cols4;
+        v[dz][u] = ok ? __ldcg(base + (z + dz) * zs + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+    for (int dz = 0; dz < 2; ++dz)
+#pragma unroll
+      for (int u = 0; u < SLOTS; ++u) s[u] = f4add(s[u], v[dz][u]);
+  }
+#pragma unroll
+  for (int u = 0; u < SLOTS; ++u) {
+    const int q = threadIdx.x + u * BF_THREADS;
+    if (q < nslots) red4[q] = s[u];
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(BF_THREADS, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, BfParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* wring = smem;
+  uint8_t* xring = smem + BF_WSTAGES * BF_W_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + BF_XSTAGES * BF_X_BYTES);
+  uint64_t* w_full = bars;
+  uint64_t* w_empty = w_full + BF_WSTAGES;
+  uint64_t* x_full = w_empty + BF_WSTAGES;
+  uint64_t* x_empty = x_full + BF_XSTAGES;
+  uint64_t* d_full = x_empty + BF_XSTAGES;  // [2]
+  uint64_t* d_empty = d_full + 2;           // [2]
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 2);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2) + 1;
+  __shared__ int last_cta;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok0 = blockIdx.x * BF_NTOK;
+  const int n0 = blockIdx.y * BF_WROWS;
+  const int nchunks = (p.K + BF_KC - 1) / BF_KC;
+  const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
+  const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
+  const int nloc = c1 - c0;
+  const int ngroups = (nloc + BF_PROMOTE - 1) / BF_PROMOTE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BF_WSTAGES; ++s) { mbar_init(smem_addr(&w_full[s]), 1); mbar_init(smem_addr(&w_empty[s]), 1); }
+    for (int s = 0; s < BF_XSTAGES; ++s) { mbar_init(smem_addr(&x_full[s]), 1); mbar_init(smem_addr(&x_empty[s]), 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(smem_addr(&d_full[b]), 1); mbar_init(smem_addr(&d_empty[b]), 4); }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) tmem_alloc(smem_addr(tmem_slot), BF_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int w_issued = 0, x_issued = 0, mma_groups = 0;
+  float acc[BF_NTOK];  // live only in the promoter warps
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // weights do not depend on the previous kernel: no griddepcontrol.wait
+      for (int i = 0; i < nloc; ++i) {
+        const int s = i % BF_WSTAGES;
+        if (!mbar_wait(smem_addr(&w_empty[s]), ((i / BF_WSTAGES) & 1) ^ 1, abort_flag)) break;
+        const uint32_t fb = smem_addr(&w_full[s]);
+        mbar_expect_tx(fb, BF_W_BYTES);
+        tma_load_2d(smem_addr(wring + s * BF_W_BYTES), &tmW, 0, (blockIdx.y * nchunks + c0 + i) * BF_WROWS, fb);
+        w_issued = i + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BF_WROWS, BF_NTOK);
+      for (int i = 0; i < nloc; ++i) {
+        const int g = i / BF_PROMOTE, b = g & 1;
+        if (i % BF_PROMOTE == 0 && g >= 2 && !mbar_wait(smem_addr(&d_empty[b]), ((g >> 1) - 1) & 1, abort_flag))
+          break;
+        const int ws = i % BF_WSTAGES, xs = i % BF_XSTAGES;
+        if (!mbar_wait(smem_addr(&w_full[ws]), (i / BF_WSTAGES) & 1, abort_flag)) break;
+        if (!mbar_wait(smem_addr(&x_full[xs]), (i / BF_XSTAGES) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * BF_D_COLS;
+        const uint64_t ad = sw128_desc(smem_addr(wring + ws * BF_W_BYTES));
+        const uint64_t bd = sw128_desc(smem_addr(xring + xs * BF_X_BYTES));
+#pragma unroll
+        for (int kk = 0; kk < BF_KC / 16; ++kk) {
+          const uint64_t adv = (uint64_t)(kk * 32) >> 4;  // 16 bf16 = 32 bytes along K
+          mma_f16_ss(d, ad + adv, bd + adv, idesc, (i % BF_PROMOTE != 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(smem_addr(&w_empty[ws]));
+        mma_commit(smem_addr(&x_empty[xs]));
+        if (i % BF_PROMOTE == BF_PROMOTE - 1 || i == nloc - 1) {
+          mma_commit(smem_addr(&d_full[b]));
+          mma_groups = g + 1;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    pdl_wait();
+    if (lane == 0) {
+      for (int i = 0; i < nloc; ++i) {
+        const int s = i % BF_XSTAGES;
+        if (!mbar_wait(smem_addr(&x_empty[s]), ((i / BF_XSTAGES) & 1) ^ 1, abort_flag)) break;
+        const uint32_t fb = smem_addr(&x_full[s]);
+        mbar_expect_tx(fb, BF_X_BYTES);
+        tma_load_2d(smem_addr(xring + s * BF_X_BYTES), &tmX, (c0 + i) * BF_KC, tok0, fb);
+        x_issued = i + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------ warps 4..7: promote accumulators
+#pragma unroll
+    for (int j = 0; j < BF_NTOK; ++j) acc[j] = 0.f;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    for (int g = 0; g < ngroups; ++g) {
+      const int b = g & 1;
+      if (!mbar_wait(smem_addr(&d_full[b]), (g >> 1) & 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + lane_base + b * BF_D_COLS;
+#pragma unroll
+      for (int cb = 0; cb < BF_NTOK; cb += 32) {
+        uint32_t r[32];
+        tmem_ld32(d + cb, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[cb + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&d_empty[b]));
+    }
+  }
+  pdl_launch_dependents();
+
+  // drain on abort: issued copies and MMAs must land before smem/TMEM go away
+  if (*abort_flag) {
+    if (threadIdx.x == 0) atomicOr(p.status, RTR_DEV_TIMEOUT);
+    if (warp == 0 && lane == 0)
+      for (int i = 0; i < w_issued; ++i) mbar_drain(smem_addr(&w_full[i % BF_WSTAGES]), (i / BF_WSTAGES) & 1);
+    if (warp == 2 && lane == 0)
+      for (int i = 0; i < x_issued; ++i) mbar_drain(smem_addr(&x_full[i % BF_XSTAGES]), (i / BF_XSTAGES) & 1);
+    if (warp == 1 && lane == 0 && mma_groups > 0) {
+      const int g = mma_groups - 1;
+      mbar_drain(smem_addr(&d_full[g & 1]), (g >> 1) & 1);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BF_TMEM_COLS);
+  }
+  if (*abort_flag) return;
+  pdl_wait();  // the epilogue reads and writes memory of earlier kernels
+
+  const bool have = warp >= 4;
+  const int quarter = warp & 3;
+  const int n = n0 + quarter * 32 + lane;  // weight row of this thread
+  const int rows = p.M - tok0 < BF_NTOK ? p.M - tok0 : BF_NTOK;
+  const int cols4 = (p.N - n0 < BF_WROWS ? p.N - n0 : BF_WROWS) >> 2;
+  float4* red4 = reinterpret_cast<float4*>(smem);  // the rings are free now
+  if (p.splits > 1) {
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    const long tstride = (long)gridDim.x * gridDim.y * (BF_NTOK * BF_WROWS);
+    if (have && n < p.N) {
+      float* w = p.ws + blockIdx.z * tstride + (long)tile * (BF_NTOK * BF_WROWS) + quarter * 32 + lane;
+#pragma unroll
+      for (int j = 0; j < BF_NTOK; ++j)
+        if (j < rows) __stcg(w + j * BF_WROWS, acc[j]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int* tk = p.tickets + tile;
+      last_cta = atomicAdd(tk, 1) == p.splits - 1;
+      if (last_cta) *tk = 0;  // re-arm for the next launch / graph replay
+    }
+    __syncthreads();
+    if (!last_cta) return;
+    __threadfence();
+    bf_splitk_sum(p, red4, rows, cols4, tile, tstride);
+    bf_tile_epilogue(p, red4, BF_WROWS / 4, tok0, n0, rows, cols4);
+    return;
+  }
+  if (have && n < p.N) {
+    float* red = reinterpret_cast<float*>(smem) + quarter * 32 + lane;
+#pragma unroll
+    for (int j = 0; j < BF_NTOK; ++j)
+      if (j < rows) red[j * BF_RLD] = acc[j];
+  }
+  __syncthreads();
+  bf_tile_epilogue(p, red4, BF_RLD / 4, tok0, n0, rows, cols4);
+}
+
+// ---------------------------------------------------------------- host side
+// 2-D bf16 row-major [rows][cols] (row stride ld elements), box [box_rows][64].
+bool make_tmap_bf16(TensorMap* out, const void* base, long rows, long cols, long ld, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (ld * 2) % 16 || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BF_KC, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(reinterpret_cast<CUtensorMap*>(out), CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// W [N, K] (fp32 source, rounded to bf16) becomes blocks
+// [N/128 tiles][K/64 chunks][128 rows][64 bf16] (zero padded): every TMA load
+// of a (tile, chunk) reads 16 KB of contiguous memory.
+__global__ void pack_bf16_kernel(const float* __restrict__ src, int N, int K, int nchunks,
+                                 __nv_bfloat16* __restrict__ dst, long total) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int k = (int)(i & 63);
+    const int r = (int)((i >> 6) & 127);
+    const long blk = i >> 13;
+    const int c = (int)(blk % nchunks);
+    const long t = blk / nchunks;
+    const long row = t * BF_WROWS + r, col = (long)c * BF_KC + k;
+    dst[i] = __float2bfloat16_rn((row < N && col < K) ? src[row * K + col] : 0.f);
+  }
+}
+
+size_t packed_weight_elems_bf16(int N, int K) {
+  return (size_t)((N + BF_WROWS - 1) / BF_WROWS) * ((K + BF_KC - 1) / BF_KC) * BF_WROWS * BF_KC;
+}
+
+cudaError_t pack_weight_tiles_bf16(const float* src, int N, int K, void* dst, cudaStream_t stream) {
+  const long total = (long)packed_weight_elems_bf16(N, K);
+  pack_bf16_kernel<<<148 * 8, 256, 0, stream>>>(src, N, K, (K + BF_KC - 1) / BF_KC,
+                                                static_cast<__nv_bfloat16*>(dst), total);
+  return cudaGetLastError();
+}
+
+bool make_tmap_packed_bf16(TensorMap* out, const void* packed, int N, int K) {
+  const long rows = (long)packed_weight_elems_bf16(N, K) / BF_KC;
+  return make_tmap_bf16(out, packed, rows, BF_KC, BF_KC, BF_WROWS);
+}
+
+cudaError_t gemm_bf16_init() {
+  return cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BF_SMEM_BYTES);
+}
+
+static int bf_splits(int tiles, int nchunks, int sms) {
+  if (tiles >= sms) return 1;
+  int s = sms / tiles;
+  if (s > nchunks / 2) s = nchunks / 2;  // keep at least two chunks per split
+  if (s > 16) s = 16;
+  return s < 1 ? 1 : s;
+}
+
+cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int ldc, const float* bias, int M, int N,
+                      int K, int epi, float* ws, size_t ws_floats, int* tickets, int max_tickets, uint32_t* status,
+                      int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope) {
+  if (epi == EPI_ROPE) {
+    if (!rope || !bias || (rope->head_dim != 64 && rope->head_dim != 128) ||
+        N != (rope->heads + 2 * rope->kv_heads) * rope->head_dim || (reinterpret_cast<uintptr_t>(bias) & 15))
+      return cudaErrorInvalidValue;
+  } else if (N % 4 || ldc % 4 || (reinterpret_cast<uintptr_t>(C) & 15)) {
+    return cudaErrorInvalidValue;
+  }
+  if (epi == EPI_BIAS && (!bias || (reinterpret_cast<uintptr_t>(bias) & 15))) return cudaErrorInvalidValue;
+  if (K % 8) return cudaErrorInvalidValue;  // TMA rows of the activations: 16-byte multiples
+  const int tt = (M + BF_NTOK - 1) / BF_NTOK, wt = (N + BF_WROWS - 1) / BF_WROWS;
+  const int nchunks = (K + BF_KC - 1) / BF_KC;
+  int splits = bf_splits(tt * wt, nchunks, sms);
+  while (splits > 1 && ((size_t)splits * tt * wt * BF_NTOK * BF_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
+  BfParams p{C, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
+  if (rope) p.rope = *rope;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tt, wt, splits);
+  cfg.blockDim = dim3(BF_THREADS);
+  cfg.dynamicSmemBytes = BF_SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel, *reinterpret_cast<const CUtensorMap*>(&tmW),
+                            *reinterpret_cast<const CUtensorMap*>(&tmX), p);
+}
+
+}  // namespace rtr

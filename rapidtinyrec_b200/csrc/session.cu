@@ -30,7 +30,10 @@
 using namespace rtr;
 
 struct LayerW {
-  float *wqkv, *bqkv, *wo, *wgu, *wd, *n_in, *n_post;
+  float *wqkv = nullptr, *bqkv = nullptr, *wo = nullptr, *wgu = nullptr, *wd = nullptr, *n_in = nullptr,
+        *n_post = nullptr;
+  // bf16 mode: the packed bf16 GEMM operands (no fp32 copies are kept)
+  void *pqkv = nullptr, *po = nullptr, *pgu = nullptr, *pd = nullptr;
 };
 
 struct rtr_session {
@@ -40,6 +43,12 @@ struct rtr_session {
   bool own_stream = false;
   bool pdl = true;
   bool use_tc = true;  // tcgen05 GEMMs (RTR_GEMM=ffma selects the FFMA kernel)
+  // bf16 mode (RTR_DTYPE_BF16): bf16 weights, activations and KV; biases and
+  // norm weights as bf16 values in fp32; logits in fp32.  The activation and
+  // KV buffers below keep their float pointers and hold bf16 elements.
+  bool bf16 = false;
+  void* embed_bf = nullptr;      // bf16 [V][H] (embedding gather)
+  void* lm_packed_bf = nullptr;  // packed bf16 LM head (the embedding when tied)
   // TMA descriptors keyed by (buffer, box rows): activations at 64/128 rows,
   // weights at 128 rows
   std::map<std::pair<const void*, int>, TensorMap> tmaps;
@@ -147,7 +156,7 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   if (c.num_beams < 1 || c.num_beams > MAX_BEAMS) return fail(nullptr, RTR_ERR_ARG, "num_beams must be in [1, 64]");
   if (c.max_prefix < 3 || c.max_prefix > 32768) return fail(nullptr, RTR_ERR_ARG, "max_prefix must be in [3, 32768]");
   if ((long)c.num_beams * c.vocab >= (1L << 32)) return fail(nullptr, RTR_ERR_ARG, "beams*vocab must fit 32 bits");
-  if (c.dtype != RTR_DTYPE_F32) return fail(nullptr, RTR_ERR_ARG, "this build serves dtype RTR_DTYPE_F32 only");
+  if (c.dtype != RTR_DTYPE_F32 && c.dtype != RTR_DTYPE_BF16) return fail(nullptr, RTR_ERR_ARG, "unknown dtype");
 
   auto* s = new rtr_session();
   s->cfg = c;
@@ -173,27 +182,54 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(beam_init());
   CREATE_TRY(gemm_tc_init());
   CREATE_TRY(attention_init());
+  CREATE_TRY(gemm_bf16_init());
   if (const char* g = std::getenv("RTR_GEMM")) s->use_tc = std::strcmp(g, "ffma") != 0;
   s->pdl = pdl_on(PDL_GEMM);
+  s->bf16 = c.dtype == RTR_DTYPE_BF16;
+  if (s->bf16 && !s->use_tc) {
+    s->err = "the bf16 mode runs on the tensor-core GEMMs only (unset RTR_GEMM)";
+    return bail(RTR_ERR_ARG);
+  }
 
   const long H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
   const long qd = (long)c.heads * D, kvd = (long)c.kv_heads * D, qkvd = qkv_dim(c);
   const long B = c.num_beams, cap = c.max_prefix;
   const long M = cap > B ? cap : B;
-  CREATE_TRY(dev_alloc(s, &s->embed, V * H));
   s->layers.resize(c.layers);
+  if (!s->bf16) {
+    CREATE_TRY(dev_alloc(s, &s->embed, V * H));
+    for (auto& l : s->layers) {
+      CREATE_TRY(dev_alloc(s, &l.wqkv, qkvd * H));
+      CREATE_TRY(dev_alloc(s, &l.wo, H * qd));
+      CREATE_TRY(dev_alloc(s, &l.wgu, 2 * I * H));
+      CREATE_TRY(dev_alloc(s, &l.wd, H * I));
+    }
+    if (c.tied_embeddings) s->lm_head = s->embed;
+    else CREATE_TRY(dev_alloc(s, &s->lm_head, V * H));
+  } else {
+    auto packed = [&](void** p, long rows, long cols) {
+      uint16_t* q = nullptr;
+      cudaError_t e = dev_alloc(s, &q, packed_weight_elems_bf16((int)rows, (int)cols));
+      *p = q;
+      return e;
+    };
+    uint16_t* eb = nullptr;
+    CREATE_TRY(dev_alloc(s, &eb, (size_t)V * H));
+    s->embed_bf = eb;
+    for (auto& l : s->layers) {
+      CREATE_TRY(packed(&l.pqkv, qkvd, H));
+      CREATE_TRY(packed(&l.po, H, qd));
+      CREATE_TRY(packed(&l.pgu, 2 * I, H));
+      CREATE_TRY(packed(&l.pd, H, I));
+    }
+    CREATE_TRY(packed(&s->lm_packed_bf, V, H));
+  }
   for (auto& l : s->layers) {
-    CREATE_TRY(dev_alloc(s, &l.wqkv, qkvd * H));
     CREATE_TRY(dev_alloc(s, &l.bqkv, qkvd));
-    CREATE_TRY(dev_alloc(s, &l.wo, H * qd));
-    CREATE_TRY(dev_alloc(s, &l.wgu, 2 * I * H));
-    CREATE_TRY(dev_alloc(s, &l.wd, H * I));
     CREATE_TRY(dev_alloc(s, &l.n_in, H));
     CREATE_TRY(dev_alloc(s, &l.n_post, H));
   }
   CREATE_TRY(dev_alloc(s, &s->norm_final, H));
-  if (c.tied_embeddings) s->lm_head = s->embed;
-  else CREATE_TRY(dev_alloc(s, &s->lm_head, V * H));
   s->weight_bytes = s->device_bytes;
 
   CREATE_TRY(dev_alloc(s, &s->kv_prefix, (size_t)c.layers * 2 * kvd * cap));
@@ -204,12 +240,14 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(dev_alloc(s, &s->q, M * qd));
   CREATE_TRY(dev_alloc(s, &s->attn, M * qd));
   CREATE_TRY(dev_alloc(s, &s->act, M * I));
-  CREATE_TRY(dev_alloc(s, &s->h_big, M * H));
-  CREATE_TRY(dev_alloc(s, &s->h_small, M * H));
-  CREATE_TRY(dev_alloc(s, &s->attn_big, M * qd));
-  CREATE_TRY(dev_alloc(s, &s->attn_small, M * qd));
-  CREATE_TRY(dev_alloc(s, &s->act_big, M * I));
-  CREATE_TRY(dev_alloc(s, &s->act_small, M * I));
+  if (!s->bf16) {
+    CREATE_TRY(dev_alloc(s, &s->h_big, M * H));
+    CREATE_TRY(dev_alloc(s, &s->h_small, M * H));
+    CREATE_TRY(dev_alloc(s, &s->attn_big, M * qd));
+    CREATE_TRY(dev_alloc(s, &s->attn_small, M * qd));
+    CREATE_TRY(dev_alloc(s, &s->act_big, M * I));
+    CREATE_TRY(dev_alloc(s, &s->act_small, M * I));
+  }
   CREATE_TRY(dev_alloc(s, &s->logits, B * V));
   long max_n = qkvd;
   if (H > max_n) max_n = H;
@@ -237,12 +275,27 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   default_rope(c, s->rope_positions, cs, sn);
   CREATE_TRY(cudaMemcpy(s->rope_cos, cs.data(), cs.size() * sizeof(float), cudaMemcpyHostToDevice));
   CREATE_TRY(cudaMemcpy(s->rope_sin, sn.data(), sn.size() * sizeof(float), cudaMemcpyHostToDevice));
+  if (s->bf16) {  // a bf16 model rotates with bf16 cos/sin
+    CREATE_TRY(round_to_bf16(s->rope_cos, (int64_t)cs.size(), 0));
+    CREATE_TRY(round_to_bf16(s->rope_sin, (int64_t)sn.size(), 0));
+    CREATE_TRY(cudaDeviceSynchronize());
+  }
 
   // TMA descriptors of the GEMM activation operands: the big and small halves
+  // (bf16 mode: the bf16 buffers themselves)
   struct Act { const float* v; float* big; float* small; long width; };
   const Act acts[3] = {{s->h, s->h_big, s->h_small, H}, {s->attn, s->attn_big, s->attn_small, qd},
                        {s->act, s->act_big, s->act_small, I}};
   for (const auto& a : acts) {
+    if (s->bf16) {
+      TensorMap m;
+      if (!make_tmap_bf16(&m, a.v, M, a.width, a.width, 64)) {
+        s->err = "cuTensorMapEncodeTiled failed for a bf16 activation buffer";
+        return bail(RTR_ERR_CUDA);
+      }
+      s->tmaps[{a.v, 64}] = m;
+      continue;
+    }
     s->split_of[a.v] = {a.big, a.small};
     for (const float* half : {a.big, a.small}) {
       TensorMap m;
@@ -297,6 +350,73 @@ int rtr_load_rope(rtr_session* s, const float* cos_host, const float* sin_host, 
   CUDA_TRY(s, cudaSetDevice(s->device));
   CUDA_TRY(s, cudaMemcpy(s->rope_cos, cos_host, bytes, cudaMemcpyHostToDevice));
   CUDA_TRY(s, cudaMemcpy(s->rope_sin, sin_host, bytes, cudaMemcpyHostToDevice));
+  if (s->bf16) {  // a bf16 model rotates with bf16 cos/sin (cos/sin .to(bfloat16))
+    CUDA_TRY(s, round_to_bf16(s->rope_cos, (int64_t)(bytes / sizeof(float)), 0));
+    CUDA_TRY(s, round_to_bf16(s->rope_sin, (int64_t)(bytes / sizeof(float)), 0));
+    CUDA_TRY(s, cudaDeviceSynchronize());
+  }
+  return RTR_OK;
+}
+
+// bf16 mode: every matrix is staged once in fp32 on the device, rounded to
+// bf16 and packed into the GEMM's tile blocks; biases and norm weights are
+// rounded in place (a bf16 model's parameters).
+static int load_weights_bf16(rtr_session* s, const void* const* tensors, int32_t src_on_device) {
+  const auto& c = s->cfg;
+  const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  const size_t H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
+  const size_t qd = c.heads * D, kvd = c.kv_heads * D, qkvd = qd + 2 * kvd;
+  const size_t f = sizeof(float);
+  size_t most = V * H;
+  for (size_t n : {qkvd * H, H * qd, 2 * I * H, H * I}) most = n > most ? n : most;
+  float* stage = nullptr;
+  CUDA_TRY(s, cudaMalloc(&stage, most * f));
+  auto cp = [&](void* dst, const void* src, size_t n) { return cudaMemcpy(dst, src, n * f, kind); };
+  auto pack = [&](void* dst, size_t rows, size_t cols) -> cudaError_t {
+    cudaError_t e = pack_weight_tiles_bf16(stage, (int)rows, (int)cols, dst, 0);
+    if (e != cudaSuccess) return e;
+    TensorMap m;
+    if (!make_tmap_packed_bf16(&m, dst, (int)rows, (int)cols)) return cudaErrorInvalidValue;
+    s->tmaps[{dst, 128}] = m;
+    return cudaDeviceSynchronize();  // the stage is reused by the next matrix
+  };
+  auto params = [&](float* dst, const void* src, size_t n) -> cudaError_t {
+    cudaError_t e = cp(dst, src, n);
+    return e != cudaSuccess ? e : round_to_bf16(dst, (int64_t)n, 0);
+  };
+  cudaError_t e = cp(stage, tensors[0], V * H);
+  if (e == cudaSuccess) e = f32_to_bf16(stage, s->embed_bf, (int64_t)(V * H), 0);
+  if (e == cudaSuccess && c.tied_embeddings) e = pack(s->lm_packed_bf, V, H);
+  for (int l = 0; l < c.layers && e == cudaSuccess; ++l) {
+    const void* const* t = tensors + 1 + 12 * l;
+    LayerW& w = s->layers[l];
+    e = cp(stage, t[0], qd * H);                                        // q, k, v rows
+    if (e == cudaSuccess) e = cp(stage + qd * H, t[2], kvd * H);
+    if (e == cudaSuccess) e = cp(stage + (qd + kvd) * H, t[4], kvd * H);
+    if (e == cudaSuccess) e = pack(w.pqkv, qkvd, H);
+    if (e == cudaSuccess) e = params(w.bqkv, t[1], qd);
+    if (e == cudaSuccess) e = params(w.bqkv + qd, t[3], kvd);
+    if (e == cudaSuccess) e = params(w.bqkv + qd + kvd, t[5], kvd);
+    if (e == cudaSuccess) e = cp(stage, t[6], H * qd);
+    if (e == cudaSuccess) e = pack(w.po, H, qd);
+    // gate/up interleaved in blocks of 16 rows
+    if (e == cudaSuccess) e = cudaMemcpy2D(stage, 32 * H * f, t[7], 16 * H * f, 16 * H * f, I / 16, kind);
+    if (e == cudaSuccess) e = cudaMemcpy2D(stage + 16 * H, 32 * H * f, t[8], 16 * H * f, 16 * H * f, I / 16, kind);
+    if (e == cudaSuccess) e = pack(w.pgu, 2 * I, H);
+    if (e == cudaSuccess) e = cp(stage, t[9], H * I);
+    if (e == cudaSuccess) e = pack(w.pd, H, I);
+    if (e == cudaSuccess) e = params(w.n_in, t[10], H);
+    if (e == cudaSuccess) e = params(w.n_post, t[11], H);
+  }
+  if (e == cudaSuccess) e = params(s->norm_final, tensors[1 + 12 * c.layers], H);
+  if (e == cudaSuccess && !c.tied_embeddings) {
+    e = cp(stage, tensors[2 + 12 * c.layers], V * H);
+    if (e == cudaSuccess) e = pack(s->lm_packed_bf, V, H);
+  }
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  cudaFree(stage);
+  if (e != cudaSuccess) return fail(s, RTR_ERR_CUDA, std::string("bf16 weight load: ") + cudaGetErrorString(e));
+  s->weights_loaded = true;
   return RTR_OK;
 }
 
@@ -310,6 +430,7 @@ int rtr_load_weights(rtr_session* s, const void* const* tensors, int32_t n_tenso
   for (int i = 0; i < n_tensors; ++i)
     if (!tensors[i]) return fail(s, RTR_ERR_ARG, "null weight tensor " + std::to_string(i));
   CUDA_TRY(s, cudaSetDevice(s->device));
+  if (s->bf16) return load_weights_bf16(s, tensors, src_on_device);
   const cudaMemcpyKind kind = src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
   const size_t H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
   const size_t qd = c.heads * D, kvd = c.kv_heads * D;
@@ -460,8 +581,68 @@ static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W,
     if (_e != cudaSuccess) return _e;      \
   } while (0)
 
+// bf16 mode: projection GEMM of the bf16 activation buffer X (its TMA map)
+// against a packed bf16 weight.
+static cudaError_t gemm16(rtr_session* s, const float* X, const void* Wp, void* C, int ldc, const float* bias, int M,
+                          int N, int K, int epi, const RopeArgs* rope = nullptr) {
+  auto x = s->tmaps.find({X, 64});
+  auto w = s->tmaps.find({Wp, 128});
+  if (x == s->tmaps.end() || w == s->tmaps.end()) return cudaErrorInvalidValue;
+  return gemm_bf16(w->second, x->second, C, ldc, bias, M, N, K, epi, s->ws, s->ws_floats, s->tickets, kTickets,
+                   s->d_status, s->sms, s->stream, s->pdl, rope);
+}
+
+// The forward of the bf16 mode: the same launches as the fp32 forward with
+// bf16 activations, KV and weights (the reference's bf16-experimental model).
+static cudaError_t forward_bf16(rtr_session* s, int t) {
+  const auto& c = s->cfg;
+  const int H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
+  const int qd = c.heads * D, kvd = c.kv_heads * D, qkvd = qkv_dim(c);
+  const int B = beams_of(s), cap = c.max_prefix;
+  const int M = t == 0 ? s->L : B;
+  const float scale = (float)std::pow((double)D, -0.5);
+  cudaStream_t st = s->stream;
+  const int32_t* ids = t == 0 ? s->d_ids : &s->beam->next_tok[0];
+  uint16_t* kvp = reinterpret_cast<uint16_t*>(s->kv_prefix);  // bf16 elements
+  uint16_t* kvs = reinterpret_cast<uint16_t*>(s->kv_suffix);
+  FWD_TRY(embed_rows_bf16(ids, 1, M, s->embed_bf, V, H, s->x, s->d_status, st));
+  for (int l = 0; l < c.layers; ++l) {
+    const LayerW& w = s->layers[l];
+    uint16_t* kp = kvp + (size_t)l * 2 * kvd * cap;
+    uint16_t* vp = kp + (size_t)kvd * cap;
+    uint16_t* ks = kvs + (size_t)l * 2 * 4 * B * kvd;
+    uint16_t* vs = ks + (size_t)4 * B * kvd;
+    const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * kvd;
+    FWD_TRY(rms_norm_rows_bf16(s->x, w.n_in, s->h, M, H, c.rms_eps, st));
+    const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
+                      reinterpret_cast<float*>(t == 0 ? kp : ks + slot),
+                      reinterpret_cast<float*>(t == 0 ? vp : vs + slot), cap, t == 0 ? -1 : t - 1, s->d_L};
+    FWD_TRY(gemm16(s, s->h, w.pqkv, nullptr, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra));
+    if (t == 0)
+      FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, nullptr, nullptr, M, cap, c.heads, c.kv_heads, D, scale, true,
+                                st));
+    else
+      FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, nullptr, nullptr, B,
+                               cap, c.heads, c.kv_heads, D, scale, s->d_status, true, st));
+    FWD_TRY(gemm16(s, s->attn, w.po, s->x, H, nullptr, M, H, qd, EPI_RESID));
+    FWD_TRY(rms_norm_rows_bf16(s->x, w.n_post, s->h, M, H, c.rms_eps, st));
+    FWD_TRY(gemm16(s, s->h, w.pgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
+    FWD_TRY(gemm16(s, s->act, w.pd, s->x, H, nullptr, M, H, I, EPI_RESID));
+  }
+  if (t == 0) {  // the last position only
+    const uint16_t* last = reinterpret_cast<const uint16_t*>(s->x) + (size_t)(M - 1) * H;
+    FWD_TRY(rms_norm_rows_bf16(last, s->norm_final, s->h, 1, H, c.rms_eps, st));
+    FWD_TRY(gemm16(s, s->h, s->lm_packed_bf, s->logits, V, nullptr, 1, V, H, EPI_STORE));
+  } else {
+    FWD_TRY(rms_norm_rows_bf16(s->x, s->norm_final, s->h, B, H, c.rms_eps, st));
+    FWD_TRY(gemm16(s, s->h, s->lm_packed_bf, s->logits, V, nullptr, B, V, H, EPI_STORE));
+  }
+  return cudaSuccess;
+}
+
 // t = 0: prefill of L rows (host L); t >= 1: decode step with beams rows.
 static cudaError_t forward(rtr_session* s, int t) {
+  if (s->bf16) return forward_bf16(s, t);
   const auto& c = s->cfg;
   const int H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
   const int qd = c.heads * D, kvd = c.kv_heads * D, qkvd = qkv_dim(c);
@@ -492,10 +673,10 @@ static cudaError_t forward(rtr_session* s, int t) {
     }
     if (t == 0) {
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
-                                scale, st));
+                                scale, false, st));
     } else {
       FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
-                               s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, st));
+                               s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st));
     }
     FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID));
     FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
@@ -707,6 +888,17 @@ int rtr_profile_gemms(rtr_session* s, int32_t M, int32_t reps, float* ms_per_pas
   CUDA_TRY(s, cudaEventCreate(&a));
   CUDA_TRY(s, cudaEventCreate(&b));
   auto pass = [&]() -> cudaError_t {
+    if (s->bf16) {
+      for (int l = 0; l < c.layers; ++l) {
+        const LayerW& w = s->layers[l];
+        FWD_TRY(gemm16(s, s->h, w.pqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));
+        FWD_TRY(gemm16(s, s->attn, w.po, s->x, H, nullptr, M, H, qd, EPI_STORE));
+        FWD_TRY(gemm16(s, s->h, w.pgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
+        FWD_TRY(gemm16(s, s->act, w.pd, s->x, H, nullptr, M, H, I, EPI_STORE));
+      }
+      return gemm16(s, s->h, s->lm_packed_bf, s->logits, c.vocab, nullptr, M < c.num_beams ? M : c.num_beams,
+                    c.vocab, H, EPI_STORE);
+    }
     for (int l = 0; l < c.layers; ++l) {
       const LayerW& w = s->layers[l];
       FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));

@@ -261,3 +261,59 @@ def test_primary_1p5b_fp32_matches_oracle(cuda):
 def test_0p5b_fp32_head_dim_64_matches_oracle(cuda):
     worst = full_size_case('qwen0.5b-fp32', n_oracle=1, n_props=4, cuda=cuda)
     print(f'qwen0.5b-fp32: max |delta score| vs oracle = {worst:.3e}')
+
+
+# ------------------------------------------------------------ bf16 mode
+def bf16_stats(got, ref):
+    """Rank-list agreement of a bf16 request with the bf16 oracle (the
+    reference's bf16-experimental model, bit-exact to its own fixture on CPU)."""
+    g = {tuple(t): i for i, t in enumerate(got['token_ids'])}
+    r = {tuple(t): i for i, t in enumerate(ref['token_ids'])}
+    common = set(g) & set(r)
+    return {'rank_list_equal': [tuple(t) for t in got['token_ids']] == [tuple(t) for t in ref['token_ids']],
+            'overlap': len(common), 'top1_equal': tuple(got['token_ids'][0]) == tuple(ref['token_ids'][0]),
+            'max_abs_delta': max(abs(got['sequence_logp'][g[s]] - ref['sequence_logp'][r[s]]) for s in common)}
+
+
+def bf16_case(name, n_users, cuda, weight_backend='native'):
+    from oracle.beam_cpu import beam_search
+    from oracle.qwen2_cpu import Qwen2Oracle
+    from rapidtinyrec_b200 import configs, workload
+    wl = configs.workload(name)
+    cfg = wl.model.with_dtype('bf16')
+    items = workload.catalog_items(wl)
+    cons = workload.constraint_dict(cfg, items)
+    users = workload.users(wl, items, count=n_users)
+    if weight_backend == 'numpy':
+        weights = workload.synth_weights(cfg, seed=wl.weight_seed, backend='numpy')
+    else:
+        weights = workload.synth_weights(cfg, seed=wl.weight_seed, device='cuda')
+    eng = make_engine(cfg, weights, cons, max_prefix=max(u.prompt_tokens for u in users))
+    cpu_w = {k: v.cpu() for k, v in weights.items()}
+    del weights
+    torch.cuda.empty_cache()
+    model = Qwen2Oracle(cfg, cpu_w, dtype=torch.bfloat16)
+    iset = set(items)
+    stats = []
+    for u in users:
+        got = eng.generate(u.prompt_token_ids)
+        check_invariants(got, cfg, iset)
+        stats.append(bf16_stats(got, beam_search(model, u.prompt_token_ids, cons, cfg.eos)))
+    eng.close()
+    changed = sum(not s['rank_list_equal'] for s in stats)
+    print(f'{name} bf16: changed rank lists {changed}/{len(stats)}, '
+          f'min overlap {min(s["overlap"] for s in stats)}/50, top-1 equal {sum(s["top1_equal"] for s in stats)}, '
+          f'max |delta score| {max(s["max_abs_delta"] for s in stats):.3e}')
+    return stats
+
+
+def test_tiny_bf16_against_the_bf16_oracle(cuda):
+    stats = bf16_case('tiny', 8, cuda, weight_backend='numpy')
+    assert min(s['overlap'] for s in stats) >= 25
+    assert max(s['max_abs_delta'] for s in stats) <= 0.5
+
+
+def test_1p5b_bf16_against_the_bf16_oracle(cuda):
+    stats = bf16_case('qwen1.5b-bf16', 1, cuda)
+    assert min(s['overlap'] for s in stats) >= 25
+    assert max(s['max_abs_delta'] for s in stats) <= 0.5
