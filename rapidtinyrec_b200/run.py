@@ -223,8 +223,6 @@ def run_folded(args):
     import torch
     precision = args.precision
     dtype = 'fp32' if precision == 'fp32' else 'bf16'
-    if dtype != 'fp32':
-        raise SystemExit('--precision bf16-experimental: the BF16 mode of the native library is not built yet')
     if not 1 <= args.repeats <= 10:
         raise SystemExit('--repeats must be between 1 and 10')
     out = args.output_root
@@ -253,15 +251,19 @@ def _folded(args, out, precision, dtype, policy):
                 'full_cohort': args.full_cohort, 'save_full_scores': args.save_full_scores,
                 'attention_layout': 'folded_query_heads', 'users': [record_of[u.cohort_index] for u in users],
                 'dtype': 'float32' if dtype == 'fp32' else 'bfloat16', 'tf32': False,
+                'numerics': ('fp32 weights and activations, 3xTF32 tensor-core projections' if dtype == 'fp32' else
+                             'bf16 weights, activations and KV (rounded where a bf16 torch model rounds), fp32 '
+                             'accumulation, fp32 log-softmax and beam scores'),
                 'hardware': torch.cuda.get_device_name(0), 'source': inp.source,
                 'model': {'layers': inp.cfg.layers, 'hidden': inp.cfg.hidden, 'heads': inp.cfg.heads,
                           'kv_heads': inp.cfg.kv_heads, 'head_dim': inp.cfg.head_dim,
                           'intermediate': inp.cfg.intermediate, 'vocab': inp.cfg.vocab, 'tied': inp.cfg.tied},
-                'engine': 'rapidtinyrec_b200 native library (tcgen05 3xTF32 projections, one decode graph per request)',
+                'engine': 'rapidtinyrec_b200 native library (tcgen05 projections, one decode graph per request)',
                 'sha256': {'librtr_b200.so': library_digest()},
                 'versions': {'torch': torch.__version__},
                 'protocol': 'Sequential folded inference, one shared physical prefix, full-vocabulary double '
-                            'normalization, beam 50, all five FP32 scores. Setup excluded; per-request prompt '
+                            'normalization, beam 50, all five FP32 scores. Explicit precision chosen at session '
+                            'creation. Setup excluded; per-request prompt '
                             'upload, prefill, decode graph and result read included (sync to sync).'}
     save(out / 'manifest.json', manifest)
     setup_started = time.perf_counter()
@@ -358,8 +360,6 @@ def summarize(records, manifest, complete=False):
 def run_prefill(args):
     import torch
     dtype = 'fp32' if args.dtype == 'float32' else 'bf16'
-    if dtype != 'fp32':
-        raise SystemExit('--dtype bfloat16: the BF16 mode of the native library is not built yet')
     inp = Inputs(args, dtype)
     n_users = len(inp.users)
     outdir = args.output_root.resolve() / f'shared_prefill_{n_users}_users'

@@ -65,6 +65,19 @@ def test_folded_cli_writes_the_reference_layout(cuda, tmp_path, tiny):
     assert json.loads((out / 'policy-restoration.json').read_text())['restored']
 
 
+def test_folded_cli_bf16_precision(cuda, tmp_path, tiny):
+    from rapidtinyrec_b200 import run
+    out = tmp_path / 'bf16'
+    run.main(['folded', '--synthetic', 'tiny', '--users', '4', '--output-root', str(out), '--repeats', '1',
+              '--precision', 'bf16-experimental'])
+    manifest = json.loads((out / 'manifest.json').read_text())
+    assert manifest['precision'] == 'bf16-experimental' and manifest['experimental'] and manifest['dtype'] == 'bfloat16'
+    summary = json.loads((out / 'summary.json').read_text())
+    assert summary['complete'] and summary['experimental']
+    for r in json.loads((out / 'requests.json').read_text()):
+        check_invariants(r['run'], tiny['cfg'], set(tiny['items']))
+
+
 def test_prefill_cli_pairs_eager_and_graph_and_resumes(cuda, tmp_path):
     from rapidtinyrec_b200 import run
     run.main(['prefill', '--synthetic', 'tiny', '--users', '3', '--output-root', str(tmp_path)])
