@@ -20,6 +20,10 @@ path - a barrier and max-reduction of the timings bracket the timed region.
   reference's timing span ``benchmark_inference.py:230-232``).
 * ``roofline``: the decode projection GEMMs (dominant kernel), algorithmic
   weight bytes per pass / device time, against the measured HBM copy peak.
+* ``concurrent`` (``--sessions S``, default 2): the same users served by S
+  independent sessions per GPU on separate streams (each request still batch
+  1), so one user's GEMMs fill another's small kernels and launch gaps;
+  ``value`` stays the sequential figure the reference's protocol measures.
 * ``--impl reference``: the reference algorithm on the host cores (the CPU
   oracle port of HF generate + the reference's processor), rank 0 only.
 """
@@ -161,7 +165,7 @@ def run_reference(args):
     wl, _, cons, users = build_workload(args.workload, args.warmup + args.steps)
     cfg = wl.model
     weights = wk.synth_weights(cfg, seed=wl.weight_seed, device='cpu')
-    warm = cpu_oracle_time(cfg, weights, cons, users[:min(args.warmup, 1)], 0, threads)
+    warm = cpu_oracle_time(cfg, weights, cons, users[:min(args.warmup, 3)], 0, threads)
     # bound the run: every step is one full request; cap the count to ~150 s of CPU work
     per = warm[0] if warm else 1.0
     k = max(1, min(args.steps, int(150.0 / max(per, 1e-3))))
@@ -202,6 +206,9 @@ def run_ours(args):
     weights = wk.synth_weights(cfg, seed=wl.weight_seed, device=f'cuda:{local}')
     tables = GpuSidConstraintTables(cons, cfg.root, cfg.newline, cfg.eos)
     engine = BeamEngine(cfg, weights, tables, max_prefix=max_prefix, device=local)
+    # extra independent sessions for the concurrent-serving measurement
+    extra = [BeamEngine(cfg, weights, tables, max_prefix=max_prefix, device=local)
+             for _ in range(max(0, args.sessions - 1))]
     weights_cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         weights_cpu = {k: v.cpu() for k, v in weights.items()}
@@ -259,6 +266,47 @@ def run_ours(args):
     e2e_total = time.perf_counter() - t0
     barrier()
     rep = engine.report()
+
+    # ---- concurrent serving: S independent sessions on their own streams,
+    # batch-1 requests dealt round-robin (device-resident prompts)
+    concurrent = None
+    if extra:
+        sessions = [(engine, stream)] + [(e, torch.cuda.Stream(device=dev)) for e in extra]
+        for e, st in sessions[1:]:
+            e.set_stream(st)
+        for k, (e, _) in enumerate(sessions):  # warm-up (graph capture)
+            e.launch_device(ids_dev[k % len(ids_dev)], users[k % len(users)].prompt_tokens)
+        for e, _ in sessions:
+            e.wait()
+        torch.cuda.synchronize(dev)
+        start = torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _, st in sessions[1:]:
+            st.wait_event(start)
+        for j, i in enumerate(timed):
+            e, _ = sessions[j % len(sessions)]
+            if j >= len(sessions):
+                e.wait()  # the session's previous request leaves its slot
+            e.launch_device(ids_dev[i], users[i].prompt_tokens)
+        ends = []
+        for e, st in sessions:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(st)
+            ends.append(ev)
+        for e, _ in sessions:
+            e.wait()
+        torch.cuda.synchronize(dev)
+        conc_ms = max(start.elapsed_time(ev) for ev in ends)
+        if world > 1:
+            t = torch.tensor([conc_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            conc_ms = float(t[0])
+        concurrent = {'sessions': len(sessions), 'value': round(args.steps * world / (conc_ms / 1000.0), 3),
+                      'unit': 'users/s', 'ms_per_step': round(conc_ms / args.steps, 3),
+                      'note': 'independent sessions (one weight copy each) on separate streams, batch-1 requests '
+                              'dealt round-robin, prompts in HBM; CUDA events, max over ranks'}
+        for e in extra:
+            e.close()
 
     # ---- roofline of the dominant kernel: the decode projection GEMMs (M = beams)
     gemm_ms = engine.profile_gemms(engine.beams, reps=5)
@@ -321,6 +369,7 @@ def run_ours(args):
                          'traffic': None, 'bytes_per_pass': gemm_bytes, 'ms_per_pass': round(gemm_ms, 4),
                          'gemm_tflops': round(gemm_flops / (gemm_ms / 1000.0) / 1e12, 2)},
             'gpu_launches': int(launches),
+            'concurrent': concurrent,
             'launches_per_user': rep['launches_per_request'],
             'clocks': ck,
         }
@@ -380,6 +429,8 @@ def main():
     ap.add_argument('--workload', default='qwen1.5b-fp32')
     ap.add_argument('--cpu-budget', type=float, default=20.0, help='seconds of CPU-baseline work (rank 0, N=1)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--sessions', type=int, default=2,
+                    help='also measure S concurrent sessions per GPU (1: sequential only)')
     args = ap.parse_args()
     if args.mode != 'bench':
         run_profile(args)
