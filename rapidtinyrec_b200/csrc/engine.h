@@ -48,6 +48,12 @@ cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap
                     float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                     size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
                     bool pdl, const RopeArgs* rope = nullptr);
+// The same GEMM with 128 activation rows per CTA (gemm_tc_wide.cu): for M > 64.
+cudaError_t gemm_tc_wide_init();
+cudaError_t gemm_tc_wide(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
+                         float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
+                         size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms,
+                         cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr);
 
 // ---- bf16 tensor-core GEMM (gemm_bf16.cu): the bf16 mode ----
 // X: bf16 activations [rows][K]; weights packed once into bf16 tile blocks.

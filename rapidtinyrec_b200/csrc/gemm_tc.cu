@@ -34,6 +34,7 @@
 #include "common.cuh"
 #include "engine.h"
 #include "tcgen05.cuh"
+#include "tc_epilogue.cuh"
 
 namespace rtr {
 
@@ -52,127 +53,6 @@ constexpr int TC_A_COLS = 2 * TC_KC;           // W_b and W_s of one chunk
 constexpr int TC_TMEM_COLS = 512;              // 2 accumulators + 4 A stages
 constexpr int TC_NBARS = 2 * TC_WSTAGES + 2 * TC_XSTAGES + 2 * TC_ASTAGES + 4;
 constexpr int TC_SMEM_BYTES = TC_WSTAGES * TC_W_BYTES + TC_XSTAGES * TC_X_BYTES + 1024 + 8 * TC_NBARS + 16;
-
-struct TcParams {
-  float* C;
-  float* C_big;     // SWIGLU: also write the split halves of the activation
-  float* C_small;
-  const float* bias;
-  int M, N, K, ldc, epi, splits;
-  float* ws;
-  int* tickets;
-  uint32_t* status;
-  RopeArgs rope;    // EPI_ROPE only
-};
-
-
-// Split-K finish, part 1, run by every thread of the last CTA to arrive on a
-// tile: sum the partial tiles in split order into a [64][128] shared tile
-// (float4 slots, four splits of loads in flight per slot).
-RTR_DEVICE void splitk_sum(const TcParams& p, float4* red4, int rows, int cols4, int tile, long tstride) {
-  constexpr int SLOTS = (TC_NTOK * TC_WROWS / 4 + TC_THREADS - 1) / TC_THREADS;
-  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (TC_NTOK * TC_WROWS));
-  const long zs = tstride >> 2;
-  const int nslots = rows * (TC_WROWS / 4);
-  float4 s[SLOTS];
-#pragma unroll
-  for (int u = 0; u < SLOTS; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int z = 0; z < p.splits; z += 4) {
-    float4 v[4][SLOTS];
-#pragma unroll
-    for (int dz = 0; dz < 4; ++dz)
-#pragma unroll
-      for (int u = 0; u < SLOTS; ++u) {
-        const int q = threadIdx.x + u * TC_THREADS;
-        const bool ok = z + dz < p.splits && q < nslots && (q & 31) < cols4;
-        v[dz][u] = ok ? __ldcg(base + (z + dz) * zs + q) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-    for (int dz = 0; dz < 4; ++dz)
-#pragma unroll
-      for (int u = 0; u < SLOTS; ++u) s[u] = f4add(s[u], v[dz][u]);  // split order (zero adds are exact)
-  }
-#pragma unroll
-  for (int u = 0; u < SLOTS; ++u) {
-    const int q = threadIdx.x + u * TC_THREADS;
-    if (q < nslots) red4[q] = s[u];
-  }
-  __syncthreads();
-}
-
-
-// Epilogue from a [rows][ld4 float4] shared tile of finished sums, run by
-// every thread of the CTA with float4 loads and stores (N, ldc and the head
-// dimension are multiples of 4; checked by the host).
-RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, int tok0, int n0, int rows, int cols4) {
-  if (p.epi == EPI_SWIGLU) {
-    // packed rows: 32 q + [0,16) gate, 32 q + [16,32) up of intermediate 16 q + [0,16)
-    for (int q = threadIdx.x; q < rows * 16; q += TC_THREADS) {
-      const int j = q >> 4, blk = (q >> 2) & 3, g4 = q & 3;
-      const int c4 = blk * 8 + g4;
-      if (c4 + 4 >= cols4) continue;  // the up half lies past N
-      const float4 g = red4[j * ld4 + c4], u = red4[j * ld4 + c4 + 4];
-      float a[4] = {silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w};
-      float b[4], sm[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) { b[e] = tf32_round(a[e]); sm[e] = a[e] - b[e]; }
-      const long o = (long)(tok0 + j) * p.ldc + ((n0 + blk * 32) >> 5) * 16 + g4 * 4;
-      *reinterpret_cast<float4*>(p.C + o) = make_float4(a[0], a[1], a[2], a[3]);
-      *reinterpret_cast<float4*>(p.C_big + o) = make_float4(b[0], b[1], b[2], b[3]);
-      *reinterpret_cast<float4*>(p.C_small + o) = make_float4(sm[0], sm[1], sm[2], sm[3]);
-    }
-    return;
-  }
-  if (p.epi == EPI_ROPE) {
-    // q/k/v projection + bias, then apply_rotary_pos_emb (modeling_qwen2.py:116-146)
-    // on q and k with separately rounded products, as rope_kv() does.  A
-    // 128-column tile holds whole heads, so each rotary partner is in the tile.
-    const RopeArgs& r = p.rope;
-    const int D = r.head_dim, half = D >> 1;
-    const int base_pos = r.slot < 0 ? 0 : *r.L_dev + r.slot;
-    for (int q = threadIdx.x; q < rows * 32; q += TC_THREADS) {
-      const int j = q >> 5, c4 = q & 31;
-      if (c4 >= cols4) continue;
-      const int col = n0 + c4 * 4, m = tok0 + j;
-      const int h = col / D, d = col % D;
-      float4 v = f4add(red4[j * ld4 + c4], *reinterpret_cast<const float4*>(p.bias + col));
-      if (h < r.heads + r.kv_heads) {
-        const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
-        const float4 pv = f4add(red4[j * ld4 + pc4], *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4));
-        int pos = r.slot < 0 ? m : base_pos;
-        if (pos < 0 || pos >= r.positions) {
-          atomicOr(p.status, RTR_DEV_BAD_LENGTH);
-          pos = 0;
-        }
-        const float4 cs = *reinterpret_cast<const float4*>(r.cos_t + (long)pos * half + (d % half));
-        const float4 sn = *reinterpret_cast<const float4*>(r.sin_t + (long)pos * half + (d % half));
-        v = d < half ? f4add_rn(f4mul(v, cs), f4mul(f4neg(pv), sn))   // x1 cos - x2 sin
-                     : f4add_rn(f4mul(v, cs), f4mul(pv, sn));          // x2 cos + x1 sin
-      }
-      float* dst;
-      if (h < r.heads) {
-        dst = r.q_out + ((long)m * r.heads + h) * D + d;
-      } else {
-        const bool is_k = h < r.heads + r.kv_heads;
-        const int g = is_k ? h - r.heads : h - r.heads - r.kv_heads;
-        float* cache = is_k ? r.k_dst : r.v_dst;
-        dst = r.slot < 0 ? cache + ((long)g * r.prefix_cap + m) * D + d : cache + ((long)m * r.kv_heads + g) * D + d;
-      }
-      *reinterpret_cast<float4*>(dst) = v;
-    }
-    return;
-  }
-  for (int q = threadIdx.x; q < rows * 32; q += TC_THREADS) {
-    const int j = q >> 5, c4 = q & 31;
-    if (c4 >= cols4) continue;
-    float4 v = red4[j * ld4 + c4];
-    const int col = n0 + c4 * 4;
-    float4* c = reinterpret_cast<float4*>(p.C + (long)(tok0 + j) * p.ldc + col);
-    if (p.epi == EPI_BIAS) v = f4add(v, *reinterpret_cast<const float4*>(p.bias + col));
-    else if (p.epi == EPI_RESID) v = f4add(*c, v);
-    *c = v;
-  }
-}
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
@@ -399,8 +279,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     if (!last_cta) return;
     __threadfence();
-    splitk_sum(p, red4, rows, cols4, tile, tstride);
-    tile_epilogue(p, red4, TC_WROWS / 4, tok0, n0, rows, cols4);
+    splitk_sum<TC_THREADS, TC_NTOK>(p, red4, rows, cols4, tile, tstride);
+    tile_epilogue<TC_THREADS>(p, red4, TC_WROWS / 4, tok0, n0, rows, cols4);
     return;
   }
   // Stage the finished tile in shared memory ([64][TC_WROWS + 4], padded so
@@ -414,7 +294,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (j < rows) red[j * RLD] = acc[j];
   }
   __syncthreads();
-  tile_epilogue(p, red4, RLD / 4, tok0, n0, rows, cols4);
+  tile_epilogue<TC_THREADS>(p, red4, RLD / 4, tok0, n0, rows, cols4);
 }
 
 // ---------------------------------------------------------------- host side
@@ -468,14 +348,6 @@ cudaError_t gemm_tc_init() {
   return cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES);
 }
 
-static int tc_splits(int tiles, int nchunks, int sms) {
-  if (tiles >= sms) return 1;
-  int s = sms / tiles;
-  if (s > nchunks / 2) s = nchunks / 2;  // keep at least two chunks per split
-  if (s > 16) s = 16;
-  return s < 1 ? 1 : s;
-}
-
 cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
                     float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                     size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
@@ -491,7 +363,7 @@ cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap
   if (epi != EPI_ROPE && (N % 4 || ldc % 4 || (reinterpret_cast<uintptr_t>(C) & 15))) return cudaErrorInvalidValue;
   const int tt = (M + TC_NTOK - 1) / TC_NTOK, wt = (N + TC_WROWS - 1) / TC_WROWS;
   const int nchunks = (K + TC_KC - 1) / TC_KC;
-  int splits = tc_splits(tt * wt, nchunks, sms);
+  int splits = tc_split_count(tt * wt, nchunks, sms);
   while (splits > 1 && ((size_t)splits * tt * wt * TC_NTOK * TC_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
   TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
   if (rope) p.rope = *rope;

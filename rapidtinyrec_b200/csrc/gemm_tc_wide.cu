@@ -1,0 +1,321 @@
+// 3xTF32 projection GEMM for 128 activation rows per CTA (the prefill, and any
+// GEMM with more than 64 rows).
+//
+// Same method as gemm_tc.cu (W split into W_b + W_s in registers and stored to
+// tensor memory, X pre-split by its producer, tensor-core accumulation promoted
+// into IEEE fp32 registers), but each MMA covers 128 activation rows:
+//
+//   D[:, 0:256] += W_b . [X_b ; X_s]      (N = 256: 128 rows of X_b, then of X_s)
+//   D[:, 0:128] += W_s . X_b              (N = 128)
+//
+// The cost of a tcgen05.mma barely depends on N, so twice the rows take the
+// same 8 instructions per 32-wide K chunk.  The 256-column accumulator leaves
+// room for 4 A stages but not for a second accumulator, so the MMA issuer
+// waits while the promoters drain it (every 8 chunks).
+//   warp 0       TMA of the W tile [128 x 32] into a 6-deep ring
+//   warp 1       MMA issuer
+//   warps 2..5   split W rows into the TMEM A stages (one lane quarter each)
+//   warps 6..13  promote: two warps per lane quarter, 64 activation rows each
+//   warp 14      TMA of [X_b ; X_s] (4 boxes of 64 rows) into a 3-deep ring
+// Epilogue: shared-memory tile, every thread stores float4s (tc_epilogue.cuh).
+// Every mbarrier wait is bounded.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "engine.h"
+#include "tc_epilogue.cuh"
+#include "tcgen05.cuh"
+
+namespace rtr {
+
+constexpr int TW_THREADS = 480;          // 15 warps
+constexpr int TW_KC = 32;
+constexpr int TW_WROWS = 128;
+constexpr int TW_NTOK = 128;
+constexpr int TW_WSTAGES = 6;
+constexpr int TW_XSTAGES = 3;
+constexpr int TW_ASTAGES = 4;
+constexpr int TW_PROMOTE = 8;
+constexpr int TW_W_BYTES = TW_WROWS * 128;        // 16 KB
+constexpr int TW_X_BYTES = 2 * TW_NTOK * 128;     // 32 KB: [X_b ; X_s]
+constexpr int TW_D_COLS = 2 * TW_NTOK;            // 256
+constexpr int TW_A_COLS = 2 * TW_KC;              // 64: W_b and W_s of one chunk
+constexpr int TW_TMEM_COLS = 512;                 // accumulator + 4 A stages
+constexpr int TW_NBARS = 2 * TW_WSTAGES + 2 * TW_XSTAGES + 2 * TW_ASTAGES + 2;
+constexpr int TW_RING_BYTES = TW_WSTAGES * TW_W_BYTES + TW_XSTAGES * TW_X_BYTES;
+constexpr int TW_SMEM_BYTES = TW_RING_BYTES + 1024 + 8 * TW_NBARS + 16;
+constexpr int TW_RLD = TW_WROWS + 4;
+static_assert(TW_NTOK * TW_RLD * 4 <= TW_RING_BYTES, "epilogue tile fits in the rings");
+static_assert(TW_D_COLS + TW_ASTAGES * TW_A_COLS <= TW_TMEM_COLS, "tensor memory budget");
+
+__global__ void __launch_bounds__(TW_THREADS, 1)
+    gemm_tc_wide_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
+                        const __grid_constant__ CUtensorMap tmXs, TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* wring = smem;
+  uint8_t* xring = smem + TW_WSTAGES * TW_W_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + TW_XSTAGES * TW_X_BYTES);
+  uint64_t* w_full = bars;
+  uint64_t* w_empty = w_full + TW_WSTAGES;
+  uint64_t* x_full = w_empty + TW_WSTAGES;
+  uint64_t* x_empty = x_full + TW_XSTAGES;
+  uint64_t* a_full = x_empty + TW_XSTAGES;
+  uint64_t* a_empty = a_full + TW_ASTAGES;
+  uint64_t* d_full = a_empty + TW_ASTAGES;
+  uint64_t* d_empty = d_full + 1;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 1) + 1;
+  __shared__ int last_cta;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok0 = blockIdx.x * TW_NTOK;
+  const int n0 = blockIdx.y * TW_WROWS;
+  const int nchunks = (p.K + TW_KC - 1) / TW_KC;
+  const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
+  const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
+  const int nloc = c1 - c0;
+  const int ngroups = (nloc + TW_PROMOTE - 1) / TW_PROMOTE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TW_WSTAGES; ++s) { mbar_init(smem_addr(&w_full[s]), 1); mbar_init(smem_addr(&w_empty[s]), 4); }
+    for (int s = 0; s < TW_XSTAGES; ++s) { mbar_init(smem_addr(&x_full[s]), 1); mbar_init(smem_addr(&x_empty[s]), 1); }
+    for (int s = 0; s < TW_ASTAGES; ++s) { mbar_init(smem_addr(&a_full[s]), 4); mbar_init(smem_addr(&a_empty[s]), 1); }
+    mbar_init(smem_addr(d_full), 1);
+    mbar_init(smem_addr(d_empty), 8);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmXb);
+    tma_prefetch_desc(&tmXs);
+  }
+  if (warp == 1) tmem_alloc(smem_addr(tmem_slot), TW_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem_a = tmem + TW_D_COLS;
+
+  int w_issued = 0, x_issued = 0, mma_groups = 0;
+  float acc[64];  // live only in the promoter warps
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // weights do not depend on the previous kernel: no griddepcontrol.wait
+      for (int i = 0; i < nloc; ++i) {
+        const int s = i % TW_WSTAGES;
+        if (!mbar_wait(smem_addr(&w_empty[s]), ((i / TW_WSTAGES) & 1) ^ 1, abort_flag)) break;
+        const uint32_t fb = smem_addr(&w_full[s]);
+        mbar_expect_tx(fb, TW_W_BYTES);
+        tma_load_2d(smem_addr(wring + s * TW_W_BYTES), &tmW, 0, (blockIdx.y * nchunks + c0 + i) * TW_WROWS, fb);
+        w_issued = i + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_cat = idesc_tf32(TW_WROWS, 2 * TW_NTOK);
+      constexpr uint32_t id_x = idesc_tf32(TW_WROWS, TW_NTOK);
+      for (int i = 0; i < nloc; ++i) {
+        const int g = i / TW_PROMOTE;
+        // single accumulator: a new group starts once the promoters drained the last one
+        if (i % TW_PROMOTE == 0 && g >= 1 && !mbar_wait(smem_addr(d_empty), (g - 1) & 1, abort_flag)) break;
+        const int as = i % TW_ASTAGES, xs = i % TW_XSTAGES;
+        if (!mbar_wait(smem_addr(&a_full[as]), (i / TW_ASTAGES) & 1, abort_flag)) break;
+        if (!mbar_wait(smem_addr(&x_full[xs]), (i / TW_XSTAGES) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t ab = tmem_a + as * TW_A_COLS, asml = ab + TW_KC;
+        const uint64_t bx = sw128_desc(smem_addr(xring + xs * TW_X_BYTES));
+#pragma unroll
+        for (int kk = 0; kk < TW_KC / 8; ++kk) {
+          const uint64_t adv = (uint64_t)(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
+          mma_tf32_ts(tmem, ab + kk * 8, bx + adv, id_cat, (i % TW_PROMOTE != 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_ts(tmem, asml + kk * 8, bx + adv, id_x, 1u);
+        }
+        mma_commit(smem_addr(&a_empty[as]));
+        mma_commit(smem_addr(&x_empty[xs]));
+        if (i % TW_PROMOTE == TW_PROMOTE - 1 || i == nloc - 1) {
+          mma_commit(smem_addr(d_full));
+          mma_groups = g + 1;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 14) {
+    pdl_wait();
+    if (lane == 0) {
+      for (int i = 0; i < nloc; ++i) {
+        const int s = i % TW_XSTAGES;
+        if (!mbar_wait(smem_addr(&x_empty[s]), ((i / TW_XSTAGES) & 1) ^ 1, abort_flag)) break;
+        const uint32_t fb = smem_addr(&x_full[s]);
+        uint8_t* st = xring + s * TW_X_BYTES;
+        mbar_expect_tx(fb, TW_X_BYTES);
+        const int kx = (c0 + i) * TW_KC;
+        tma_load_2d(smem_addr(st), &tmXb, kx, tok0, fb);
+        tma_load_2d(smem_addr(st + 64 * 128), &tmXb, kx, tok0 + 64, fb);
+        tma_load_2d(smem_addr(st + 128 * 128), &tmXs, kx, tok0, fb);
+        tma_load_2d(smem_addr(st + 192 * 128), &tmXs, kx, tok0 + 64, fb);
+        x_issued = i + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp <= 5) {
+    // --------------------------- warps 2..5: split W rows into TMEM
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    for (int i = 0; i < nloc; ++i) {
+      const int ws = i % TW_WSTAGES, as = i % TW_ASTAGES;
+      if (!mbar_wait(smem_addr(&w_full[ws]), (i / TW_WSTAGES) & 1, abort_flag)) break;
+      const uint8_t* tile = wring + ws * TW_W_BYTES + row * 128;
+      uint32_t big[TW_KC], small[TW_KC];
+#pragma unroll
+      for (int c = 0; c < TW_KC / 4; ++c) {  // undo the 128B swizzle: chunk c lives at c ^ (row % 8)
+        const float4 v = *reinterpret_cast<const float4*>(tile + ((c ^ (row & 7)) << 4));
+        big[4 * c] = __float_as_uint(v.x); big[4 * c + 1] = __float_as_uint(v.y);
+        big[4 * c + 2] = __float_as_uint(v.z); big[4 * c + 3] = __float_as_uint(v.w);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&w_empty[ws]));
+#pragma unroll
+      for (int k = 0; k < TW_KC; ++k) {
+        const float w = __uint_as_float(big[k]);
+        const float bv = tf32_round(w);
+        big[k] = __float_as_uint(bv);
+        small[k] = __float_as_uint(w - bv);
+      }
+      if (!mbar_wait(smem_addr(&a_empty[as]), ((i / TW_ASTAGES) & 1) ^ 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t a = tmem_a + lane_base + as * TW_A_COLS;
+      tmem_st32(a, big);
+      tmem_st32(a + TW_KC, small);
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&a_full[as]));
+    }
+  } else {
+    // ------------ warps 6..13: promote (lane quarter warp & 3, rows half * 64 ..)
+    pdl_wait();
+    const int quarter = warp & 3, half = (warp - 6) >> 2;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+    for (int g = 0; g < ngroups; ++g) {
+      if (!mbar_wait(smem_addr(d_full), g & 1, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + lane_base + half * 64;
+#pragma unroll
+      for (int cb = 0; cb < 64; cb += 16) {
+        uint32_t r[16], s[16];
+        tmem_ld16(d + cb, r);             // W_b.X_b + W_s.X_b
+        tmem_ld16(d + TW_NTOK + cb, s);   // W_b.X_s
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[cb + j] += __uint_as_float(r[j]) + __uint_as_float(s[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(d_empty));
+    }
+  }
+  pdl_launch_dependents();
+
+  // drain on abort: issued copies and MMAs must land before smem/TMEM go away
+  if (*abort_flag) {
+    if (threadIdx.x == 0) atomicOr(p.status, RTR_DEV_TIMEOUT);
+    if (warp == 0 && lane == 0)
+      for (int i = 0; i < w_issued; ++i) mbar_drain(smem_addr(&w_full[i % TW_WSTAGES]), (i / TW_WSTAGES) & 1);
+    if (warp == 14 && lane == 0)
+      for (int i = 0; i < x_issued; ++i) mbar_drain(smem_addr(&x_full[i % TW_XSTAGES]), (i / TW_XSTAGES) & 1);
+    if (warp == 1 && lane == 0 && mma_groups > 0) mbar_drain(smem_addr(d_full), (mma_groups - 1) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TW_TMEM_COLS);
+  }
+  if (*abort_flag) return;
+
+  const bool have = warp >= 6 && warp <= 13;
+  const int quarter = warp & 3, half = (warp - 6) >> 2;
+  const int col = quarter * 32 + lane;     // weight row of this thread within the tile
+  const int n = n0 + col;
+  const int rows = p.M - tok0 < TW_NTOK ? p.M - tok0 : TW_NTOK;
+  const int cols4 = (p.N - n0 < TW_WROWS ? p.N - n0 : TW_WROWS) >> 2;
+  float4* red4 = reinterpret_cast<float4*>(smem);  // the rings are free now
+  if (p.splits > 1) {
+    // partial tiles are tile-contiguous: ws[(split * tiles + tile)][row][128]
+    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+    const long tstride = (long)gridDim.x * gridDim.y * (TW_NTOK * TW_WROWS);
+    if (have && n < p.N) {
+      float* w = p.ws + blockIdx.z * tstride + (long)tile * (TW_NTOK * TW_WROWS) + half * 64 * TW_WROWS + col;
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (half * 64 + j < rows) __stcg(w + j * TW_WROWS, acc[j]);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int* tk = p.tickets + tile;
+      last_cta = atomicAdd(tk, 1) == p.splits - 1;
+      if (last_cta) *tk = 0;  // re-arm for the next launch / graph replay
+    }
+    __syncthreads();
+    if (!last_cta) return;
+    __threadfence();
+    splitk_sum<TW_THREADS, TW_NTOK>(p, red4, rows, cols4, tile, tstride);
+    tile_epilogue<TW_THREADS>(p, red4, TW_WROWS / 4, tok0, n0, rows, cols4);
+    return;
+  }
+  if (have && n < p.N) {
+    float* red = reinterpret_cast<float*>(smem) + half * 64 * TW_RLD + col;
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+      if (half * 64 + j < rows) red[j * TW_RLD] = acc[j];
+  }
+  __syncthreads();
+  tile_epilogue<TW_THREADS>(p, red4, TW_RLD / 4, tok0, n0, rows, cols4);
+}
+
+cudaError_t gemm_tc_wide_init() {
+  return cudaFuncSetAttribute(gemm_tc_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TW_SMEM_BYTES);
+}
+
+// Same arguments and checks as gemm_tc(); the activation tensor maps keep
+// their 64-row boxes (four loads fill one 128-row stage).
+cudaError_t gemm_tc_wide(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
+                         float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
+                         size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms,
+                         cudaStream_t stream, bool pdl, const RopeArgs* rope) {
+  if (epi == EPI_SWIGLU && (!C_big || !C_small)) return cudaErrorInvalidValue;
+  if (epi == EPI_ROPE) {
+    if (!rope || !bias || (rope->head_dim != 64 && rope->head_dim != 128) ||
+        N != (rope->heads + 2 * rope->kv_heads) * rope->head_dim || (reinterpret_cast<uintptr_t>(bias) & 15))
+      return cudaErrorInvalidValue;
+  }
+  if (epi != EPI_ROPE && (N % 4 || ldc % 4 || (reinterpret_cast<uintptr_t>(C) & 15))) return cudaErrorInvalidValue;
+  const int tt = (M + TW_NTOK - 1) / TW_NTOK, wt = (N + TW_WROWS - 1) / TW_WROWS;
+  const int nchunks = (K + TW_KC - 1) / TW_KC;
+  int splits = tc_split_count(tt * wt, nchunks, sms);
+  while (splits > 1 && ((size_t)splits * tt * wt * TW_NTOK * TW_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
+  TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
+  if (rope) p.rope = *rope;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tt, wt, splits);
+  cfg.blockDim = dim3(TW_THREADS);
+  cfg.dynamicSmemBytes = TW_SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_wide_kernel, *reinterpret_cast<const CUtensorMap*>(&tmW),
+                            *reinterpret_cast<const CUtensorMap*>(&tmXb),
+                            *reinterpret_cast<const CUtensorMap*>(&tmXs), p);
+}
+
+}  // namespace rtr

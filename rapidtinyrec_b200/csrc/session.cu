@@ -43,6 +43,7 @@ struct rtr_session {
   bool own_stream = false;
   bool pdl = true;
   bool use_tc = true;  // tcgen05 GEMMs (RTR_GEMM=ffma selects the FFMA kernel)
+  bool tc_wide = true;  // 128-row tcgen05 GEMM for M > 64 (RTR_TC_WIDE=0: the 64-row kernel only)
   // bf16 mode (RTR_DTYPE_BF16): bf16 weights, activations and KV; biases and
   // norm weights as bf16 values in fp32; logits in fp32.  The activation and
   // KV buffers below keep their float pointers and hold bf16 elements.
@@ -181,9 +182,11 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(gemm_init());
   CREATE_TRY(beam_init());
   CREATE_TRY(gemm_tc_init());
+  CREATE_TRY(gemm_tc_wide_init());
   CREATE_TRY(attention_init());
   CREATE_TRY(gemm_bf16_init());
   if (const char* g = std::getenv("RTR_GEMM")) s->use_tc = std::strcmp(g, "ffma") != 0;
+  if (const char* g = std::getenv("RTR_TC_WIDE")) s->tc_wide = std::strcmp(g, "0") != 0;
   s->pdl = pdl_on(PDL_GEMM);
   s->bf16 = c.dtype == RTR_DTYPE_BF16;
   if (s->bf16 && !s->use_tc) {
@@ -568,6 +571,10 @@ static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W,
       cb = out->second.first;
       cs = out->second.second;
     }
+    // more than 64 rows (the prefill): one 128-row MMA per instruction instead of two 64-row ones
+    if (M > 64 && s->tc_wide)
+      return gemm_tc_wide(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws,
+                          s->ws_floats, s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope);
     return gemm_tc(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws, s->ws_floats,
                    s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope);
   }
