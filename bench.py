@@ -389,13 +389,17 @@ def run_profile(args):
       cudaProfilerStart/Stop (use ncu --profile-from-start off).
     profile-gemms: a model cut to --layers layers; every projection GEMM of one
       forward over --rows rows runs twice (warm-up pass + one timed pass).
+    profile-phases: device time of each phase of a request (CUDA events on the
+      session's stream): prefill + step 0 and each decode step through the
+      per-step entry points, the whole request through the captured graph, and
+      the GEMM passes at the decode and prefill row counts.
     """
     import dataclasses
     import torch
     from rapidtinyrec_b200 import workload as wk
     from rapidtinyrec_b200.constraints import GpuSidConstraintTables
     from rapidtinyrec_b200.engine import BeamEngine
-    wl, _, cons, users = build_workload(args.workload, 2)
+    wl, _, cons, users = build_workload(args.workload, max(2, args.users))
     cfg = wl.model if args.layers is None else dataclasses.replace(wl.model, layers=args.layers)
     weights = wk.synth_weights(cfg, seed=wl.weight_seed, device='cuda')
     engine = BeamEngine(cfg, weights, GpuSidConstraintTables(cons, cfg.root, cfg.newline, cfg.eos),
@@ -411,6 +415,39 @@ def run_profile(args):
         torch.cuda.profiler.stop()
         print(json.dumps({'mode': args.mode, 'prompt_tokens': users[1].prompt_tokens,
                           'wall_ms': 1000 * (time.perf_counter() - t0), 'report': engine.report()}))
+    elif args.mode == 'profile-phases':
+        st = torch.cuda.Stream()
+        engine.set_stream(st)
+        dev_ids = [torch.tensor(u.prompt_token_ids, dtype=torch.int32, device='cuda') for u in users]
+        for u in users[:3]:  # warm-up: graph capture and first launches
+            engine.generate(u.prompt_token_ids)
+        phases = {'prefill_and_step0': [], 'step1': [], 'step2': [], 'step3': [], 'step4': [], 'request_graph': []}
+        for i, u in enumerate(users):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(8)]
+            torch.cuda.synchronize()
+            ev[0].record(st)
+            engine._check(engine.lib.rtr_prefill(engine.handle, dev_ids[i].data_ptr(), u.prompt_tokens, 1))
+            ev[1].record(st)
+            for t in range(1, 5):
+                engine.decode_step(t)
+                ev[t + 1].record(st)
+            engine.read_results()
+            ev[6].record(st)
+            engine.launch_device(dev_ids[i], u.prompt_tokens)
+            ev[7].record(st)
+            engine.wait()
+            torch.cuda.synchronize()
+            phases['prefill_and_step0'].append(ev[0].elapsed_time(ev[1]))
+            for t in range(1, 5):
+                phases[f'step{t}'].append(ev[t].elapsed_time(ev[t + 1]))
+            phases['request_graph'].append(ev[6].elapsed_time(ev[7]))
+        lengths = [u.prompt_tokens for u in users]
+        med_len = int(statistics.median(lengths))
+        print(json.dumps({'mode': args.mode, 'workload': args.workload, 'users': len(users),
+                          'prompt_tokens_median': med_len,
+                          'median_ms': {k: round(statistics.median(v), 4) for k, v in phases.items()},
+                          'gemm_pass_ms': {'decode_rows50': round(engine.profile_gemms(engine.beams, reps=5), 4),
+                                           f'prefill_rows{med_len}': round(engine.profile_gemms(med_len, reps=5), 4)}}))
     else:
         print(json.dumps({'mode': args.mode, 'rows': args.rows, 'layers': cfg.layers,
                           'ms_per_pass': engine.profile_gemms(args.rows, reps=1)}))
@@ -419,7 +456,9 @@ def run_profile(args):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument('--mode', choices=('bench', 'profile-request', 'profile-gemms'), default='bench')
+    ap.add_argument('--mode', choices=('bench', 'profile-request', 'profile-gemms', 'profile-phases'),
+                    default='bench')
+    ap.add_argument('--users', type=int, default=12, help='profile-phases: requests timed')
     ap.add_argument('--rows', type=int, default=50, help='profile-gemms: activation rows')
     ap.add_argument('--layers', type=int, default=None, help='profile modes: cut the model to this many layers')
     ap.add_argument('--gpus', type=int, default=1)

@@ -7,11 +7,11 @@
 // A CTA owns 128 weight rows (the MMA M side) x 64 activation rows (the MMA
 // N side) for a range of K, walked in 32-wide chunks (one 128-byte row):
 //   warp 0     TMA of the W tile [128 x 32] into a 6-deep shared ring (128B swizzle)
-//   warp 10    TMA of the activation tile (its own warp, so a wait on the
+//   warp 10    TMA of the activation tiles (its own warp, so a wait on the
 //              MMA-paced activation ring never stalls the weight stream): the
-//              big and small halves of X, which the
-//              producing kernels already split (X_b = tf32(X), X_s = X - X_b), are
-//              stacked into one [128 x 32] operand [X_b ; X_s]
+//              big and small halves of X, which the producing kernels already
+//              split (X_b = tf32(X), X_s = X - X_b), stacked per chunk into one
+//              [128 x 32] operand [X_b ; X_s]
 //   warps 2..5 (one TMEM lane quarter each, thread = weight row) read their row
 //              of W, split it in registers (W_b = tf32(W), W_s = W - W_b), store
 //              both into tensor memory and free the W stage at once
@@ -21,6 +21,10 @@
 //   warps 6..9 promote: the tensor core's fp32 accumulation drifts over long K,
 //              so every 4 chunks the accumulator (double-buffered in TMEM) is
 //              added into IEEE fp32 registers; they also run the epilogue.
+// The A operand and the activation tiles move in stages of two chunks: one
+// MMA thread issues ~60 cycles of tensor work per instruction, and its own
+// waits and commits cost as much again unless they are amortised over a
+// stage (16 MMAs per wait pair and commit).
 // Every role has its own ring, so loading, splitting, MMA and promotion of
 // different chunks overlap.  Small GEMMs split K over CTAs; the
 // last CTA to arrive sums the partial tiles in split order (deterministic).
@@ -39,20 +43,24 @@
 namespace rtr {
 
 constexpr int TC_THREADS = 352;          // 11 warps
-constexpr int TC_KC = 32;                // fp32 per 128-byte row
+constexpr int TC_KC = 32;                // fp32 per 128-byte row: one K chunk
 constexpr int TC_WROWS = 128;            // MMA M
 constexpr int TC_NTOK = 64;              // activation rows per CTA
-constexpr int TC_WSTAGES = 6;            // W ring depth
-constexpr int TC_XSTAGES = 4;            // activation ring depth
-constexpr int TC_ASTAGES = 4;            // TMEM A-operand stages
-constexpr int TC_PROMOTE = 4;            // chunks accumulated in TMEM per promotion
+constexpr int TC_WSTAGES = 6;            // W ring depth (chunks)
+constexpr int TC_CPS = 2;                // chunks per A/X stage
+constexpr int TC_STAGES = 2;             // A/X stages (each TC_CPS chunks)
+constexpr int TC_PROMOTE = 4;            // chunks accumulated in TMEM per promotion (2 stages)
 constexpr int TC_W_BYTES = TC_WROWS * 128;
-constexpr int TC_X_BYTES = 2 * TC_NTOK * 128;  // [X_b ; X_s]
-constexpr int TC_D_COLS = 2 * TC_NTOK;         // one accumulator buffer
-constexpr int TC_A_COLS = 2 * TC_KC;           // W_b and W_s of one chunk
-constexpr int TC_TMEM_COLS = 512;              // 2 accumulators + 4 A stages
-constexpr int TC_NBARS = 2 * TC_WSTAGES + 2 * TC_XSTAGES + 2 * TC_ASTAGES + 4;
-constexpr int TC_SMEM_BYTES = TC_WSTAGES * TC_W_BYTES + TC_XSTAGES * TC_X_BYTES + 1024 + 8 * TC_NBARS + 16;
+constexpr int TC_XC_BYTES = 2 * TC_NTOK * 128;        // [X_b ; X_s] of one chunk
+constexpr int TC_X_BYTES = TC_CPS * TC_XC_BYTES;      // one stage
+constexpr int TC_D_COLS = 2 * TC_NTOK;                // one accumulator buffer
+constexpr int TC_AC_COLS = 2 * TC_KC;                 // W_b and W_s of one chunk
+constexpr int TC_A_COLS = TC_CPS * TC_AC_COLS;        // one stage
+constexpr int TC_TMEM_COLS = 512;                     // 2 accumulators + 2 A stages
+constexpr int TC_NBARS = 2 * TC_WSTAGES + 3 * TC_STAGES + 4;
+constexpr int TC_SMEM_BYTES = TC_WSTAGES * TC_W_BYTES + TC_STAGES * TC_X_BYTES + 1024 + 8 * TC_NBARS + 16;
+static_assert(2 * TC_D_COLS + TC_STAGES * TC_A_COLS <= TC_TMEM_COLS, "tensor memory budget");
+static_assert(TC_PROMOTE == TC_STAGES * TC_CPS, "one promotion group = one pass over the stages");
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
@@ -61,14 +69,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* wring = smem;
   uint8_t* xring = smem + TC_WSTAGES * TC_W_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + TC_XSTAGES * TC_X_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + TC_STAGES * TC_X_BYTES);
   uint64_t* w_full = bars;
   uint64_t* w_empty = w_full + TC_WSTAGES;
-  uint64_t* x_full = w_empty + TC_WSTAGES;
-  uint64_t* x_empty = x_full + TC_XSTAGES;
-  uint64_t* a_full = x_empty + TC_XSTAGES;
-  uint64_t* a_empty = a_full + TC_ASTAGES;
-  uint64_t* d_full = a_empty + TC_ASTAGES;  // [2]
+  uint64_t* x_full = w_empty + TC_WSTAGES;  // [TC_STAGES] activation stage landed (TMA)
+  uint64_t* a_full = x_full + TC_STAGES;    // [TC_STAGES] split weights stored in TMEM
+  uint64_t* s_empty = a_full + TC_STAGES;   // [TC_STAGES] MMAs of the stage done (frees A and X)
+  uint64_t* d_full = s_empty + TC_STAGES;   // [2]
   uint64_t* d_empty = d_full + 2;           // [2]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2) + 1;
@@ -81,12 +88,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
   const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
   const int nloc = c1 - c0;
+  const int nstages = (nloc + TC_CPS - 1) / TC_CPS;
   const int ngroups = (nloc + TC_PROMOTE - 1) / TC_PROMOTE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_WSTAGES; ++s) { mbar_init(smem_addr(&w_full[s]), 1); mbar_init(smem_addr(&w_empty[s]), 4); }
-    for (int s = 0; s < TC_XSTAGES; ++s) { mbar_init(smem_addr(&x_full[s]), 1); mbar_init(smem_addr(&x_empty[s]), 1); }
-    for (int s = 0; s < TC_ASTAGES; ++s) { mbar_init(smem_addr(&a_full[s]), 4); mbar_init(smem_addr(&a_empty[s]), 1); }
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(smem_addr(&x_full[s]), 1);
+      mbar_init(smem_addr(&a_full[s]), 4);
+      mbar_init(smem_addr(&s_empty[s]), 1);
+    }
     for (int b = 0; b < 2; ++b) { mbar_init(smem_addr(&d_full[b]), 1); mbar_init(smem_addr(&d_empty[b]), 4); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -121,33 +132,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
+    // The issuing thread's own instruction stream bounds the MMA rate, so the
+    // loop is unrolled over the stages (stage indices, descriptors and the
+    // accumulate flags are compile-time) and a stage of two chunks costs one
+    // wait pair and one commit.
     if (lane == 0) {
       constexpr uint32_t id_cat = idesc_tf32(TC_WROWS, 2 * TC_NTOK);
       constexpr uint32_t id_x = idesc_tf32(TC_WROWS, TC_NTOK);
-      for (int i = 0; i < nloc; ++i) {
-        const int g = i / TC_PROMOTE, b = g & 1;
-        if (i % TC_PROMOTE == 0 && g >= 2 &&
-            !mbar_wait(smem_addr(&d_empty[b]), ((g >> 1) - 1) & 1, abort_flag))
-          break;
-        const int as = i % TC_ASTAGES, xs = i % TC_XSTAGES;
-        if (!mbar_wait(smem_addr(&a_full[as]), (i / TC_ASTAGES) & 1, abort_flag)) break;
-        if (!mbar_wait(smem_addr(&x_full[xs]), (i / TC_XSTAGES) & 1, abort_flag)) break;
-        tc_fence_after();
+      const uint64_t bx0 = sw128_desc(smem_addr(xring));
+      bool ok = true;
+      for (int j = 0; ok && j * TC_STAGES < nstages; ++j) {  // one promotion group per pass
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(smem_addr(&d_empty[b]), ((j >> 1) - 1) & 1, abort_flag)) break;
         const uint32_t d = tmem + b * TC_D_COLS;
-        const uint32_t ab = tmem_a + as * TC_A_COLS, asml = ab + TC_KC;
-        const uint64_t bx = sw128_desc(smem_addr(xring + xs * TC_X_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < TC_KC / 8; ++kk) {
-          const uint64_t adv = (uint64_t)(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
-          mma_tf32_ts(d, ab + kk * 8, bx + adv, id_cat, (i % TC_PROMOTE != 0 || kk > 0) ? 1u : 0u);
-          mma_tf32_ts(d, asml + kk * 8, bx + adv, id_x, 1u);
+        for (int u = 0; u < TC_STAGES; ++u) {
+          const int q = j * TC_STAGES + u;
+          if (q >= nstages) break;
+          if (!mbar_wait(smem_addr(&a_full[u]), j & 1, abort_flag) ||
+              !mbar_wait(smem_addr(&x_full[u]), j & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < TC_CPS; ++c) {
+            if (c > 0 && q * TC_CPS + c >= nloc) break;
+            const uint32_t ab = tmem_a + u * TC_A_COLS + c * TC_AC_COLS;
+            const uint64_t bx = bx0 + (uint64_t)((u * TC_X_BYTES + c * TC_XC_BYTES) >> 4);
+#pragma unroll
+            for (int kk = 0; kk < TC_KC / 8; ++kk) {  // 8 tf32 = 32 bytes along K
+              mma_tf32_ts(d, ab + kk * 8, bx + 2 * kk, id_cat, (u | c | kk) ? 1u : 0u);
+              mma_tf32_ts(d, ab + TC_KC + kk * 8, bx + 2 * kk, id_x, 1u);
+            }
+          }
+          mma_commit(smem_addr(&s_empty[u]));
         }
-        mma_commit(smem_addr(&a_empty[as]));
-        mma_commit(smem_addr(&x_empty[xs]));
-        if (i % TC_PROMOTE == TC_PROMOTE - 1 || i == nloc - 1) {
-          mma_commit(smem_addr(&d_full[b]));
-          mma_groups = g + 1;
-        }
+        if (!ok) break;
+        mma_commit(smem_addr(&d_full[b]));
+        mma_groups = j + 1;
       }
     }
     __syncwarp();
@@ -155,15 +178,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // --------------------------------------- activation producer (TMA)
     pdl_wait();
     if (lane == 0) {
-      for (int i = 0; i < nloc; ++i) {
-        const int s = i % TC_XSTAGES;
-        if (!mbar_wait(smem_addr(&x_empty[s]), ((i / TC_XSTAGES) & 1) ^ 1, abort_flag)) break;
+      for (int q = 0; q < nstages; ++q) {
+        const int s = q % TC_STAGES;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / TC_STAGES) & 1) ^ 1, abort_flag)) break;
+        const int nc = nloc - q * TC_CPS < TC_CPS ? nloc - q * TC_CPS : TC_CPS;
         const uint32_t fb = smem_addr(&x_full[s]);
         uint8_t* st = xring + s * TC_X_BYTES;
-        mbar_expect_tx(fb, TC_X_BYTES);
-        tma_load_2d(smem_addr(st), &tmXb, (c0 + i) * TC_KC, tok0, fb);
-        tma_load_2d(smem_addr(st + TC_X_BYTES / 2), &tmXs, (c0 + i) * TC_KC, tok0, fb);
-        x_issued = i + 1;
+        mbar_expect_tx(fb, nc * TC_XC_BYTES);
+        for (int c = 0; c < nc; ++c) {
+          const int kx = (c0 + q * TC_CPS + c) * TC_KC;
+          tma_load_2d(smem_addr(st + c * TC_XC_BYTES), &tmXb, kx, tok0, fb);
+          tma_load_2d(smem_addr(st + c * TC_XC_BYTES + TC_XC_BYTES / 2), &tmXs, kx, tok0, fb);
+        }
+        x_issued = q + 1;
       }
     }
     __syncwarp();
@@ -173,15 +200,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int row = quarter * 32 + lane;  // TMEM lane = weight row of the tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     for (int i = 0; i < nloc; ++i) {
-      const int ws = i % TC_WSTAGES, as = i % TC_ASTAGES;
+      const int ws = i % TC_WSTAGES, q = i / TC_CPS, c = i % TC_CPS, s = q % TC_STAGES;
       if (!mbar_wait(smem_addr(&w_full[ws]), (i / TC_WSTAGES) & 1, abort_flag)) break;
       const uint8_t* tile = wring + ws * TC_W_BYTES + row * 128;
       uint32_t big[TC_KC], small[TC_KC];
 #pragma unroll
-      for (int c = 0; c < TC_KC / 4; ++c) {  // undo the 128B swizzle: chunk c lives at c ^ (row % 8)
-        const float4 v = *reinterpret_cast<const float4*>(tile + ((c ^ (row & 7)) << 4));
-        big[4 * c] = __float_as_uint(v.x); big[4 * c + 1] = __float_as_uint(v.y);
-        big[4 * c + 2] = __float_as_uint(v.z); big[4 * c + 3] = __float_as_uint(v.w);
+      for (int k4 = 0; k4 < TC_KC / 4; ++k4) {  // undo the 128B swizzle: chunk k4 lives at k4 ^ (row % 8)
+        const float4 v = *reinterpret_cast<const float4*>(tile + ((k4 ^ (row & 7)) << 4));
+        big[4 * k4] = __float_as_uint(v.x); big[4 * k4 + 1] = __float_as_uint(v.y);
+        big[4 * k4 + 2] = __float_as_uint(v.z); big[4 * k4 + 3] = __float_as_uint(v.w);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&w_empty[ws]));  // the row is in registers
@@ -192,15 +219,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         big[k] = __float_as_uint(bv);
         small[k] = __float_as_uint(w - bv);
       }
-      if (!mbar_wait(smem_addr(&a_empty[as]), ((i / TC_ASTAGES) & 1) ^ 1, abort_flag)) break;
+      // the first chunk of a stage waits until the MMAs of its last use are done
+      if (c == 0 && !mbar_wait(smem_addr(&s_empty[s]), ((q / TC_STAGES) & 1) ^ 1, abort_flag)) break;
       tc_fence_after();
-      const uint32_t a = tmem_a + lane_base + as * TC_A_COLS;
+      const uint32_t a = tmem_a + lane_base + s * TC_A_COLS + c * TC_AC_COLS;
       tmem_st32(a, big);
       tmem_st32(a + TC_KC, small);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&a_full[as]));
+      if (c == TC_CPS - 1 || i == nloc - 1) {  // the stage is complete
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&a_full[s]));
+      }
     }
   } else {
     // ------------------------- warps 6..9: promote accumulators, epilogue
@@ -239,7 +269,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0 && lane == 0)
       for (int i = 0; i < w_issued; ++i) mbar_drain(smem_addr(&w_full[i % TC_WSTAGES]), (i / TC_WSTAGES) & 1);
     if (warp == 10 && lane == 0)
-      for (int i = 0; i < x_issued; ++i) mbar_drain(smem_addr(&x_full[i % TC_XSTAGES]), (i / TC_XSTAGES) & 1);
+      for (int q = 0; q < x_issued; ++q) mbar_drain(smem_addr(&x_full[q % TC_STAGES]), (q / TC_STAGES) & 1);
     if (warp == 1 && lane == 0 && mma_groups > 0) {
       const int g = mma_groups - 1;
       mbar_drain(smem_addr(&d_full[g & 1]), (g >> 1) & 1);
