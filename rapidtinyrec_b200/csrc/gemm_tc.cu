@@ -46,10 +46,11 @@ constexpr int TC_THREADS = 352;          // 11 warps
 constexpr int TC_KC = 32;                // fp32 per 128-byte row: one K chunk
 constexpr int TC_WROWS = 128;            // MMA M
 constexpr int TC_NTOK = 64;              // activation rows per CTA
-constexpr int TC_WSTAGES = 6;            // W ring depth (chunks)
-constexpr int TC_CPS = 2;                // chunks per A/X stage
-constexpr int TC_STAGES = 2;             // A/X stages (each TC_CPS chunks)
-constexpr int TC_PROMOTE = 4;            // chunks accumulated in TMEM per promotion (2 stages)
+constexpr int TC_WSTAGES = 5;            // W ring depth (chunks)
+constexpr int TC_CPS = 2;                // chunks per stage
+constexpr int TC_STAGES = 2;             // TMEM A-operand stages
+constexpr int TC_XSTAGES = 4;            // activation stages: X lands ~1 us after it is asked for
+constexpr int TC_PROMOTE = 8;            // chunks accumulated in TMEM per promotion (4 stages)
 constexpr int TC_W_BYTES = TC_WROWS * 128;
 constexpr int TC_XC_BYTES = 2 * TC_NTOK * 128;        // [X_b ; X_s] of one chunk
 constexpr int TC_X_BYTES = TC_CPS * TC_XC_BYTES;      // one stage
@@ -57,10 +58,11 @@ constexpr int TC_D_COLS = 2 * TC_NTOK;                // one accumulator buffer
 constexpr int TC_AC_COLS = 2 * TC_KC;                 // W_b and W_s of one chunk
 constexpr int TC_A_COLS = TC_CPS * TC_AC_COLS;        // one stage
 constexpr int TC_TMEM_COLS = 512;                     // 2 accumulators + 2 A stages
-constexpr int TC_NBARS = 2 * TC_WSTAGES + 3 * TC_STAGES + 4;
-constexpr int TC_SMEM_BYTES = TC_WSTAGES * TC_W_BYTES + TC_STAGES * TC_X_BYTES + 1024 + 8 * TC_NBARS + 16;
+constexpr int TC_NBARS = 2 * TC_WSTAGES + 2 * TC_XSTAGES + 2 * TC_STAGES + 4;
+constexpr int TC_SMEM_BYTES = TC_WSTAGES * TC_W_BYTES + TC_XSTAGES * TC_X_BYTES + 1024 + 8 * TC_NBARS + 16;
 static_assert(2 * TC_D_COLS + TC_STAGES * TC_A_COLS <= TC_TMEM_COLS, "tensor memory budget");
-static_assert(TC_PROMOTE == TC_STAGES * TC_CPS, "one promotion group = one pass over the stages");
+constexpr int TC_GSTAGES = TC_PROMOTE / TC_CPS;       // stages per promotion group
+static_assert(TC_GSTAGES % TC_STAGES == 0 && TC_GSTAGES % TC_XSTAGES == 0, "a group starts on stage 0");
 
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
@@ -69,12 +71,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* wring = smem;
   uint8_t* xring = smem + TC_WSTAGES * TC_W_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + TC_STAGES * TC_X_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + TC_XSTAGES * TC_X_BYTES);
   uint64_t* w_full = bars;
   uint64_t* w_empty = w_full + TC_WSTAGES;
-  uint64_t* x_full = w_empty + TC_WSTAGES;  // [TC_STAGES] activation stage landed (TMA)
-  uint64_t* a_full = x_full + TC_STAGES;    // [TC_STAGES] split weights stored in TMEM
-  uint64_t* s_empty = a_full + TC_STAGES;   // [TC_STAGES] MMAs of the stage done (frees A and X)
+  uint64_t* x_full = w_empty + TC_WSTAGES;  // [TC_XSTAGES] activation stage landed (TMA)
+  uint64_t* x_empty = x_full + TC_XSTAGES;  // [TC_XSTAGES] its MMAs are done (relayed by warp 2)
+  uint64_t* a_full = x_empty + TC_XSTAGES;  // [TC_STAGES] split weights stored, activations landed
+  uint64_t* s_empty = a_full + TC_STAGES;   // [TC_STAGES] MMAs of the stage done (frees A)
   uint64_t* d_full = s_empty + TC_STAGES;   // [2]
   uint64_t* d_empty = d_full + 2;           // [2]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 2);
@@ -93,11 +96,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_WSTAGES; ++s) { mbar_init(smem_addr(&w_full[s]), 1); mbar_init(smem_addr(&w_empty[s]), 4); }
-    for (int s = 0; s < TC_STAGES; ++s) {
-      mbar_init(smem_addr(&x_full[s]), 1);
-      mbar_init(smem_addr(&a_full[s]), 4);
-      mbar_init(smem_addr(&s_empty[s]), 1);
-    }
+    for (int s = 0; s < TC_XSTAGES; ++s) { mbar_init(smem_addr(&x_full[s]), 1); mbar_init(smem_addr(&x_empty[s]), 1); }
+    for (int s = 0; s < TC_STAGES; ++s) { mbar_init(smem_addr(&a_full[s]), 4); mbar_init(smem_addr(&s_empty[s]), 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(smem_addr(&d_full[b]), 1); mbar_init(smem_addr(&d_empty[b]), 4); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -141,16 +141,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       constexpr uint32_t id_x = idesc_tf32(TC_WROWS, TC_NTOK);
       const uint64_t bx0 = sw128_desc(smem_addr(xring));
       bool ok = true;
-      for (int j = 0; ok && j * TC_STAGES < nstages; ++j) {  // one promotion group per pass
+      for (int j = 0; ok && j * TC_GSTAGES < nstages; ++j) {  // one promotion group
         const int b = j & 1;
         if (j >= 2 && !mbar_wait(smem_addr(&d_empty[b]), ((j >> 1) - 1) & 1, abort_flag)) break;
         const uint32_t d = tmem + b * TC_D_COLS;
 #pragma unroll
-        for (int u = 0; u < TC_STAGES; ++u) {
-          const int q = j * TC_STAGES + u;
+        for (int u = 0; u < TC_GSTAGES; ++u) {
+          const int q = j * TC_GSTAGES + u, s = u % TC_STAGES;
           if (q >= nstages) break;
-          if (!mbar_wait(smem_addr(&a_full[u]), j & 1, abort_flag) ||
-              !mbar_wait(smem_addr(&x_full[u]), j & 1, abort_flag)) {
+          // the converters fold the activation stage's arrival into a_full
+          if (!mbar_wait(smem_addr(&a_full[s]), (u / TC_STAGES) & 1, abort_flag)) {
             ok = false;
             break;
           }
@@ -158,15 +158,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
           for (int c = 0; c < TC_CPS; ++c) {
             if (c > 0 && q * TC_CPS + c >= nloc) break;
-            const uint32_t ab = tmem_a + u * TC_A_COLS + c * TC_AC_COLS;
-            const uint64_t bx = bx0 + (uint64_t)((u * TC_X_BYTES + c * TC_XC_BYTES) >> 4);
+            const uint32_t ab = tmem_a + s * TC_A_COLS + c * TC_AC_COLS;
+            const uint64_t bx = bx0 + (uint64_t)(((u % TC_XSTAGES) * TC_X_BYTES + c * TC_XC_BYTES) >> 4);
 #pragma unroll
             for (int kk = 0; kk < TC_KC / 8; ++kk) {  // 8 tf32 = 32 bytes along K
               mma_tf32_ts(d, ab + kk * 8, bx + 2 * kk, id_cat, (u | c | kk) ? 1u : 0u);
               mma_tf32_ts(d, ab + TC_KC + kk * 8, bx + 2 * kk, id_x, 1u);
             }
           }
-          mma_commit(smem_addr(&s_empty[u]));
+          mma_commit(smem_addr(&s_empty[s]));
         }
         if (!ok) break;
         mma_commit(smem_addr(&d_full[b]));
@@ -179,8 +179,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     pdl_wait();
     if (lane == 0) {
       for (int q = 0; q < nstages; ++q) {
-        const int s = q % TC_STAGES;
-        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / TC_STAGES) & 1) ^ 1, abort_flag)) break;
+        const int s = q % TC_XSTAGES;
+        if (!mbar_wait(smem_addr(&x_empty[s]), ((q / TC_XSTAGES) & 1) ^ 1, abort_flag)) break;
         const int nc = nloc - q * TC_CPS < TC_CPS ? nloc - q * TC_CPS : TC_CPS;
         const uint32_t fb = smem_addr(&x_full[s]);
         uint8_t* st = xring + s * TC_X_BYTES;
@@ -220,7 +220,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         small[k] = __float_as_uint(w - bv);
       }
       // the first chunk of a stage waits until the MMAs of its last use are done
-      if (c == 0 && !mbar_wait(smem_addr(&s_empty[s]), ((q / TC_STAGES) & 1) ^ 1, abort_flag)) break;
+      if (c == 0) {
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / TC_STAGES) & 1) ^ 1, abort_flag)) break;
+        // the MMAs of stage q - TC_STAGES are done: relay the release of its activation stage
+        if (warp == 2 && lane == 0 && q >= TC_STAGES) mbar_arrive(smem_addr(&x_empty[(q - TC_STAGES) % TC_XSTAGES]));
+      }
       tc_fence_after();
       const uint32_t a = tmem_a + lane_base + s * TC_A_COLS + c * TC_AC_COLS;
       tmem_st32(a, big);
@@ -228,7 +232,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (c == TC_CPS - 1 || i == nloc - 1) {  // the stage is complete
         tmem_st_wait();
         tc_fence_before();
+        // one converter also waits for the stage's activation tiles, so the
+        // MMA thread waits on a single barrier per stage
+        const bool x_ok =
+            warp != 2 || mbar_wait(smem_addr(&x_full[q % TC_XSTAGES]), (q / TC_XSTAGES) & 1, abort_flag);
         __syncwarp();
+        if (!x_ok) break;
         if (lane == 0) mbar_arrive(smem_addr(&a_full[s]));
       }
     }
@@ -269,7 +278,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0 && lane == 0)
       for (int i = 0; i < w_issued; ++i) mbar_drain(smem_addr(&w_full[i % TC_WSTAGES]), (i / TC_WSTAGES) & 1);
     if (warp == 10 && lane == 0)
-      for (int q = 0; q < x_issued; ++q) mbar_drain(smem_addr(&x_full[q % TC_STAGES]), (q / TC_STAGES) & 1);
+      for (int q = 0; q < x_issued; ++q) mbar_drain(smem_addr(&x_full[q % TC_XSTAGES]), (q / TC_XSTAGES) & 1);
     if (warp == 1 && lane == 0 && mma_groups > 0) {
       const int g = mma_groups - 1;
       mbar_drain(smem_addr(&d_full[g & 1]), (g >> 1) & 1);

@@ -8,15 +8,17 @@
 //   D[:, 0:256] += W_b . [X_b ; X_s]      (N = 256: 128 rows of X_b, then of X_s)
 //   D[:, 0:128] += W_s . X_b              (N = 128)
 //
-// The cost of a tcgen05.mma barely depends on N, so twice the rows take the
-// same 8 instructions per 32-wide K chunk.  The 256-column accumulator leaves
-// room for 4 A stages but not for a second accumulator, so the MMA issuer
-// waits while the promoters drain it (every 8 chunks).
-//   warp 0       TMA of the W tile [128 x 32] into a 6-deep ring
-//   warp 1       MMA issuer
-//   warps 2..5   split W rows into the TMEM A stages (one lane quarter each)
+// A tf32 MMA of N <= 128 costs ~60 cycles and one of N = 256 ~130, so twice
+// the rows take the same 8 instructions per 32-wide K chunk at ~1.5x the
+// tensor time.  The 256-column accumulator leaves room for 2 A stages of two
+// chunks but not for a second accumulator, so the MMA issuer waits while the
+// promoters drain it (every 8 chunks).
+//   warp 0       TMA of the W tile [128 x 32] into a 5-deep ring
+//   warp 1       MMA issuer (one wait and one commit per stage of two chunks)
+//   warps 2..5   split W rows into the TMEM A stages (one lane quarter each);
+//                warp 2 also waits for the stage's activation tiles
 //   warps 6..13  promote: two warps per lane quarter, 64 activation rows each
-//   warp 14      TMA of [X_b ; X_s] (4 boxes of 64 rows) into a 3-deep ring
+//   warp 14      TMA of [X_b ; X_s] (4 boxes of 64 rows per chunk), 2 stages
 // Epilogue: shared-memory tile, every thread stores float4s (tc_epilogue.cuh).
 // Every mbarrier wait is bounded.
 #include <cuda.h>
@@ -33,21 +35,25 @@ constexpr int TW_THREADS = 480;          // 15 warps
 constexpr int TW_KC = 32;
 constexpr int TW_WROWS = 128;
 constexpr int TW_NTOK = 128;
-constexpr int TW_WSTAGES = 6;
-constexpr int TW_XSTAGES = 3;
-constexpr int TW_ASTAGES = 4;
-constexpr int TW_PROMOTE = 8;
+constexpr int TW_WSTAGES = 5;            // W ring depth (chunks)
+constexpr int TW_CPS = 2;                // chunks per A/X stage
+constexpr int TW_STAGES = 2;             // A/X stages
+constexpr int TW_PROMOTE = 8;            // chunks per promotion
+constexpr int TW_GSTAGES = TW_PROMOTE / TW_CPS;
 constexpr int TW_W_BYTES = TW_WROWS * 128;        // 16 KB
-constexpr int TW_X_BYTES = 2 * TW_NTOK * 128;     // 32 KB: [X_b ; X_s]
+constexpr int TW_XC_BYTES = 2 * TW_NTOK * 128;    // 32 KB: [X_b ; X_s] of one chunk
+constexpr int TW_X_BYTES = TW_CPS * TW_XC_BYTES;  // one stage
 constexpr int TW_D_COLS = 2 * TW_NTOK;            // 256
-constexpr int TW_A_COLS = 2 * TW_KC;              // 64: W_b and W_s of one chunk
-constexpr int TW_TMEM_COLS = 512;                 // accumulator + 4 A stages
-constexpr int TW_NBARS = 2 * TW_WSTAGES + 2 * TW_XSTAGES + 2 * TW_ASTAGES + 2;
-constexpr int TW_RING_BYTES = TW_WSTAGES * TW_W_BYTES + TW_XSTAGES * TW_X_BYTES;
+constexpr int TW_AC_COLS = 2 * TW_KC;             // W_b and W_s of one chunk
+constexpr int TW_A_COLS = TW_CPS * TW_AC_COLS;    // one stage
+constexpr int TW_TMEM_COLS = 512;                 // accumulator + 2 A stages
+constexpr int TW_NBARS = 2 * TW_WSTAGES + 3 * TW_STAGES + 2;
+constexpr int TW_RING_BYTES = TW_WSTAGES * TW_W_BYTES + TW_STAGES * TW_X_BYTES;
 constexpr int TW_SMEM_BYTES = TW_RING_BYTES + 1024 + 8 * TW_NBARS + 16;
 constexpr int TW_RLD = TW_WROWS + 4;
 static_assert(TW_NTOK * TW_RLD * 4 <= TW_RING_BYTES, "epilogue tile fits in the rings");
-static_assert(TW_D_COLS + TW_ASTAGES * TW_A_COLS <= TW_TMEM_COLS, "tensor memory budget");
+static_assert(TW_D_COLS + TW_STAGES * TW_A_COLS <= TW_TMEM_COLS, "tensor memory budget");
+static_assert(TW_GSTAGES % TW_STAGES == 0, "a group starts on stage 0");
 
 __global__ void __launch_bounds__(TW_THREADS, 1)
     gemm_tc_wide_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXb,
@@ -56,14 +62,13 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* wring = smem;
   uint8_t* xring = smem + TW_WSTAGES * TW_W_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + TW_XSTAGES * TW_X_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + TW_STAGES * TW_X_BYTES);
   uint64_t* w_full = bars;
   uint64_t* w_empty = w_full + TW_WSTAGES;
-  uint64_t* x_full = w_empty + TW_WSTAGES;
-  uint64_t* x_empty = x_full + TW_XSTAGES;
-  uint64_t* a_full = x_empty + TW_XSTAGES;
-  uint64_t* a_empty = a_full + TW_ASTAGES;
-  uint64_t* d_full = a_empty + TW_ASTAGES;
+  uint64_t* x_full = w_empty + TW_WSTAGES;  // [TW_STAGES] activation stage landed (TMA)
+  uint64_t* a_full = x_full + TW_STAGES;    // [TW_STAGES] split weights stored, activations landed
+  uint64_t* s_empty = a_full + TW_STAGES;   // [TW_STAGES] MMAs of the stage done (frees A and X)
+  uint64_t* d_full = s_empty + TW_STAGES;
   uint64_t* d_empty = d_full + 1;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 1) + 1;
@@ -76,12 +81,16 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
   const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
   const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
   const int nloc = c1 - c0;
+  const int nstages = (nloc + TW_CPS - 1) / TW_CPS;
   const int ngroups = (nloc + TW_PROMOTE - 1) / TW_PROMOTE;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TW_WSTAGES; ++s) { mbar_init(smem_addr(&w_full[s]), 1); mbar_init(smem_addr(&w_empty[s]), 4); }
-    for (int s = 0; s < TW_XSTAGES; ++s) { mbar_init(smem_addr(&x_full[s]), 1); mbar_init(smem_addr(&x_empty[s]), 1); }
-    for (int s = 0; s < TW_ASTAGES; ++s) { mbar_init(smem_addr(&a_full[s]), 4); mbar_init(smem_addr(&a_empty[s]), 1); }
+    for (int s = 0; s < TW_STAGES; ++s) {
+      mbar_init(smem_addr(&x_full[s]), 1);
+      mbar_init(smem_addr(&a_full[s]), 4);
+      mbar_init(smem_addr(&s_empty[s]), 1);
+    }
     mbar_init(smem_addr(d_full), 1);
     mbar_init(smem_addr(d_empty), 8);
     *abort_flag = 0;
@@ -114,49 +123,63 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
+    // MMA issuer: stage indices, descriptors and accumulate flags are
+    // compile-time; one wait and one commit per stage of two chunks.
     if (lane == 0) {
       constexpr uint32_t id_cat = idesc_tf32(TW_WROWS, 2 * TW_NTOK);
       constexpr uint32_t id_x = idesc_tf32(TW_WROWS, TW_NTOK);
-      for (int i = 0; i < nloc; ++i) {
-        const int g = i / TW_PROMOTE;
+      const uint64_t bx0 = sw128_desc(smem_addr(xring));
+      bool ok = true;
+      for (int j = 0; ok && j * TW_GSTAGES < nstages; ++j) {
         // single accumulator: a new group starts once the promoters drained the last one
-        if (i % TW_PROMOTE == 0 && g >= 1 && !mbar_wait(smem_addr(d_empty), (g - 1) & 1, abort_flag)) break;
-        const int as = i % TW_ASTAGES, xs = i % TW_XSTAGES;
-        if (!mbar_wait(smem_addr(&a_full[as]), (i / TW_ASTAGES) & 1, abort_flag)) break;
-        if (!mbar_wait(smem_addr(&x_full[xs]), (i / TW_XSTAGES) & 1, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t ab = tmem_a + as * TW_A_COLS, asml = ab + TW_KC;
-        const uint64_t bx = sw128_desc(smem_addr(xring + xs * TW_X_BYTES));
+        if (j >= 1 && !mbar_wait(smem_addr(d_empty), (j - 1) & 1, abort_flag)) break;
 #pragma unroll
-        for (int kk = 0; kk < TW_KC / 8; ++kk) {
-          const uint64_t adv = (uint64_t)(kk * 32) >> 4;  // 8 tf32 = 32 bytes along K
-          mma_tf32_ts(tmem, ab + kk * 8, bx + adv, id_cat, (i % TW_PROMOTE != 0 || kk > 0) ? 1u : 0u);
-          mma_tf32_ts(tmem, asml + kk * 8, bx + adv, id_x, 1u);
+        for (int u = 0; u < TW_GSTAGES; ++u) {
+          const int q = j * TW_GSTAGES + u, s = u % TW_STAGES;
+          if (q >= nstages) break;
+          if (!mbar_wait(smem_addr(&a_full[s]), (u / TW_STAGES) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < TW_CPS; ++c) {
+            if (c > 0 && q * TW_CPS + c >= nloc) break;
+            const uint32_t ab = tmem_a + s * TW_A_COLS + c * TW_AC_COLS;
+            const uint64_t bx = bx0 + (uint64_t)((s * TW_X_BYTES + c * TW_XC_BYTES) >> 4);
+#pragma unroll
+            for (int kk = 0; kk < TW_KC / 8; ++kk) {  // 8 tf32 = 32 bytes along K
+              mma_tf32_ts(tmem, ab + kk * 8, bx + 2 * kk, id_cat, (u | c | kk) ? 1u : 0u);
+              mma_tf32_ts(tmem, ab + TW_KC + kk * 8, bx + 2 * kk, id_x, 1u);
+            }
+          }
+          mma_commit(smem_addr(&s_empty[s]));
         }
-        mma_commit(smem_addr(&a_empty[as]));
-        mma_commit(smem_addr(&x_empty[xs]));
-        if (i % TW_PROMOTE == TW_PROMOTE - 1 || i == nloc - 1) {
-          mma_commit(smem_addr(d_full));
-          mma_groups = g + 1;
-        }
+        if (!ok) break;
+        mma_commit(smem_addr(d_full));
+        mma_groups = j + 1;
       }
     }
     __syncwarp();
   } else if (warp == 14) {
     pdl_wait();
     if (lane == 0) {
-      for (int i = 0; i < nloc; ++i) {
-        const int s = i % TW_XSTAGES;
-        if (!mbar_wait(smem_addr(&x_empty[s]), ((i / TW_XSTAGES) & 1) ^ 1, abort_flag)) break;
+      for (int q = 0; q < nstages; ++q) {
+        const int s = q % TW_STAGES;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / TW_STAGES) & 1) ^ 1, abort_flag)) break;
+        const int nc = nloc - q * TW_CPS < TW_CPS ? nloc - q * TW_CPS : TW_CPS;
         const uint32_t fb = smem_addr(&x_full[s]);
         uint8_t* st = xring + s * TW_X_BYTES;
-        mbar_expect_tx(fb, TW_X_BYTES);
-        const int kx = (c0 + i) * TW_KC;
-        tma_load_2d(smem_addr(st), &tmXb, kx, tok0, fb);
-        tma_load_2d(smem_addr(st + 64 * 128), &tmXb, kx, tok0 + 64, fb);
-        tma_load_2d(smem_addr(st + 128 * 128), &tmXs, kx, tok0, fb);
-        tma_load_2d(smem_addr(st + 192 * 128), &tmXs, kx, tok0 + 64, fb);
-        x_issued = i + 1;
+        mbar_expect_tx(fb, nc * TW_XC_BYTES);
+        for (int c = 0; c < nc; ++c) {
+          const int kx = (c0 + q * TW_CPS + c) * TW_KC;
+          uint8_t* sc = st + c * TW_XC_BYTES;
+          tma_load_2d(smem_addr(sc), &tmXb, kx, tok0, fb);
+          tma_load_2d(smem_addr(sc + 64 * 128), &tmXb, kx, tok0 + 64, fb);
+          tma_load_2d(smem_addr(sc + 128 * 128), &tmXs, kx, tok0, fb);
+          tma_load_2d(smem_addr(sc + 192 * 128), &tmXs, kx, tok0 + 64, fb);
+        }
+        x_issued = q + 1;
       }
     }
     __syncwarp();
@@ -166,15 +189,15 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     for (int i = 0; i < nloc; ++i) {
-      const int ws = i % TW_WSTAGES, as = i % TW_ASTAGES;
+      const int ws = i % TW_WSTAGES, q = i / TW_CPS, c = i % TW_CPS, s = q % TW_STAGES;
       if (!mbar_wait(smem_addr(&w_full[ws]), (i / TW_WSTAGES) & 1, abort_flag)) break;
       const uint8_t* tile = wring + ws * TW_W_BYTES + row * 128;
       uint32_t big[TW_KC], small[TW_KC];
 #pragma unroll
-      for (int c = 0; c < TW_KC / 4; ++c) {  // undo the 128B swizzle: chunk c lives at c ^ (row % 8)
-        const float4 v = *reinterpret_cast<const float4*>(tile + ((c ^ (row & 7)) << 4));
-        big[4 * c] = __float_as_uint(v.x); big[4 * c + 1] = __float_as_uint(v.y);
-        big[4 * c + 2] = __float_as_uint(v.z); big[4 * c + 3] = __float_as_uint(v.w);
+      for (int k4 = 0; k4 < TW_KC / 4; ++k4) {  // undo the 128B swizzle: chunk k4 lives at k4 ^ (row % 8)
+        const float4 v = *reinterpret_cast<const float4*>(tile + ((k4 ^ (row & 7)) << 4));
+        big[4 * k4] = __float_as_uint(v.x); big[4 * k4 + 1] = __float_as_uint(v.y);
+        big[4 * k4 + 2] = __float_as_uint(v.z); big[4 * k4 + 3] = __float_as_uint(v.w);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&w_empty[ws]));
@@ -185,15 +208,21 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
         big[k] = __float_as_uint(bv);
         small[k] = __float_as_uint(w - bv);
       }
-      if (!mbar_wait(smem_addr(&a_empty[as]), ((i / TW_ASTAGES) & 1) ^ 1, abort_flag)) break;
+      if (c == 0 && !mbar_wait(smem_addr(&s_empty[s]), ((q / TW_STAGES) & 1) ^ 1, abort_flag)) break;
       tc_fence_after();
-      const uint32_t a = tmem_a + lane_base + as * TW_A_COLS;
+      const uint32_t a = tmem_a + lane_base + s * TW_A_COLS + c * TW_AC_COLS;
       tmem_st32(a, big);
       tmem_st32(a + TW_KC, small);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&a_full[as]));
+      if (c == TW_CPS - 1 || i == nloc - 1) {  // the stage is complete
+        tmem_st_wait();
+        tc_fence_before();
+        // one converter also waits for the stage's activation tiles, so the
+        // MMA thread waits on a single barrier per stage
+        const bool x_ok = warp != 2 || mbar_wait(smem_addr(&x_full[s]), (q / TW_STAGES) & 1, abort_flag);
+        __syncwarp();
+        if (!x_ok) break;
+        if (lane == 0) mbar_arrive(smem_addr(&a_full[s]));
+      }
     }
   } else {
     // ------------ warps 6..13: promote (lane quarter warp & 3, rows half * 64 ..)
@@ -228,7 +257,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
     if (warp == 0 && lane == 0)
       for (int i = 0; i < w_issued; ++i) mbar_drain(smem_addr(&w_full[i % TW_WSTAGES]), (i / TW_WSTAGES) & 1);
     if (warp == 14 && lane == 0)
-      for (int i = 0; i < x_issued; ++i) mbar_drain(smem_addr(&x_full[i % TW_XSTAGES]), (i / TW_XSTAGES) & 1);
+      for (int q = 0; q < x_issued; ++q) mbar_drain(smem_addr(&x_full[q % TW_STAGES]), (q / TW_STAGES) & 1);
     if (warp == 1 && lane == 0 && mma_groups > 0) mbar_drain(smem_addr(d_full), (mma_groups - 1) & 1);
   }
   tc_fence_before();
