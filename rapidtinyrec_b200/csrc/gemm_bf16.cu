@@ -5,10 +5,14 @@
 //
 // A CTA owns 128 weight rows (MMA M) x 64 activation rows (MMA N) for a range
 // of K, walked in 64-element chunks (one 128-byte row of bf16):
-//   warp 0     TMA of the packed W tile [128 x 64] into an 8-deep ring (128B swizzle)
+//   warp 0     TMA of the packed W tiles [128 x 64] (128B swizzle)
+//   warp 2     TMA of the activation tiles [64 x 64]
+//              both into a 4-deep ring of stages of two chunks; a stage has one
+//              full barrier (both producers arrive) and one empty barrier
 //   warp 1     MMA issuer: tcgen05.mma kind::f16, A = W, B = X, both from shared
-//              memory, 4 instructions (K = 16 each) per chunk
-//   warp 2     TMA of the activation tile [64 x 64] into a 4-deep ring
+//              memory, 4 instructions (K = 16 each) per chunk; one wait and one
+//              commit per stage, stage indices compile-time (the issuing
+//              thread's own instruction stream is what bounds the MMA rate)
 //   warps 4..7 promote the TMEM accumulator (double-buffered) into fp32
 //              registers every 4 chunks, as the 3xTF32 kernel does
 // Epilogues round where a bf16 torch model rounds (the reference's
@@ -32,15 +36,20 @@ constexpr int BF_THREADS = 256;          // 8 warps
 constexpr int BF_KC = 64;                // bf16 per 128-byte row
 constexpr int BF_WROWS = 128;            // MMA M
 constexpr int BF_NTOK = 64;              // activation rows per CTA (MMA N)
-constexpr int BF_WSTAGES = 8;
-constexpr int BF_XSTAGES = 4;
-constexpr int BF_PROMOTE = 4;
-constexpr int BF_W_BYTES = BF_WROWS * 128;
-constexpr int BF_X_BYTES = BF_NTOK * 128;
+constexpr int BF_CPS = 2;                // chunks per stage
+constexpr int BF_STAGES = 4;             // ring depth in stages
+constexpr int BF_PROMOTE = 4;            // chunks per promotion (K = 256: the tensor core's fp32
+                                         // accumulation drifts past 1 bf16 ulp at K = 512)
+constexpr int BF_GSTAGES = BF_PROMOTE / BF_CPS;
+constexpr int BF_WC_BYTES = BF_WROWS * 128;           // one chunk of W
+constexpr int BF_XC_BYTES = BF_NTOK * 128;            // one chunk of X
+constexpr int BF_W_BYTES = BF_CPS * BF_WC_BYTES;      // one stage
+constexpr int BF_X_BYTES = BF_CPS * BF_XC_BYTES;
 constexpr int BF_D_COLS = BF_NTOK;
 constexpr int BF_TMEM_COLS = 2 * BF_D_COLS;   // 128: double-buffered accumulator
-constexpr int BF_NBARS = 2 * BF_WSTAGES + 2 * BF_XSTAGES + 4;
-constexpr int BF_RING_BYTES = BF_WSTAGES * BF_W_BYTES + BF_XSTAGES * BF_X_BYTES;
+constexpr int BF_NBARS = 2 * BF_STAGES + 4;
+constexpr int BF_RING_BYTES = BF_STAGES * (BF_W_BYTES + BF_X_BYTES);
+static_assert(2 * BF_GSTAGES == BF_STAGES, "one pass over the ring = both accumulator buffers");
 constexpr int BF_SMEM_BYTES = BF_RING_BYTES + 1024 + 8 * BF_NBARS + 16;
 constexpr int BF_RLD = BF_WROWS + 4;          // epilogue tile row stride (floats)
 static_assert(BF_NTOK * BF_RLD * 4 <= BF_RING_BYTES, "epilogue tile fits in the rings");
@@ -181,13 +190,11 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* wring = smem;
-  uint8_t* xring = smem + BF_WSTAGES * BF_W_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + BF_XSTAGES * BF_X_BYTES);
-  uint64_t* w_full = bars;
-  uint64_t* w_empty = w_full + BF_WSTAGES;
-  uint64_t* x_full = w_empty + BF_WSTAGES;
-  uint64_t* x_empty = x_full + BF_XSTAGES;
-  uint64_t* d_full = x_empty + BF_XSTAGES;  // [2]
+  uint8_t* xring = smem + BF_STAGES * BF_W_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + BF_STAGES * BF_X_BYTES);
+  uint64_t* s_full = bars;                  // [BF_STAGES] W and X of the stage landed (2 arrivals + bytes)
+  uint64_t* s_empty = s_full + BF_STAGES;   // [BF_STAGES] the stage's MMAs are done
+  uint64_t* d_full = s_empty + BF_STAGES;   // [2]
   uint64_t* d_empty = d_full + 2;           // [2]
   volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 2);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2) + 1;
@@ -200,11 +207,11 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
   const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
   const int nloc = c1 - c0;
+  const int nstages = (nloc + BF_CPS - 1) / BF_CPS;
   const int ngroups = (nloc + BF_PROMOTE - 1) / BF_PROMOTE;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < BF_WSTAGES; ++s) { mbar_init(smem_addr(&w_full[s]), 1); mbar_init(smem_addr(&w_empty[s]), 1); }
-    for (int s = 0; s < BF_XSTAGES; ++s) { mbar_init(smem_addr(&x_full[s]), 1); mbar_init(smem_addr(&x_empty[s]), 1); }
+    for (int s = 0; s < BF_STAGES; ++s) { mbar_init(smem_addr(&s_full[s]), 2); mbar_init(smem_addr(&s_empty[s]), 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(smem_addr(&d_full[b]), 1); mbar_init(smem_addr(&d_empty[b]), 4); }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -223,40 +230,58 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // weights do not depend on the previous kernel: no griddepcontrol.wait
-      for (int i = 0; i < nloc; ++i) {
-        const int s = i % BF_WSTAGES;
-        if (!mbar_wait(smem_addr(&w_empty[s]), ((i / BF_WSTAGES) & 1) ^ 1, abort_flag)) break;
-        const uint32_t fb = smem_addr(&w_full[s]);
-        mbar_expect_tx(fb, BF_W_BYTES);
-        tma_load_2d(smem_addr(wring + s * BF_W_BYTES), &tmW, 0, (blockIdx.y * nchunks + c0 + i) * BF_WROWS, fb);
-        w_issued = i + 1;
+      for (int q = 0; q < nstages; ++q) {
+        const int s = q % BF_STAGES;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / BF_STAGES) & 1) ^ 1, abort_flag)) break;
+        const int nc = nloc - q * BF_CPS < BF_CPS ? nloc - q * BF_CPS : BF_CPS;
+        const uint32_t fb = smem_addr(&s_full[s]);
+        mbar_expect_tx(fb, nc * BF_WC_BYTES);
+        for (int c = 0; c < nc; ++c)
+          tma_load_2d(smem_addr(wring + s * BF_W_BYTES + c * BF_WC_BYTES), &tmW, 0,
+                      (blockIdx.y * nchunks + c0 + q * BF_CPS + c) * BF_WROWS, fb);
+        w_issued = q + 1;
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(BF_WROWS, BF_NTOK);
-      for (int i = 0; i < nloc; ++i) {
-        const int g = i / BF_PROMOTE, b = g & 1;
-        if (i % BF_PROMOTE == 0 && g >= 2 && !mbar_wait(smem_addr(&d_empty[b]), ((g >> 1) - 1) & 1, abort_flag))
-          break;
-        const int ws = i % BF_WSTAGES, xs = i % BF_XSTAGES;
-        if (!mbar_wait(smem_addr(&w_full[ws]), (i / BF_WSTAGES) & 1, abort_flag)) break;
-        if (!mbar_wait(smem_addr(&x_full[xs]), (i / BF_XSTAGES) & 1, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t d = tmem + b * BF_D_COLS;
-        const uint64_t ad = sw128_desc(smem_addr(wring + ws * BF_W_BYTES));
-        const uint64_t bd = sw128_desc(smem_addr(xring + xs * BF_X_BYTES));
+      const uint64_t ad0 = sw128_desc(smem_addr(wring)), bd0 = sw128_desc(smem_addr(xring));
+      bool ok = true;
+      // one pass over the ring = two promotion groups, one per accumulator buffer
+      for (int jj = 0; ok && jj * BF_STAGES < nstages; ++jj) {
 #pragma unroll
-        for (int kk = 0; kk < BF_KC / 16; ++kk) {
-          const uint64_t adv = (uint64_t)(kk * 32) >> 4;  // 16 bf16 = 32 bytes along K
-          mma_f16_ss(d, ad + adv, bd + adv, idesc, (i % BF_PROMOTE != 0 || kk > 0) ? 1u : 0u);
-        }
-        mma_commit(smem_addr(&w_empty[ws]));
-        mma_commit(smem_addr(&x_empty[xs]));
-        if (i % BF_PROMOTE == BF_PROMOTE - 1 || i == nloc - 1) {
+        for (int b = 0; b < 2; ++b) {
+          const int j = 2 * jj + b;  // promotion group
+          if (j * BF_GSTAGES >= nstages) break;
+          if (j >= 2 && !mbar_wait(smem_addr(&d_empty[b]), (jj - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t d = tmem + b * BF_D_COLS;
+#pragma unroll
+          for (int u = 0; u < BF_GSTAGES; ++u) {
+            const int q = j * BF_GSTAGES + u, s = b * BF_GSTAGES + u;
+            if (q >= nstages) break;
+            if (!mbar_wait(smem_addr(&s_full[s]), jj & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < BF_CPS; ++c) {
+              if (c > 0 && q * BF_CPS + c >= nloc) break;
+              const uint64_t ad = ad0 + (uint64_t)((s * BF_W_BYTES + c * BF_WC_BYTES) >> 4);
+              const uint64_t bd = bd0 + (uint64_t)((s * BF_X_BYTES + c * BF_XC_BYTES) >> 4);
+#pragma unroll
+              for (int kk = 0; kk < BF_KC / 16; ++kk)  // 16 bf16 = 32 bytes along K
+                mma_f16_ss(d, ad + 2 * kk, bd + 2 * kk, idesc, (u | c | kk) ? 1u : 0u);
+            }
+            mma_commit(smem_addr(&s_empty[s]));
+          }
+          if (!ok) break;
           mma_commit(smem_addr(&d_full[b]));
-          mma_groups = g + 1;
+          mma_groups = j + 1;
         }
       }
     }
@@ -264,13 +289,15 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   } else if (warp == 2) {
     pdl_wait();
     if (lane == 0) {
-      for (int i = 0; i < nloc; ++i) {
-        const int s = i % BF_XSTAGES;
-        if (!mbar_wait(smem_addr(&x_empty[s]), ((i / BF_XSTAGES) & 1) ^ 1, abort_flag)) break;
-        const uint32_t fb = smem_addr(&x_full[s]);
-        mbar_expect_tx(fb, BF_X_BYTES);
-        tma_load_2d(smem_addr(xring + s * BF_X_BYTES), &tmX, (c0 + i) * BF_KC, tok0, fb);
-        x_issued = i + 1;
+      for (int q = 0; q < nstages; ++q) {
+        const int s = q % BF_STAGES;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / BF_STAGES) & 1) ^ 1, abort_flag)) break;
+        const int nc = nloc - q * BF_CPS < BF_CPS ? nloc - q * BF_CPS : BF_CPS;
+        const uint32_t fb = smem_addr(&s_full[s]);
+        mbar_expect_tx(fb, nc * BF_XC_BYTES);
+        for (int c = 0; c < nc; ++c)
+          tma_load_2d(smem_addr(xring + s * BF_X_BYTES + c * BF_XC_BYTES), &tmX, (c0 + q * BF_CPS + c) * BF_KC, tok0, fb);
+        x_issued = q + 1;
       }
     }
     __syncwarp();
@@ -302,10 +329,12 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   // drain on abort: issued copies and MMAs must land before smem/TMEM go away
   if (*abort_flag) {
     if (threadIdx.x == 0) atomicOr(p.status, RTR_DEV_TIMEOUT);
+    // (a stage whose other producer gave up never completes: the drain then
+    // waits out its bound, which only delays the exit of an aborted CTA)
     if (warp == 0 && lane == 0)
-      for (int i = 0; i < w_issued; ++i) mbar_drain(smem_addr(&w_full[i % BF_WSTAGES]), (i / BF_WSTAGES) & 1);
+      for (int q = 0; q < w_issued; ++q) mbar_drain(smem_addr(&s_full[q % BF_STAGES]), (q / BF_STAGES) & 1);
     if (warp == 2 && lane == 0)
-      for (int i = 0; i < x_issued; ++i) mbar_drain(smem_addr(&x_full[i % BF_XSTAGES]), (i / BF_XSTAGES) & 1);
+      for (int q = 0; q < x_issued; ++q) mbar_drain(smem_addr(&s_full[q % BF_STAGES]), (q / BF_STAGES) & 1);
     if (warp == 1 && lane == 0 && mma_groups > 0) {
       const int g = mma_groups - 1;
       mbar_drain(smem_addr(&d_full[g & 1]), (g >> 1) & 1);
