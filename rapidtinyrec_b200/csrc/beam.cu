@@ -190,7 +190,10 @@ struct SelShared {
   float c_score[2 * MAX_BEAMS], c_run[2 * MAX_BEAMS], c_fin[3 * MAX_BEAMS];
   int32_t c_beam[2 * MAX_BEAMS], c_tok[2 * MAX_BEAMS], c_hit[2 * MAX_BEAMS];
   int32_t n_run[MAX_BEAMS], n_fin[MAX_BEAMS];
+  float nf_score[MAX_BEAMS];   // the new finished set, for the stop test
+  int32_t nf_done[MAX_BEAMS];
   unsigned hist[256];
+  unsigned char fmark[2 * MAX_BEAMS + MAX_WIDTH];  // row 0's allowed columns below K + width
   uint64_t prefix, mask;
   int krem, done, counter, finite;
   float red[33];
@@ -319,17 +322,28 @@ __global__ void __launch_bounds__(SEL_THREADS) beam_select_kernel(BeamState* st,
     sh.sorted[rank] = k;
   }
   __syncthreads();
-  if (tid == 0 && kk < K) {
-    // -inf entries in ascending flat index: row 0's non-allowed columns
-    int c = 0;
-    for (int pos = kk; pos < K; ++pos) {
-      for (;; ++c) {
-        bool allowed = false;
-        for (int j = 0; j < width && !allowed; ++j) allowed = st->cols[step][0][j] == c;
-        if (!allowed) break;
+  if (kk < K) {
+    // -inf entries in ascending flat index: row 0's non-allowed columns.  They
+    // are among the first K + width columns: mark row 0's allowed ones there,
+    // then warp 0 compacts the unmarked ones with ballots.
+    const int range = K + width;
+    for (int i = tid; i < range; i += nt) sh.fmark[i] = 0;
+    __syncthreads();
+    for (int j = tid; j < width; j += nt) {
+      const int c = st->cols[step][0][j];
+      if (c >= 0 && c < range) sh.fmark[c] = 1;
+    }
+    __syncthreads();
+    if (tid < 32) {
+      int pos = kk;
+      for (int base = 0; base < range && pos < K; base += 32) {
+        const int c = base + tid;
+        const bool free = c < range && !sh.fmark[c];
+        const unsigned m = __ballot_sync(0xffffffffu, free);
+        const int r = pos + __popc(m & ((1u << tid) - 1u));
+        if (free && r < K) sh.sorted[r] = cand_key(-INFINITY, (uint32_t)c);
+        pos += __popc(m);
       }
-      sh.sorted[pos] = cand_key(-INFINITY, (uint32_t)c);
-      ++c;
     }
   }
   __syncthreads();
@@ -396,6 +410,7 @@ __global__ void __launch_bounds__(SEL_THREADS) beam_select_kernel(BeamState* st,
     if (m < beams) {
       for (int t = 0; t < NSTEPS; ++t) { st->fin_tok[n][t] = sh.f_tok[m][t]; st->fin_par[n][t] = sh.f_par[m][t]; }
       st->fin_done[n] = sh.f_done[m];
+      sh.nf_done[n] = sh.f_done[m];
     } else {
       const int c = m - beams, pc = sh.c_beam[c];
       for (int t = 0; t < NSTEPS; ++t) {
@@ -403,18 +418,20 @@ __global__ void __launch_bounds__(SEL_THREADS) beam_select_kernel(BeamState* st,
         st->fin_par[n][t] = t < step ? sh.o_par[pc][t] : (t == step ? pc : -1);
       }
       st->fin_done[n] = sh.c_hit[c] && c < beams;
+      sh.nf_done[n] = sh.c_hit[c] && c < beams;
     }
     st->fin_score[n] = sh.c_fin[m];
+    sh.nf_score[n] = sh.c_fin[m];
   }
   __syncthreads();
 
   // 7. early-stop heuristic and the loop condition (utils.py:2876-2943)
   if (tid == 0) {
     float worst = INFINITY;
-    for (int b = 0; b < beams; ++b) worst = fminf(worst, st->fin_score[b]);
-    const float best_running = st->run_score[0] / 1.0f;
+    for (int b = 0; b < beams; ++b) worst = fminf(worst, sh.nf_score[b]);
+    const float best_running = sh.c_run[sh.n_run[0]] / 1.0f;
     bool improvable = false;
-    for (int b = 0; b < beams; ++b) improvable |= best_running > (st->fin_done[b] ? worst : -1.0e9f);
+    for (int b = 0; b < beams; ++b) improvable |= best_running > (sh.nf_done[b] ? worst : -1.0e9f);
     const int unsat = st->unsatisfied && improvable;
     st->unsatisfied = unsat;
     bool all_hits = true;
