@@ -54,6 +54,13 @@ def percentile(values, q):
     return ordered[lo] + (ordered[hi] - ordered[lo]) * (idx - lo)
 
 
+# DRAM bytes of one decode GEMM pass (every projection at M = 50 plus the LM
+# head): ncu dram__bytes_read.sum + dram__bytes_write.sum of a one-layer cut
+# (`--mode profile-gemms --rows 50 --layers 1`), the layer's share scaled by
+# the layer count.  Workloads without a capture report null.
+GEMM_PASS_TRAFFIC = {'qwen1.5b-fp32': 6.426e9, 'qwen1.5b-bf16': 3.169e9}
+
+
 def measured_peaks():
     p = ROOT / 'MEASURED_PEAKS.json'
     if p.exists():
@@ -366,7 +373,11 @@ def run_ours(args):
             'roofline': {'bound': 'hbm', 'kernel': gemm_kernel,
                          'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
                          'frac': round(achieved / peak, 4), 'peak_source': peak_kind,
-                         'traffic': None, 'bytes_per_pass': gemm_bytes, 'ms_per_pass': round(gemm_ms, 4),
+                         'traffic': GEMM_PASS_TRAFFIC.get(args.workload), 'traffic_source':
+                             'ncu dram__bytes_read+write of a one-layer cut, layer share x layers + LM head'
+                             if args.workload in GEMM_PASS_TRAFFIC
+                             else None,
+                         'bytes_per_pass': gemm_bytes, 'ms_per_pass': round(gemm_ms, 4),
                          'gemm_tflops': round(gemm_flops / (gemm_ms / 1000.0) / 1e12, 2)},
             'gpu_launches': int(launches),
             'concurrent': concurrent,

@@ -187,6 +187,16 @@ int rtr_get_report(const rtr_session* s, rtr_report* out);
  * scratch; the session must not have a request in flight. */
 int rtr_profile_gemms(rtr_session* s, int32_t M, int32_t reps, float* ms_per_pass);
 
+/* Test hook (no reference counterpart): C[M, N] = X[M, K] . W[N, K]^T (fp32,
+ * row-major, device pointers) through one projection-GEMM kernel: 0 the
+ * engine's dispatch (64-row kernel for M <= 64, else 128-row), 1 the 64-row
+ * tcgen05 3xTF32 kernel, 2 the 128-row one, 3 the bf16 kernel (X and W rounded
+ * to bf16 first; C holds the bf16-rounded products as fp32), 4 the FFMA
+ * kernel.  N must be a multiple of 4 and K of 4 (8 for the bf16 kernel, 32 for
+ * FFMA).  Scratch is allocated per call; blocks until done. */
+int rtr_gemm_check(int32_t device, const float* x_dev, const float* w_dev, float* c_dev, int32_t M, int32_t N,
+                   int32_t K, int32_t kernel);
+
 /* Processed scores of step t (0..4) as a dense [B, V] float32 device matrix:
  * the double-normalised log-probabilities at allowed columns and -inf
  * elsewhere, i.e. GenerateBeamOutput.scores[t] (the --save-full-scores

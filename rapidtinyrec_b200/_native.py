@@ -22,7 +22,7 @@ EXPORTS = (
     'rtr_decode_step', 'rtr_read_results', 'rtr_generate', 'rtr_step_scores',
     'rtr_lookup_width', 'rtr_constraint_lookup', 'rtr_constraint_process',
     'rtr_synth_fill_host', 'rtr_synth_fill_device', 'rtr_launch', 'rtr_wait', 'rtr_get_report',
-    'rtr_profile_gemms', 'rtr_constraint_process_static',
+    'rtr_profile_gemms', 'rtr_constraint_process_static', 'rtr_gemm_check',
 )
 
 
@@ -104,6 +104,7 @@ def load():
         'rtr_wait': (P, ctypes.POINTER(ResultC)),
         'rtr_get_report': (P, ctypes.POINTER(ReportC)),
         'rtr_profile_gemms': (P, I32, I32, ctypes.POINTER(F)),
+        'rtr_gemm_check': (I32, P, P, P, I32, I32, I32, I32),
         'rtr_constraint_process_static': (P, I32, P, I32, I32, P, P),
     }
     for name, args in sig.items():
@@ -136,3 +137,18 @@ def synth_fill(tensor, seed, tid, scale, offset):
     else:
         check(lib.rtr_synth_fill_host(ctypes.c_void_p(tensor.data_ptr()), tensor.numel(), seed, tid,
                                       scale, offset))
+
+
+def gemm(x, w, kernel=0):
+    """``x @ w.T`` (fp32 CUDA tensors) through one of the engine's projection-GEMM
+    kernels: 0 the engine's dispatch, 1 the 64-row and 2 the 128-row tcgen05
+    3xTF32 kernels, 3 the bf16 kernel, 4 the FFMA kernel (``rtr_gemm_check``)."""
+    import torch
+    x = x.contiguous()
+    w = w.contiguous()
+    M, K = x.shape
+    N = w.shape[0]
+    c = torch.empty((M, N), dtype=torch.float32, device=x.device)
+    torch.cuda.synchronize(x.device)
+    check(load().rtr_gemm_check(x.device.index or 0, x.data_ptr(), w.data_ptr(), c.data_ptr(), M, N, K, kernel))
+    return c

@@ -1,0 +1,100 @@
+"""The projection GEMM kernels against a float64 product, through the C ABI
+(``rtr_gemm_check``): every decode and prefill shape of the 1.5B and 0.5B
+models, ragged row counts around the 64/128-row tiles, K of one and three
+chunks, split-K and no split, run-to-run determinism."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+# tf32 split products: error relative to sum |x w| (measured 5e-8 .. 4.3e-7)
+TF32X3_TOL = 1e-6
+
+
+@pytest.fixture(scope='module')
+def dev():
+    if not torch.cuda.is_available():
+        pytest.fail('CUDA device required for -m gpu tests')
+    return torch.device('cuda:0')
+
+
+def operands(dev, M, N, K, seed):
+    g = torch.Generator(device='cpu').manual_seed(seed)
+    x = torch.randn(M, K, generator=g).to(dev)
+    w = (0.03 * torch.randn(N, K, generator=g)).to(dev)
+    return x, w
+
+
+def rel_err(c, x, w):
+    ref = x.double() @ w.double().T
+    mag = x.double().abs() @ w.double().abs().T
+    return ((c.double() - ref).abs() / mag.clamp_min(1e-30)).max().item()
+
+
+SHAPES = [
+    (50, 2048, 1536), (50, 1536, 1536), (50, 17920, 1536), (50, 1536, 8960),   # 1.5B decode
+    (50, 1152, 896), (50, 896, 4864),                                             # 0.5B decode
+    (237, 2048, 1536), (237, 17920, 1536), (237, 1536, 8960), (352, 1536, 1536),  # prefill
+    (1, 512, 1536), (37, 1536, 1536), (64, 896, 4864), (65, 2048, 1536), (129, 1536, 1536),
+    (50, 256, 96), (50, 512, 32), (50, 132, 64), (200, 4, 1536),
+]
+
+
+@pytest.mark.parametrize('M,N,K', SHAPES)
+@pytest.mark.parametrize('kernel', [1, 2])
+def test_tf32x3_kernels_match_float64(dev, M, N, K, kernel):
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, M, N, K, seed=M * 7 + N + K)
+    c = _native.gemm(x, w, kernel)
+    err = rel_err(c, x, w)
+    assert err <= TF32X3_TOL, f'kernel {kernel} {M}x{N}x{K}: {err:.3e}'
+
+
+def test_dispatch_and_determinism(dev):
+    from rapidtinyrec_b200 import _native
+    for M in (50, 237):
+        x, w = operands(dev, M, 2048, 1536, seed=M)
+        a = _native.gemm(x, w, 0)
+        b = _native.gemm(x, w, 0)
+        assert torch.equal(a, b)                                  # fixed split order, no atomics
+        assert torch.equal(a, _native.gemm(x, w, 1 if M <= 64 else 2))
+
+
+def test_64_and_128_row_kernels_agree_bitwise_up_to_64_rows(dev):
+    """Both promote the tensor-core accumulator every 8 chunks in the same order."""
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, 50, 1536, 8960, seed=3)
+    assert torch.equal(_native.gemm(x, w, 1), _native.gemm(x, w, 2))
+
+
+@pytest.mark.parametrize('M,N,K', [(50, 256, 64), (50, 256, 192), (50, 256, 1536), (50, 256, 8960),
+                                   (50, 17920, 1536), (50, 1536, 8960), (237, 2048, 1536)])
+def test_bf16_kernel_within_one_bf16_ulp_of_the_rounded_product(dev, M, N, K):
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, M, N, K, seed=K + N)
+    xb, wb = x.bfloat16().float(), w.bfloat16().float()
+    want = (xb.double() @ wb.double().T).float().bfloat16().float()
+    got = _native.gemm(x, w, 3)
+    # one bf16 ulp of the result, plus the fp32 accumulation error where the sum cancels
+    mag = (xb.double().abs() @ wb.double().abs().T).float()
+    tol = want.abs() / 128.0 + 2e-6 * mag
+    bad = ((got - want).abs() > tol).sum().item()
+    assert bad == 0, f'{bad} of {got.numel()} beyond one bf16 ulp'
+    assert ((got - want).abs() <= want.abs() / 128.0).float().mean().item() > 0.999
+
+
+@pytest.mark.parametrize('M,N,K', [(50, 2048, 1536), (50, 1536, 8960), (237, 1536, 1536)])
+def test_ffma_kernel_matches_float64(dev, M, N, K):
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, M, N, K, seed=5)
+    assert rel_err(_native.gemm(x, w, 4), x, w) <= TF32X3_TOL
+
+
+def test_bad_shapes_are_rejected(dev):
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, 8, 6, 64, seed=1)
+    with pytest.raises(_native.NativeError):
+        _native.gemm(x, w, 1)                        # N not a multiple of 4
+    x, w = operands(dev, 8, 8, 40, seed=1)
+    with pytest.raises(_native.NativeError):
+        _native.gemm(x, w, 4)                        # FFMA needs K % 32 == 0
