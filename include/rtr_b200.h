@@ -177,6 +177,7 @@ typedef struct {
   int64_t h2d_bytes_per_request;  /* prompt ids + length                       */
   int64_t d2h_bytes_per_request;  /* the result record                         */
   int64_t tensor_core_gemm;       /* 1: tcgen05 3xTF32 projections, 0: FFMA    */
+  int64_t norm_fold;              /* 1: RMSNorms folded into the GEMMs         */
 } rtr_report;
 int rtr_get_report(const rtr_session* s, rtr_report* out);
 

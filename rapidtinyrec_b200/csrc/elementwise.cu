@@ -10,7 +10,8 @@ namespace rtr {
 
 // ---------------------------------------------------------------- embedding
 __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* table, int vocab,
-                             int hidden, float* x, uint32_t* status) {
+                             int hidden, float* x, uint32_t* status, float* x_big, float* x_small, float* ss,
+                             int ss_ld) {
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
@@ -21,12 +22,33 @@ __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* ta
   }
   const float4* src = reinterpret_cast<const float4*>(table + (long)tok * hidden);
   float4* dst = reinterpret_cast<float4*>(x + (long)m * hidden);
-  for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) dst[i] = src[i];
+  if (!x_big) {
+    for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) dst[i] = src[i];
+    return;
+  }
+  // warp w takes 128-column chunks w, w + warps, ...: copy, split and the
+  // chunk's sum of squares (lane sums of 4 squares, then a shuffle tree)
+  const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  float4* big = reinterpret_cast<float4*>(x_big + (long)m * hidden);
+  float4* small = reinterpret_cast<float4*>(x_small + (long)m * hidden);
+  for (int chunk = threadIdx.x >> 5; chunk < hidden / 128; chunk += warps) {
+    const int i = chunk * 32 + lane;
+    const float4 v = src[i];
+    dst[i] = v;
+    const float4 b = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
+    big[i] = b;
+    small[i] = make_float4(v.x - b.x, v.y - b.y, v.z - b.z, v.w - b.w);
+    const float sq = warp_sum((v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w));
+    if (lane == 0 && ss) ss[(long)chunk * ss_ld + m] = sq;
+  }
 }
 
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
-                       int hidden, float* x, uint32_t* status, cudaStream_t stream) {
-  return launch_pdl(PDL_EMBED, embed_kernel, dim3(M), dim3(128), 0, stream, ids, ids_stride, table, vocab, hidden, x, status);
+                       int hidden, float* x, uint32_t* status, cudaStream_t stream, float* x_big, float* x_small,
+                       float* ss, int ss_ld) {
+  if (x_big && (hidden % 128 || !x_small)) return cudaErrorInvalidValue;
+  return launch_pdl(PDL_EMBED, embed_kernel, dim3(M), dim3(128), 0, stream, ids, ids_stride, table, vocab, hidden, x,
+                    status, x_big, x_small, ss, ss_ld);
 }
 
 // ------------------------------------------------------------------ RMSNorm

@@ -25,6 +25,20 @@ struct RopeArgs {
   const int32_t* L_dev;    // decode: prefix length (position = *L_dev + slot)
 };
 
+// RMSNorm folded into the projection GEMMs (3xTF32 path): the norm weight is
+// folded into the packed weight's columns, the producer of the residual stream
+// (embedding, o_proj / down_proj epilogues) writes x's tf32 split and per-row
+// partial sums of squares over 128-column chunks (ss[chunk * ld + row]), and
+// the consuming GEMM scales each output row by 1 / sqrt(sum / hidden + eps).
+struct NormFold {
+  float* ss_out;           // producer (EPI_RESID): partial sums of squares of the new x
+  const float* ss_in;      // consumer: partials of the GEMM's input rows
+  int ld;                  // row stride of a chunk's partials (rows capacity)
+  int parts;               // chunks per row (hidden / 128)
+  int hidden;
+  float eps;
+};
+
 // ---- GEMM (gemm_ffma.cu) ----
 cudaError_t gemm_init();
 size_t gemm_workspace_floats(int max_m, int max_n, int sms);
@@ -41,19 +55,21 @@ bool make_tmap_f32(TensorMap* out, const float* base, long rows, long cols, long
 cudaError_t gemm_tc_init();
 // Weights are packed once into tile-contiguous blocks for the tensor-core GEMM.
 size_t packed_weight_floats(int N, int K);
-cudaError_t pack_weight_tiles(const float* src, int N, int K, float* dst, cudaStream_t stream);
+cudaError_t pack_weight_tiles(const float* src, int N, int K, float* dst, cudaStream_t stream,
+                              const float* col_scale = nullptr);  // W[n][k] * col_scale[k] when given
 bool make_tmap_packed(TensorMap* out, const float* packed, int N, int K);
 // Activations are consumed as a (big, small) pair: big = tf32(x), small = x - big.
 cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
                     float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                     size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
-                    bool pdl, const RopeArgs* rope = nullptr);
+                    bool pdl, const RopeArgs* rope = nullptr, const NormFold* fold = nullptr);
 // The same GEMM with 128 activation rows per CTA (gemm_tc_wide.cu): for M > 64.
 cudaError_t gemm_tc_wide_init();
 cudaError_t gemm_tc_wide(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
                          float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                          size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms,
-                         cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr);
+                         cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr,
+                         const NormFold* fold = nullptr);
 
 // ---- bf16 tensor-core GEMM (gemm_bf16.cu): the bf16 mode ----
 // X: bf16 activations [rows][K]; weights packed once into bf16 tile blocks.
@@ -69,8 +85,11 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
                       int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr);
 
 // ---- element-wise (elementwise.cu) ----
+// x = table[ids]; with x_big/x_small (optional) also x's tf32 split and, with
+// ss (optional), x's per-row partial sums of squares (NormFold layout).
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
-                       int hidden, float* x, uint32_t* status, cudaStream_t stream);
+                       int hidden, float* x, uint32_t* status, cudaStream_t stream, float* x_big = nullptr,
+                       float* x_small = nullptr, float* ss = nullptr, int ss_ld = 0);
 // h = w * (x * rsqrt(mean(x^2) + eps)); h_big/h_small (optional) get the tf32 split of h.
 cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big, float* h_small, int M, int hidden,
                           float eps, cudaStream_t stream);

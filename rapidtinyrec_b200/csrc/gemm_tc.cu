@@ -352,11 +352,12 @@ bool make_tmap_f32(TensorMap* out, const float* base, long rows, long cols, long
   return r == CUDA_SUCCESS;
 }
 
-// Weight layout for the tensor-core GEMM: W [N, K] becomes blocks
+// Weight layout for the tensor-core GEMM (optionally with an RMSNorm weight
+// folded into the columns: W[n][k] * col_scale[k]): W [N, K] becomes blocks
 // [N/128 tiles][K/32 chunks][128 rows][32 floats] (zero padded), so every TMA
 // load of a (tile, chunk) reads 16 KB of contiguous memory.
 __global__ void pack_tiles_kernel(const float* __restrict__ src, int N, int K, int nchunks, float* __restrict__ dst,
-                                  long total) {
+                                  long total, const float* __restrict__ col_scale) {
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
     const int k = (int)(i & 31);
     const int r = (int)((i >> 5) & 127);
@@ -364,7 +365,7 @@ __global__ void pack_tiles_kernel(const float* __restrict__ src, int N, int K, i
     const int c = (int)(blk % nchunks);
     const long t = blk / nchunks;
     const long row = t * TC_WROWS + r, col = (long)c * TC_KC + k;
-    dst[i] = (row < N && col < K) ? src[row * K + col] : 0.f;
+    dst[i] = (row < N && col < K) ? (col_scale ? src[row * K + col] * col_scale[col] : src[row * K + col]) : 0.f;
   }
 }
 
@@ -372,9 +373,9 @@ size_t packed_weight_floats(int N, int K) {
   return (size_t)((N + TC_WROWS - 1) / TC_WROWS) * ((K + TC_KC - 1) / TC_KC) * TC_WROWS * TC_KC;
 }
 
-cudaError_t pack_weight_tiles(const float* src, int N, int K, float* dst, cudaStream_t stream) {
+cudaError_t pack_weight_tiles(const float* src, int N, int K, float* dst, cudaStream_t stream, const float* col_scale) {
   const long total = (long)packed_weight_floats(N, K);
-  pack_tiles_kernel<<<148 * 8, 256, 0, stream>>>(src, N, K, (K + TC_KC - 1) / TC_KC, dst, total);
+  pack_tiles_kernel<<<148 * 8, 256, 0, stream>>>(src, N, K, (K + TC_KC - 1) / TC_KC, dst, total, col_scale);
   return cudaGetLastError();
 }
 
@@ -390,7 +391,7 @@ cudaError_t gemm_tc_init() {
 cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
                     float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                     size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
-                    bool pdl, const RopeArgs* rope) {
+                    bool pdl, const RopeArgs* rope, const NormFold* fold) {
   if (epi == EPI_SWIGLU && (!C_big || !C_small)) return cudaErrorInvalidValue;
   if (epi == EPI_ROPE) {
     // whole heads per 128-row tile, float4 pairs, q/k/v row layout
@@ -400,12 +401,15 @@ cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap
   }
   // float4 epilogue: column counts, row strides and bases in 16-byte units
   if (epi != EPI_ROPE && (N % 4 || ldc % 4 || (reinterpret_cast<uintptr_t>(C) & 15))) return cudaErrorInvalidValue;
+  if (fold && fold->ss_out && (epi != EPI_RESID || !C_big || !C_small || fold->parts * 128 != N)) return cudaErrorInvalidValue;
+  if (fold && fold->ss_in && (epi == EPI_RESID || fold->hidden != K)) return cudaErrorInvalidValue;
   const int tt = (M + TC_NTOK - 1) / TC_NTOK, wt = (N + TC_WROWS - 1) / TC_WROWS;
   const int nchunks = (K + TC_KC - 1) / TC_KC;
   int splits = tc_split_count(tt * wt, nchunks, sms);
   while (splits > 1 && ((size_t)splits * tt * wt * TC_NTOK * TC_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
-  TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
+  TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}, {}};
   if (rope) p.rope = *rope;
+  if (fold) p.fold = *fold;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tt, wt, splits);
   cfg.blockDim = dim3(TC_THREADS);

@@ -318,7 +318,7 @@ cudaError_t gemm_tc_wide_init() {
 cudaError_t gemm_tc_wide(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
                          float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                          size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms,
-                         cudaStream_t stream, bool pdl, const RopeArgs* rope) {
+                         cudaStream_t stream, bool pdl, const RopeArgs* rope, const NormFold* fold) {
   if (epi == EPI_SWIGLU && (!C_big || !C_small)) return cudaErrorInvalidValue;
   if (epi == EPI_ROPE) {
     if (!rope || !bias || (rope->head_dim != 64 && rope->head_dim != 128) ||
@@ -326,12 +326,15 @@ cudaError_t gemm_tc_wide(const TensorMap& tmW, const TensorMap& tmXb, const Tens
       return cudaErrorInvalidValue;
   }
   if (epi != EPI_ROPE && (N % 4 || ldc % 4 || (reinterpret_cast<uintptr_t>(C) & 15))) return cudaErrorInvalidValue;
+  if (fold && fold->ss_out && (epi != EPI_RESID || !C_big || !C_small || fold->parts * 128 != N)) return cudaErrorInvalidValue;
+  if (fold && fold->ss_in && (epi == EPI_RESID || fold->hidden != K)) return cudaErrorInvalidValue;
   const int tt = (M + TW_NTOK - 1) / TW_NTOK, wt = (N + TW_WROWS - 1) / TW_WROWS;
   const int nchunks = (K + TW_KC - 1) / TW_KC;
   int splits = tc_split_count(tt * wt, nchunks, sms);
   while (splits > 1 && ((size_t)splits * tt * wt * TW_NTOK * TW_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
-  TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
+  TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}, {}};
   if (rope) p.rope = *rope;
+  if (fold) p.fold = *fold;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tt, wt, splits);
   cfg.blockDim = dim3(TW_THREADS);

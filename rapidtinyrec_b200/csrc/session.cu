@@ -44,6 +44,12 @@ struct rtr_session {
   bool pdl = true;
   bool use_tc = true;  // tcgen05 GEMMs (RTR_GEMM=ffma selects the FFMA kernel)
   bool tc_wide = true;  // 128-row tcgen05 GEMM for M > 64 (RTR_TC_WIDE=0: the 64-row kernel only)
+  // RMSNorm folded into the 3xTF32 GEMMs (fp32 tensor-core path, hidden % 128 == 0;
+  // RTR_NORM_FOLD=0 keeps the separate norm kernels): norm weights folded into the
+  // packed q/k/v, gate/up and LM-head columns, row scales from partial sums of squares
+  bool fold = false;
+  float *x_big = nullptr, *x_small = nullptr, *ss = nullptr;  // split and partials of the residual stream
+  int ss_ld = 0;
   // bf16 mode (RTR_DTYPE_BF16): bf16 weights, activations and KV; biases and
   // norm weights as bf16 values in fp32; logits in fp32.  The activation and
   // KV buffers below keep their float pointers and hold bf16 elements.
@@ -187,6 +193,8 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(gemm_bf16_init());
   if (const char* g = std::getenv("RTR_GEMM")) s->use_tc = std::strcmp(g, "ffma") != 0;
   if (const char* g = std::getenv("RTR_TC_WIDE")) s->tc_wide = std::strcmp(g, "0") != 0;
+  s->fold = s->use_tc && c.dtype != RTR_DTYPE_BF16 && c.hidden % 128 == 0;
+  if (const char* g = std::getenv("RTR_NORM_FOLD")) s->fold = s->fold && std::strcmp(g, "0") != 0;
   s->pdl = pdl_on(PDL_GEMM);
   s->bf16 = c.dtype == RTR_DTYPE_BF16;
   if (s->bf16 && !s->use_tc) {
@@ -251,6 +259,12 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
     CREATE_TRY(dev_alloc(s, &s->act_big, M * I));
     CREATE_TRY(dev_alloc(s, &s->act_small, M * I));
   }
+  if (s->fold) {
+    CREATE_TRY(dev_alloc(s, &s->x_big, M * H));
+    CREATE_TRY(dev_alloc(s, &s->x_small, M * H));
+    s->ss_ld = (int)M;
+    CREATE_TRY(dev_alloc(s, &s->ss, (H / 128) * M));
+  }
   CREATE_TRY(dev_alloc(s, &s->logits, B * V));
   long max_n = qkvd;
   if (H > max_n) max_n = H;
@@ -287,9 +301,10 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   // TMA descriptors of the GEMM activation operands: the big and small halves
   // (bf16 mode: the bf16 buffers themselves)
   struct Act { const float* v; float* big; float* small; long width; };
-  const Act acts[3] = {{s->h, s->h_big, s->h_small, H}, {s->attn, s->attn_big, s->attn_small, qd},
-                       {s->act, s->act_big, s->act_small, I}};
+  const Act acts[4] = {{s->h, s->h_big, s->h_small, H}, {s->attn, s->attn_big, s->attn_small, qd},
+                       {s->act, s->act_big, s->act_small, I}, {s->x, s->x_big, s->x_small, H}};
   for (const auto& a : acts) {
+    if (a.v == s->x && !s->fold) continue;
     if (s->bf16) {
       TensorMap m;
       if (!make_tmap_bf16(&m, a.v, M, a.width, a.width, 64)) {
@@ -463,7 +478,7 @@ int rtr_load_weights(rtr_session* s, const void* const* tensors, int32_t n_tenso
   // Tensor-core GEMM operands: every weight matrix packed into tile-contiguous
   // blocks (allocated once), with its TMA descriptor keyed by the original matrix
   if (s->use_tc) {
-    auto wmap = [&](const float* w, long rows, long cols) -> cudaError_t {
+    auto wmap = [&](const float* w, long rows, long cols, const float* col_scale = nullptr) -> cudaError_t {
       float* packed = nullptr;
       auto it = s->packed.find(w);
       if (it == s->packed.end()) {
@@ -473,19 +488,20 @@ int rtr_load_weights(rtr_session* s, const void* const* tensors, int32_t n_tenso
       } else {
         packed = it->second;
       }
-      cudaError_t e = pack_weight_tiles(w, (int)rows, (int)cols, packed, 0);
+      cudaError_t e = pack_weight_tiles(w, (int)rows, (int)cols, packed, 0, col_scale);
       if (e != cudaSuccess) return e;
       TensorMap m;
       if (!make_tmap_packed(&m, packed, (int)rows, (int)cols)) return cudaErrorInvalidValue;
       s->tmaps[{w, 128}] = m;
       return cudaSuccess;
     };
-    CUDA_TRY(s, wmap(s->lm_head, V, H));
+    // with the norm fold, the LM head, q/k/v and gate/up carry their norm's weight
+    CUDA_TRY(s, wmap(s->lm_head, V, H, s->fold ? s->norm_final : nullptr));
     for (int l = 0; l < c.layers; ++l) {
       const LayerW& w = s->layers[l];
-      CUDA_TRY(s, wmap(w.wqkv, qd + 2 * kvd, H));
+      CUDA_TRY(s, wmap(w.wqkv, qd + 2 * kvd, H, s->fold ? w.n_in : nullptr));
       CUDA_TRY(s, wmap(w.wo, H, qd));
-      CUDA_TRY(s, wmap(w.wgu, 2 * I, H));
+      CUDA_TRY(s, wmap(w.wgu, 2 * I, H, s->fold ? w.n_post : nullptr));
       CUDA_TRY(s, wmap(w.wd, H, I));
     }
     CUDA_TRY(s, cudaDeviceSynchronize());
@@ -555,7 +571,8 @@ int rtr_load_constraints(rtr_session* s, const rtr_constraint_tables* t) {
 // Projection GEMM: the tcgen05 3xTF32 kernel on the tf32 split of activation
 // buffer A and the weight matrix W (the FFMA kernel when RTR_GEMM=ffma).
 static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W, float* C, int ldc,
-                        const float* bias, int M, int N, int K, int epi, const RopeArgs* rope = nullptr) {
+                        const float* bias, int M, int N, int K, int epi, const RopeArgs* rope = nullptr,
+                        const NormFold* fold = nullptr) {
   if (s->use_tc) {
     auto sp = s->split_of.find(A);
     if (sp == s->split_of.end()) return cudaErrorInvalidValue;
@@ -565,7 +582,7 @@ static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W,
     if (xb == s->tmaps.end() || xs == s->tmaps.end() || w == s->tmaps.end()) return cudaErrorInvalidValue;
     float* cb = nullptr;
     float* cs = nullptr;
-    if (epi == EPI_SWIGLU) {
+    if (epi == EPI_SWIGLU || (fold && fold->ss_out)) {
       auto out = s->split_of.find(C);
       if (out == s->split_of.end()) return cudaErrorInvalidValue;
       cb = out->second.first;
@@ -574,9 +591,9 @@ static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W,
     // more than 64 rows (the prefill): one 128-row MMA per instruction instead of two 64-row ones
     if (M > 64 && s->tc_wide)
       return gemm_tc_wide(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws,
-                          s->ws_floats, s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope);
+                          s->ws_floats, s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope, fold);
     return gemm_tc(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws, s->ws_floats,
-                   s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope);
+                   s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope, fold);
   }
   return gemm_f32(A, lda, W, C, ldc, bias, M, N, K, epi, s->ws, s->ws_floats, s->tickets, s->sms,
                   s->stream, s->pdl);
@@ -658,6 +675,41 @@ static cudaError_t forward(rtr_session* s, int t) {
   const float scale = (float)std::pow((double)D, -0.5);
   cudaStream_t st = s->stream;
   const int32_t* ids = t == 0 ? s->d_ids : &s->beam->next_tok[0];
+  if (s->fold) {
+    // RMSNorm folded into the GEMMs: the residual stream's producers write x, its
+    // split and partial sums of squares; q/k/v, gate/up and the LM head scale rows
+    const NormFold in{nullptr, s->ss, s->ss_ld, H / 128, H, c.rms_eps};
+    const NormFold out{s->ss, nullptr, s->ss_ld, H / 128, H, c.rms_eps};
+    FWD_TRY(embed_rows(ids, 1, M, s->embed, V, H, s->x, s->d_status, st, s->x_big, s->x_small, s->ss, s->ss_ld));
+    for (int l = 0; l < c.layers; ++l) {
+      const LayerW& w = s->layers[l];
+      float* kp = s->kv_prefix + (size_t)l * 2 * kvd * cap;
+      float* vp = kp + (size_t)kvd * cap;
+      float* ks = s->kv_suffix + (size_t)l * 2 * 4 * B * kvd;
+      float* vs = ks + (size_t)4 * B * kvd;
+      const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * kvd;
+      const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
+                        t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L};
+      FWD_TRY(gemm(s, s->x, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra, &in));
+      if (t == 0) {
+        FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
+                                  scale, false, st));
+      } else {
+        FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
+                                 s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st));
+      }
+      FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID, nullptr, &out));
+      FWD_TRY(gemm(s, s->x, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU, nullptr, &in));
+      FWD_TRY(gemm(s, s->act, I, w.wd, s->x, H, nullptr, M, H, I, EPI_RESID, nullptr, &out));
+    }
+    if (t == 0) {  // the prefill's last row: explicit norm and the unfolded LM head (GEMV)
+      FWD_TRY(rms_norm_rows(s->x + (size_t)(M - 1) * H, s->norm_final, s->h, nullptr, nullptr, 1, H, c.rms_eps, st));
+      FWD_TRY(gemv_f32(s->h, s->lm_head, s->logits, V, H, st));
+    } else {
+      FWD_TRY(gemm(s, s->x, H, s->lm_head, s->logits, V, nullptr, B, V, H, EPI_STORE, nullptr, &in));
+    }
+    return cudaSuccess;
+  }
   FWD_TRY(embed_rows(ids, 1, M, s->embed, V, H, s->x, s->d_status, st));
   for (int l = 0; l < c.layers; ++l) {
     const LayerW& w = s->layers[l];
@@ -720,8 +772,11 @@ static int ready(rtr_session* s) {
 // Kernels one forward pass launches: embedding, per layer RMSNorm, q/k/v GEMM,
 // RoPE + cache write (fused into the q/k/v GEMM on the tensor-core path),
 // attention, o GEMM, RMSNorm, gate/up GEMM, down GEMM; then the final RMSNorm
-// and the LM head.  The step tail is 4 (max, two sums, beam selection).
-static int64_t forward_kernels(const rtr_session* s) {
+// and the LM head.  With the norm fold the per-layer RMSNorms vanish and the
+// decode step's final norm lives in the LM-head GEMM (the prefill keeps it for
+// its one-row GEMV).  The step tail is 4 (max, two sums, beam selection).
+static int64_t forward_kernels(const rtr_session* s, bool prefill) {
+  if (s->fold) return 1 + 5 * (int64_t)s->cfg.layers + (prefill ? 2 : 1);
   return 1 + (s->use_tc ? 7 : 8) * (int64_t)s->cfg.layers + 2;
 }
 static constexpr int64_t kTailKernels = 4;
@@ -741,7 +796,7 @@ static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t 
   CUDA_TRY(s, beam_reset(s->beam, s->d_ids, s->d_L, beams_of(s), s->stream));
   CUDA_TRY(s, forward(s, 0));
   CUDA_TRY(s, beam_step(s->beam, s->logits, 1, s->cfg.vocab, beams_of(s), 0, s->tb, s->d_status, s->stream));
-  s->launches += 1 + forward_kernels(s) + kTailKernels;  // beam_reset, forward, step tail
+  s->launches += 1 + forward_kernels(s, true) + kTailKernels;  // beam_reset, forward, step tail
   s->steps_done = 0;
   s->in_flight = false;
   return RTR_OK;
@@ -781,7 +836,7 @@ int rtr_decode_step(rtr_session* s, int32_t t) {
   if (s->steps_done != t - 1) return fail(s, RTR_ERR_STATE, "decode steps must follow prefill in order");
   CUDA_TRY(s, cudaSetDevice(s->device));
   CUDA_TRY(s, decode_and_tail(s, t));
-  s->launches += forward_kernels(s) + kTailKernels;
+  s->launches += forward_kernels(s, false) + kTailKernels;
   s->steps_done = t;
   return RTR_OK;
 }
@@ -868,7 +923,8 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   out->requests = s->requests;
   out->kernel_launches = s->launches;
   // beam_reset + NSTEPS x (forward + step tail) + beam_finalize
-  out->launches_per_request = 1 + NSTEPS * (forward_kernels(s) + kTailKernels) + 1;
+  out->launches_per_request =
+      1 + forward_kernels(s, true) + (NSTEPS - 1) * forward_kernels(s, false) + NSTEPS * kTailKernels + 1;
   out->graph_kernel_nodes = s->graph_kernels;
   out->prefix_bytes_written = (int64_t)c.layers * 2 * kvd * s->L * (int64_t)sizeof(float);
   out->prefix_bytes_reordered = 0;
@@ -879,6 +935,7 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   out->h2d_bytes_per_request = (int64_t)s->L * 4 + 4;
   out->d2h_bytes_per_request = (int64_t)sizeof(DevResult);
   out->tensor_core_gemm = s->use_tc ? 1 : 0;
+  out->norm_fold = s->fold ? 1 : 0;
   return RTR_OK;
 }
 

@@ -18,6 +18,7 @@ struct TcParams {
   int* tickets;
   uint32_t* status;
   RopeArgs rope;    // EPI_ROPE only
+  NormFold fold;    // ss_in: scale rows by their RMS factor; ss_out: EPI_RESID partials
 };
 
 
@@ -77,13 +78,30 @@ RTR_DEVICE void splitk_sum(const TcParams& p, float4* red4, int rows, int cols4,
 // dimension are multiples of 4; checked by the host).
 template <int THREADS>
 RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, int tok0, int n0, int rows, int cols4) {
+  // RMSNorm folded into this GEMM: row scale 1 / sqrt(mean(x^2) + eps) from
+  // the producer's partial sums of squares, summed in chunk order
+  __shared__ float rsc[128];
+  const bool scaled = p.fold.ss_in != nullptr;
+  if (scaled) {
+    for (int j = threadIdx.x; j < rows; j += THREADS) {
+      float ss = 0.f;
+      for (int t = 0; t < p.fold.parts; ++t) ss += p.fold.ss_in[(long)t * p.fold.ld + tok0 + j];
+      rsc[j] = 1.0f / sqrtf(ss / (float)p.fold.hidden + p.fold.eps);
+    }
+    __syncthreads();
+  }
+  auto row_scale = [&](float4 v, int j) {
+    if (!scaled) return v;
+    const float r = rsc[j];
+    return make_float4(v.x * r, v.y * r, v.z * r, v.w * r);
+  };
   if (p.epi == EPI_SWIGLU) {
     // packed rows: 32 q + [0,16) gate, 32 q + [16,32) up of intermediate 16 q + [0,16)
     for (int q = threadIdx.x; q < rows * 16; q += THREADS) {
       const int j = q >> 4, blk = (q >> 2) & 3, g4 = q & 3;
       const int c4 = blk * 8 + g4;
       if (c4 + 4 >= cols4) continue;  // the up half lies past N
-      const float4 g = red4[j * ld4 + c4], u = red4[j * ld4 + c4 + 4];
+      const float4 g = row_scale(red4[j * ld4 + c4], j), u = row_scale(red4[j * ld4 + c4 + 4], j);
       float a[4] = {silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w};
       float b[4], sm[4];
 #pragma unroll
@@ -107,10 +125,11 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
       if (c4 >= cols4) continue;
       const int col = n0 + c4 * 4, m = tok0 + j;
       const int h = col / D, d = col % D;
-      float4 v = f4add(red4[j * ld4 + c4], *reinterpret_cast<const float4*>(p.bias + col));
+      float4 v = f4add(row_scale(red4[j * ld4 + c4], j), *reinterpret_cast<const float4*>(p.bias + col));
       if (h < r.heads + r.kv_heads) {
         const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
-        const float4 pv = f4add(red4[j * ld4 + pc4], *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4));
+        const float4 pv =
+            f4add(row_scale(red4[j * ld4 + pc4], j), *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4));
         int pos = r.slot < 0 ? m : base_pos;
         if (pos < 0 || pos >= r.positions) {
           atomicOr(p.status, RTR_DEV_BAD_LENGTH);
@@ -134,10 +153,30 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
     }
     return;
   }
+  if (p.epi == EPI_RESID && p.fold.ss_out) {
+    // x += y, its tf32 split, and the row's sum of squares over this 128-column
+    // tile (a warp holds one row: lane = float4 column)
+    for (int q = threadIdx.x; q < rows * 32; q += THREADS) {
+      const int j = q >> 5, c4 = q & 31;
+      const bool ok = c4 < cols4;
+      const long o = (long)(tok0 + j) * p.ldc + n0 + c4 * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (ok) {
+        v = f4add(*reinterpret_cast<const float4*>(p.C + o), red4[j * ld4 + c4]);
+        *reinterpret_cast<float4*>(p.C + o) = v;
+        const float4 b = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
+        *reinterpret_cast<float4*>(p.C_big + o) = b;
+        *reinterpret_cast<float4*>(p.C_small + o) = make_float4(v.x - b.x, v.y - b.y, v.z - b.z, v.w - b.w);
+      }
+      const float sq = warp_sum((v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w));
+      if (c4 == 0) p.fold.ss_out[(long)(n0 >> 7) * p.fold.ld + tok0 + j] = sq;
+    }
+    return;
+  }
   for (int q = threadIdx.x; q < rows * 32; q += THREADS) {
     const int j = q >> 5, c4 = q & 31;
     if (c4 >= cols4) continue;
-    float4 v = red4[j * ld4 + c4];
+    float4 v = row_scale(red4[j * ld4 + c4], j);
     const int col = n0 + c4 * 4;
     float4* c = reinterpret_cast<float4*>(p.C + (long)(tok0 + j) * p.ldc + col);
     if (p.epi == EPI_BIAS) v = f4add(v, *reinterpret_cast<const float4*>(p.bias + col));

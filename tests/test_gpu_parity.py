@@ -188,11 +188,16 @@ def test_report_counts_match_the_captured_graph(tiny_engine, tiny):
     tiny_engine.generate(tiny['users'][0].prompt_token_ids)
     rep = tiny_engine.report()
     cfg = tiny['cfg']
-    forward = 1 + 7 * cfg.layers + 2          # embed, 7 per layer (RoPE fused), final norm, LM head
+    if rep['norm_fold']:
+        # embed, 5 per layer (norms folded into q/k/v and gate/up, RoPE into q/k/v),
+        # LM head (final norm folded) / the prefill's final norm + GEMV
+        decode, prefill = 1 + 5 * cfg.layers + 1, 1 + 5 * cfg.layers + 2
+    else:
+        decode = prefill = 1 + 7 * cfg.layers + 2  # embed, 7 per layer (RoPE fused), final norm, LM head
     tail = 4                                  # max, two sums, beam selection
-    assert rep['graph_kernel_nodes'] == 4 * (forward + tail) + 1   # decode steps 1-4, finalize
-    assert rep['launches_per_request'] == 1 + forward + tail + rep['graph_kernel_nodes']
-    assert rep['tensor_core_gemm'] == 1
+    assert rep['graph_kernel_nodes'] == 4 * (decode + tail) + 1   # decode steps 1-4, finalize
+    assert rep['launches_per_request'] == 1 + prefill + tail + rep['graph_kernel_nodes']
+    assert rep['tensor_core_gemm'] == 1 and rep['norm_fold'] == 1
 
 
 def test_contract_violations_raise(tiny_engine, tiny):
