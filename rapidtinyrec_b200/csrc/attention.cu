@@ -216,6 +216,27 @@ cudaError_t attention_prefill(const void* q, const void* k_prefix, const void* v
 }
 
 // ------------------------------------------------------------------- decode
+// One CTA per (query head, 8 beams); the prefix's 64-key chunks stream through
+// a double-buffered shared ring (cp.async).  Shared-memory wavefronts bound
+// this kernel (a 128-bit LDS costs 4 of them whatever its reuse), so each
+// phase tiles registers to load every element once per many FMAs:
+//   A  scores: warp w takes a slice of head_dim/8 dimensions; lane = 4 beams x
+//      4 keys (keys kg, kg+16, kg+32, kg+48), 16 partial dot products;
+//   B  warp = beam: sums the 8 warps' partials of its 64 scores, online
+//      softmax (m, l stay in this warp's registers);
+//   C  warp w takes keys 8w..8w+7; lane = head_dim/32 output dimensions x 8
+//      beams, accumulated across chunks and summed over the warps at the end.
+// The beams' suffix rows (found through the ancestry table, the direct-reorder
+// parent gather) are staged at the start and folded in by warp = beam.
+constexpr int DQLD_PAD = 4;           // q rows: float4 columns of 8 beams in distinct banks
+constexpr int DSLD = AK + 4;          // partial-score rows: the two beam halves 16 banks apart
+
+template <int HD, typename T>
+constexpr size_t decode_smem_bytes() {
+  return (size_t)(2 * AK * kld<HD, T>() + 2 * AK * HD + 2 * DBEAMS * 4 * HD) * sizeof(T) +
+         (size_t)(DBEAMS * (HD + DQLD_PAD) + AWARPS * DBEAMS * DSLD + DBEAMS * AK + DBEAMS * 8) * sizeof(float);
+}
+
 template <int HD, typename T>
 __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     const T* __restrict__ q, const T* __restrict__ kp, const T* __restrict__ vp,
@@ -223,17 +244,23 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     const int32_t* __restrict__ L_dev, T* __restrict__ out, float* __restrict__ out_big,
     float* __restrict__ out_small, int beams, int cap, int heads, int kv_heads, int t, float scale,
     uint32_t* __restrict__ status) {
-  constexpr int VEC = HD / 32;
+  constexpr int VEC = HD / 32, QLD = HD + DQLD_PAD, E = 16 / (int)sizeof(T);
+  constexpr int AD4 = HD / 4 / AWARPS;  // float4 columns per warp in phase A
+  static_assert(DBEAMS == 8 && AWARPS == 8 && AK == 64, "tiling assumes 8 beams, 8 warps, 64-key chunks");
   pdl_launch_dependents();
   pdl_wait();
   extern __shared__ __align__(16) unsigned char asmem[];
   T* kbuf = reinterpret_cast<T*>(asmem);
   T* vbuf = kbuf + 2 * AK * kld<HD, T>();
-  float* qs = reinterpret_cast<float*>(vbuf + 2 * AK * HD);  // [DBEAMS][HD]
+  T* sufk = vbuf + 2 * AK * HD;                                  // [DBEAMS][4][HD]
+  T* sufv = sufk + DBEAMS * 4 * HD;
+  float* qs = reinterpret_cast<float*>(sufv + DBEAMS * 4 * HD);  // [DBEAMS][QLD]
+  float* part = qs + DBEAMS * QLD;                               // [AWARPS][DBEAMS][DSLD] partial scores
+  float* pr = part + AWARPS * DBEAMS * DSLD;                     // [DBEAMS][AK] probabilities
+  float* corr_s = pr + DBEAMS * AK;                              // [DBEAMS]
   const int h = blockIdx.x, g = h / (heads / kv_heads);
   const int b0 = blockIdx.y * DBEAMS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int b = b0 + warp;
   int L = *L_dev;
   if (L < 1 || L > cap) {  // the prefill recorded no valid prefix: attend to the suffix only
     if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
@@ -243,57 +270,159 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   const T* vbase = vp + (long)g * cap * HD;
   const int nchunks = (L + AK - 1) / AK;
 
+  // the suffix rows of the 8 beams (slot s < t - 1: row anc[b][s]; slot t - 1: row b)
+  for (int i = threadIdx.x; i < DBEAMS * 4 * (HD / E); i += ATHREADS) {
+    const int bb = i / (4 * (HD / E)), sl = (i / (HD / E)) % 4, d = (i % (HD / E)) * E;
+    const int b = b0 + bb;
+    if (b >= beams || sl >= t) continue;
+    int row = (sl == t - 1) ? b : anc[b * 4 + sl];
+    if (row < 0 || row >= beams) {
+      if (d == 0) atomicOr(status, RTR_DEV_BAD_PARENT);
+      row = b;
+    }
+    const long off = (((long)sl * beams + row) * kv_heads + g) * HD + d;
+    cp_async16(sufk + (bb * 4 + sl) * HD + d, ksuf + off, true);
+    cp_async16(sufv + (bb * 4 + sl) * HD + d, vsuf + off, true);
+  }
+  cp_async_commit();
   if (nchunks > 0) load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, 0, L, 0);
+  else cp_async_commit();
   for (int i = threadIdx.x; i < DBEAMS * HD / 4; i += ATHREADS) {
     const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (b0 + r < beams) v = ld4f(q + ((long)(b0 + r) * heads + h) * HD + d);
-    *reinterpret_cast<float4*>(qs + r * HD + d) = v;
+    *reinterpret_cast<float4*>(qs + r * QLD + d) = v;
   }
-  float m = -INFINITY, l = 0.f, acc[VEC];
+  const int abg = lane >> 4, akg = lane & 15;  // phase A: beams 4abg.., keys akg + 16j
+  float m = -INFINITY, l = 0.f;                // phase B state of beam `warp`
+  float acc[DBEAMS][VEC];                      // phase C: this warp's keys, dimensions lane*VEC..
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) acc[i] = 0.f;
+  for (int b = 0; b < DBEAMS; ++b)
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) acc[b][i] = 0.f;
+
   for (int c = 0; c < nchunks; ++c) {
     if (c + 1 < nchunks) load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, (c + 1) * AK, L, (c + 1) & 1);
     else cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    if (b < beams)
-      chunk_update<HD, T>(qs + warp * HD, kbuf + (c & 1) * AK * kld<HD, T>(), vbuf + (c & 1) * AK * HD, c * AK, L, scale,
-                       m, l, acc);
+    const T* kc = kbuf + (c & 1) * AK * kld<HD, T>();
+    const T* vc = vbuf + (c & 1) * AK * HD;
+    {  // A: 4 beams x 4 keys over this warp's dimension slice
+      float ps[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ps[i][j] = 0.f;
+#pragma unroll
+      for (int u = 0; u < AD4; ++u) {
+        const int d = (warp * AD4 + u) * 4;
+        float4 qq[4], kk[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) qq[i] = *reinterpret_cast<const float4*>(qs + (4 * abg + i) * QLD + d);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) kk[j] = ld4f(kc + (akg + 16 * j) * kld<HD, T>() + d);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            ps[i][j] = fmaf(qq[i].x, kk[j].x, ps[i][j]);
+            ps[i][j] = fmaf(qq[i].y, kk[j].y, ps[i][j]);
+            ps[i][j] = fmaf(qq[i].z, kk[j].z, ps[i][j]);
+            ps[i][j] = fmaf(qq[i].w, kk[j].w, ps[i][j]);
+          }
+      }
+      float* pw = part + warp * DBEAMS * DSLD;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) pw[(4 * abg + i) * DSLD + akg + 16 * j] = ps[i][j];
+    }
+    __syncthreads();
+    {  // B: beam `warp`, keys lane and lane + 32; partials summed in warp order
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int w = 0; w < AWARPS; ++w) {
+        s0 += part[(w * DBEAMS + warp) * DSLD + lane];
+        s1 += part[(w * DBEAMS + warp) * DSLD + lane + 32];
+      }
+      const int k0 = c * AK;
+      s0 = k0 + lane < L ? s0 * scale : -INFINITY;
+      s1 = k0 + lane + 32 < L ? s1 * scale : -INFINITY;
+      const float mn = fmaxf(m, warp_max(fmaxf(s0, s1)));  // finite: key k0 is always valid
+      const float corr = expf(m - mn);
+      const float p0 = expf(s0 - mn), p1 = expf(s1 - mn);
+      l = l * corr + warp_sum(p0 + p1);
+      m = mn;
+      pr[warp * AK + lane] = p0;
+      pr[warp * AK + lane + 32] = p1;
+      if (lane == 0) corr_s[warp] = corr;
+    }
+    __syncthreads();
+    {  // C: acc = acc * corr + P.V over keys 8 warp .. 8 warp + 7
+#pragma unroll
+      for (int b = 0; b < DBEAMS; ++b) {
+        const float cr = corr_s[b];
+#pragma unroll
+        for (int i = 0; i < VEC; ++i) acc[b][i] *= cr;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int key = warp * 8 + k;
+        float x[VEC];
+        load_vec(vc + key * HD + lane * VEC, x);
+#pragma unroll
+        for (int b = 0; b < DBEAMS; ++b) {
+          const float p = pr[b * AK + key];  // broadcast
+#pragma unroll
+          for (int i = 0; i < VEC; ++i) acc[b][i] = fmaf(p, x[i], acc[b][i]);
+        }
+      }
+    }
     __syncthreads();  // the slot is refilled by the next iteration's load
   }
-  if (nchunks == 0) __syncthreads();  // q rows staged
-  if (b >= beams) return;
-
-  // the beam's suffix: slot s < t - 1 lives in row anc[b][s], slot t - 1 in row b
-  const float* qrow = qs + warp * HD + lane * VEC;
+  cp_async_wait<0>();
+  // sum the warps' P.V partials (the K ring is free now): beam `warp`, dims lane*VEC..
+  float* red = reinterpret_cast<float*>(kbuf);  // [AWARPS][DBEAMS][HD]
+#pragma unroll
+  for (int b = 0; b < DBEAMS; ++b)
+#pragma unroll
+    for (int i = 0; i < VEC; ++i) red[(warp * DBEAMS + b) * HD + lane * VEC + i] = acc[b][i];
+  __syncthreads();
+  float a[VEC];
+#pragma unroll
+  for (int i = 0; i < VEC; ++i) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < AWARPS; ++w) v += red[(w * DBEAMS + warp) * HD + lane * VEC + i];
+    a[i] = v;
+  }
+  // the beam's suffix keys, then the output
+  const int b = b0 + warp;
   float qv[VEC];
 #pragma unroll
-  for (int i = 0; i < VEC; ++i) qv[i] = qrow[i];
-  for (int s = 0; s < t; ++s) {
-    int row = (s == t - 1) ? b : anc[b * 4 + s];
-    if (row < 0 || row >= beams) {
-      if (lane == 0) atomicOr(status, RTR_DEV_BAD_PARENT);
-      row = b;
-    }
-    const long off = (((long)s * beams + row) * kv_heads + g) * HD + lane * VEC;
+  for (int i = 0; i < VEC; ++i) qv[i] = qs[warp * QLD + lane * VEC + i];
+  for (int sl = 0; sl < t; ++sl) {
+    float kx[VEC], vx[VEC];
+    load_vec(sufk + (warp * 4 + sl) * HD + lane * VEC, kx);
+    load_vec(sufv + (warp * 4 + sl) * HD + lane * VEC, vx);
     float d = 0.f;
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) d = fmaf(qv[i], to_f32(ksuf[off + i]), d);
-    const float sc = warp_sum(d) * scale;
-    const float mn = fmaxf(m, sc);
+    for (int i = 0; i < VEC; ++i) d = fmaf(qv[i], kx[i], d);
+    const float sk = warp_sum(d) * scale;
+    const float mn = fmaxf(m, sk);
     const float corr = expf(m - mn);
-    const float p = expf(sc - mn);
+    const float p = expf(sk - mn);
     l = l * corr + p;
     m = mn;
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] = fmaf(p, to_f32(vsuf[off + i]), acc[i] * corr);
+    for (int i = 0; i < VEC; ++i) a[i] = fmaf(p, vx[i], a[i] * corr);
   }
-  const float inv = 1.0f / l;
+  if (b < beams) {
+    const float inv = 1.0f / l;
 #pragma unroll
-  for (int i = 0; i < VEC; ++i)
-    store_out(out, out_big, out_small, ((long)b * heads + h) * HD + lane * VEC + i, acc[i] * inv);
+    for (int i = 0; i < VEC; ++i) store_out(out, out_big, out_small, ((long)b * heads + h) * HD + lane * VEC + i, a[i] * inv);
+  }
 }
 
 template <int HD, typename T>
@@ -302,7 +431,7 @@ static cudaError_t launch_decode(const void* q, const void* kp, const void* vp, 
                                  int beams, int cap, int heads, int kv_heads, float scale, uint32_t* status,
                                  cudaStream_t stream) {
   dim3 grid(heads, (beams + DBEAMS - 1) / DBEAMS);
-  return launch_pdl(PDL_ATTN, decode_attn_kernel<HD, T>, grid, dim3(ATHREADS), attn_smem_bytes<HD, T>(DBEAMS), stream,
+  return launch_pdl(PDL_ATTN, decode_attn_kernel<HD, T>, grid, dim3(ATHREADS), decode_smem_bytes<HD, T>(), stream,
                     static_cast<const T*>(q), static_cast<const T*>(kp), static_cast<const T*>(vp),
                     static_cast<const T*>(ks), static_cast<const T*>(vs), anc, L_dev, static_cast<T*>(out), ob, os,
                     beams, cap, heads, kv_heads, t, scale, status);
@@ -334,7 +463,7 @@ static cudaError_t attn_set_smem() {
                                        (int)attn_smem_bytes<HD, T>(PQ));
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(decode_attn_kernel<HD, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)attn_smem_bytes<HD, T>(DBEAMS));
+                             (int)decode_smem_bytes<HD, T>());
   return e;
 }
 
