@@ -212,7 +212,7 @@ def run_ours(args):
     max_prefix = max(wl.prompt_max, max(u.prompt_tokens for u in users))
     weights = wk.synth_weights(cfg, seed=wl.weight_seed, device=f'cuda:{local}')
     tables = GpuSidConstraintTables(cons, cfg.root, cfg.newline, cfg.eos)
-    engine = BeamEngine(cfg, weights, tables, max_prefix=max_prefix, device=local)
+    engine = BeamEngine(cfg, weights, tables, max_prefix=max_prefix, device=local, max_users=max(1, args.batch))
     # extra independent sessions for the concurrent-serving measurement
     extra = [BeamEngine(cfg, weights, tables, max_prefix=max_prefix, device=local)
              for _ in range(max(0, args.sessions - 1))]
@@ -315,6 +315,39 @@ def run_ours(args):
         for e in extra:
             e.close()
 
+    # ---- batched serving: groups of U users share each decode step (one session,
+    # one weight copy; every projection GEMM at U x 50 rows)
+    batched = None
+    if args.batch > 1:
+        U = args.batch
+        groups = [list(range(args.warmup + k, min(args.warmup + k + U, args.warmup + args.steps)))
+                  for k in range(0, args.steps, U)]
+        groups = [g for g in groups if len(g) == U] or groups[:1]
+        for _ in range(2):  # warm-up (graph capture for U users)
+            engine.launch_batch_device([ids_dev[i] for i in range(U)], [users[i].prompt_tokens for i in range(U)])
+            engine.wait_batch()
+        torch.cuda.synchronize(dev)
+        bev = [torch.cuda.Event(enable_timing=True) for _ in range(len(groups) + 1)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        bev[0].record(stream)
+        for k, g in enumerate(groups):  # queued back to back, like the batch-1 timed region
+            engine.launch_batch_device([ids_dev[i] for i in g], [users[i].prompt_tokens for i in g])
+            bev[k + 1].record(stream)
+        engine.wait_batch()
+        torch.cuda.synchronize(dev)
+        b_ms = bev[0].elapsed_time(bev[-1])
+        n_batched = sum(len(g) for g in groups)
+        if world > 1:
+            t = torch.tensor([b_ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            b_ms = float(t[0])
+        batched = {'users_per_batch': U, 'value': round(n_batched * world / (b_ms / 1000.0), 3), 'unit': 'users/s',
+                   'ms_per_batch': round(b_ms / len(groups), 3),
+                   'note': 'one session, U users per request: each user prefilled on its own, then decode steps '
+                           '1-4 for all U users in one graph (GEMMs at U x 50 rows); prompts in HBM; CUDA events, '
+                           'max over ranks'}
+
     # ---- roofline of the dominant kernel: the decode projection GEMMs (M = beams)
     gemm_ms = engine.profile_gemms(engine.beams, reps=5)
     gemm_bytes = gemm_weight_bytes(cfg)
@@ -381,6 +414,7 @@ def run_ours(args):
                          'gemm_tflops': round(gemm_flops / (gemm_ms / 1000.0) / 1e12, 2)},
             'gpu_launches': int(launches),
             'concurrent': concurrent,
+            'batched': batched,
             'launches_per_user': rep['launches_per_request'],
             'clocks': ck,
         }
@@ -479,6 +513,8 @@ def main():
     ap.add_argument('--workload', default='qwen1.5b-fp32')
     ap.add_argument('--cpu-budget', type=float, default=20.0, help='seconds of CPU-baseline work (rank 0, N=1)')
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--batch', type=int, default=4,
+                    help='users per batched request for the batched-serving measurement (1: skip)')
     ap.add_argument('--sessions', type=int, default=2,
                     help='also measure S concurrent sessions per GPU (1: sequential only)')
     args = ap.parse_args()

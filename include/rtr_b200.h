@@ -91,6 +91,11 @@ typedef struct {
  * benchmark_inference.py:93-121 (CompiledForward, PrefixArena,
  * PrefixReplayPool, ReorderSuffix).  Allocates all device state. */
 int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** out);
+/* The same session sized for up to max_users (1..8) users per request: each
+ * user gets its own prefix arena, beam state and result; rtr_launch_batch runs
+ * their decode steps together (no reference counterpart: the reference serves
+ * one user per request). */
+int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t max_users, rtr_session** out);
 int rtr_session_destroy(rtr_session* s);
 
 /* Text of the last error of this session (or of the last failed create when
@@ -148,6 +153,19 @@ int rtr_read_results(rtr_session* s, const rtr_result* out);
 /* Whole request: prefill + steps 1..4 (one CUDA graph) + result copy.
  * Replaces benchmark_inference.generate (:123-148). */
 int rtr_generate(rtr_session* s, const int32_t* ids_host, int32_t L, const rtr_result* out);
+
+/* Batched requests (sessions from rtr_session_create_batched): n_users prompts
+ * ids[u] of lengths L[u]; every user's prefill runs on its own, then one decode
+ * graph runs steps 1-4 for all n users, each projection GEMM at n x beams rows.
+ * Each user's ranking equals its batch-1 result (same kernels and, up to two
+ * users, the same split-K partition; beyond that the GEMM partition can change
+ * the last bits).  out points to n_users results.  One status word covers the
+ * batch: a device check that fails for one user fails the batch. */
+int rtr_launch_batch(rtr_session* s, const int32_t* const* ids, const int32_t* L, int32_t n_users,
+                     int32_t ids_on_device);
+int rtr_wait_batch(rtr_session* s, const rtr_result* out);
+int rtr_generate_batch(rtr_session* s, const int32_t* const* ids_host, const int32_t* L, int32_t n_users,
+                       const rtr_result* out);
 
 /* The two halves of rtr_generate for callers that overlap requests with host
  * work: rtr_launch enqueues prefill + the decode graph + the result copy on the

@@ -23,6 +23,7 @@ EXPORTS = (
     'rtr_lookup_width', 'rtr_constraint_lookup', 'rtr_constraint_process',
     'rtr_synth_fill_host', 'rtr_synth_fill_device', 'rtr_launch', 'rtr_wait', 'rtr_get_report',
     'rtr_profile_gemms', 'rtr_constraint_process_static', 'rtr_gemm_check',
+    'rtr_session_create_batched', 'rtr_launch_batch', 'rtr_wait_batch', 'rtr_generate_batch',
 )
 
 
@@ -105,6 +106,10 @@ def load():
         'rtr_get_report': (P, ctypes.POINTER(ReportC)),
         'rtr_profile_gemms': (P, I32, I32, ctypes.POINTER(F)),
         'rtr_gemm_check': (I32, P, P, P, I32, I32, I32, I32),
+        'rtr_session_create_batched': (ctypes.POINTER(ModelConfigC), ctypes.c_int, I32, ctypes.POINTER(P)),
+        'rtr_launch_batch': (P, P, P, I32, I32),
+        'rtr_wait_batch': (P, ctypes.POINTER(ResultC)),
+        'rtr_generate_batch': (P, P, P, I32, ctypes.POINTER(ResultC)),
         'rtr_constraint_process_static': (P, I32, P, I32, I32, P, P),
     }
     for name, args in sig.items():

@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     const T* __restrict__ ksuf, const T* __restrict__ vsuf, const int32_t* __restrict__ anc,
     const int32_t* __restrict__ L_dev, T* __restrict__ out, float* __restrict__ out_big,
     float* __restrict__ out_small, int beams, int cap, int heads, int kv_heads, int t, float scale,
-    uint32_t* __restrict__ status) {
+    uint32_t* __restrict__ status, int users, long prefix_user_stride, int anc_user_stride) {
   constexpr int VEC = HD / 32, QLD = HD + DQLD_PAD, E = 16 / (int)sizeof(T);
   constexpr int AD4 = HD / 4 / AWARPS;  // float4 columns per warp in phase A
   static_assert(DBEAMS == 8 && AWARPS == 8 && AK == 64, "tiling assumes 8 beams, 8 warps, 64-key chunks");
@@ -259,15 +259,18 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   float* pr = part + AWARPS * DBEAMS * DSLD;                     // [DBEAMS][AK] probabilities
   float* corr_s = pr + DBEAMS * AK;                              // [DBEAMS]
   const int h = blockIdx.x, g = h / (heads / kv_heads);
-  const int b0 = blockIdx.y * DBEAMS;
+  // batched decode: user u owns rows u * beams .. (its own prefix, length and ancestry)
+  const int gpu = (beams + DBEAMS - 1) / DBEAMS, u = blockIdx.y / gpu;
+  const int b0 = (blockIdx.y % gpu) * DBEAMS, r0 = u * beams, rows = users * beams;
+  anc += (long)u * anc_user_stride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int L = *L_dev;
+  int L = L_dev[u];
   if (L < 1 || L > cap) {  // the prefill recorded no valid prefix: attend to the suffix only
     if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
     L = 0;
   }
-  const T* kbase = kp + (long)g * cap * HD;
-  const T* vbase = vp + (long)g * cap * HD;
+  const T* kbase = kp + u * prefix_user_stride + (long)g * cap * HD;
+  const T* vbase = vp + u * prefix_user_stride + (long)g * cap * HD;
   const int nchunks = (L + AK - 1) / AK;
 
   // the suffix rows of the 8 beams (slot s < t - 1: row anc[b][s]; slot t - 1: row b)
@@ -280,7 +283,7 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
       if (d == 0) atomicOr(status, RTR_DEV_BAD_PARENT);
       row = b;
     }
-    const long off = (((long)sl * beams + row) * kv_heads + g) * HD + d;
+    const long off = (((long)sl * rows + r0 + row) * kv_heads + g) * HD + d;
     cp_async16(sufk + (bb * 4 + sl) * HD + d, ksuf + off, true);
     cp_async16(sufv + (bb * 4 + sl) * HD + d, vsuf + off, true);
   }
@@ -290,7 +293,7 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   for (int i = threadIdx.x; i < DBEAMS * HD / 4; i += ATHREADS) {
     const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (b0 + r < beams) v = ld4f(q + ((long)(b0 + r) * heads + h) * HD + d);
+    if (b0 + r < beams) v = ld4f(q + ((long)(r0 + b0 + r) * heads + h) * HD + d);
     *reinterpret_cast<float4*>(qs + r * QLD + d) = v;
   }
   const int abg = lane >> 4, akg = lane & 15;  // phase A: beams 4abg.., keys akg + 16j
@@ -421,7 +424,8 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   if (b < beams) {
     const float inv = 1.0f / l;
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) store_out(out, out_big, out_small, ((long)b * heads + h) * HD + lane * VEC + i, a[i] * inv);
+    for (int i = 0; i < VEC; ++i)
+      store_out(out, out_big, out_small, ((long)(r0 + b) * heads + h) * HD + lane * VEC + i, a[i] * inv);
   }
 }
 
@@ -429,31 +433,33 @@ template <int HD, typename T>
 static cudaError_t launch_decode(const void* q, const void* kp, const void* vp, const void* ks, const void* vs,
                                  const int32_t* anc, const int32_t* L_dev, int t, void* out, float* ob, float* os,
                                  int beams, int cap, int heads, int kv_heads, float scale, uint32_t* status,
-                                 cudaStream_t stream) {
-  dim3 grid(heads, (beams + DBEAMS - 1) / DBEAMS);
+                                 cudaStream_t stream, const DecodeUsers& du) {
+  dim3 grid(heads, du.users * ((beams + DBEAMS - 1) / DBEAMS));
   return launch_pdl(PDL_ATTN, decode_attn_kernel<HD, T>, grid, dim3(ATHREADS), decode_smem_bytes<HD, T>(), stream,
                     static_cast<const T*>(q), static_cast<const T*>(kp), static_cast<const T*>(vp),
                     static_cast<const T*>(ks), static_cast<const T*>(vs), anc, L_dev, static_cast<T*>(out), ob, os,
-                    beams, cap, heads, kv_heads, t, scale, status);
+                    beams, cap, heads, kv_heads, t, scale, status, du.users, du.prefix_user_stride,
+                    du.anc_user_stride);
 }
 
 cudaError_t attention_decode(const void* q, const void* k_prefix, const void* v_prefix, const void* k_suffix,
                              const void* v_suffix, const int32_t* anc, const int32_t* L_dev, int t, void* out,
                              float* out_big, float* out_small, int beams, int prefix_cap, int heads, int kv_heads,
-                             int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream) {
-  if (t < 1 || t > 4 || beams > MAX_BEAMS) return cudaErrorInvalidValue;
+                             int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream,
+                             const DecodeUsers& du) {
+  if (t < 1 || t > 4 || beams > MAX_BEAMS || du.users < 1) return cudaErrorInvalidValue;
   if (head_dim == 128)
     return bf16 ? launch_decode<128, __nv_bfloat16>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out,
                                                     nullptr, nullptr, beams, prefix_cap, heads, kv_heads, scale, status,
-                                                    stream)
+                                                    stream, du)
                 : launch_decode<128, float>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out, out_big,
-                                            out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream);
+                                            out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream, du);
   if (head_dim == 64)
     return bf16 ? launch_decode<64, __nv_bfloat16>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out,
                                                    nullptr, nullptr, beams, prefix_cap, heads, kv_heads, scale, status,
-                                                   stream)
+                                                   stream, du)
                 : launch_decode<64, float>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out, out_big,
-                                           out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream);
+                                           out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream, du);
   return cudaErrorInvalidValue;
 }
 

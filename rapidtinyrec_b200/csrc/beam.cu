@@ -118,13 +118,14 @@ __host__ __device__ int lookup_width_of(const DevTables& tb, int step) {
 int lookup_width(const DevTables& tb, int step) { return lookup_width_of(tb, step); }
 
 // -------------------------------------------------- vocabulary passes
-__global__ void tail_max_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+__global__ void tail_max_kernel(const float* __restrict__ logits, int vocab, BeamState* st, int rows_per_user) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[33];
-  const int row = blockIdx.x, sp = blockIdx.y;
+  st += blockIdx.x / rows_per_user;  // batched decode: each user's rows feed its own state
+  const int grow = blockIdx.x, row = blockIdx.x % rows_per_user, sp = blockIdx.y;
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
-  const float* x = logits + (long)row * vocab;
+  const float* x = logits + (long)grow * vocab;
   float m = -INFINITY;
   for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) m = fmaxf(m, x[i]);
   m = block_max(m, red);
@@ -137,13 +138,14 @@ __device__ __forceinline__ float row_max(const BeamState* st, int row) {
   return m;
 }
 
-__global__ void tail_sum1_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+__global__ void tail_sum1_kernel(const float* __restrict__ logits, int vocab, BeamState* st, int rows_per_user) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[33];
-  const int row = blockIdx.x, sp = blockIdx.y;
+  st += blockIdx.x / rows_per_user;  // batched decode: each user's rows feed its own state
+  const int grow = blockIdx.x, row = blockIdx.x % rows_per_user, sp = blockIdx.y;
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
-  const float* x = logits + (long)row * vocab;
+  const float* x = logits + (long)grow * vocab;
   const float m = row_max(st, row);
   float s = 0.f;
   for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) s += expf(x[i] - m);
@@ -151,13 +153,14 @@ __global__ void tail_sum1_kernel(const float* __restrict__ logits, int vocab, Be
   if (threadIdx.x == 0) st->part[row][sp][1] = s;
 }
 
-__global__ void tail_sum2_kernel(const float* __restrict__ logits, int vocab, BeamState* st) {
+__global__ void tail_sum2_kernel(const float* __restrict__ logits, int vocab, BeamState* st, int rows_per_user) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[33];
-  const int row = blockIdx.x, sp = blockIdx.y;
+  st += blockIdx.x / rows_per_user;  // batched decode: each user's rows feed its own state
+  const int grow = blockIdx.x, row = blockIdx.x % rows_per_user, sp = blockIdx.y;
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
-  const float* x = logits + (long)row * vocab;
+  const float* x = logits + (long)grow * vocab;
   const float m = row_max(st, row);
   float s1 = 0.f;
   for (int k = 0; k < TAIL_SPLITS; ++k) s1 += st->part[row][k][1];
@@ -206,6 +209,8 @@ __global__ void __launch_bounds__(SEL_THREADS) beam_select_kernel(BeamState* st,
   pdl_wait();
   extern __shared__ uint64_t cand[];
   __shared__ SelShared sh;
+  st += blockIdx.x;  // batched decode: one block per user
+  logits += (long)blockIdx.x * rows * vocab;
   const int tid = threadIdx.x, nt = blockDim.x;
   const int K = 2 * beams;
   const int width = lookup_width_of(tb, step);
@@ -449,16 +454,16 @@ cudaError_t beam_init() {
 }
 
 cudaError_t beam_step(BeamState* st, const float* logits, int rows, int vocab, int beams, int step,
-                      const DevTables& tb, uint32_t* status, cudaStream_t stream) {
-  dim3 grid(rows, TAIL_SPLITS);
-  cudaError_t e = launch_pdl(PDL_TAIL, tail_max_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st);
-  if (e == cudaSuccess) e = launch_pdl(PDL_TAIL, tail_sum1_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st);
-  if (e == cudaSuccess) e = launch_pdl(PDL_TAIL, tail_sum2_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st);
+                      const DevTables& tb, uint32_t* status, cudaStream_t stream, int users) {
+  dim3 grid(rows * users, TAIL_SPLITS);
+  cudaError_t e = launch_pdl(PDL_TAIL, tail_max_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
+  if (e == cudaSuccess) e = launch_pdl(PDL_TAIL, tail_sum1_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
+  if (e == cudaSuccess) e = launch_pdl(PDL_TAIL, tail_sum2_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
   const int width = lookup_width_of(tb, step);
   const size_t need = (size_t)beams * width * sizeof(uint64_t);
   if (e == cudaSuccess)
-    e = launch_pdl(PDL_TAIL, beam_select_kernel, dim3(1), dim3(SEL_THREADS), need, stream, st, logits, rows, vocab, beams, step,
-                   tb, status);
+    e = launch_pdl(PDL_TAIL, beam_select_kernel, dim3(users), dim3(SEL_THREADS), need, stream, st, logits, rows, vocab,
+                   beams, step, tb, status);
   return e;
 }
 
@@ -491,6 +496,8 @@ cudaError_t beam_reset(BeamState* st, const int32_t* ids_dev, const int32_t* L_d
 
 // transition_logp = scores[t][beam_indices[i][t], token[i][t]] (compute_transition_scores)
 __global__ void beam_finalize_kernel(const BeamState* st, int beams, DevResult* res, const uint32_t* status) {
+  st += blockIdx.x;  // one block per user
+  res += blockIdx.x;
   const int i = threadIdx.x;
   if (i < beams) {
     for (int t = 0; t < NSTEPS; ++t) {
@@ -514,8 +521,8 @@ __global__ void beam_finalize_kernel(const BeamState* st, int beams, DevResult* 
 }
 
 cudaError_t beam_finalize(const BeamState* st, int beams, DevResult* res, const uint32_t* status,
-                          cudaStream_t stream) {
-  beam_finalize_kernel<<<1, MAX_BEAMS, 0, stream>>>(st, beams, res, status);
+                          cudaStream_t stream, int users) {
+  beam_finalize_kernel<<<users, MAX_BEAMS, 0, stream>>>(st, beams, res, status);
   return cudaGetLastError();
 }
 

@@ -9,13 +9,19 @@
 namespace rtr {
 
 // ---------------------------------------------------------------- embedding
+// Row m's token: ids[(m / grp_rows) * grp_stride + (m % grp_rows) * ids_stride]
+// (groups: the users of a batched decode step, each with its own beam state).
+__device__ __forceinline__ int row_token(const int32_t* ids, int m, int ids_stride, int grp_rows, long grp_stride) {
+  return ids[(long)(m / grp_rows) * grp_stride + (long)(m % grp_rows) * ids_stride];
+}
+
 __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* table, int vocab,
                              int hidden, float* x, uint32_t* status, float* x_big, float* x_small, float* ss,
-                             int ss_ld) {
+                             int ss_ld, int grp_rows, long grp_stride) {
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
-  int tok = ids[(long)m * ids_stride];
+  int tok = row_token(ids, m, ids_stride, grp_rows, grp_stride);
   if (tok < 0 || tok >= vocab) {
     if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_TOKEN);
     tok = 0;
@@ -45,10 +51,11 @@ __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* ta
 
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
                        int hidden, float* x, uint32_t* status, cudaStream_t stream, float* x_big, float* x_small,
-                       float* ss, int ss_ld) {
+                       float* ss, int ss_ld, int grp_rows, long grp_stride) {
   if (x_big && (hidden % 128 || !x_small)) return cudaErrorInvalidValue;
+  if (grp_rows <= 0) grp_rows = M;
   return launch_pdl(PDL_EMBED, embed_kernel, dim3(M), dim3(128), 0, stream, ids, ids_stride, table, vocab, hidden, x,
-                    status, x_big, x_small, ss, ss_ld);
+                    status, x_big, x_small, ss, ss_ld, grp_rows, grp_stride);
 }
 
 // ------------------------------------------------------------------ RMSNorm
@@ -96,11 +103,11 @@ cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big
 // The bf16 model of the reference's bf16-experimental opt-in: embeddings,
 // residual stream and norms in bf16, reductions in fp32.
 __global__ void embed_bf16_kernel(const int32_t* ids, int ids_stride, const __nv_bfloat16* table, int vocab,
-                                  int hidden, __nv_bfloat16* x, uint32_t* status) {
+                                  int hidden, __nv_bfloat16* x, uint32_t* status, int grp_rows, long grp_stride) {
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
-  int tok = ids[(long)m * ids_stride];
+  int tok = row_token(ids, m, ids_stride, grp_rows, grp_stride);
   if (tok < 0 || tok >= vocab) {
     if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_TOKEN);
     tok = 0;
@@ -111,9 +118,11 @@ __global__ void embed_bf16_kernel(const int32_t* ids, int ids_stride, const __nv
 }
 
 cudaError_t embed_rows_bf16(const int32_t* ids, int ids_stride, int M, const void* table, int vocab, int hidden,
-                            void* x, uint32_t* status, cudaStream_t stream) {
+                            void* x, uint32_t* status, cudaStream_t stream, int grp_rows, long grp_stride) {
+  if (grp_rows <= 0) grp_rows = M;
   return launch_pdl(PDL_EMBED, embed_bf16_kernel, dim3(M), dim3(128), 0, stream, ids, ids_stride,
-                    static_cast<const __nv_bfloat16*>(table), vocab, hidden, static_cast<__nv_bfloat16*>(x), status);
+                    static_cast<const __nv_bfloat16*>(table), vocab, hidden, static_cast<__nv_bfloat16*>(x), status,
+                    grp_rows, grp_stride);
 }
 
 // Qwen2RMSNorm on a bf16 model (modeling_qwen2.py:258-263): the variance in

@@ -23,6 +23,7 @@ struct RopeArgs {
   int prefix_cap;
   int slot;                // < 0: prefill (row m at position m); else decode suffix slot
   const int32_t* L_dev;    // decode: prefix length (position = *L_dev + slot)
+  int rows_per_user = 0;   // batched decode: row m belongs to user m / rows_per_user (L_dev[user])
 };
 
 // RMSNorm folded into the projection GEMMs (3xTF32 path): the norm weight is
@@ -89,7 +90,8 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
 // ss (optional), x's per-row partial sums of squares (NormFold layout).
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
                        int hidden, float* x, uint32_t* status, cudaStream_t stream, float* x_big = nullptr,
-                       float* x_small = nullptr, float* ss = nullptr, int ss_ld = 0);
+                       float* x_small = nullptr, float* ss = nullptr, int ss_ld = 0, int grp_rows = 0,
+                       long grp_stride = 0);  // row m: ids[(m / grp_rows) * grp_stride + (m % grp_rows) * ids_stride]
 // h = w * (x * rsqrt(mean(x^2) + eps)); h_big/h_small (optional) get the tf32 split of h.
 cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big, float* h_small, int M, int hidden,
                           float eps, cudaStream_t stream);
@@ -107,7 +109,7 @@ void synth_fill_host(float* dst, int64_t n, uint64_t seed, uint64_t tid, float s
 cudaError_t f32_to_bf16(const float* src, void* dst, int64_t n, cudaStream_t stream);
 // bf16 mode (bf16 activations; norm weights and biases as bf16 values in fp32)
 cudaError_t embed_rows_bf16(const int32_t* ids, int ids_stride, int M, const void* table, int vocab, int hidden,
-                            void* x, uint32_t* status, cudaStream_t stream);
+                            void* x, uint32_t* status, cudaStream_t stream, int grp_rows = 0, long grp_stride = 0);
 cudaError_t rms_norm_rows_bf16(const void* x, const float* w, void* h, int M, int hidden, float eps,
                                cudaStream_t stream);
 cudaError_t gemv_bf16(const void* x, const void* W, float* y, int N, int K, cudaStream_t stream);
@@ -119,12 +121,21 @@ cudaError_t round_to_bf16(float* v, int64_t n, cudaStream_t stream);
 cudaError_t attention_prefill(const void* q, const void* k_prefix, const void* v_prefix, void* out, float* out_big,
                               float* out_small, int L, int prefix_cap, int heads, int kv_heads, int head_dim,
                               float scale, bool bf16, cudaStream_t stream);
-// Decode attention over the shared prefix (length *L_dev) and `t` suffix
+// Users of a batched decode step: user u owns rows u * beams .. u * beams + beams - 1,
+// its prefix at k/v_prefix + u * prefix_user_stride, its length L_dev[u] and its
+// ancestry table at anc + u * anc_user_stride.
+struct DecodeUsers {
+  int users = 1;
+  long prefix_user_stride = 0;  // elements
+  int anc_user_stride = 0;      // int32 elements
+};
+// Decode attention over the shared prefix (length L_dev[user]) and `t` suffix
 // slots; suffix slot s of beam b lives in row anc[b*4+s] (slot t-1: row b).
 cudaError_t attention_decode(const void* q, const void* k_prefix, const void* v_prefix, const void* k_suffix,
                              const void* v_suffix, const int32_t* anc, const int32_t* L_dev, int t, void* out,
                              float* out_big, float* out_small, int beams, int prefix_cap, int heads, int kv_heads,
-                             int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream);
+                             int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream,
+                             const DecodeUsers& du = DecodeUsers{});
 cudaError_t attention_init();
 
 // ---- constraints + beam step (beam.cu) ----
@@ -179,10 +190,11 @@ cudaError_t beam_init();
 cudaError_t beam_reset(BeamState* st, const int32_t* ids_dev, const int32_t* L_dev, int beams,
                        cudaStream_t stream);
 // Full step tail on logits [rows, V] (rows = 1 at step 0, otherwise beams).
+// `users` consecutive beam states, each with `rows` logits rows (1 at step 0, else beams)
 cudaError_t beam_step(BeamState* st, const float* logits, int rows, int vocab, int beams, int step,
-                      const DevTables& tb, uint32_t* status, cudaStream_t stream);
+                      const DevTables& tb, uint32_t* status, cudaStream_t stream, int users = 1);
 cudaError_t beam_finalize(const BeamState* st, int beams, DevResult* res, const uint32_t* status,
-                          cudaStream_t stream);
+                          cudaStream_t stream, int users = 1);
 cudaError_t beam_dense_scores(const BeamState* st, int step, int beams, int vocab, float* out,
                               cudaStream_t stream);
 int lookup_width(const DevTables& tb, int step);

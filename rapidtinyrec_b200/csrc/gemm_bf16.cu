@@ -103,7 +103,7 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
   if (p.epi == EPI_ROPE) {
     const RopeArgs& r = p.rope;
     const int D = r.head_dim, half = D >> 1;
-    const int base_pos = r.slot < 0 ? 0 : *r.L_dev + r.slot;
+
     for (int q = threadIdx.x; q < rows * 32; q += BF_THREADS) {
       const int j = q >> 5, c4 = q & 31;
       if (c4 >= cols4) continue;
@@ -113,7 +113,8 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
       if (h < r.heads + r.kv_heads) {
         const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
         const float4 pv = rbf4(f4add(red4[j * ld4 + pc4], *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4)));
-        int pos = r.slot < 0 ? m : base_pos;
+        // decode: position L + slot, L of the row's user in a batched step
+        int pos = r.slot < 0 ? m : r.L_dev[r.rows_per_user ? m / r.rows_per_user : 0] + r.slot;
         if (pos < 0 || pos >= r.positions) {
           atomicOr(p.status, RTR_DEV_BAD_LENGTH);
           pos = 0;

@@ -36,6 +36,9 @@ struct LayerW {
   void *pqkv = nullptr, *po = nullptr, *pgu = nullptr, *pd = nullptr;
 };
 
+static constexpr int kTickets = 4096;  // split-K tickets: one per output tile
+static constexpr int kMaxUsers = 8;
+
 struct rtr_session {
   rtr_model_config cfg{};
   int device = 0, sms = 148;
@@ -96,7 +99,15 @@ struct rtr_session {
   int L = 0;
   int steps_done = -1;
   bool in_flight = false;
-  cudaGraphExec_t graph = nullptr;
+  // batched decode (rtr_session_create_batched): up to max_users users share each
+  // decode step's GEMMs; user u has its own prefix arena, length, beam state and
+  // result.  The per-step entry points serve user 0.
+  int max_users = 1;
+  int step_users = 1;        // users of the request in flight
+  int cur_user = 0;          // the user whose prefill runs
+  long prefix_user = 0;      // prefix-arena elements per user
+  int Ls[kMaxUsers] = {};
+  cudaGraphExec_t graphs[kMaxUsers + 1] = {};  // decode graph per batch size
   // counters (rtr_get_report)
   int64_t requests = 0, launches = 0, graph_kernels = 0;
   int64_t weight_bytes = 0, device_bytes = 0;
@@ -116,6 +127,11 @@ static int fail(rtr_session* s, int code, const std::string& msg) {
       return fail((s), RTR_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e)); \
   } while (0)
 
+static void drop_graphs(rtr_session* s) {
+  for (auto& g : s->graphs)
+    if (g) { cudaGraphExecDestroy(g); g = nullptr; }
+}
+
 template <typename T>
 static cudaError_t dev_alloc(rtr_session* s, T** p, size_t count) {
   void* raw = nullptr;
@@ -127,7 +143,7 @@ static cudaError_t dev_alloc(rtr_session* s, T** p, size_t count) {
   return cudaSuccess;
 }
 
-static constexpr int kTickets = 4096;  // split-K tickets: one per output tile
+  // split-K tickets: one per output tile
 
 static int beams_of(const rtr_session* s) { return s->cfg.num_beams; }
 static int qkv_dim(const rtr_model_config& c) { return (c.heads + 2 * c.kv_heads) * c.head_dim; }
@@ -152,7 +168,12 @@ extern "C" {
 const char* rtr_last_error(const rtr_session* s) { return s ? s->err.c_str() : g_create_error.c_str(); }
 
 int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** out) {
+  return rtr_session_create_batched(cfg, device, 1, out);
+}
+
+int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t max_users, rtr_session** out) {
   if (!cfg || !out) return fail(nullptr, RTR_ERR_ARG, "null config or output pointer");
+  if (max_users < 1 || max_users > kMaxUsers) return fail(nullptr, RTR_ERR_ARG, "max_users must be in [1, 8]");
   const rtr_model_config& c = *cfg;
   if (c.layers < 1 || c.hidden < 16 || c.heads < 1 || c.kv_heads < 1 || c.vocab < 16)
     return fail(nullptr, RTR_ERR_ARG, "non-positive model dimension");
@@ -168,6 +189,7 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   auto* s = new rtr_session();
   s->cfg = c;
   s->device = device;
+  s->max_users = max_users;
   auto bail = [&](int code) {
     g_create_error = s->err;
     rtr_session_destroy(s);
@@ -201,11 +223,15 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
     s->err = "the bf16 mode runs on the tensor-core GEMMs only (unset RTR_GEMM)";
     return bail(RTR_ERR_ARG);
   }
+  if (max_users > 1 && !s->use_tc) {
+    s->err = "batched sessions run on the tensor-core GEMMs only (unset RTR_GEMM)";
+    return bail(RTR_ERR_ARG);
+  }
 
   const long H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
   const long qd = (long)c.heads * D, kvd = (long)c.kv_heads * D, qkvd = qkv_dim(c);
-  const long B = c.num_beams, cap = c.max_prefix;
-  const long M = cap > B ? cap : B;
+  const long B = c.num_beams, cap = c.max_prefix, U = max_users;
+  const long M = cap > B * U ? cap : B * U;  // activation rows: a prefill or a batched decode step
   s->layers.resize(c.layers);
   if (!s->bf16) {
     CREATE_TRY(dev_alloc(s, &s->embed, V * H));
@@ -243,8 +269,9 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
   CREATE_TRY(dev_alloc(s, &s->norm_final, H));
   s->weight_bytes = s->device_bytes;
 
-  CREATE_TRY(dev_alloc(s, &s->kv_prefix, (size_t)c.layers * 2 * kvd * cap));
-  CREATE_TRY(dev_alloc(s, &s->kv_suffix, (size_t)c.layers * 2 * 4 * B * kvd));
+  s->prefix_user = (long)c.layers * 2 * kvd * cap;
+  CREATE_TRY(dev_alloc(s, &s->kv_prefix, (size_t)s->prefix_user * U));
+  CREATE_TRY(dev_alloc(s, &s->kv_suffix, (size_t)c.layers * 2 * 4 * B * U * kvd));
   CREATE_TRY(dev_alloc(s, &s->x, M * H));
   CREATE_TRY(dev_alloc(s, &s->h, M * H));
   CREATE_TRY(dev_alloc(s, &s->qkv, M * qkvd));
@@ -265,25 +292,29 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
     s->ss_ld = (int)M;
     CREATE_TRY(dev_alloc(s, &s->ss, (H / 128) * M));
   }
-  CREATE_TRY(dev_alloc(s, &s->logits, B * V));
+  CREATE_TRY(dev_alloc(s, &s->logits, B * U * V));
   long max_n = qkvd;
   if (H > max_n) max_n = H;
   if (2 * I > max_n) max_n = 2 * I;
   s->ws_floats = gemm_workspace_floats(64, (int)max_n, s->sms);
+  // the tensor-core GEMMs split K only while tiles x splits <= SMs: a full set of
+  // 128 x 128 partial tiles (the 128-row kernel) must fit, or a GEMM would run
+  // with fewer splits than its 64-row twin and round differently
+  if (s->ws_floats < (size_t)s->sms * 128 * 128) s->ws_floats = (size_t)s->sms * 128 * 128;
   CREATE_TRY(dev_alloc(s, &s->ws, s->ws_floats));
   CREATE_TRY(dev_alloc(s, &s->tickets, kTickets));
   CREATE_TRY(dev_alloc(s, &s->proc_scratch, (size_t)PROC_MAX_ROWS * PROC_SPLITS * 2));
   CREATE_TRY(cudaMemset(s->tickets, 0, kTickets * sizeof(int)));
-  CREATE_TRY(dev_alloc(s, &s->beam, 1));
-  CREATE_TRY(cudaMemset(s->beam, 0, sizeof(BeamState)));
-  CREATE_TRY(dev_alloc(s, &s->dres, 1));
+  CREATE_TRY(dev_alloc(s, &s->beam, U));
+  CREATE_TRY(cudaMemset(s->beam, 0, U * sizeof(BeamState)));
+  CREATE_TRY(dev_alloc(s, &s->dres, U));
   CREATE_TRY(dev_alloc(s, &s->d_ids, cap));
-  CREATE_TRY(dev_alloc(s, &s->d_L, 1));
+  CREATE_TRY(dev_alloc(s, &s->d_L, U));
   CREATE_TRY(dev_alloc(s, &s->d_status, 1));
   CREATE_TRY(cudaMemset(s->d_status, 0, sizeof(uint32_t)));
-  CREATE_TRY(cudaMallocHost(&s->hres, sizeof(DevResult)));
-  CREATE_TRY(cudaMallocHost(&s->h_L, sizeof(int32_t)));
-  CREATE_TRY(cudaMallocHost(&s->h_ids, cap * sizeof(int32_t)));
+  CREATE_TRY(cudaMallocHost(&s->hres, U * sizeof(DevResult)));
+  CREATE_TRY(cudaMallocHost(&s->h_L, U * sizeof(int32_t)));
+  CREATE_TRY(cudaMallocHost(&s->h_ids, U * cap * sizeof(int32_t)));
 
   s->rope_positions = (int)cap + 8;
   CREATE_TRY(dev_alloc(s, &s->rope_cos, (size_t)s->rope_positions * D / 2));
@@ -332,7 +363,8 @@ int rtr_session_create(const rtr_model_config* cfg, int device, rtr_session** ou
 int rtr_session_destroy(rtr_session* s) {
   if (!s) return RTR_OK;
   cudaSetDevice(s->device);
-  if (s->graph) cudaGraphExecDestroy(s->graph);
+  for (auto& g : s->graphs)
+    if (g) cudaGraphExecDestroy(g);
   for (void* p : s->allocs) cudaFree(p);
   if (s->tvalid) cudaFree(s->tvalid);
   if (s->t1) cudaFree(s->t1);
@@ -349,7 +381,7 @@ int rtr_session_destroy(rtr_session* s) {
 int rtr_set_stream(rtr_session* s, void* stream) {
   if (!s) return RTR_ERR_ARG;
   CUDA_TRY(s, cudaSetDevice(s->device));
-  if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+  drop_graphs(s);
   if (s->own_stream) { cudaStreamDestroy(s->stream); s->own_stream = false; }
   if (stream) {
     s->stream = static_cast<cudaStream_t>(stream);
@@ -560,7 +592,7 @@ int rtr_load_constraints(rtr_session* s, const rtr_constraint_tables* t) {
   d.valid = s->tvalid;
   d.first_tokens = s->tfirst; d.n_first = t->n_first;
   d.newline = t->newline; d.eos = t->eos;
-  if (s->graph) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+  drop_graphs(s);
   s->tables_loaded = true;
   return RTR_OK;
 }
@@ -623,31 +655,37 @@ static cudaError_t forward_bf16(rtr_session* s, int t) {
   const int H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
   const int qd = c.heads * D, kvd = c.kv_heads * D, qkvd = qkv_dim(c);
   const int B = beams_of(s), cap = c.max_prefix;
-  const int M = t == 0 ? s->L : B;
+  // t = 0: user cur_user's prefill; t >= 1: one decode step of step_users users
+  const int n = s->step_users, RB = B * s->max_users;
+  const int M = t == 0 ? s->Ls[s->cur_user] : B * n;
+  const long pre_off = t == 0 ? (long)s->cur_user * s->prefix_user : 0;
+  const DecodeUsers du{n, s->prefix_user, (int)(sizeof(BeamState) / sizeof(int32_t))};
   const float scale = (float)std::pow((double)D, -0.5);
   cudaStream_t st = s->stream;
   const int32_t* ids = t == 0 ? s->d_ids : &s->beam->next_tok[0];
-  uint16_t* kvp = reinterpret_cast<uint16_t*>(s->kv_prefix);  // bf16 elements
+  const int id_rows = t == 0 ? 0 : B;  // decode: user m / B's beam m % B
+  const long id_stride = (long)(sizeof(BeamState) / sizeof(int32_t));
+  uint16_t* kvp = reinterpret_cast<uint16_t*>(s->kv_prefix) + pre_off;  // bf16 elements
   uint16_t* kvs = reinterpret_cast<uint16_t*>(s->kv_suffix);
-  FWD_TRY(embed_rows_bf16(ids, 1, M, s->embed_bf, V, H, s->x, s->d_status, st));
+  FWD_TRY(embed_rows_bf16(ids, 1, M, s->embed_bf, V, H, s->x, s->d_status, st, id_rows, id_stride));
   for (int l = 0; l < c.layers; ++l) {
     const LayerW& w = s->layers[l];
     uint16_t* kp = kvp + (size_t)l * 2 * kvd * cap;
     uint16_t* vp = kp + (size_t)kvd * cap;
-    uint16_t* ks = kvs + (size_t)l * 2 * 4 * B * kvd;
-    uint16_t* vs = ks + (size_t)4 * B * kvd;
-    const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * kvd;
+    uint16_t* ks = kvs + (size_t)l * 2 * 4 * RB * kvd;
+    uint16_t* vs = ks + (size_t)4 * RB * kvd;
+    const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * n * kvd;
     FWD_TRY(rms_norm_rows_bf16(s->x, w.n_in, s->h, M, H, c.rms_eps, st));
     const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
                       reinterpret_cast<float*>(t == 0 ? kp : ks + slot),
-                      reinterpret_cast<float*>(t == 0 ? vp : vs + slot), cap, t == 0 ? -1 : t - 1, s->d_L};
+                      reinterpret_cast<float*>(t == 0 ? vp : vs + slot), cap, t == 0 ? -1 : t - 1, s->d_L, B};
     FWD_TRY(gemm16(s, s->h, w.pqkv, nullptr, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra));
     if (t == 0)
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, nullptr, nullptr, M, cap, c.heads, c.kv_heads, D, scale, true,
                                 st));
     else
       FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, nullptr, nullptr, B,
-                               cap, c.heads, c.kv_heads, D, scale, s->d_status, true, st));
+                               cap, c.heads, c.kv_heads, D, scale, s->d_status, true, st, du));
     FWD_TRY(gemm16(s, s->attn, w.po, s->x, H, nullptr, M, H, qd, EPI_RESID));
     FWD_TRY(rms_norm_rows_bf16(s->x, w.n_post, s->h, M, H, c.rms_eps, st));
     FWD_TRY(gemm16(s, s->h, w.pgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
@@ -658,8 +696,8 @@ static cudaError_t forward_bf16(rtr_session* s, int t) {
     FWD_TRY(rms_norm_rows_bf16(last, s->norm_final, s->h, 1, H, c.rms_eps, st));
     FWD_TRY(gemm16(s, s->h, s->lm_packed_bf, s->logits, V, nullptr, 1, V, H, EPI_STORE));
   } else {
-    FWD_TRY(rms_norm_rows_bf16(s->x, s->norm_final, s->h, B, H, c.rms_eps, st));
-    FWD_TRY(gemm16(s, s->h, s->lm_packed_bf, s->logits, V, nullptr, B, V, H, EPI_STORE));
+    FWD_TRY(rms_norm_rows_bf16(s->x, s->norm_final, s->h, M, H, c.rms_eps, st));
+    FWD_TRY(gemm16(s, s->h, s->lm_packed_bf, s->logits, V, nullptr, M, V, H, EPI_STORE));
   }
   return cudaSuccess;
 }
@@ -671,32 +709,39 @@ static cudaError_t forward(rtr_session* s, int t) {
   const int H = c.hidden, V = c.vocab, I = c.intermediate, D = c.head_dim;
   const int qd = c.heads * D, kvd = c.kv_heads * D, qkvd = qkv_dim(c);
   const int B = beams_of(s), cap = c.max_prefix;
-  const int M = t == 0 ? s->L : B;
+  // t = 0: user cur_user's prefill; t >= 1: one decode step of step_users users
+  const int n = s->step_users, RB = B * s->max_users;
+  const int M = t == 0 ? s->Ls[s->cur_user] : B * n;
+  const long pre_off = t == 0 ? (long)s->cur_user * s->prefix_user : 0;
+  const DecodeUsers du{n, s->prefix_user, (int)(sizeof(BeamState) / sizeof(int32_t))};
   const float scale = (float)std::pow((double)D, -0.5);
   cudaStream_t st = s->stream;
   const int32_t* ids = t == 0 ? s->d_ids : &s->beam->next_tok[0];
+  const int id_rows = t == 0 ? 0 : B;  // decode: user m / B's beam m % B
+  const long id_stride = (long)(sizeof(BeamState) / sizeof(int32_t));
   if (s->fold) {
     // RMSNorm folded into the GEMMs: the residual stream's producers write x, its
     // split and partial sums of squares; q/k/v, gate/up and the LM head scale rows
     const NormFold in{nullptr, s->ss, s->ss_ld, H / 128, H, c.rms_eps};
     const NormFold out{s->ss, nullptr, s->ss_ld, H / 128, H, c.rms_eps};
-    FWD_TRY(embed_rows(ids, 1, M, s->embed, V, H, s->x, s->d_status, st, s->x_big, s->x_small, s->ss, s->ss_ld));
+    FWD_TRY(embed_rows(ids, 1, M, s->embed, V, H, s->x, s->d_status, st, s->x_big, s->x_small, s->ss, s->ss_ld,
+                       id_rows, id_stride));
     for (int l = 0; l < c.layers; ++l) {
       const LayerW& w = s->layers[l];
-      float* kp = s->kv_prefix + (size_t)l * 2 * kvd * cap;
+      float* kp = s->kv_prefix + pre_off + (size_t)l * 2 * kvd * cap;
       float* vp = kp + (size_t)kvd * cap;
-      float* ks = s->kv_suffix + (size_t)l * 2 * 4 * B * kvd;
-      float* vs = ks + (size_t)4 * B * kvd;
-      const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * kvd;
+      float* ks = s->kv_suffix + (size_t)l * 2 * 4 * RB * kvd;
+      float* vs = ks + (size_t)4 * RB * kvd;
+      const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * n * kvd;
       const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
-                        t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L};
+                        t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L, B};
       FWD_TRY(gemm(s, s->x, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra, &in));
       if (t == 0) {
         FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
                                   scale, false, st));
       } else {
         FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
-                                 s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st));
+                                 s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st, du));
       }
       FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID, nullptr, &out));
       FWD_TRY(gemm(s, s->x, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU, nullptr, &in));
@@ -706,23 +751,24 @@ static cudaError_t forward(rtr_session* s, int t) {
       FWD_TRY(rms_norm_rows(s->x + (size_t)(M - 1) * H, s->norm_final, s->h, nullptr, nullptr, 1, H, c.rms_eps, st));
       FWD_TRY(gemv_f32(s->h, s->lm_head, s->logits, V, H, st));
     } else {
-      FWD_TRY(gemm(s, s->x, H, s->lm_head, s->logits, V, nullptr, B, V, H, EPI_STORE, nullptr, &in));
+      FWD_TRY(gemm(s, s->x, H, s->lm_head, s->logits, V, nullptr, M, V, H, EPI_STORE, nullptr, &in));
     }
     return cudaSuccess;
   }
-  FWD_TRY(embed_rows(ids, 1, M, s->embed, V, H, s->x, s->d_status, st));
+  FWD_TRY(embed_rows(ids, 1, M, s->embed, V, H, s->x, s->d_status, st, nullptr, nullptr, nullptr, 0, id_rows,
+                     id_stride));
   for (int l = 0; l < c.layers; ++l) {
     const LayerW& w = s->layers[l];
-    float* kp = s->kv_prefix + (size_t)l * 2 * kvd * cap;
+    float* kp = s->kv_prefix + pre_off + (size_t)l * 2 * kvd * cap;
     float* vp = kp + (size_t)kvd * cap;
-    float* ks = s->kv_suffix + (size_t)l * 2 * 4 * B * kvd;
-    float* vs = ks + (size_t)4 * B * kvd;
+    float* ks = s->kv_suffix + (size_t)l * 2 * 4 * RB * kvd;
+    float* vs = ks + (size_t)4 * RB * kvd;
     FWD_TRY(rms_norm_rows(s->x, w.n_in, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
-    const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * kvd;
+    const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * n * kvd;
     if (s->use_tc) {
       // q/k/v projection with RoPE and the cache write fused into its epilogue
       const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
-                        t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L};
+                        t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L, B};
       FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra));
     } else {
       FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));
@@ -735,7 +781,7 @@ static cudaError_t forward(rtr_session* s, int t) {
                                 scale, false, st));
     } else {
       FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
-                               s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st));
+                               s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st, du));
     }
     FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID));
     FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
@@ -746,20 +792,21 @@ static cudaError_t forward(rtr_session* s, int t) {
     FWD_TRY(rms_norm_rows(s->x + (size_t)(M - 1) * H, s->norm_final, s->h, nullptr, nullptr, 1, H, c.rms_eps, st));
     FWD_TRY(gemv_f32(s->h, s->lm_head, s->logits, V, H, st));
   } else {
-    FWD_TRY(rms_norm_rows(s->x, s->norm_final, s->h, s->h_big, s->h_small, B, H, c.rms_eps, st));
-    FWD_TRY(gemm(s, s->h, H, s->lm_head, s->logits, V, nullptr, B, V, H, EPI_STORE));
+    FWD_TRY(rms_norm_rows(s->x, s->norm_final, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
+    FWD_TRY(gemm(s, s->h, H, s->lm_head, s->logits, V, nullptr, M, V, H, EPI_STORE));
   }
   return cudaSuccess;
 }
 
 static cudaError_t decode_and_tail(rtr_session* s, int t) {
   FWD_TRY(forward(s, t));
-  return beam_step(s->beam, s->logits, beams_of(s), s->cfg.vocab, beams_of(s), t, s->tb, s->d_status, s->stream);
+  return beam_step(s->beam, s->logits, beams_of(s), s->cfg.vocab, beams_of(s), t, s->tb, s->d_status, s->stream,
+                   s->step_users);
 }
 
 static cudaError_t finalize_and_copy(rtr_session* s) {
-  FWD_TRY(beam_finalize(s->beam, beams_of(s), s->dres, s->d_status, s->stream));
-  return cudaMemcpyAsync(s->hres, s->dres, sizeof(DevResult), cudaMemcpyDeviceToHost, s->stream);
+  FWD_TRY(beam_finalize(s->beam, beams_of(s), s->dres, s->d_status, s->stream, s->step_users));
+  return cudaMemcpyAsync(s->hres, s->dres, s->step_users * sizeof(DevResult), cudaMemcpyDeviceToHost, s->stream);
 }
 
 static int ready(rtr_session* s) {
@@ -781,29 +828,38 @@ static int64_t forward_kernels(const rtr_session* s, bool prefill) {
 }
 static constexpr int64_t kTailKernels = 4;
 
-static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t on_device) {
+static int check_prompt(rtr_session* s, const int32_t* ids, int32_t L) {
   if (!ids) return fail(s, RTR_ERR_ARG, "null ids");
   if (L < 3 || L > s->cfg.max_prefix)
     return fail(s, RTR_ERR_ARG, "Expected one complete history within prefix capacity (3 <= L <= max_prefix)");
+  return RTR_OK;
+}
+
+// Prefill of user u (its own prefix arena, length slot and beam state) and its
+// step 0.  User 0 also clears the batch's status word.
+static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t on_device, int u = 0) {
+  if (int r = check_prompt(s, ids, L)) return r;
   if (int r = ready(s)) return r;
   CUDA_TRY(s, cudaSetDevice(s->device));
   s->L = L;
-  *s->h_L = L;
-  CUDA_TRY(s, cudaMemcpyAsync(s->d_L, s->h_L, sizeof(int32_t), cudaMemcpyHostToDevice, s->stream));
+  s->Ls[u] = L;
+  s->cur_user = u;
+  s->h_L[u] = L;
+  CUDA_TRY(s, cudaMemcpyAsync(s->d_L + u, s->h_L + u, sizeof(int32_t), cudaMemcpyHostToDevice, s->stream));
   CUDA_TRY(s, cudaMemcpyAsync(s->d_ids, ids, (size_t)L * sizeof(int32_t),
                               on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s->stream));
-  CUDA_TRY(s, cudaMemsetAsync(s->d_status, 0, sizeof(uint32_t), s->stream));
-  CUDA_TRY(s, beam_reset(s->beam, s->d_ids, s->d_L, beams_of(s), s->stream));
+  if (u == 0) CUDA_TRY(s, cudaMemsetAsync(s->d_status, 0, sizeof(uint32_t), s->stream));
+  CUDA_TRY(s, beam_reset(s->beam + u, s->d_ids, s->d_L + u, beams_of(s), s->stream));
   CUDA_TRY(s, forward(s, 0));
-  CUDA_TRY(s, beam_step(s->beam, s->logits, 1, s->cfg.vocab, beams_of(s), 0, s->tb, s->d_status, s->stream));
+  CUDA_TRY(s, beam_step(s->beam + u, s->logits, 1, s->cfg.vocab, beams_of(s), 0, s->tb, s->d_status, s->stream));
   s->launches += 1 + forward_kernels(s, true) + kTailKernels;  // beam_reset, forward, step tail
   s->steps_done = 0;
   s->in_flight = false;
   return RTR_OK;
 }
 
-static int check_result(rtr_session* s, const rtr_result* out) {
-  const DevResult& r = *s->hres;
+static int check_result(rtr_session* s, const rtr_result* out, int u = 0) {
+  const DevResult& r = s->hres[u];
   const uint32_t st = r.status;
   if (st & (RTR_DEV_BAD_TOKEN | RTR_DEV_BAD_PARENT | RTR_DEV_BAD_LENGTH | RTR_DEV_TOO_MANY_CAND | RTR_DEV_NAN_SCORE |
             RTR_DEV_TIMEOUT))
@@ -827,6 +883,8 @@ extern "C" {
 
 int rtr_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t ids_on_device) {
   if (!s) return RTR_ERR_ARG;
+  if (s->in_flight) return fail(s, RTR_ERR_STATE, "request in flight");
+  s->step_users = 1;
   return stage_prefill(s, ids, L, ids_on_device);
 }
 
@@ -851,14 +909,18 @@ int rtr_read_results(rtr_session* s, const rtr_result* out) {
   return check_result(s, out);
 }
 
-int rtr_launch(rtr_session* s, const int32_t* ids, int32_t L, int32_t ids_on_device) {
-  if (!s) return RTR_ERR_ARG;
-  if (!ids) return fail(s, RTR_ERR_ARG, "null ids");
-  if (L < 3 || L > s->cfg.max_prefix)
-    return fail(s, RTR_ERR_ARG, "Expected one complete history within prefix capacity (3 <= L <= max_prefix)");
+// One request of n users: each user's prefill (and step 0) runs eagerly, then
+// one captured graph runs decode steps 1-4 for all n users together (every
+// projection GEMM at n * beams rows) and copies the results out.
+static int launch_batch(rtr_session* s, const int32_t* const* ids, const int32_t* L, int32_t n, int32_t ids_on_device) {
+  if (!ids || !L) return fail(s, RTR_ERR_ARG, "null ids or lengths");
+  if (n < 1 || n > s->max_users) return fail(s, RTR_ERR_ARG, "user count must be in [1, max_users]");
+  for (int u = 0; u < n; ++u)
+    if (int r = check_prompt(s, ids[u], L[u])) return r;
   if (int r = ready(s)) return r;
   CUDA_TRY(s, cudaSetDevice(s->device));
-  if (!s->graph) {
+  s->step_users = n;
+  if (!s->graphs[n]) {
     cudaGraph_t g = nullptr;
     CUDA_TRY(s, cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
     cudaError_t e = cudaSuccess;
@@ -870,49 +932,80 @@ int rtr_launch(rtr_session* s, const int32_t* ids, int32_t L, int32_t ids_on_dev
       return fail(s, RTR_ERR_CUDA, std::string("decode graph capture: ") +
                                        cudaGetErrorString(e != cudaSuccess ? e : e2));
     }
-    size_t n = 0;
-    cudaGraphGetNodes(g, nullptr, &n);
-    std::vector<cudaGraphNode_t> nodes(n);
-    cudaGraphGetNodes(g, nodes.data(), &n);
+    size_t nodes_n = 0;
+    cudaGraphGetNodes(g, nullptr, &nodes_n);
+    std::vector<cudaGraphNode_t> nodes(nodes_n);
+    cudaGraphGetNodes(g, nodes.data(), &nodes_n);
     s->graph_kernels = 0;
     for (auto node : nodes) {
       cudaGraphNodeType ty;
       if (cudaGraphNodeGetType(node, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++s->graph_kernels;
     }
-    e = cudaGraphInstantiate(&s->graph, g, 0);
+    e = cudaGraphInstantiate(&s->graphs[n], g, 0);
     cudaGraphDestroy(g);
-    if (e != cudaSuccess) { s->graph = nullptr; return fail(s, RTR_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e)); }
+    if (e != cudaSuccess) {
+      s->graphs[n] = nullptr;
+      return fail(s, RTR_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+    }
   }
   // Device ids may be queued behind a request in flight (stream order keeps
   // them apart); host ids reuse the pinned staging buffer, so wait first.
   if (s->in_flight && !ids_on_device) CUDA_TRY(s, cudaStreamSynchronize(s->stream));
-  const int32_t* src = ids;
-  if (!ids_on_device) {
-    // stage the prompt through pinned memory so the copy is asynchronous
-    memcpy(s->h_ids, ids, (size_t)L * sizeof(int32_t));
-    src = s->h_ids;
+  for (int u = 0; u < n; ++u) {
+    const int32_t* src = ids[u];
+    if (!ids_on_device) {
+      // stage the prompt through pinned memory so the copy is asynchronous
+      int32_t* pin = s->h_ids + (size_t)u * s->cfg.max_prefix;
+      memcpy(pin, ids[u], (size_t)L[u] * sizeof(int32_t));
+      src = pin;
+    }
+    if (int r = stage_prefill(s, src, L[u], ids_on_device, u)) return r;
   }
-  if (int r = stage_prefill(s, src, L, ids_on_device)) return r;
-  CUDA_TRY(s, cudaGraphLaunch(s->graph, s->stream));
+  CUDA_TRY(s, cudaGraphLaunch(s->graphs[n], s->stream));
   s->launches += s->graph_kernels;
-  s->requests += 1;
+  s->requests += n;
   s->steps_done = NSTEPS - 1;
   s->in_flight = true;
   return RTR_OK;
 }
 
-int rtr_wait(rtr_session* s, const rtr_result* out) {
+int rtr_launch(rtr_session* s, const int32_t* ids, int32_t L, int32_t ids_on_device) {
+  if (!s) return RTR_ERR_ARG;
+  return launch_batch(s, &ids, &L, 1, ids_on_device);
+}
+
+int rtr_launch_batch(rtr_session* s, const int32_t* const* ids, const int32_t* L, int32_t n_users,
+                     int32_t ids_on_device) {
+  if (!s) return RTR_ERR_ARG;
+  return launch_batch(s, ids, L, n_users, ids_on_device);
+}
+
+int rtr_wait_batch(rtr_session* s, const rtr_result* out) {
   if (!s) return RTR_ERR_ARG;
   if (!s->in_flight) return fail(s, RTR_ERR_STATE, "no request in flight");
   CUDA_TRY(s, cudaSetDevice(s->device));
   s->in_flight = false;
   CUDA_TRY(s, cudaStreamSynchronize(s->stream));
-  return check_result(s, out);
+  for (int u = 0; u < s->step_users; ++u)
+    if (int r = check_result(s, out ? out + u : nullptr, u)) return r;
+  return RTR_OK;
+}
+
+int rtr_wait(rtr_session* s, const rtr_result* out) {
+  if (!s) return RTR_ERR_ARG;
+  if (s->in_flight && s->step_users != 1) return fail(s, RTR_ERR_STATE, "a batch is in flight: use rtr_wait_batch");
+  return rtr_wait_batch(s, out);
 }
 
 int rtr_generate(rtr_session* s, const int32_t* ids_host, int32_t L, const rtr_result* out) {
   if (int r = rtr_launch(s, ids_host, L, 0)) return r;
   return rtr_wait(s, out);
+}
+
+int rtr_generate_batch(rtr_session* s, const int32_t* const* ids_host, const int32_t* L, int32_t n_users,
+                       const rtr_result* out) {
+  if (int r = rtr_launch_batch(s, ids_host, L, n_users, 0)) return r;
+  return rtr_wait_batch(s, out);
 }
 
 int rtr_get_report(const rtr_session* s, rtr_report* out) {
@@ -941,7 +1034,8 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
 
 int rtr_profile_gemms(rtr_session* s, int32_t M, int32_t reps, float* ms_per_pass) {
   if (!s || !ms_per_pass || reps < 1) return RTR_ERR_ARG;
-  if (M < 1 || M > (s->cfg.max_prefix > s->cfg.num_beams ? s->cfg.max_prefix : s->cfg.num_beams))
+  const int rows = s->cfg.num_beams * s->max_users;
+  if (M < 1 || M > (s->cfg.max_prefix > rows ? s->cfg.max_prefix : rows))
     return fail(s, RTR_ERR_ARG, "M outside the activation buffers");
   if (s->in_flight) return fail(s, RTR_ERR_STATE, "request in flight");
   if (!s->weights_loaded) return fail(s, RTR_ERR_STATE, "weights not loaded");

@@ -119,7 +119,7 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
     // 128-column tile holds whole heads, so each rotary partner is in the tile.
     const RopeArgs& r = p.rope;
     const int D = r.head_dim, half = D >> 1;
-    const int base_pos = r.slot < 0 ? 0 : *r.L_dev + r.slot;
+
     for (int q = threadIdx.x; q < rows * 32; q += THREADS) {
       const int j = q >> 5, c4 = q & 31;
       if (c4 >= cols4) continue;
@@ -130,7 +130,8 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
         const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
         const float4 pv =
             f4add(row_scale(red4[j * ld4 + pc4], j), *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4));
-        int pos = r.slot < 0 ? m : base_pos;
+        // decode: position L + slot, L of the row's user in a batched step
+        int pos = r.slot < 0 ? m : r.L_dev[r.rows_per_user ? m / r.rows_per_user : 0] + r.slot;
         if (pos < 0 || pos >= r.positions) {
           atomicOr(p.status, RTR_DEV_BAD_LENGTH);
           pos = 0;

@@ -55,20 +55,21 @@ def weight_order(cfg: ModelConfig):
 
 class BeamEngine:
     def __init__(self, cfg: ModelConfig, weights, tables, max_prefix: int, device: int = 0,
-                 num_beams: int = NUM_BEAMS):
+                 num_beams: int = NUM_BEAMS, max_users: int = 1):
         import torch
         self.lib = _native.load()
         self.cfg = cfg
         self.beams = num_beams
         self.device = device
         self.max_prefix = max_prefix
+        self.max_users = max_users
         c = _native.ModelConfigC(layers=cfg.layers, hidden=cfg.hidden, heads=cfg.heads, kv_heads=cfg.kv_heads,
                                  head_dim=cfg.head_dim, intermediate=cfg.intermediate, vocab=cfg.vocab,
                                  tied_embeddings=int(cfg.tied), rms_eps=cfg.rms_eps, rope_theta=cfg.rope_theta,
                                  dtype=_native.RTR_DTYPE_F32 if cfg.dtype == 'fp32' else _native.RTR_DTYPE_BF16,
                                  max_prefix=max_prefix, num_beams=num_beams)
         handle = ctypes.c_void_p()
-        _native.check(self.lib.rtr_session_create(ctypes.byref(c), device, ctypes.byref(handle)))
+        _native.check(self.lib.rtr_session_create_batched(ctypes.byref(c), device, max_users, ctypes.byref(handle)))
         self.handle = handle
         try:
             if weights is not None:
@@ -87,6 +88,16 @@ class BeamEngine:
         i32p, f32p = ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_float)
         self._result = _native.ResultC(self._tok.ctypes.data_as(i32p), self._par.ctypes.data_as(i32p),
                                        self._seq.ctypes.data_as(f32p), self._trans.ctypes.data_as(f32p))
+        # one result record per user of a batch
+        self._btok = np.zeros((max_users, num_beams * NUM_STEPS), dtype=np.int32)
+        self._bpar = np.zeros_like(self._btok)
+        self._bseq = np.zeros((max_users, num_beams), dtype=np.float32)
+        self._btrans = np.zeros((max_users, num_beams * NUM_STEPS), dtype=np.float32)
+        self._bresults = (_native.ResultC * max_users)(*[
+            _native.ResultC(self._btok[u].ctypes.data_as(i32p), self._bpar[u].ctypes.data_as(i32p),
+                            self._bseq[u].ctypes.data_as(f32p), self._btrans[u].ctypes.data_as(f32p))
+            for u in range(max_users)])
+        self._batch_n = 0
         del torch
 
     # ------------------------------------------------------------ plumbing
@@ -134,6 +145,14 @@ class BeamEngine:
                 'sequence_logp': self._seq.tolist(),
                 'transition_logp': self._trans.reshape(b, NUM_STEPS).tolist()}
 
+    def _batch_records(self, n):
+        b = self.beams
+        return [{'beam_indices': self._bpar[u].reshape(b, NUM_STEPS).tolist(),
+                 'score_dtypes': ['torch.float32'] * NUM_STEPS,
+                 'token_ids': self._btok[u].reshape(b, NUM_STEPS).tolist(),
+                 'sequence_logp': self._bseq[u].tolist(),
+                 'transition_logp': self._btrans[u].reshape(b, NUM_STEPS).tolist()} for u in range(n)]
+
     @staticmethod
     def _ids(prompt_ids):
         ids = np.ascontiguousarray(np.asarray(prompt_ids, dtype=np.int32).reshape(-1))
@@ -145,6 +164,28 @@ class BeamEngine:
         ids = self._ids(prompt_ids)
         self._check(self.lib.rtr_generate(self.handle, ids.ctypes.data, len(ids), ctypes.byref(self._result)))
         return self._record()
+
+    def generate_batch(self, prompts):
+        """Several users in one request (session built with ``max_users``): each
+        user's prefill, then their decode steps together; one record per user."""
+        ids = [self._ids(p) for p in prompts]
+        n = len(ids)
+        ptrs = (ctypes.c_void_p * n)(*[a.ctypes.data for a in ids])
+        lens = (ctypes.c_int32 * n)(*[len(a) for a in ids])
+        self._check(self.lib.rtr_generate_batch(self.handle, ptrs, lens, n, self._bresults))
+        return self._batch_records(n)
+
+    def launch_batch_device(self, ids_dev, lengths):
+        """Enqueue one batched request whose prompts already sit in device memory."""
+        n = len(ids_dev)
+        ptrs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in ids_dev])
+        lens = (ctypes.c_int32 * n)(*lengths)
+        self._check(self.lib.rtr_launch_batch(self.handle, ptrs, lens, n, 1))
+        self._batch_n = n
+
+    def wait_batch(self):
+        self._check(self.lib.rtr_wait_batch(self.handle, self._bresults))
+        return self._batch_records(self._batch_n)
 
     def generate_raw(self, ids: np.ndarray):
         """``generate`` without building the Python record (for timing loops)."""
