@@ -20,6 +20,7 @@ from __future__ import annotations
 import collections
 import dataclasses
 import json
+import re
 from pathlib import Path
 
 from .configs import ModelConfig
@@ -102,3 +103,26 @@ def load_release(release_root: Path, reference_results: Path, dtype: str = 'fp32
     if cfg.tied:
         weights.pop('lm_head.weight', None)
     return Release(cfg, weights, constraints, users, records)
+
+
+def sid_tokens(tokenizer, sid: str):
+    """Token ids of one SID string such as ``<a_12><b_3><c_44>`` (one added token
+    per code, as the reference's auditor maps them, audit_results.py:117-119)."""
+    codes = re.findall(r'<[^>]+>', sid)
+    ids = tokenizer.convert_tokens_to_ids(codes)
+    if len(ids) != 3 or any(i is None or i == tokenizer.unk_token_id for i in ids):
+        raise ValueError(f'target SID {sid!r} is not three known code tokens')
+    return tuple(int(i) for i in ids)
+
+
+def load_targets(release_root: Path, reference_results: Path) -> dict:
+    """Held-out target SID of every cohort user (``target_sid`` in the reference
+    manifest), as token triples keyed by cohort index."""
+    from transformers import AutoTokenizer
+    tok = AutoTokenizer.from_pretrained(Path(release_root) / CHECKPOINT, local_files_only=True)
+    manifest = json.loads((Path(reference_results) / 'manifest.json').read_text())
+    out = {}
+    for u in manifest['users']:
+        if u.get('target_sid'):
+            out[int(u['cohort_index'])] = sid_tokens(tok, u['target_sid'])
+    return out

@@ -1,4 +1,4 @@
-"""Drop-in runner: ``python -m rapidtinyrec_b200.run folded|prefill ...``.
+"""Drop-in runner: ``python -m rapidtinyrec_b200.run folded|prefill|quality ...``.
 
 Same entry points, flags and per-request output layout as the reference's
 ``python -m rapidtinyrec.run`` (``run.py:9-19``):
@@ -14,6 +14,12 @@ Same entry points, flags and per-request output layout as the reference's
 * ``prefill`` (``benchmark.py:129-404``): one paired request per user,
   ``users/{i:04d}.json`` with ``runs.{baseline,shared}`` and a ``comparison``,
   plus ``summary.json``; ``--resume`` continues a partial run.
+* ``quality`` (no reference subcommand: the measurements of the reference's BF16
+  study, ``docs/precision-results.md:14-39``, and its auditor's target metrics,
+  ``audit_results.py:117-137``): compares a candidate ``folded`` run with a
+  control run of the same users (``quality.py``); target SIDs come from the
+  reference manifest's ``target_sid`` through the release tokenizer, or from
+  ``--targets``.  Needs no GPU.
 
 Inputs: the real release (``--release-root``; the frozen cohort comes from
 ``--reference-results``, see ``release.py``) or a seeded synthetic workload
@@ -449,13 +455,76 @@ def build_parser():
     p.add_argument('--output-root', type=Path, default=Path('results'))
     p.add_argument('--dtype', choices=('float32', 'bfloat16'), default='float32')
     p.add_argument('--resume', action='store_true')
+    q = sub.add_parser('quality', help='precision report: a candidate folded run against a control run')
+    q.add_argument('--control', type=Path, required=True, help='folded output of the control (e.g. fp32)')
+    q.add_argument('--candidate', type=Path, required=True, help='folded output of the candidate (e.g. bf16)')
+    q.add_argument('--release-root', type=Path, help='release whose tokenizer maps the target SIDs')
+    q.add_argument('--reference-results', type=Path, help='reference results whose manifest holds target_sid')
+    q.add_argument('--targets', type=Path, help='JSON {cohort_index: [t1, t2, t3]} (instead of the release)')
+    q.add_argument('--output', type=Path, required=True)
+    q.add_argument('--resamples', type=int, default=10000, help='paired user-bootstrap resamples')
+    q.add_argument('--users', type=int, default=None, help=argparse.SUPPRESS)
     return ap
+
+
+def read_run(out: Path):
+    """First-repeat records of a folded output, keyed by cohort index."""
+    rows = json.loads((Path(out) / 'requests.json').read_text())
+    recs, lengths = {}, {}
+    for r in rows:
+        if r['repeat'] == 0:
+            recs[int(r['cohort_index'])] = r['run']
+            lengths[int(r['cohort_index'])] = int(r['prompt_tokens'])
+    if not recs:
+        raise SystemExit(f'{out}: no first-repeat requests')
+    return recs, lengths
+
+
+def run_quality(args):
+    """The reference's BF16-study measurements (docs/precision-results.md:14-39):
+    target HitRate/NDCG per arm, paired changes with bootstrap intervals, and
+    rank-list agreement, overall and per prompt length."""
+    from . import quality
+    control, lengths = read_run(args.control)
+    candidate, _ = read_run(args.candidate)
+    common = sorted(set(control) & set(candidate))
+    if not common:
+        raise SystemExit('the two runs share no users')
+    control = {u: control[u] for u in common}
+    candidate = {u: candidate[u] for u in common}
+    targets = None
+    if args.targets is not None:
+        targets = {int(k): tuple(v) for k, v in json.loads(args.targets.read_text()).items()}
+    elif args.release_root is not None:
+        if args.reference_results is None:
+            raise SystemExit('--release-root needs --reference-results (the manifest with target_sid)')
+        from .release import load_targets
+        targets = load_targets(args.release_root, args.reference_results)
+    if targets is not None:
+        targets = {u: targets[u] for u in common if u in targets} if all(u in targets for u in common) else None
+        if targets is None:
+            raise SystemExit('targets do not cover every compared user')
+    report = quality.compare(control, candidate, targets, {u: lengths[u] for u in common}, resamples=args.resamples)
+    report['control'] = str(Path(args.control).resolve())
+    report['candidate'] = str(Path(args.candidate).resolve())
+    for name, path in (('control_manifest', args.control), ('candidate_manifest', args.candidate)):
+        m = Path(path) / 'manifest.json'
+        if m.exists():
+            man = json.loads(m.read_text())
+            report[name] = {k: man.get(k) for k in ('precision', 'dtype', 'experimental', 'variant')}
+    report['targets'] = 'given' if targets is not None else 'none (rank-list agreement only)'
+    args.output.parent.mkdir(parents=True, exist_ok=True)
+    save(args.output, report)
+    announce({'quality_report': str(args.output), **report['agreement']})
+    return report
 
 
 def main(argv=None):
     args = build_parser().parse_args(argv)
     if args.users is not None and args.users < 1:
         raise SystemExit('--users must be positive')
+    if args.mode == 'quality':  # reads finished runs: no GPU needed
+        return run_quality(args)
     import torch
     if not torch.cuda.is_available():
         raise SystemExit('a CUDA GPU is required (the engine has no CPU path)')

@@ -81,7 +81,8 @@ def write_fake_release(root, sids, n_users=3, hidden=64, heads=4, kv_heads=2, in
         body = [int(x) for x in rng.choice(words, size=4 + 2 * i)]
         hist = [vocab[t] for s in sids[i:i + 2] for t in ('<' + x for x in s.split('<')[1:])]
         ids = body + hist + rootids
-        users.append({'cohort_index': i, 'prompt_tokens': len(ids), 'user_id': f'u{i}', 'prompt_token_ids': ids})
+        users.append({'cohort_index': i, 'prompt_tokens': len(ids), 'user_id': f'u{i}', 'prompt_token_ids': ids,
+                      'target_sid': sids[(i + 2) % len(sids)]})  # the held-out next item
     res = root / 'reference_results'
     res.mkdir()
     (res / 'manifest.json').write_text(json.dumps({'users': users}))

@@ -115,3 +115,30 @@ def test_release_path_matches_the_oracle(cuda, tmp_path):
         worst = max(worst, compare_records(r['run'], ref))
     assert worst <= SCORE_TOL
     print(f'release path: max |delta score| vs oracle = {worst:.3e}')
+
+
+def test_quality_report_bf16_against_fp32_with_release_targets(cuda, tmp_path):
+    """The reference's BF16 study on a release-layout checkpoint: two folded runs,
+    then the quality report with the manifest's target SIDs."""
+    from rapidtinyrec_b200 import run
+    sids = [f'<a_{a}><b_{b}><c_{c}>' for a, b, c in itertools.islice(itertools.product(range(8), repeat=3), 0, 512, 6)]
+    res, _ = write_fake_release(tmp_path, sids, n_users=4, hidden=128, heads=2, kv_heads=1, intermediate=128)
+    outs = {}
+    for prec in ('fp32', 'bf16-experimental'):
+        outs[prec] = tmp_path / prec
+        run.main(['folded', '--release-root', str(tmp_path), '--reference-results', str(res), '--output-root',
+                  str(outs[prec]), '--full-cohort', '--repeats', '1', '--precision', prec])
+    report_path = tmp_path / 'quality.json'
+    run.main(['quality', '--control', str(outs['fp32']), '--candidate', str(outs['bf16-experimental']),
+              '--release-root', str(tmp_path), '--reference-results', str(res), '--output', str(report_path),
+              '--resamples', '500'])
+    rep = json.loads(report_path.read_text())
+    agr = rep['agreement']
+    assert agr['users'] == 4 and agr['total_rank_positions'] == 200
+    assert 0 <= agr['changed_full_ranking_lists'] <= 4 and agr['min_top50_overlap'] >= 25
+    for arm in ('control', 'candidate'):
+        m = rep['target_sid_metrics'][arm]
+        assert m['50']['hits'] >= m['10']['hits'] >= m['1']['hits']
+    assert rep['candidate_manifest']['precision'] == 'bf16-experimental'
+    lo, hi = rep['paired_differences_at_10']['hit_rate']['bootstrap_95']
+    assert lo <= rep['paired_differences_at_10']['hit_rate']['mean'] <= hi

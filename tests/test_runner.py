@@ -44,6 +44,17 @@ def test_release_loader_builds_config_trie_and_weights(fake_release):
     assert rel.user_records[1]['user_id'] == 'u1'
 
 
+def test_release_targets_map_sid_strings_to_tokens(fake_release):
+    root, res, vocab, sids = fake_release
+    targets = release.load_targets(root, res)
+    for u in range(3):
+        s = sids[(u + 2) % len(sids)]
+        assert targets[u] == tuple(vocab[t] for t in ('<' + x for x in s.split('<')[1:]))
+    tok, _ = fake_tokenizer()
+    with pytest.raises(ValueError, match='three'):
+        release.sid_tokens(tok, '<a_1><b_2>')
+
+
 def test_release_loader_rejects_a_foreign_root(fake_release):
     root, res, vocab, _ = fake_release
     tok, _ = fake_tokenizer()
