@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "engine.h"
+#include "tc_epilogue.cuh"
 #include "tcgen05.cuh"
 
 namespace rtr {
@@ -47,7 +48,7 @@ constexpr int BF_W_BYTES = BF_CPS * BF_WC_BYTES;      // one stage
 constexpr int BF_X_BYTES = BF_CPS * BF_XC_BYTES;
 constexpr int BF_D_COLS = BF_NTOK;
 constexpr int BF_TMEM_COLS = 2 * BF_D_COLS;   // 128: double-buffered accumulator
-constexpr int BF_NBARS = 2 * BF_STAGES + 4;
+constexpr int BF_NBARS = 2 * BF_STAGES + 5;
 constexpr int BF_RING_BYTES = BF_STAGES * (BF_W_BYTES + BF_X_BYTES);
 static_assert(2 * BF_GSTAGES == BF_STAGES, "one pass over the ring = both accumulator buffers");
 constexpr int BF_SMEM_BYTES = BF_RING_BYTES + 1024 + 8 * BF_NBARS + 16;
@@ -153,11 +154,12 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
   }
 }
 
-// Split-K part 1 (last CTA of a tile): partials summed in split order into a
-// [64][128] shared tile.
-RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int rows, int cols4, int tile, long tstride) {
+// Split-K sum (a CTA finishing a tile): rows [row0, row0 + rows) of the
+// partials summed in split order into the same rows of a [64][128] shared tile.
+RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int row0, int rows, int cols4, int tile, long tstride) {
   constexpr int SLOTS = (BF_NTOK * BF_WROWS / 4 + BF_THREADS - 1) / BF_THREADS;
-  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (BF_NTOK * BF_WROWS));
+  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (BF_NTOK * BF_WROWS)) + row0 * 32;
+  red4 += row0 * 32;
   const long zs = tstride >> 2;
   const int nslots = rows * (BF_WROWS / 4);
   float4 s[SLOTS];
@@ -197,9 +199,10 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   uint64_t* s_empty = s_full + BF_STAGES;   // [BF_STAGES] the stage's MMAs are done
   uint64_t* d_full = s_empty + BF_STAGES;   // [2]
   uint64_t* d_empty = d_full + 2;           // [2]
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 2);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2) + 1;
-  __shared__ int last_cta;
+  uint64_t* red_bar = d_empty + 2;         // split-K finish: every CTA of the cluster arrived
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 1) + 1;
+  __shared__ int go;                        // this cluster finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * BF_NTOK;
@@ -214,6 +217,8 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < BF_STAGES; ++s) { mbar_init(smem_addr(&s_full[s]), 2); mbar_init(smem_addr(&s_empty[s]), 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(smem_addr(&d_full[b]), 1); mbar_init(smem_addr(&d_empty[b]), 4); }
+    mbar_init(smem_addr(red_bar), cluster_ncta());
+    go = 0;
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmW);
@@ -222,6 +227,7 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   if (warp == 1) tmem_alloc(smem_addr(tmem_slot), BF_TMEM_COLS);
   tc_fence_before();
   __syncthreads();
+  if (cluster_ncta() > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -367,16 +373,10 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int* tk = p.tickets + tile;
-      last_cta = atomicAdd(tk, 1) == p.splits - 1;
-      if (last_cta) *tk = 0;  // re-arm for the next launch / graph replay
-    }
-    __syncthreads();
-    if (!last_cta) return;
-    __threadfence();
-    bf_splitk_sum(p, red4, rows, cols4, tile, tstride);
-    bf_tile_epilogue(p, red4, BF_WROWS / 4, tok0, n0, rows, cols4);
+    int r0 = 0, r1 = 0;
+    if (!splitk_claim(p, smem_addr(red_bar), &go, rows, tile, r0, r1)) return;
+    bf_splitk_sum(p, red4, r0, r1 - r0, cols4, tile, tstride);
+    bf_tile_epilogue(p, red4 + r0 * 32, BF_WROWS / 4, tok0 + r0, n0, r1 - r0, cols4);
     return;
   }
   if (have && n < p.N) {
@@ -436,16 +436,16 @@ bool make_tmap_packed_bf16(TensorMap* out, const void* packed, int N, int K) {
   return make_tmap_bf16(out, packed, rows, BF_KC, BF_KC, BF_WROWS);
 }
 
-cudaError_t gemm_bf16_init() {
-  return cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BF_SMEM_BYTES);
-}
+static int g_bf_clusters[kMaxDevices][TC_MAX_CLUSTER + 1];
 
-static int bf_splits(int tiles, int nchunks, int sms) {
-  if (tiles >= sms) return 1;
-  int s = sms / tiles;
-  if (s > nchunks / 2) s = nchunks / 2;  // keep at least two chunks per split
-  if (s > 16) s = 16;
-  return s < 1 ? 1 : s;
+cudaError_t gemm_bf16_init() {
+  cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BF_SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  return query_cluster_waves(reinterpret_cast<const void*>(gemm_bf16_kernel), BF_THREADS, BF_SMEM_BYTES,
+                             g_bf_clusters[dev], TC_MAX_CLUSTER);
 }
 
 cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int ldc, const float* bias, int M, int N,
@@ -462,8 +462,12 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
   if (K % 8) return cudaErrorInvalidValue;  // TMA rows of the activations: 16-byte multiples
   const int tt = (M + BF_NTOK - 1) / BF_NTOK, wt = (N + BF_WROWS - 1) / BF_WROWS;
   const int nchunks = (K + BF_KC - 1) / BF_KC;
-  int splits = bf_splits(tt * wt, nchunks, sms);
-  while (splits > 1 && ((size_t)splits * tt * wt * BF_NTOK * BF_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
+  // a 64-element bf16 chunk row is 128 bytes, as a 32-element tf32 one: the same plan
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const SplitPlan plan = tc_split_plan(tt * wt, nchunks, sms, g_bf_clusters[dev < kMaxDevices ? dev : 0],
+                                       TC_MAX_CLUSTER, ws_floats, (long)BF_NTOK * BF_WROWS, max_tickets);
+  const int splits = plan.splits, cs = plan.cluster;
   BfParams p{C, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
   if (rope) p.rope = *rope;
   cudaLaunchConfig_t cfg = {};
@@ -471,11 +475,15 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
   cfg.blockDim = dim3(BF_THREADS);
   cfg.dynamicSmemBytes = BF_SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = cs;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = cs > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel, *reinterpret_cast<const CUtensorMap*>(&tmW),
                             *reinterpret_cast<const CUtensorMap*>(&tmX), p);
 }

@@ -26,8 +26,10 @@
 // waits and commits cost as much again unless they are amortised over a
 // stage (16 MMAs per wait pair and commit).
 // Every role has its own ring, so loading, splitting, MMA and promotion of
-// different chunks overlap.  Small GEMMs split K over CTAs; the
-// last CTA to arrive sums the partial tiles in split order (deterministic).
+// different chunks overlap.  Small GEMMs split K over CTAs, launched as
+// clusters of consecutive splits; the cluster holding the last partial to
+// arrive sums the partial tiles in split order (deterministic), each CTA a
+// slice of the rows.
 // Every mbarrier wait is bounded (~1 s): on expiry the CTA records
 // RTR_DEV_TIMEOUT, stops issuing work, drains what it issued and frees TMEM.
 #include <cuda.h>
@@ -58,7 +60,7 @@ constexpr int TC_D_COLS = 2 * TC_NTOK;                // one accumulator buffer
 constexpr int TC_AC_COLS = 2 * TC_KC;                 // W_b and W_s of one chunk
 constexpr int TC_A_COLS = TC_CPS * TC_AC_COLS;        // one stage
 constexpr int TC_TMEM_COLS = 512;                     // 2 accumulators + 2 A stages
-constexpr int TC_NBARS = 2 * TC_WSTAGES + 2 * TC_XSTAGES + 2 * TC_STAGES + 4;
+constexpr int TC_NBARS = 2 * TC_WSTAGES + 2 * TC_XSTAGES + 2 * TC_STAGES + 5;
 constexpr int TC_SMEM_BYTES = TC_WSTAGES * TC_W_BYTES + TC_XSTAGES * TC_X_BYTES + 1024 + 8 * TC_NBARS + 16;
 static_assert(2 * TC_D_COLS + TC_STAGES * TC_A_COLS <= TC_TMEM_COLS, "tensor memory budget");
 constexpr int TC_GSTAGES = TC_PROMOTE / TC_CPS;       // stages per promotion group
@@ -80,9 +82,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t* s_empty = a_full + TC_STAGES;   // [TC_STAGES] MMAs of the stage done (frees A)
   uint64_t* d_full = s_empty + TC_STAGES;   // [2]
   uint64_t* d_empty = d_full + 2;           // [2]
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 2);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 2) + 1;
-  __shared__ int last_cta;
+  uint64_t* red_bar = d_empty + 2;         // split-K finish: every CTA of the cluster arrived
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 1) + 1;
+  __shared__ int go;                        // this cluster finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * TC_NTOK;
@@ -99,6 +102,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     for (int s = 0; s < TC_XSTAGES; ++s) { mbar_init(smem_addr(&x_full[s]), 1); mbar_init(smem_addr(&x_empty[s]), 1); }
     for (int s = 0; s < TC_STAGES; ++s) { mbar_init(smem_addr(&a_full[s]), 4); mbar_init(smem_addr(&s_empty[s]), 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(smem_addr(&d_full[b]), 1); mbar_init(smem_addr(&d_empty[b]), 4); }
+    mbar_init(smem_addr(red_bar), cluster_ncta());
+    go = 0;
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmW);
@@ -108,6 +113,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 1) tmem_alloc(smem_addr(tmem_slot), TC_TMEM_COLS);
   tc_fence_before();
   __syncthreads();
+  if (cluster_ncta() > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_a = tmem + 2 * TC_D_COLS;  // A stages after the two accumulators
@@ -310,16 +316,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int* tk = p.tickets + tile;
-      last_cta = atomicAdd(tk, 1) == p.splits - 1;
-      if (last_cta) *tk = 0;  // re-arm for the next launch / graph replay
-    }
-    __syncthreads();
-    if (!last_cta) return;
-    __threadfence();
-    splitk_sum<TC_THREADS, TC_NTOK>(p, red4, rows, cols4, tile, tstride);
-    tile_epilogue<TC_THREADS>(p, red4, TC_WROWS / 4, tok0, n0, rows, cols4);
+    splitk_finish<TC_THREADS, TC_NTOK>(p, red4, smem_addr(red_bar), &go, tok0, n0, rows, cols4, tile, tstride);
     return;
   }
   // Stage the finished tile in shared memory ([64][TC_WROWS + 4], padded so
@@ -384,8 +381,16 @@ bool make_tmap_packed(TensorMap* out, const float* packed, int N, int K) {
   return make_tmap_f32(out, packed, rows, TC_KC, TC_KC, TC_WROWS);
 }
 
+int g_tc_clusters[kMaxDevices][TC_MAX_CLUSTER + 1];
+
 cudaError_t gemm_tc_init() {
-  return cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES);
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_BYTES);
+  if (e != cudaSuccess) return e;
+  int dev = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  return query_cluster_waves(reinterpret_cast<const void*>(gemm_tc_kernel), TC_THREADS, TC_SMEM_BYTES,
+                             g_tc_clusters[dev], TC_MAX_CLUSTER);
 }
 
 cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap& tmXs, float* C, float* C_big,
@@ -405,8 +410,11 @@ cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap
   if (fold && fold->ss_in && (epi == EPI_RESID || fold->hidden != K)) return cudaErrorInvalidValue;
   const int tt = (M + TC_NTOK - 1) / TC_NTOK, wt = (N + TC_WROWS - 1) / TC_WROWS;
   const int nchunks = (K + TC_KC - 1) / TC_KC;
-  int splits = tc_split_count(tt * wt, nchunks, sms);
-  while (splits > 1 && ((size_t)splits * tt * wt * TC_NTOK * TC_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const SplitPlan plan = tc_split_plan(tt * wt, nchunks, sms, g_tc_clusters[dev < kMaxDevices ? dev : 0], TC_MAX_CLUSTER,
+                                       ws_floats, (long)TC_NTOK * TC_WROWS, max_tickets);
+  const int splits = plan.splits, cs = plan.cluster;
   TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}, {}};
   if (rope) p.rope = *rope;
   if (fold) p.fold = *fold;
@@ -415,11 +423,15 @@ cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = TC_SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = cs;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = cs > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, *reinterpret_cast<const CUtensorMap*>(&tmW),
                             *reinterpret_cast<const CUtensorMap*>(&tmXb), *reinterpret_cast<const CUtensorMap*>(&tmXs),
                             p);

@@ -47,7 +47,7 @@ constexpr int TW_D_COLS = 2 * TW_NTOK;            // 256
 constexpr int TW_AC_COLS = 2 * TW_KC;             // W_b and W_s of one chunk
 constexpr int TW_A_COLS = TW_CPS * TW_AC_COLS;    // one stage
 constexpr int TW_TMEM_COLS = 512;                 // accumulator + 2 A stages
-constexpr int TW_NBARS = 2 * TW_WSTAGES + 3 * TW_STAGES + 2;
+constexpr int TW_NBARS = 2 * TW_WSTAGES + 3 * TW_STAGES + 3;
 constexpr int TW_RING_BYTES = TW_WSTAGES * TW_W_BYTES + TW_STAGES * TW_X_BYTES;
 constexpr int TW_SMEM_BYTES = TW_RING_BYTES + 1024 + 8 * TW_NBARS + 16;
 constexpr int TW_RLD = TW_WROWS + 4;
@@ -70,9 +70,10 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
   uint64_t* s_empty = a_full + TW_STAGES;   // [TW_STAGES] MMAs of the stage done (frees A and X)
   uint64_t* d_full = s_empty + TW_STAGES;
   uint64_t* d_empty = d_full + 1;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(d_empty + 1);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_empty + 1) + 1;
-  __shared__ int last_cta;
+  uint64_t* red_bar = d_empty + 1;         // split-K finish: every CTA of the cluster arrived
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 1) + 1;
+  __shared__ int go;                        // this cluster finishes the tile
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * TW_NTOK;
@@ -93,6 +94,8 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
     }
     mbar_init(smem_addr(d_full), 1);
     mbar_init(smem_addr(d_empty), 8);
+    mbar_init(smem_addr(red_bar), cluster_ncta());
+    go = 0;
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     tma_prefetch_desc(&tmW);
@@ -102,6 +105,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
   if (warp == 1) tmem_alloc(smem_addr(tmem_slot), TW_TMEM_COLS);
   tc_fence_before();
   __syncthreads();
+  if (cluster_ncta() > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_a = tmem + TW_D_COLS;
@@ -287,16 +291,7 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int* tk = p.tickets + tile;
-      last_cta = atomicAdd(tk, 1) == p.splits - 1;
-      if (last_cta) *tk = 0;  // re-arm for the next launch / graph replay
-    }
-    __syncthreads();
-    if (!last_cta) return;
-    __threadfence();
-    splitk_sum<TW_THREADS, TW_NTOK>(p, red4, rows, cols4, tile, tstride);
-    tile_epilogue<TW_THREADS>(p, red4, TW_WROWS / 4, tok0, n0, rows, cols4);
+    splitk_finish<TW_THREADS, TW_NTOK>(p, red4, smem_addr(red_bar), &go, tok0, n0, rows, cols4, tile, tstride);
     return;
   }
   if (have && n < p.N) {
@@ -330,8 +325,11 @@ cudaError_t gemm_tc_wide(const TensorMap& tmW, const TensorMap& tmXb, const Tens
   if (fold && fold->ss_in && (epi == EPI_RESID || fold->hidden != K)) return cudaErrorInvalidValue;
   const int tt = (M + TW_NTOK - 1) / TW_NTOK, wt = (N + TW_WROWS - 1) / TW_WROWS;
   const int nchunks = (K + TW_KC - 1) / TW_KC;
-  int splits = tc_split_count(tt * wt, nchunks, sms);
-  while (splits > 1 && ((size_t)splits * tt * wt * TW_NTOK * TW_WROWS > ws_floats || tt * wt > max_tickets)) --splits;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const SplitPlan plan = tc_split_plan(tt * wt, nchunks, sms, g_tc_clusters[dev < kMaxDevices ? dev : 0], TC_MAX_CLUSTER,
+                                       ws_floats, (long)TW_NTOK * TW_WROWS, max_tickets);
+  const int splits = plan.splits, cs = plan.cluster;
   TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}, {}};
   if (rope) p.rope = *rope;
   if (fold) p.fold = *fold;
@@ -340,11 +338,15 @@ cudaError_t gemm_tc_wide(const TensorMap& tmW, const TensorMap& tmXb, const Tens
   cfg.blockDim = dim3(TW_THREADS);
   cfg.dynamicSmemBytes = TW_SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = cs;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = cs > 1 ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, gemm_tc_wide_kernel, *reinterpret_cast<const CUtensorMap*>(&tmW),
                             *reinterpret_cast<const CUtensorMap*>(&tmXb),
                             *reinterpret_cast<const CUtensorMap*>(&tmXs), p);

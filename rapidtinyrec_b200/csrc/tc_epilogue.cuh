@@ -32,19 +32,97 @@ inline int tc_split_count(int tiles, int nchunks, int sms) {
   return s < 1 ? 1 : s;
 }
 
-// Split-K finish, part 1, run by every thread of the last CTA to arrive on a
-// tile: sum the partial tiles in split order into a [NTOK][128] shared tile
-// (float4 slots, four splits of loads in flight per slot).
+// Split-K clusters: at most this many CTAs (consecutive splits of one tile).
+constexpr int TC_MAX_CLUSTER = 8;
+constexpr int kMaxDevices = 16;
+
+// Clusters of CTAs that one wave of a one-CTA-per-SM kernel holds, per
+// cluster size (index), per device; filled by gemm_tc_init() and used by both
+// tf32 kernels.
+extern int g_tc_clusters[kMaxDevices][TC_MAX_CLUSTER + 1];
+
+// For cluster sizes 2..max_cs: how many clusters of that size one wave of
+// `kernel` holds (cudaOccupancyMaxActiveClusters); 0 where it is not known.
+inline cudaError_t query_cluster_waves(const void* kernel, int threads, int smem, int* out, int max_cs) {
+  out[0] = out[1] = 0;
+  for (int cs = 2; cs <= max_cs; ++cs) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, 1, cs);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = cs;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    out[cs] = n;
+  }
+  return cudaSuccess;
+}
+
+// Split-K plan of the tf32 kernels: the split count and the cluster size
+// that finishes each tile.  Candidates run from the SM-filling count
+// (tc_split_count) down to half of it; each takes every cluster size up to the
+// cap (RTR_TC_CLUSTER, default 8) that divides it and whose clusters all fit
+// in one wave.  The plan with the least modelled time wins, the model fitted
+// to launches timed back to back on B200 at M = 50:
+//   weight stream  max(0.1 us per chunk of a split, the tiles' weight bytes
+//                  at 6.5 TB/s scaled by the share of SMs the grid uses)
+//   finish         3.1 ns per split per row of the slice (64 / cluster rows)
+//   clusters       0.5 us per CTA beyond two (co-scheduling a larger cluster
+//                  on one GPC delays its start)
+// Both kernels take the same plan for the same tiles and K (one CTA per SM
+// in both, one wave table, 64 nominal rows), so their sums agree bit for bit.
+struct SplitPlan {
+  int splits, cluster;
+};
+inline SplitPlan tc_split_plan(int tiles, int nchunks, int sms, const int* waves, int max_cs, size_t ws_floats,
+                               long tile_floats, int max_tickets) {
+  static const int cap = [] {
+    const char* e = getenv("RTR_TC_CLUSTER");
+    const int v = e ? atoi(e) : 8;
+    return v < 1 ? 1 : v;
+  }();
+  int s0 = tc_split_count(tiles, nchunks, sms);
+  while (s0 > 1 && ((size_t)s0 * tiles * tile_floats > ws_floats || tiles > max_tickets)) --s0;
+  SplitPlan best{s0, 1};
+  if (s0 < 2) return best;
+  const double stream_us = (double)tiles * 128 * nchunks * 32 * 4 / 6.5e6;  // all SMs streaming
+  double best_t = 1e30;
+  for (int s = s0; s >= 2 && 2 * s >= s0; --s) {
+    const double share = (double)tiles * s / sms;
+    const double t_main = fmax(0.1 * ((nchunks + s - 1) / s), stream_us / (share < 1.0 ? share : 1.0));
+    for (int c = 1; c <= (cap < max_cs ? cap : max_cs); ++c) {
+      if (s % c != 0 || (c > 1 && (long)tiles * (s / c) > waves[c])) continue;
+      const double t = t_main + 0.0031 * s * ((64 + c - 1) / c) + (c > 2 ? 0.5 * (c - 2) : 0.0);
+      if (t < best_t - 1e-9) { best_t = t; best = SplitPlan{s, c}; }
+    }
+  }
+  return best;
+}
+
+// Split-K sum, run by every thread of a CTA finishing a tile: rows
+// [row0, row0 + rows) of the partial tiles summed in split order into the same
+// rows of a [NTOK][128] shared tile (float4 slots, four splits of loads in
+// flight per slot).
 template <int THREADS, int NTOK>
-RTR_DEVICE void splitk_sum(const TcParams& p, float4* red4, int rows, int cols4, int tile, long tstride) {
+RTR_DEVICE void splitk_sum(const TcParams& p, float4* red4, int row0, int rows, int cols4, int tile, long tstride) {
   constexpr int SLOTS = (NTOK * 128 / 4 + THREADS - 1) / THREADS;
-  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (NTOK * 128));
+  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (NTOK * 128)) + row0 * 32;
+  red4 += row0 * 32;
   const long zs = tstride >> 2;
   const int nslots = rows * 32;
   // slots in groups of G keep four splits of loads in flight without running out of registers
   constexpr int G = SLOTS < 6 ? SLOTS : 3;
 #pragma unroll 1
-  for (int u0 = 0; u0 < SLOTS; u0 += G) {
+  for (int u0 = 0; u0 < SLOTS && u0 * THREADS < nslots; u0 += G) {
     float4 s[G];
 #pragma unroll
     for (int u = 0; u < G; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -71,7 +149,6 @@ RTR_DEVICE void splitk_sum(const TcParams& p, float4* red4, int rows, int cols4,
   }
   __syncthreads();
 }
-
 
 // Epilogue from a [rows][ld4 float4] shared tile of finished sums, run by
 // every thread of the CTA with float4 loads and stores (N, ldc and the head
@@ -184,6 +261,57 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
     else if (p.epi == EPI_RESID) v = f4add(*c, v);
     *c = v;
   }
+}
+
+// Split-K finish, claim step, after every thread of the CTA has stored its
+// partial tile (then __threadfence + __syncthreads).  A tile's splits are
+// launched as clusters of consecutive splits; the cluster holding the last
+// partial to arrive finishes the tile, each of its CTAs summing a slice of the
+// rows over all splits in split order (the bits one CTA summing every row
+// would get) and running the epilogue on that slice.  Returns whether this
+// CTA finishes rows [r0, r1).  `red_bar` (count = cluster size) and `*go` (0)
+// were set before the start-up cluster barrier.
+template <class P>
+RTR_DEVICE bool splitk_claim(const P& p, uint32_t red_bar, int* go, int rows, int tile, int& r0, int& r1) {
+  const uint32_t cs = cluster_ncta();
+  if (threadIdx.x == 0) {
+    int* tk = p.tickets + tile;
+    const bool last = atomicAdd(tk, 1) == p.splits - 1;
+    if (last) {
+      *tk = 0;  // re-arm for the next launch / graph replay
+      __threadfence();
+    }
+    if (cs == 1) {
+      *go = last;
+    } else {
+      const uint32_t goa = smem_addr(go);
+      for (uint32_t r = 0; r < cs; ++r) {
+        if (last) st_cluster_u32(cluster_map(goa, r), 1u);
+        mbar_arrive_remote(cluster_map(red_bar, r));
+      }
+      // every CTA of the cluster has arrived: no remote access to this CTA follows
+      if (!mbar_wait_cluster(red_bar, 0)) {
+        atomicOr(p.status, RTR_DEV_TIMEOUT);
+        *go = 0;
+      }
+    }
+  }
+  __syncthreads();
+  if (!*reinterpret_cast<volatile int*>(go)) return false;
+  __threadfence();
+  const int r = (int)cluster_rank();
+  r0 = r * rows / (int)cs;
+  r1 = (r + 1) * rows / (int)cs;
+  return r1 > r0;
+}
+
+template <int THREADS, int NTOK>
+RTR_DEVICE void splitk_finish(const TcParams& p, float4* red4, uint32_t red_bar, int* go, int tok0, int n0,
+                              int rows, int cols4, int tile, long tstride) {
+  int r0 = 0, r1 = 0;
+  if (!splitk_claim(p, red_bar, go, rows, tile, r0, r1)) return;
+  splitk_sum<THREADS, NTOK>(p, red4, r0, r1 - r0, cols4, tile, tstride);
+  tile_epilogue<THREADS>(p, red4 + r0 * 32, 32, tok0 + r0, n0, r1 - r0, cols4);
 }
 
 }  // namespace rtr
