@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 1) + 1;
   __shared__ int go;                        // this cluster finishes the tile
+  __shared__ float prsc[TC_NTOK];           // persistent launch: row scales of the folded RMSNorm
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * TC_NTOK;
@@ -93,7 +94,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const int nchunks = (p.K + TC_KC - 1) / TC_KC;
   const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
   const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
-  const int nloc = c1 - c0;
+  // Persistent launch (fewer CTAs than weight tiles; one split, whole
+  // promotion groups per tile): this CTA runs weight tiles blockIdx.y,
+  // blockIdx.y + gridDim.y, ... as one chunk stream, and the promoters store
+  // each finished tile while the next one streams.
+  const int wtiles = (p.N + TC_WROWS - 1) / TC_WROWS;
+  const bool persist = (int)gridDim.y < wtiles;
+  const int ntl = persist ? (wtiles - (int)blockIdx.y + (int)gridDim.y - 1) / (int)gridDim.y : 1;
+  const int nloc_t = c1 - c0;  // chunks of one tile
+  const int nloc = nloc_t * ntl;
   const int nstages = (nloc + TC_CPS - 1) / TC_CPS;
   const int ngroups = (nloc + TC_PROMOTE - 1) / TC_PROMOTE;
 
@@ -131,7 +140,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t fb = smem_addr(&w_full[s]);
         mbar_expect_tx(fb, TC_W_BYTES);
         // packed weights: the [128 x 32] block of (tile, chunk) is 16 KB contiguous
-        tma_load_2d(smem_addr(wring + s * TC_W_BYTES), &tmW, 0, (blockIdx.y * nchunks + c0 + i) * TC_WROWS, fb);
+        const int y = (int)blockIdx.y + (i / nloc_t) * (int)gridDim.y;
+        tma_load_2d(smem_addr(wring + s * TC_W_BYTES), &tmW, 0, (y * nchunks + c0 + i % nloc_t) * TC_WROWS, fb);
         w_issued = i + 1;
       }
     }
@@ -192,7 +202,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         uint8_t* st = xring + s * TC_X_BYTES;
         mbar_expect_tx(fb, nc * TC_XC_BYTES);
         for (int c = 0; c < nc; ++c) {
-          const int kx = (c0 + q * TC_CPS + c) * TC_KC;
+          const int kx = (c0 + (q * TC_CPS + c) % nloc_t) * TC_KC;
           tma_load_2d(smem_addr(st + c * TC_XC_BYTES), &tmXb, kx, tok0, fb);
           tma_load_2d(smem_addr(st + c * TC_XC_BYTES + TC_XC_BYTES / 2), &tmXs, kx, tok0, fb);
         }
@@ -202,50 +212,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncwarp();
   } else if (warp <= 5) {
     // ------------------------------- warps 2..5: split W rows into TMEM
+    // A stage's two chunks are read from shared memory together (16
+    // independent loads in flight: the reads queue behind the TMA writes and
+    // the MMAs' operand reads), split, and stored once the MMAs of the
+    // stage's previous use are done.
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // TMEM lane = weight row of the tile
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-    for (int i = 0; i < nloc; ++i) {
-      const int ws = i % TC_WSTAGES, q = i / TC_CPS, c = i % TC_CPS, s = q % TC_STAGES;
-      if (!mbar_wait(smem_addr(&w_full[ws]), (i / TC_WSTAGES) & 1, abort_flag)) break;
-      const uint8_t* tile = wring + ws * TC_W_BYTES + row * 128;
-      uint32_t big[TC_KC], small[TC_KC];
+    for (int q = 0; q < nstages; ++q) {
+      const int s = q % TC_STAGES;
+      const int nc = nloc - q * TC_CPS < TC_CPS ? nloc - q * TC_CPS : TC_CPS;
+      uint32_t v[TC_CPS][TC_KC];
+      bool ok = true;
 #pragma unroll
-      for (int k4 = 0; k4 < TC_KC / 4; ++k4) {  // undo the 128B swizzle: chunk k4 lives at k4 ^ (row % 8)
-        const float4 v = *reinterpret_cast<const float4*>(tile + ((k4 ^ (row & 7)) << 4));
-        big[4 * k4] = __float_as_uint(v.x); big[4 * k4 + 1] = __float_as_uint(v.y);
-        big[4 * k4 + 2] = __float_as_uint(v.z); big[4 * k4 + 3] = __float_as_uint(v.w);
+      for (int c = 0; c < TC_CPS; ++c) {
+        if (c < nc) {
+          const int i = q * TC_CPS + c, ws = i % TC_WSTAGES;
+          if (!mbar_wait(smem_addr(&w_full[ws]), (i / TC_WSTAGES) & 1, abort_flag)) { ok = false; break; }
+          const uint8_t* tile = wring + ws * TC_W_BYTES + row * 128;
+#pragma unroll
+          for (int k4 = 0; k4 < TC_KC / 4; ++k4) {  // undo the 128B swizzle: chunk k4 lives at k4 ^ (row % 8)
+            const float4 f = *reinterpret_cast<const float4*>(tile + ((k4 ^ (row & 7)) << 4));
+            v[c][4 * k4] = __float_as_uint(f.x); v[c][4 * k4 + 1] = __float_as_uint(f.y);
+            v[c][4 * k4 + 2] = __float_as_uint(f.z); v[c][4 * k4 + 3] = __float_as_uint(f.w);
+          }
+        }
       }
+      if (!ok) break;
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&w_empty[ws]));  // the row is in registers
-#pragma unroll
-      for (int k = 0; k < TC_KC; ++k) {
-        const float w = __uint_as_float(big[k]);
-        const float bv = tf32_round(w);
-        big[k] = __float_as_uint(bv);
-        small[k] = __float_as_uint(w - bv);
-      }
-      // the first chunk of a stage waits until the MMAs of its last use are done
-      if (c == 0) {
-        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / TC_STAGES) & 1) ^ 1, abort_flag)) break;
-        // the MMAs of stage q - TC_STAGES are done: relay the release of its activation stage
-        if (warp == 2 && lane == 0 && q >= TC_STAGES) mbar_arrive(smem_addr(&x_empty[(q - TC_STAGES) % TC_XSTAGES]));
-      }
+      if (lane == 0)  // the rows are in registers
+        for (int c = 0; c < nc; ++c) mbar_arrive(smem_addr(&w_empty[(q * TC_CPS + c) % TC_WSTAGES]));
+      // the stage waits until the MMAs of its last use are done
+      if (!mbar_wait(smem_addr(&s_empty[s]), ((q / TC_STAGES) & 1) ^ 1, abort_flag)) break;
+      // the MMAs of stage q - TC_STAGES are done: relay the release of its activation stage
+      if (warp == 2 && lane == 0 && q >= TC_STAGES) mbar_arrive(smem_addr(&x_empty[(q - TC_STAGES) % TC_XSTAGES]));
       tc_fence_after();
-      const uint32_t a = tmem_a + lane_base + s * TC_A_COLS + c * TC_AC_COLS;
-      tmem_st32(a, big);
-      tmem_st32(a + TC_KC, small);
-      if (c == TC_CPS - 1 || i == nloc - 1) {  // the stage is complete
-        tmem_st_wait();
-        tc_fence_before();
-        // one converter also waits for the stage's activation tiles, so the
-        // MMA thread waits on a single barrier per stage
-        const bool x_ok =
-            warp != 2 || mbar_wait(smem_addr(&x_full[q % TC_XSTAGES]), (q / TC_XSTAGES) & 1, abort_flag);
-        __syncwarp();
-        if (!x_ok) break;
-        if (lane == 0) mbar_arrive(smem_addr(&a_full[s]));
+#pragma unroll
+      for (int c = 0; c < TC_CPS; ++c) {
+        if (c < nc) {
+          uint32_t big[TC_KC];
+#pragma unroll
+          for (int k = 0; k < TC_KC; ++k) {
+            const float w = __uint_as_float(v[c][k]);
+            const float bv = tf32_round(w);
+            big[k] = __float_as_uint(bv);
+            v[c][k] = __float_as_uint(w - bv);
+          }
+          const uint32_t a = tmem_a + lane_base + s * TC_A_COLS + c * TC_AC_COLS;
+          tmem_st32(a, big);
+          tmem_st32(a + TC_KC, v[c]);
+        }
       }
+      tmem_st_wait();
+      tc_fence_before();
+      // one converter also waits for the stage's activation tiles, so the
+      // MMA thread waits on a single barrier per stage
+      const bool x_ok = warp != 2 || mbar_wait(smem_addr(&x_full[q % TC_XSTAGES]), (q / TC_XSTAGES) & 1, abort_flag);
+      __syncwarp();
+      if (!x_ok) break;
+      if (lane == 0) mbar_arrive(smem_addr(&a_full[s]));
     }
   } else {
     // ------------------------- warps 6..9: promote accumulators, epilogue
@@ -253,11 +278,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 #pragma unroll
     for (int j = 0; j < TC_NTOK; ++j) acc[j] = 0.f;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const int gpt = ngroups / ntl;  // promotion groups per tile
+    const int prow = p.M - tok0 < TC_NTOK ? p.M - tok0 : TC_NTOK;
+    if (persist && p.fold.ss_in) {
+      // the folded RMSNorm's row scales, as tile_epilogue computes them
+      const int t = threadIdx.x - 6 * 32;
+      if (t < prow) {
+        float ss = 0.f;
+        for (int k = 0; k < p.fold.parts; ++k) ss += p.fold.ss_in[(long)k * p.fold.ld + tok0 + t];
+        prsc[t] = 1.0f / sqrtf(ss / (float)p.fold.hidden + p.fold.eps);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the four promoter warps
+    }
     for (int g = 0; g < ngroups; ++g) {
       const int b = g & 1;
       if (!mbar_wait(smem_addr(&d_full[b]), (g >> 1) & 1, abort_flag)) break;
       tc_fence_after();
       const uint32_t d = tmem + lane_base + b * TC_D_COLS;
+      // persistent launch, last group of a tile: store the finished tile from
+      // registers (EPI_STORE, the products tile_epilogue forms) and restart
+      const bool tile_done = persist && (g + 1) % gpt == 0;
+      const int n = ((int)blockIdx.y + (g / gpt) * (int)gridDim.y) * TC_WROWS + (warp & 3) * 32 + lane;
 #pragma unroll
       for (int cb = 0; cb < TC_NTOK; cb += 32) {
         uint32_t r[32];
@@ -270,6 +311,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[cb + j] += part[j] + __uint_as_float(r[j]);
+        if (tile_done) {
+          float* c = p.C + (long)(tok0 + cb) * p.ldc + n;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (cb + j < prow && n < p.N) *c = p.fold.ss_in ? acc[cb + j] * prsc[cb + j] : acc[cb + j];
+            acc[cb + j] = 0.f;
+            c += p.ldc;
+          }
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -296,7 +346,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, TC_TMEM_COLS);
   }
-  if (*abort_flag) return;
+  if (*abort_flag || persist) return;
 
   const bool have = warp >= 6 && warp <= 9;
   const int quarter = warp & 3;
@@ -418,8 +468,15 @@ cudaError_t gemm_tc(const TensorMap& tmW, const TensorMap& tmXb, const TensorMap
   TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}, {}};
   if (rope) p.rope = *rope;
   if (fold) p.fold = *fold;
+  // many weight tiles of one row tile (the LM head): one persistent CTA per
+  // SM instead of waves of one-tile CTAs (RTR_TC_PERSIST=0 turns it off)
+  static const bool persist_on = [] {
+    const char* e = getenv("RTR_TC_PERSIST");
+    return !(e && e[0] == '0');
+  }();
+  const bool persist = persist_on && splits == 1 && tt == 1 && epi == EPI_STORE && wt > sms && nchunks % TC_PROMOTE == 0;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tt, wt, splits);
+  cfg.gridDim = dim3(tt, persist ? sms : wt, splits);
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = TC_SMEM_BYTES;
   cfg.stream = stream;
