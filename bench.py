@@ -384,7 +384,8 @@ def run_ours(args):
         if cfg.dtype == 'bf16':
             gemm_kernel = 'gemm_bf16_kernel (tcgen05 kind::f16'
         else:
-            gemm_kernel = 'gemm_tc_kernel (tcgen05 3xTF32' if rep['tensor_core_gemm'] else 'gemm_f32_kernel (FFMA'
+            gemm_kernel = {2: 'gemm_f16x2_kernel (tcgen05 fp16 pairs', 1: 'gemm_tc_kernel (tcgen05 3xTF32'}.get(
+                rep['tensor_core_gemm'], 'gemm_f32_kernel (FFMA')
         gemm_kernel += f', decode projections + LM head, M={engine.beams})'
         line = {
             'metric': METRIC, 'value': round(value, 3), 'unit': 'users/s', 'n_gpus': world, 'steps': args.steps,

@@ -194,7 +194,8 @@ typedef struct {
   int64_t device_bytes;           /* all device memory the session holds       */
   int64_t h2d_bytes_per_request;  /* prompt ids + length                       */
   int64_t d2h_bytes_per_request;  /* the result record                         */
-  int64_t tensor_core_gemm;       /* 1: tcgen05 3xTF32 projections, 0: FFMA    */
+  int64_t tensor_core_gemm;       /* 2: tcgen05 fp16-pair projections (fp32
+                                     default), 1: tcgen05 3xTF32, 0: FFMA      */
   int64_t norm_fold;              /* 1: RMSNorms folded into the GEMMs         */
 } rtr_report;
 int rtr_get_report(const rtr_session* s, rtr_report* out);
@@ -208,11 +209,13 @@ int rtr_profile_gemms(rtr_session* s, int32_t M, int32_t reps, float* ms_per_pas
 
 /* Test hook (no reference counterpart): C[M, N] = X[M, K] . W[N, K]^T (fp32,
  * row-major, device pointers) through one projection-GEMM kernel: 0 the
- * engine's dispatch (64-row kernel for M <= 64, else 128-row), 1 the 64-row
- * tcgen05 3xTF32 kernel, 2 the 128-row one, 3 the bf16 kernel (X and W rounded
- * to bf16 first; C holds the bf16-rounded products as fp32), 4 the FFMA
- * kernel.  N must be a multiple of 4 and K of 4 (8 for the bf16 kernel, 32 for
- * FFMA).  Scratch is allocated per call; blocks until done. */
+ * engine's fp32 dispatch (= 5), 1 the 64-row tcgen05 3xTF32 kernel, 2 the
+ * 128-row one, 3 the bf16 kernel (X and W rounded to bf16 first; C holds the
+ * bf16-rounded products as fp32), 4 the FFMA kernel, 5 the tcgen05 fp16-pair
+ * kernel (X and W as fp16 (hi, lo) pairs; 64-row CTAs for M <= 64, else
+ * 128-row).  N must be a multiple of 4 and K of 4 (8 for the bf16 and
+ * fp16-pair kernels, 32 for FFMA).  Scratch is allocated per call; blocks
+ * until done. */
 int rtr_gemm_check(int32_t device, const float* x_dev, const float* w_dev, float* c_dev, int32_t M, int32_t N,
                    int32_t K, int32_t kernel);
 

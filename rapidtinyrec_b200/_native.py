@@ -146,8 +146,9 @@ def synth_fill(tensor, seed, tid, scale, offset):
 
 def gemm(x, w, kernel=0):
     """``x @ w.T`` (fp32 CUDA tensors) through one of the engine's projection-GEMM
-    kernels: 0 the engine's dispatch, 1 the 64-row and 2 the 128-row tcgen05
-    3xTF32 kernels, 3 the bf16 kernel, 4 the FFMA kernel (``rtr_gemm_check``)."""
+    kernels: 0 the engine's fp32 dispatch (the fp16-pair kernel), 1 the 64-row
+    and 2 the 128-row tcgen05 3xTF32 kernels, 3 the bf16 kernel, 4 the FFMA
+    kernel, 5 the tcgen05 fp16-pair kernel (``rtr_gemm_check``)."""
     import torch
     x = x.contiguous()
     w = w.contiguous()

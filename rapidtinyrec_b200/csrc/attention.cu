@@ -49,8 +49,10 @@ RTR_DEVICE float4 ld4f(const __nv_bfloat16* p) {
 }
 // Output element i of a row: fp32 rows also get their tf32 split (the 3xTF32
 // GEMM operands); bf16 rows are rounded once.
-RTR_DEVICE void store_out(float* out, float* big, float* small, long i, float v) { store_split(out, big, small, i, v); }
-RTR_DEVICE void store_out(__nv_bfloat16* out, float*, float*, long i, float v) { out[i] = __float2bfloat16_rn(v); }
+RTR_DEVICE void store_out(float* out, float* big, float* small, long i, float v, int fmt) {
+  store_split(out, big, small, i, v, fmt);
+}
+RTR_DEVICE void store_out(__nv_bfloat16* out, float*, float*, long i, float v, int) { out[i] = __float2bfloat16_rn(v); }
 
 // Stage keys [k0, k0 + AK) of one KV group into ring slot `buf` (zero rows
 // past `kend`); one cp.async group.
@@ -133,7 +135,7 @@ template <int HD, typename T>
 __global__ void __launch_bounds__(ATHREADS) prefill_attn_kernel(
     const T* __restrict__ q, const T* __restrict__ kp, const T* __restrict__ vp,
     T* __restrict__ out, float* __restrict__ out_big, float* __restrict__ out_small, int L, int cap, int heads,
-    int kv_heads, float scale) {
+    int kv_heads, float scale, int xfmt) {
   constexpr int VEC = HD / 32, ROWS = PQ / AWARPS;
   pdl_launch_dependents();
   pdl_wait();
@@ -185,33 +187,33 @@ __global__ void __launch_bounds__(ATHREADS) prefill_attn_kernel(
     const float inv = 1.0f / l[r];
 #pragma unroll
     for (int i = 0; i < VEC; ++i)
-      store_out(out, out_big, out_small, ((long)qpos * heads + h) * HD + lane * VEC + i, acc[r][i] * inv);
+      store_out(out, out_big, out_small, ((long)qpos * heads + h) * HD + lane * VEC + i, acc[r][i] * inv, xfmt);
   }
 }
 
 template <int HD, typename T>
 static cudaError_t launch_prefill(const void* q, const void* kp, const void* vp, void* out, float* ob, float* os, int L,
-                                  int cap, int heads, int kv_heads, float scale, cudaStream_t stream) {
+                                  int cap, int heads, int kv_heads, float scale, cudaStream_t stream, int xfmt) {
   dim3 grid((L + PQ - 1) / PQ, heads);
   return launch_pdl(PDL_ATTN, prefill_attn_kernel<HD, T>, grid, dim3(ATHREADS), attn_smem_bytes<HD, T>(PQ), stream,
                     static_cast<const T*>(q), static_cast<const T*>(kp), static_cast<const T*>(vp), static_cast<T*>(out),
-                    ob, os, L, cap, heads, kv_heads, scale);
+                    ob, os, L, cap, heads, kv_heads, scale, xfmt);
 }
 
 cudaError_t attention_prefill(const void* q, const void* k_prefix, const void* v_prefix, void* out, float* out_big,
                               float* out_small, int L, int prefix_cap, int heads, int kv_heads, int head_dim,
-                              float scale, bool bf16, cudaStream_t stream) {
+                              float scale, bool bf16, cudaStream_t stream, int xfmt) {
   if (L <= 0 || L > prefix_cap) return cudaErrorInvalidValue;
   if (head_dim == 128)
     return bf16 ? launch_prefill<128, __nv_bfloat16>(q, k_prefix, v_prefix, out, nullptr, nullptr, L, prefix_cap, heads,
-                                                     kv_heads, scale, stream)
+                                                     kv_heads, scale, stream, 0)
                 : launch_prefill<128, float>(q, k_prefix, v_prefix, out, out_big, out_small, L, prefix_cap, heads,
-                                             kv_heads, scale, stream);
+                                             kv_heads, scale, stream, xfmt);
   if (head_dim == 64)
     return bf16 ? launch_prefill<64, __nv_bfloat16>(q, k_prefix, v_prefix, out, nullptr, nullptr, L, prefix_cap, heads,
-                                                    kv_heads, scale, stream)
+                                                    kv_heads, scale, stream, 0)
                 : launch_prefill<64, float>(q, k_prefix, v_prefix, out, out_big, out_small, L, prefix_cap, heads,
-                                            kv_heads, scale, stream);
+                                            kv_heads, scale, stream, xfmt);
   return cudaErrorInvalidValue;
 }
 
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     const T* __restrict__ ksuf, const T* __restrict__ vsuf, const int32_t* __restrict__ anc,
     const int32_t* __restrict__ L_dev, T* __restrict__ out, float* __restrict__ out_big,
     float* __restrict__ out_small, int beams, int cap, int heads, int kv_heads, int t, float scale,
-    uint32_t* __restrict__ status, int users, long prefix_user_stride, int anc_user_stride) {
+    uint32_t* __restrict__ status, int users, long prefix_user_stride, int anc_user_stride, int xfmt) {
   constexpr int VEC = HD / 32, QLD = HD + DQLD_PAD, E = 16 / (int)sizeof(T);
   constexpr int AD4 = HD / 4 / AWARPS;  // float4 columns per warp in phase A
   static_assert(DBEAMS == 8 && AWARPS == 8 && AK == 64, "tiling assumes 8 beams, 8 warps, 64-key chunks");
@@ -425,7 +427,7 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     const float inv = 1.0f / l;
 #pragma unroll
     for (int i = 0; i < VEC; ++i)
-      store_out(out, out_big, out_small, ((long)(r0 + b) * heads + h) * HD + lane * VEC + i, a[i] * inv);
+      store_out(out, out_big, out_small, ((long)(r0 + b) * heads + h) * HD + lane * VEC + i, a[i] * inv, xfmt);
   }
 }
 
@@ -433,33 +435,35 @@ template <int HD, typename T>
 static cudaError_t launch_decode(const void* q, const void* kp, const void* vp, const void* ks, const void* vs,
                                  const int32_t* anc, const int32_t* L_dev, int t, void* out, float* ob, float* os,
                                  int beams, int cap, int heads, int kv_heads, float scale, uint32_t* status,
-                                 cudaStream_t stream, const DecodeUsers& du) {
+                                 cudaStream_t stream, const DecodeUsers& du, int xfmt) {
   dim3 grid(heads, du.users * ((beams + DBEAMS - 1) / DBEAMS));
   return launch_pdl(PDL_ATTN, decode_attn_kernel<HD, T>, grid, dim3(ATHREADS), decode_smem_bytes<HD, T>(), stream,
                     static_cast<const T*>(q), static_cast<const T*>(kp), static_cast<const T*>(vp),
                     static_cast<const T*>(ks), static_cast<const T*>(vs), anc, L_dev, static_cast<T*>(out), ob, os,
                     beams, cap, heads, kv_heads, t, scale, status, du.users, du.prefix_user_stride,
-                    du.anc_user_stride);
+                    du.anc_user_stride, xfmt);
 }
 
 cudaError_t attention_decode(const void* q, const void* k_prefix, const void* v_prefix, const void* k_suffix,
                              const void* v_suffix, const int32_t* anc, const int32_t* L_dev, int t, void* out,
                              float* out_big, float* out_small, int beams, int prefix_cap, int heads, int kv_heads,
                              int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream,
-                             const DecodeUsers& du) {
+                             const DecodeUsers& du, int xfmt) {
   if (t < 1 || t > 4 || beams > MAX_BEAMS || du.users < 1) return cudaErrorInvalidValue;
   if (head_dim == 128)
     return bf16 ? launch_decode<128, __nv_bfloat16>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out,
                                                     nullptr, nullptr, beams, prefix_cap, heads, kv_heads, scale, status,
-                                                    stream, du)
+                                                    stream, du, 0)
                 : launch_decode<128, float>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out, out_big,
-                                            out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream, du);
+                                            out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream, du,
+                                            xfmt);
   if (head_dim == 64)
     return bf16 ? launch_decode<64, __nv_bfloat16>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out,
                                                    nullptr, nullptr, beams, prefix_cap, heads, kv_heads, scale, status,
-                                                   stream, du)
+                                                   stream, du, 0)
                 : launch_decode<64, float>(q, k_prefix, v_prefix, k_suffix, v_suffix, anc, L_dev, t, out, out_big,
-                                           out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream, du);
+                                           out_small, beams, prefix_cap, heads, kv_heads, scale, status, stream, du,
+                                           xfmt);
   return cudaErrorInvalidValue;
 }
 

@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -57,14 +58,54 @@ RTR_DEVICE float tf32_round(float x) {
   return __uint_as_float(r);
 }
 
-// Store x and its tf32 split (big = tf32(x), small = x - big, exact) when the
-// split outputs are present; the tensor-core GEMMs consume the split pair.
-RTR_DEVICE void store_split(float* out, float* big, float* small, long i, float x) {
+// GEMM operand split of an activation, in one of two formats:
+//   SPLIT_TF32  big = tf32(x), small = x - big (both exact fp32; the 3xTF32
+//               kernels read them from fp32 planes)
+//   SPLIT_F16   x = 16 (hi + lo / 2048) with hi = fp16(x / 16) and
+//               lo = fp16((x / 16 - hi) * 2048): two fp16 planes (the first
+//               half of the big/small allocations) for the fp16-pair kernel.
+//               22 significant bits for |x| up to 16 * 65504.
+enum : int { SPLIT_TF32 = 0, SPLIT_F16 = 1 };
+constexpr float kPairScale = 16.0f;       // activations enter the fp16 pair scaled by 1/16
+constexpr float kPairLo = 2048.0f;        // lo carries the remainder scaled by 2^11
+
+RTR_DEVICE void pair_split(float x, __half& hi, __half& lo) {
+  const float xs = x * (1.0f / kPairScale);
+  hi = __float2half_rn(xs);
+  lo = __float2half_rn((xs - __half2float(hi)) * kPairLo);  // xs - hi is exact
+}
+
+// Store x and its split when the split outputs are present; the tensor-core
+// GEMMs consume the split pair.
+RTR_DEVICE void store_split(float* out, float* big, float* small, long i, float x, int fmt = SPLIT_TF32) {
   out[i] = x;
   if (big) {
-    const float b = tf32_round(x);
-    big[i] = b;
-    small[i] = x - b;
+    if (fmt == SPLIT_F16) {
+      __half h, l;
+      pair_split(x, h, l);
+      reinterpret_cast<__half*>(big)[i] = h;
+      reinterpret_cast<__half*>(small)[i] = l;
+    } else {
+      const float b = tf32_round(x);
+      big[i] = b;
+      small[i] = x - b;
+    }
+  }
+}
+
+// The split of four consecutive elements [i, i + 4) (i a multiple of 4).
+RTR_DEVICE void store_split4(float* big, float* small, long i, float4 v, int fmt) {
+  if (fmt == SPLIT_F16) {
+    __align__(8) __half h[4];
+    __align__(8) __half l[4];
+    pair_split(v.x, h[0], l[0]); pair_split(v.y, h[1], l[1]);
+    pair_split(v.z, h[2], l[2]); pair_split(v.w, h[3], l[3]);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(big) + i) = *reinterpret_cast<const uint2*>(h);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(small) + i) = *reinterpret_cast<const uint2*>(l);
+  } else {
+    const float4 b = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
+    *reinterpret_cast<float4*>(big + i) = b;
+    *reinterpret_cast<float4*>(small + i) = make_float4(v.x - b.x, v.y - b.y, v.z - b.z, v.w - b.w);
   }
 }
 

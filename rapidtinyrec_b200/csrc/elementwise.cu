@@ -17,7 +17,7 @@ __device__ __forceinline__ int row_token(const int32_t* ids, int m, int ids_stri
 
 __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* table, int vocab,
                              int hidden, float* x, uint32_t* status, float* x_big, float* x_small, float* ss,
-                             int ss_ld, int grp_rows, long grp_stride) {
+                             int ss_ld, int grp_rows, long grp_stride, int xfmt) {
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
@@ -35,15 +35,11 @@ __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* ta
   // warp w takes 128-column chunks w, w + warps, ...: copy, split and the
   // chunk's sum of squares (lane sums of 4 squares, then a shuffle tree)
   const int lane = threadIdx.x & 31, warps = blockDim.x >> 5;
-  float4* big = reinterpret_cast<float4*>(x_big + (long)m * hidden);
-  float4* small = reinterpret_cast<float4*>(x_small + (long)m * hidden);
   for (int chunk = threadIdx.x >> 5; chunk < hidden / 128; chunk += warps) {
     const int i = chunk * 32 + lane;
     const float4 v = src[i];
     dst[i] = v;
-    const float4 b = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
-    big[i] = b;
-    small[i] = make_float4(v.x - b.x, v.y - b.y, v.z - b.z, v.w - b.w);
+    store_split4(x_big, x_small, (long)m * hidden + 4 * i, v, xfmt);
     const float sq = warp_sum((v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w));
     if (lane == 0 && ss) ss[(long)chunk * ss_ld + m] = sq;
   }
@@ -51,17 +47,17 @@ __global__ void embed_kernel(const int32_t* ids, int ids_stride, const float* ta
 
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
                        int hidden, float* x, uint32_t* status, cudaStream_t stream, float* x_big, float* x_small,
-                       float* ss, int ss_ld, int grp_rows, long grp_stride) {
+                       float* ss, int ss_ld, int grp_rows, long grp_stride, int xfmt) {
   if (x_big && (hidden % 128 || !x_small)) return cudaErrorInvalidValue;
   if (grp_rows <= 0) grp_rows = M;
   return launch_pdl(PDL_EMBED, embed_kernel, dim3(M), dim3(128), 0, stream, ids, ids_stride, table, vocab, hidden, x,
-                    status, x_big, x_small, ss, ss_ld, grp_rows, grp_stride);
+                    status, x_big, x_small, ss, ss_ld, grp_rows, grp_stride, xfmt);
 }
 
 // ------------------------------------------------------------------ RMSNorm
 // Qwen2RMSNorm.forward (modeling_qwen2.py:258-263): w * (x * rsqrt(mean(x^2) + eps)).
 __global__ void rms_norm_kernel(const float* x, const float* w, float* h, float* h_big, float* h_small, int hidden,
-                                float eps) {
+                                float eps, int xfmt) {
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
@@ -87,16 +83,17 @@ __global__ void rms_norm_kernel(const float* x, const float* w, float* h, float*
   const long row = (long)m * hidden;
   for (int i = threadIdx.x; i < hidden / 4; i += blockDim.x) {
     const float4 v = xr[i], g = wr[i];
-    store_split(h, h_big, h_small, row + 4 * i, g.x * (v.x * r));
-    store_split(h, h_big, h_small, row + 4 * i + 1, g.y * (v.y * r));
-    store_split(h, h_big, h_small, row + 4 * i + 2, g.z * (v.z * r));
-    store_split(h, h_big, h_small, row + 4 * i + 3, g.w * (v.w * r));
+    store_split(h, h_big, h_small, row + 4 * i, g.x * (v.x * r), xfmt);
+    store_split(h, h_big, h_small, row + 4 * i + 1, g.y * (v.y * r), xfmt);
+    store_split(h, h_big, h_small, row + 4 * i + 2, g.z * (v.z * r), xfmt);
+    store_split(h, h_big, h_small, row + 4 * i + 3, g.w * (v.w * r), xfmt);
   }
 }
 
 cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big, float* h_small, int M, int hidden,
-                          float eps, cudaStream_t stream) {
-  return launch_pdl(PDL_NORM, rms_norm_kernel, dim3(M), dim3(256), 0, stream, x, w, h, h_big, h_small, hidden, eps);
+                          float eps, cudaStream_t stream, int xfmt) {
+  return launch_pdl(PDL_NORM, rms_norm_kernel, dim3(M), dim3(256), 0, stream, x, w, h, h_big, h_small, hidden, eps,
+                    xfmt);
 }
 
 // ------------------------------------------------------------- bf16 mode

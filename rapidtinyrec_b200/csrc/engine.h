@@ -72,6 +72,23 @@ cudaError_t gemm_tc_wide(const TensorMap& tmW, const TensorMap& tmXb, const Tens
                          cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr,
                          const NormFold* fold = nullptr);
 
+// ---- fp16-pair tensor-core GEMM (gemm_f16x2.cu): the fp32 path's default ----
+// Weights packed once as fp16 (hi, lo) pairs (4 bytes a weight); activations
+// consumed as SPLIT_F16 planes (hi, lo) written by their producers.  Same
+// arguments, epilogues and split-K as gemm_tc; 64-row CTAs for M <= 64,
+// 128-row CTAs above.
+size_t packed_weight_elems_f16x2(int N, int K);
+cudaError_t pack_weight_tiles_f16x2(const float* src, int N, int K, void* dst, cudaStream_t stream,
+                                    const float* col_scale = nullptr);
+// fp16 row-major [rows][cols], row stride ld elements; TMA box [box_rows][64]
+bool make_tmap_f16(TensorMap* out, const void* base, long rows, long cols, long ld, int box_rows);
+bool make_tmap_packed_f16x2(TensorMap* out, const void* packed, int N, int K);
+cudaError_t gemm_f16x2_init();
+cudaError_t gemm_f16x2(const TensorMap& tmW, const TensorMap& tmXh, const TensorMap& tmXl, float* C, float* C_big,
+                       float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
+                       size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
+                       bool pdl, const RopeArgs* rope = nullptr, const NormFold* fold = nullptr);
+
 // ---- bf16 tensor-core GEMM (gemm_bf16.cu): the bf16 mode ----
 // X: bf16 activations [rows][K]; weights packed once into bf16 tile blocks.
 // C is bf16 except EPI_STORE (fp32 copies of the bf16 logits); bias holds bf16
@@ -86,15 +103,17 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
                       int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr);
 
 // ---- element-wise (elementwise.cu) ----
-// x = table[ids]; with x_big/x_small (optional) also x's tf32 split and, with
-// ss (optional), x's per-row partial sums of squares (NormFold layout).
+// x = table[ids]; with x_big/x_small (optional) also x's GEMM split (format
+// xfmt: SPLIT_TF32 or SPLIT_F16, common.cuh) and, with ss (optional), x's
+// per-row partial sums of squares (NormFold layout).
 cudaError_t embed_rows(const int32_t* ids, int ids_stride, int M, const float* table, int vocab,
                        int hidden, float* x, uint32_t* status, cudaStream_t stream, float* x_big = nullptr,
                        float* x_small = nullptr, float* ss = nullptr, int ss_ld = 0, int grp_rows = 0,
-                       long grp_stride = 0);  // row m: ids[(m / grp_rows) * grp_stride + (m % grp_rows) * ids_stride]
-// h = w * (x * rsqrt(mean(x^2) + eps)); h_big/h_small (optional) get the tf32 split of h.
+                       long grp_stride = 0,  // row m: ids[(m / grp_rows) * grp_stride + (m % grp_rows) * ids_stride]
+                       int xfmt = 0);
+// h = w * (x * rsqrt(mean(x^2) + eps)); h_big/h_small (optional) get the GEMM split of h.
 cudaError_t rms_norm_rows(const float* x, const float* w, float* h, float* h_big, float* h_small, int M, int hidden,
-                          float eps, cudaStream_t stream);
+                          float eps, cudaStream_t stream, int xfmt = 0);
 // RoPE on q and k of a [M, qkv_dim] projection; q -> q_out [M, Hq*D], k/v ->
 // cache rows.  Prefill (slot < 0): row m is position m, K/V go to the prefix
 // arena [Hkv][cap][D] at position m.  Decode (slot >= 0): every row is at
@@ -116,11 +135,11 @@ cudaError_t gemv_bf16(const void* x, const void* W, float* y, int N, int K, cuda
 cudaError_t round_to_bf16(float* v, int64_t n, cudaStream_t stream);
 
 // ---- attention (attention.cu) ----
-// out_big/out_small (optional, fp32 only) receive the tf32 split of out.
-// bf16: q, K/V and out are bf16 (the bf16 mode); otherwise fp32.
+// out_big/out_small (optional, fp32 only) receive the GEMM split of out
+// (format xfmt).  bf16: q, K/V and out are bf16 (the bf16 mode); otherwise fp32.
 cudaError_t attention_prefill(const void* q, const void* k_prefix, const void* v_prefix, void* out, float* out_big,
                               float* out_small, int L, int prefix_cap, int heads, int kv_heads, int head_dim,
-                              float scale, bool bf16, cudaStream_t stream);
+                              float scale, bool bf16, cudaStream_t stream, int xfmt = 0);
 // Users of a batched decode step: user u owns rows u * beams .. u * beams + beams - 1,
 // its prefix at k/v_prefix + u * prefix_user_stride, its length L_dev[u] and its
 // ancestry table at anc + u * anc_user_stride.
@@ -135,7 +154,7 @@ cudaError_t attention_decode(const void* q, const void* k_prefix, const void* v_
                              const void* v_suffix, const int32_t* anc, const int32_t* L_dev, int t, void* out,
                              float* out_big, float* out_small, int beams, int prefix_cap, int heads, int kv_heads,
                              int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream,
-                             const DecodeUsers& du = DecodeUsers{});
+                             const DecodeUsers& du = DecodeUsers{}, int xfmt = 0);
 cudaError_t attention_init();
 
 // ---- constraints + beam step (beam.cu) ----

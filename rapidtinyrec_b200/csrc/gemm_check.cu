@@ -21,21 +21,27 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
   }
 }
 
+__global__ void split_pair_kernel(const float* __restrict__ x, __half* __restrict__ hi, __half* __restrict__ lo,
+                                  long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    pair_split(x[i], hi[i], lo[i]);
+}
+
 static int gemm_check_impl(int device, const float* x, const float* w, float* c, int M, int N, int K, int kernel) {
-  if (!x || !w || !c || M < 1 || N < 1 || K < 1 || N % 4 || kernel < 0 || kernel > 4) return RTR_ERR_ARG;
+  if (!x || !w || !c || M < 1 || N < 1 || K < 1 || N % 4 || kernel < 0 || kernel > 5) return RTR_ERR_ARG;
   if (kernel == 4 && K % 32) return RTR_ERR_ARG;  // the FFMA kernel walks K in 32-wide slabs
   if (cudaSetDevice(device) != cudaSuccess) return RTR_ERR_CUDA;
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return RTR_ERR_CUDA;
   if (gemm_init() != cudaSuccess || gemm_tc_init() != cudaSuccess || gemm_tc_wide_init() != cudaSuccess ||
-      gemm_bf16_init() != cudaSuccess)
+      gemm_bf16_init() != cudaSuccess || gemm_f16x2_init() != cudaSuccess)
     return RTR_ERR_CUDA;
   // split-K partials: the tensor-core kernels split only while tiles x splits <= SMs
   const size_t ws_floats = kernel == 4 ? gemm_workspace_floats(M, N, sms) : (size_t)sms * 128 * 128;
   const int tc_tiles = ((M + 63) / 64) * ((N + 127) / 128);
   const int max_tickets = kernel == 4 ? gemm_tile_count(M, N) : tc_tiles;
   float *ws = nullptr, *xb = nullptr, *xs = nullptr, *wp = nullptr;
-  void *xh = nullptr, *wh = nullptr;
+  void *xh = nullptr, *xh2 = nullptr, *wh = nullptr;
   int* tickets = nullptr;
   uint32_t* status = nullptr;
   cudaStream_t stream = nullptr;
@@ -46,7 +52,26 @@ static int gemm_check_impl(int device, const float* x, const float* w, float* c,
   if (e == cudaSuccess) e = cudaMalloc(&status, sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMemsetAsync(tickets, 0, max_tickets * sizeof(int), stream);
   if (e == cudaSuccess) e = cudaMemsetAsync(status, 0, sizeof(uint32_t), stream);
-  if (e == cudaSuccess && (kernel <= 2)) {
+  if (e == cudaSuccess && (kernel == 0 || kernel == 5)) {
+    // the fp16-pair kernel (the engine's fp32 GEMM): activations split into
+    // (hi, lo) fp16 planes, weights packed into pair blocks
+    const long n = (long)M * K;
+    e = cudaMalloc(&xh, n * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&xh2, n * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&wh, packed_weight_elems_f16x2(N, K) * 2);
+    if (e == cudaSuccess) {
+      split_pair_kernel<<<sms * 4, 256, 0, stream>>>(x, static_cast<__half*>(xh), static_cast<__half*>(xh2), n);
+      e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = pack_weight_tiles_f16x2(w, N, K, wh, stream);
+    TensorMap tw, txh, txl;
+    if (e == cudaSuccess && (!make_tmap_packed_f16x2(&tw, wh, N, K) || !make_tmap_f16(&txh, xh, M, K, K, 64) ||
+                             !make_tmap_f16(&txl, xh2, M, K, K, 64)))
+      rc = RTR_ERR_ARG;  // K rows must be 16-byte aligned for TMA
+    if (e == cudaSuccess && rc == RTR_OK)
+      e = gemm_f16x2(tw, txh, txl, c, nullptr, nullptr, N, nullptr, M, N, K, EPI_STORE, ws, ws_floats, tickets,
+                     max_tickets, status, sms, stream, false);
+  } else if (e == cudaSuccess && (kernel <= 2)) {
     const long n = (long)M * K;
     e = cudaMalloc(&xb, n * sizeof(float));
     if (e == cudaSuccess) e = cudaMalloc(&xs, n * sizeof(float));
@@ -61,7 +86,7 @@ static int gemm_check_impl(int device, const float* x, const float* w, float* c,
                              !make_tmap_f32(&txs, xs, M, K, K, 64)))
       rc = RTR_ERR_ARG;  // K rows must be 16-byte aligned for TMA
     if (e == cudaSuccess && rc == RTR_OK) {
-      const bool wide = kernel == 2 || (kernel == 0 && M > 64);
+      const bool wide = kernel == 2;
       e = wide ? gemm_tc_wide(tw, txb, txs, c, nullptr, nullptr, N, nullptr, M, N, K, EPI_STORE, ws, ws_floats,
                               tickets, max_tickets, status, sms, stream, false)
                : gemm_tc(tw, txb, txs, c, nullptr, nullptr, N, nullptr, M, N, K, EPI_STORE, ws, ws_floats, tickets,
@@ -87,7 +112,7 @@ static int gemm_check_impl(int device, const float* x, const float* w, float* c,
   if (e != cudaSuccess) rc = RTR_ERR_CUDA;
   else if (rc == RTR_OK && st != 0) rc = RTR_ERR_DEVICE;
   cudaFree(ws); cudaFree(tickets); cudaFree(status); cudaFree(xb); cudaFree(xs); cudaFree(wp);
-  cudaFree(xh); cudaFree(wh);
+  cudaFree(xh); cudaFree(xh2); cudaFree(wh);
   if (stream) cudaStreamDestroy(stream);
   return rc;
 }

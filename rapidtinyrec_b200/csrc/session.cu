@@ -47,6 +47,10 @@ struct rtr_session {
   bool pdl = true;
   bool use_tc = true;  // tcgen05 GEMMs (RTR_GEMM=ffma selects the FFMA kernel)
   bool tc_wide = true;  // 128-row tcgen05 GEMM for M > 64 (RTR_TC_WIDE=0: the 64-row kernel only)
+  // GEMM operand format of the fp32 tensor-core path: SPLIT_F16, the fp16-pair
+  // kernel (default), or SPLIT_TF32, the 3xTF32 kernels (RTR_GEMM=tf32); every
+  // activation producer writes its split in this format
+  int xfmt = SPLIT_TF32;
   // RMSNorm folded into the 3xTF32 GEMMs (fp32 tensor-core path, hidden % 128 == 0;
   // RTR_NORM_FOLD=0 keeps the separate norm kernels): norm weights folded into the
   // packed q/k/v, gate/up and LM-head columns, row scales from partial sums of squares
@@ -213,12 +217,18 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
   CREATE_TRY(gemm_tc_wide_init());
   CREATE_TRY(attention_init());
   CREATE_TRY(gemm_bf16_init());
-  if (const char* g = std::getenv("RTR_GEMM")) s->use_tc = std::strcmp(g, "ffma") != 0;
+  CREATE_TRY(gemm_f16x2_init());
+  bool tf32 = false;
+  if (const char* g = std::getenv("RTR_GEMM")) {
+    s->use_tc = std::strcmp(g, "ffma") != 0;
+    tf32 = std::strcmp(g, "tf32") == 0;
+  }
   if (const char* g = std::getenv("RTR_TC_WIDE")) s->tc_wide = std::strcmp(g, "0") != 0;
   s->fold = s->use_tc && c.dtype != RTR_DTYPE_BF16 && c.hidden % 128 == 0;
   if (const char* g = std::getenv("RTR_NORM_FOLD")) s->fold = s->fold && std::strcmp(g, "0") != 0;
   s->pdl = pdl_on(PDL_GEMM);
   s->bf16 = c.dtype == RTR_DTYPE_BF16;
+  s->xfmt = s->use_tc && !s->bf16 && !tf32 ? SPLIT_F16 : SPLIT_TF32;
   if (s->bf16 && !s->use_tc) {
     s->err = "the bf16 mode runs on the tensor-core GEMMs only (unset RTR_GEMM)";
     return bail(RTR_ERR_ARG);
@@ -348,7 +358,9 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
     s->split_of[a.v] = {a.big, a.small};
     for (const float* half : {a.big, a.small}) {
       TensorMap m;
-      if (!make_tmap_f32(&m, half, M, a.width, a.width, 64)) {
+      const bool ok = s->xfmt == SPLIT_F16 ? make_tmap_f16(&m, half, M, a.width, a.width, 64)
+                                           : make_tmap_f32(&m, half, M, a.width, a.width, 64);
+      if (!ok) {
         s->err = "cuTensorMapEncodeTiled failed for an activation buffer";
         return bail(RTR_ERR_CUDA);
       }
@@ -511,19 +523,25 @@ int rtr_load_weights(rtr_session* s, const void* const* tensors, int32_t n_tenso
   // blocks (allocated once), with its TMA descriptor keyed by the original matrix
   if (s->use_tc) {
     auto wmap = [&](const float* w, long rows, long cols, const float* col_scale = nullptr) -> cudaError_t {
+      const bool f16 = s->xfmt == SPLIT_F16;
       float* packed = nullptr;
       auto it = s->packed.find(w);
       if (it == s->packed.end()) {
-        cudaError_t e = dev_alloc(s, &packed, packed_weight_floats((int)rows, (int)cols));
+        const size_t floats = f16 ? packed_weight_elems_f16x2((int)rows, (int)cols) / 2
+                                  : packed_weight_floats((int)rows, (int)cols);
+        cudaError_t e = dev_alloc(s, &packed, floats);
         if (e != cudaSuccess) return e;
         s->packed[w] = packed;
       } else {
         packed = it->second;
       }
-      cudaError_t e = pack_weight_tiles(w, (int)rows, (int)cols, packed, 0, col_scale);
+      cudaError_t e = f16 ? pack_weight_tiles_f16x2(w, (int)rows, (int)cols, packed, 0, col_scale)
+                          : pack_weight_tiles(w, (int)rows, (int)cols, packed, 0, col_scale);
       if (e != cudaSuccess) return e;
       TensorMap m;
-      if (!make_tmap_packed(&m, packed, (int)rows, (int)cols)) return cudaErrorInvalidValue;
+      if (!(f16 ? make_tmap_packed_f16x2(&m, packed, (int)rows, (int)cols)
+                : make_tmap_packed(&m, packed, (int)rows, (int)cols)))
+        return cudaErrorInvalidValue;
       s->tmaps[{w, 128}] = m;
       return cudaSuccess;
     };
@@ -600,8 +618,9 @@ int rtr_load_constraints(rtr_session* s, const rtr_constraint_tables* t) {
 }  // extern "C"
 
 // ------------------------------------------------------------------ forward
-// Projection GEMM: the tcgen05 3xTF32 kernel on the tf32 split of activation
-// buffer A and the weight matrix W (the FFMA kernel when RTR_GEMM=ffma).
+// Projection GEMM on the split of activation buffer A and the weight matrix W:
+// the fp16-pair tcgen05 kernel, the 3xTF32 ones (RTR_GEMM=tf32) or the FFMA
+// kernel (RTR_GEMM=ffma).
 static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W, float* C, int ldc,
                         const float* bias, int M, int N, int K, int epi, const RopeArgs* rope = nullptr,
                         const NormFold* fold = nullptr) {
@@ -620,6 +639,9 @@ static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W,
       cb = out->second.first;
       cs = out->second.second;
     }
+    if (s->xfmt == SPLIT_F16)
+      return gemm_f16x2(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws, s->ws_floats,
+                        s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope, fold);
     // more than 64 rows (the prefill): one 128-row MMA per instruction instead of two 64-row ones
     if (M > 64 && s->tc_wide)
       return gemm_tc_wide(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws,
@@ -725,7 +747,7 @@ static cudaError_t forward(rtr_session* s, int t) {
     const NormFold in{nullptr, s->ss, s->ss_ld, H / 128, H, c.rms_eps};
     const NormFold out{s->ss, nullptr, s->ss_ld, H / 128, H, c.rms_eps};
     FWD_TRY(embed_rows(ids, 1, M, s->embed, V, H, s->x, s->d_status, st, s->x_big, s->x_small, s->ss, s->ss_ld,
-                       id_rows, id_stride));
+                       id_rows, id_stride, s->xfmt));
     for (int l = 0; l < c.layers; ++l) {
       const LayerW& w = s->layers[l];
       float* kp = s->kv_prefix + pre_off + (size_t)l * 2 * kvd * cap;
@@ -738,10 +760,11 @@ static cudaError_t forward(rtr_session* s, int t) {
       FWD_TRY(gemm(s, s->x, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra, &in));
       if (t == 0) {
         FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
-                                  scale, false, st));
+                                  scale, false, st, s->xfmt));
       } else {
         FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
-                                 s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st, du));
+                                 s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st, du,
+                                 s->xfmt));
       }
       FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID, nullptr, &out));
       FWD_TRY(gemm(s, s->x, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU, nullptr, &in));
@@ -763,7 +786,7 @@ static cudaError_t forward(rtr_session* s, int t) {
     float* vp = kp + (size_t)kvd * cap;
     float* ks = s->kv_suffix + (size_t)l * 2 * 4 * RB * kvd;
     float* vs = ks + (size_t)4 * RB * kvd;
-    FWD_TRY(rms_norm_rows(s->x, w.n_in, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
+    FWD_TRY(rms_norm_rows(s->x, w.n_in, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st, s->xfmt));
     const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * n * kvd;
     if (s->use_tc) {
       // q/k/v projection with RoPE and the cache write fused into its epilogue
@@ -778,13 +801,14 @@ static cudaError_t forward(rtr_session* s, int t) {
     }
     if (t == 0) {
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
-                                scale, false, st));
+                                scale, false, st, s->xfmt));
     } else {
       FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
-                               s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st, du));
+                               s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st, du,
+                               s->xfmt));
     }
     FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID));
-    FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
+    FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st, s->xfmt));
     FWD_TRY(gemm(s, s->h, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
     FWD_TRY(gemm(s, s->act, I, w.wd, s->x, H, nullptr, M, H, I, EPI_RESID));
   }
@@ -792,7 +816,7 @@ static cudaError_t forward(rtr_session* s, int t) {
     FWD_TRY(rms_norm_rows(s->x + (size_t)(M - 1) * H, s->norm_final, s->h, nullptr, nullptr, 1, H, c.rms_eps, st));
     FWD_TRY(gemv_f32(s->h, s->lm_head, s->logits, V, H, st));
   } else {
-    FWD_TRY(rms_norm_rows(s->x, s->norm_final, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st));
+    FWD_TRY(rms_norm_rows(s->x, s->norm_final, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st, s->xfmt));
     FWD_TRY(gemm(s, s->h, H, s->lm_head, s->logits, V, nullptr, M, V, H, EPI_STORE));
   }
   return cudaSuccess;
@@ -1027,7 +1051,7 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   out->device_bytes = s->device_bytes;
   out->h2d_bytes_per_request = (int64_t)s->L * 4 + 4;
   out->d2h_bytes_per_request = (int64_t)sizeof(DevResult);
-  out->tensor_core_gemm = s->use_tc ? 1 : 0;
+  out->tensor_core_gemm = s->use_tc ? (s->xfmt == SPLIT_F16 ? 2 : 1) : 0;
   out->norm_fold = s->fold ? 1 : 0;
   return RTR_OK;
 }

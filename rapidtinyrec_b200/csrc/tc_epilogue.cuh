@@ -19,6 +19,7 @@ struct TcParams {
   uint32_t* status;
   RopeArgs rope;    // EPI_ROPE only
   NormFold fold;    // ss_in: scale rows by their RMS factor; ss_out: EPI_RESID partials
+  int xfmt;         // split written for the next GEMM: SPLIT_TF32 or SPLIT_F16
 };
 
 
@@ -179,14 +180,10 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
       const int c4 = blk * 8 + g4;
       if (c4 + 4 >= cols4) continue;  // the up half lies past N
       const float4 g = row_scale(red4[j * ld4 + c4], j), u = row_scale(red4[j * ld4 + c4 + 4], j);
-      float a[4] = {silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w};
-      float b[4], sm[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) { b[e] = tf32_round(a[e]); sm[e] = a[e] - b[e]; }
+      const float4 a = make_float4(silu_f(g.x) * u.x, silu_f(g.y) * u.y, silu_f(g.z) * u.z, silu_f(g.w) * u.w);
       const long o = (long)(tok0 + j) * p.ldc + ((n0 + blk * 32) >> 5) * 16 + g4 * 4;
-      *reinterpret_cast<float4*>(p.C + o) = make_float4(a[0], a[1], a[2], a[3]);
-      *reinterpret_cast<float4*>(p.C_big + o) = make_float4(b[0], b[1], b[2], b[3]);
-      *reinterpret_cast<float4*>(p.C_small + o) = make_float4(sm[0], sm[1], sm[2], sm[3]);
+      *reinterpret_cast<float4*>(p.C + o) = a;
+      store_split4(p.C_big, p.C_small, o, a, p.xfmt);
     }
     return;
   }
@@ -242,9 +239,7 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
       if (ok) {
         v = f4add(*reinterpret_cast<const float4*>(p.C + o), red4[j * ld4 + c4]);
         *reinterpret_cast<float4*>(p.C + o) = v;
-        const float4 b = make_float4(tf32_round(v.x), tf32_round(v.y), tf32_round(v.z), tf32_round(v.w));
-        *reinterpret_cast<float4*>(p.C_big + o) = b;
-        *reinterpret_cast<float4*>(p.C_small + o) = make_float4(v.x - b.x, v.y - b.y, v.z - b.z, v.w - b.w);
+        store_split4(p.C_big, p.C_small, o, v, p.xfmt);
       }
       const float sq = warp_sum((v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w));
       if (c4 == 0) p.fold.ss_out[(long)(n0 >> 7) * p.fold.ld + tok0 + j] = sq;

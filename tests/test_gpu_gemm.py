@@ -50,6 +50,26 @@ def test_tf32x3_kernels_match_float64(dev, M, N, K, kernel):
     assert err <= TF32X3_TOL, f'kernel {kernel} {M}x{N}x{K}: {err:.3e}'
 
 
+@pytest.mark.parametrize('M,N,K', SHAPES)
+def test_fp16_pair_kernel_matches_float64(dev, M, N, K):
+    """The fp32 path's GEMM: 22-bit fp16 pairs, three products (measured
+    2e-8 .. 7e-8 of sum |x w|, below the 3xTF32 kernels)."""
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, M, N, K, seed=M * 7 + N + K)
+    err = rel_err(_native.gemm(x, w, 5), x, w)
+    assert err <= TF32X3_TOL, f'fp16-pair {M}x{N}x{K}: {err:.3e}'
+
+
+def test_fp16_pair_kernel_keeps_large_and_small_activations(dev):
+    """Activations far from 1 (hundreds, 1e-4) stay within the tolerance: the
+    pair's scale keeps them inside the fp16 range."""
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, 50, 2048, 1536, seed=11)
+    x[:, ::97] *= 300.0
+    x[:, 5::89] *= 1e-4
+    assert rel_err(_native.gemm(x, w, 5), x, w) <= TF32X3_TOL
+
+
 def test_dispatch_and_determinism(dev):
     from rapidtinyrec_b200 import _native
     for M in (50, 237):
@@ -57,7 +77,18 @@ def test_dispatch_and_determinism(dev):
         a = _native.gemm(x, w, 0)
         b = _native.gemm(x, w, 0)
         assert torch.equal(a, b)                                  # fixed split order, no atomics
-        assert torch.equal(a, _native.gemm(x, w, 1 if M <= 64 else 2))
+        assert torch.equal(a, _native.gemm(x, w, 5))
+        c = _native.gemm(x, w, 1 if M <= 64 else 2)
+        assert torch.equal(c, _native.gemm(x, w, 1 if M <= 64 else 2))
+
+
+@pytest.mark.parametrize('N,K', [(1536, 8960), (2048, 1536), (256, 688)])
+def test_fp16_pair_rows_agree_bitwise_in_64_and_128_row_ctas(dev, N, K):
+    """Rows of a 64-row CTA equal the same rows inside a 128-row CTA (same
+    split-K plan, same promotion order): a two-user batch matches batch 1."""
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, 100, N, K, seed=N + K)
+    assert torch.equal(_native.gemm(x[:50].contiguous(), w, 5), _native.gemm(x, w, 5)[:50])
 
 
 def test_64_and_128_row_kernels_agree_bitwise_up_to_64_rows(dev):

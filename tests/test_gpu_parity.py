@@ -197,7 +197,7 @@ def test_report_counts_match_the_captured_graph(tiny_engine, tiny):
     tail = 4                                  # max, two sums, beam selection
     assert rep['graph_kernel_nodes'] == 4 * (decode + tail) + 1   # decode steps 1-4, finalize
     assert rep['launches_per_request'] == 1 + prefill + tail + rep['graph_kernel_nodes']
-    assert rep['tensor_core_gemm'] == 1 and rep['norm_fold'] == 1
+    assert rep['tensor_core_gemm'] == 2 and rep['norm_fold'] == 1
 
 
 def test_contract_violations_raise(tiny_engine, tiny):
