@@ -58,7 +58,8 @@ def percentile(values, q):
 # head): ncu dram__bytes_read.sum + dram__bytes_write.sum of a one-layer cut
 # (`--mode profile-gemms --rows 50 --layers 1`), the layer's share scaled by
 # the layer count.  Workloads without a capture report null.
-GEMM_PASS_TRAFFIC = {'qwen1.5b-fp32': 6.426e9, 'qwen1.5b-bf16': 3.169e9}
+GEMM_PASS_TRAFFIC = {'qwen1.5b-fp32': 6.317e9, 'qwen1.5b-bf16': 3.169e9}
+GEMM_PASS_TRAFFIC_TF32 = {'qwen1.5b-fp32': 6.426e9}   # the 3xTF32 kernels (RTR_GEMM=tf32)
 
 
 def measured_peaks():
@@ -407,7 +408,8 @@ def run_ours(args):
             'roofline': {'bound': 'hbm', 'kernel': gemm_kernel,
                          'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
                          'frac': round(achieved / peak, 4), 'peak_source': peak_kind,
-                         'traffic': GEMM_PASS_TRAFFIC.get(args.workload), 'traffic_source':
+                         'traffic': (GEMM_PASS_TRAFFIC_TF32 if rep['tensor_core_gemm'] == 1
+                                     else GEMM_PASS_TRAFFIC).get(args.workload), 'traffic_source':
                              'ncu dram__bytes_read+write of a one-layer cut, layer share x layers + LM head'
                              if args.workload in GEMM_PASS_TRAFFIC
                              else None,
