@@ -408,7 +408,7 @@ def run_ours(args):
             'roofline': {'bound': 'hbm', 'kernel': gemm_kernel,
                          'achieved': round(achieved, 1), 'peak': peak, 'unit': 'GB/s',
                          'frac': round(achieved / peak, 4), 'peak_source': peak_kind,
-                         'traffic': (GEMM_PASS_TRAFFIC_TF32 if rep['tensor_core_gemm'] == 1
+                         'traffic': (GEMM_PASS_TRAFFIC_TF32 if cfg.dtype == 'fp32' and rep['tensor_core_gemm'] == 1
                                      else GEMM_PASS_TRAFFIC).get(args.workload), 'traffic_source':
                              'ncu dram__bytes_read+write of a one-layer cut, layer share x layers + LM head'
                              if args.workload in GEMM_PASS_TRAFFIC
