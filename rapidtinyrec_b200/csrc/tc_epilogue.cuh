@@ -77,15 +77,18 @@ inline cudaError_t query_cluster_waves(const void* kernel, int threads, int smem
 //   weight stream  max(0.1 us per chunk of a split, the tiles' weight bytes
 //                  at 6.5 TB/s scaled by the share of SMs the grid uses)
 //   finish         3.1 ns per split per row of the slice (64 / cluster rows)
-//   clusters       0.5 us per CTA beyond two (co-scheduling a larger cluster
-//                  on one GPC delays its start)
+//   clusters       cluster_us per CTA beyond two: 0.5 us for the 3xTF32
+//                  kernels (co-scheduling a larger cluster of 11-warp CTAs on
+//                  one GPC delayed its start), 0 for the fp16-pair kernel
+//                  (8 splits in clusters of 4 measured fastest for o_proj and
+//                  q/k/v at M = 50)
 // Both kernels take the same plan for the same tiles and K (one CTA per SM
 // in both, one wave table, 64 nominal rows), so their sums agree bit for bit.
 struct SplitPlan {
   int splits, cluster;
 };
 inline SplitPlan tc_split_plan(int tiles, int nchunks, int sms, const int* waves, int max_cs, size_t ws_floats,
-                               long tile_floats, int max_tickets) {
+                               long tile_floats, int max_tickets, double cluster_us = 0.5) {
   static const int cap = [] {
     const char* e = getenv("RTR_TC_CLUSTER");
     const int v = e ? atoi(e) : 8;
@@ -102,7 +105,7 @@ inline SplitPlan tc_split_plan(int tiles, int nchunks, int sms, const int* waves
     const double t_main = fmax(0.1 * ((nchunks + s - 1) / s), stream_us / (share < 1.0 ? share : 1.0));
     for (int c = 1; c <= (cap < max_cs ? cap : max_cs); ++c) {
       if (s % c != 0 || (c > 1 && (long)tiles * (s / c) > waves[c])) continue;
-      const double t = t_main + 0.0031 * s * ((64 + c - 1) / c) + (c > 2 ? 0.5 * (c - 2) : 0.0);
+      const double t = t_main + 0.0031 * s * ((64 + c - 1) / c) + (c > 2 ? cluster_us * (c - 2) : 0.0);
       if (t < best_t - 1e-9) { best_t = t; best = SplitPlan{s, c}; }
     }
   }
