@@ -2,7 +2,7 @@
 //
 // Prefill: causal GQA attention of one request (sdpa_attention_forward with
 // is_causal=True, transformers integrations/sdpa_attention.py:40-104).  A CTA
-// owns 16 query positions of one query head, two per warp.
+// owns 32 query positions of one query head, register-tiled (below).
 //
 // Decode: the reference's folded_sdpa (rapidtinyrec/folded_attention.py:16-31)
 // maps query head h to KV head h / (Hq/Hkv) and attends over
@@ -15,9 +15,7 @@
 // Both stream the prefix K/V rows of the head's KV group through a
 // double-buffered shared ring of 64-key chunks with cp.async (K rows padded by
 // four floats so the float4 score reads of 8 consecutive keys hit distinct
-// banks), and every warp runs an online softmax over its query rows: lane j
-// scores keys j and j + 32 of the chunk, then accumulates P.V over its own
-// HD/32 output dimensions.
+// banks), with an online softmax over each query row.
 #include <math.h>
 
 #include "common.cuh"
@@ -28,16 +26,13 @@ namespace rtr {
 constexpr int AK = 64;         // keys per chunk
 constexpr int AWARPS = 8;      // warps per CTA
 constexpr int ATHREADS = AWARPS * 32;
-constexpr int PQ = 16;         // prefill query positions per CTA (2 per warp)
+constexpr int PT_Q = 32;       // prefill query positions per CTA
 constexpr int DBEAMS = AWARPS; // decode beams per CTA (1 per warp)
 
 // Prefix K/V rows are staged in their storage type T (fp32, or bf16 in the
 // bf16 mode); K rows are padded so 16-byte copies stay aligned and the score
 // reads of consecutive keys spread over the banks.  q lives in fp32.
 template <int HD, typename T> __host__ __device__ constexpr int kld() { return HD + 16 / (int)sizeof(T); }
-template <int HD, typename T> constexpr size_t attn_smem_bytes(int qrows) {
-  return (size_t)(2 * AK * kld<HD, T>() + 2 * AK * HD) * sizeof(T) + (size_t)qrows * HD * sizeof(float);
-}
 
 // Four consecutive elements as floats.
 RTR_DEVICE float4 ld4f(const float* p) { return *reinterpret_cast<const float4*>(p); }
@@ -90,112 +85,162 @@ RTR_DEVICE void load_vec(const __nv_bfloat16* src, float (&x)[2]) {
   x[0] = v.x; x[1] = v.y;
 }
 
-// One warp, one query row (q in shared memory), one staged chunk of keys
-// [k0, k0 + AK): online-softmax update of (m, l, acc) over keys < kend.
-template <int HD, typename T>
-RTR_DEVICE void chunk_update(const float* qrow, const T* kc, const T* vc, int k0, int kend, float scale,
-                             float& m, float& l, float (&acc)[HD / 32]) {
-  constexpr int VEC = HD / 32;
-  const int lane = threadIdx.x & 31;
-  const float4* q4 = reinterpret_cast<const float4*>(qrow);
-  const T* ka = kc + lane * kld<HD, T>();
-  const T* kb = kc + (lane + 32) * kld<HD, T>();
-  float s0 = 0.f, s1 = 0.f;
-#pragma unroll 8
-  for (int d = 0; d < HD / 4; ++d) {
-    const float4 qq = q4[d], a = ld4f(ka + 4 * d), b = ld4f(kb + 4 * d);
-    s0 = fmaf(qq.x, a.x, s0); s0 = fmaf(qq.y, a.y, s0); s0 = fmaf(qq.z, a.z, s0); s0 = fmaf(qq.w, a.w, s0);
-    s1 = fmaf(qq.x, b.x, s1); s1 = fmaf(qq.y, b.y, s1); s1 = fmaf(qq.z, b.z, s1); s1 = fmaf(qq.w, b.w, s1);
-  }
-  s0 = k0 + lane < kend ? s0 * scale : -INFINITY;
-  s1 = k0 + lane + 32 < kend ? s1 * scale : -INFINITY;
-  const float mn = fmaxf(m, warp_max(fmaxf(s0, s1)));  // finite: key k0 is always valid
-  const float corr = expf(m - mn);
-  const float p0 = expf(s0 - mn), p1 = expf(s1 - mn);
-  l = l * corr + warp_sum(p0 + p1);
-  m = mn;
-#pragma unroll
-  for (int i = 0; i < VEC; ++i) acc[i] *= corr;
-  const T* va = vc + lane * VEC;
-#pragma unroll 4
-  for (int j = 0; j < 32; ++j) {
-    const float pa = __shfl_sync(0xffffffffu, p0, j), pb = __shfl_sync(0xffffffffu, p1, j);
-    float x[VEC], y[VEC];
-    load_vec(va + j * HD, x);
-    load_vec(va + (j + 32) * HD, y);
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] = fmaf(pa, x[i], acc[i]);
-#pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[i] = fmaf(pb, y[i], acc[i]);
-  }
+// ------------------------------------------------------------------ prefill
+// Register-tiled causal attention: a CTA owns PT_Q = 32 query rows of one
+// query head and walks the keys in staged 64-key chunks.  Thread (ty, tx) =
+// (tid / 16, tid % 16) owns rows 2 ty, 2 ty + 1:
+//   scores  keys tx + 16 j (j < 4): a 2 x 4 tile, per 4 dimensions two q
+//           float4 and four K float4 loads for 32 FMAs (K rows padded so the
+//           16 keys of a half-warp hit distinct banks; the other half-warp
+//           reads the same keys)
+//   softmax online per row across the 16 lanes of the half-warp (shuffles)
+//   P.V     P goes through shared memory; dimensions 4 tx .. 4 tx + 3 (and
+//           + 64 for head_dim 128): per 4 keys two P float4 and HD / 64 * 4 V
+//           float4 loads for HD / 2 FMAs
+template <int HD, typename T> constexpr size_t prefill_smem_bytes() {
+  return (size_t)(2 * AK * kld<HD, T>() + 2 * AK * HD) * sizeof(T) +
+         (size_t)(PT_Q * (HD + 4) + PT_Q * (AK + 4)) * sizeof(float);
 }
 
-// ------------------------------------------------------------------ prefill
 template <int HD, typename T>
-__global__ void __launch_bounds__(ATHREADS) prefill_attn_kernel(
+__global__ void __launch_bounds__(ATHREADS, 1) prefill_attn_kernel(
     const T* __restrict__ q, const T* __restrict__ kp, const T* __restrict__ vp,
     T* __restrict__ out, float* __restrict__ out_big, float* __restrict__ out_small, int L, int cap, int heads,
     int kv_heads, float scale, int xfmt) {
-  constexpr int VEC = HD / 32, ROWS = PQ / AWARPS;
+  constexpr int QLD = HD + 4, PLD = AK + 4, KLD = kld<HD, T>();
+  constexpr int NV = HD / 64;  // float4 column groups of the output per thread
+  static_assert(ATHREADS == 256 && PT_Q == 32 && AK == 64, "tiling assumes 256 threads, 32 rows, 64 keys");
   pdl_launch_dependents();
   pdl_wait();
   extern __shared__ __align__(16) unsigned char asmem[];
   T* kbuf = reinterpret_cast<T*>(asmem);
-  T* vbuf = kbuf + 2 * AK * kld<HD, T>();
-  float* qs = reinterpret_cast<float*>(vbuf + 2 * AK * HD);  // [PQ][HD]
+  T* vbuf = kbuf + 2 * AK * KLD;
+  float* qs = reinterpret_cast<float*>(vbuf + 2 * AK * HD);  // [PT_Q][QLD]
+  float* ps = qs + PT_Q * QLD;                                // [PT_Q][PLD]
   const int h = blockIdx.y, g = h / (heads / kv_heads);
-  const int q0 = blockIdx.x * PQ;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q0 = blockIdx.x * PT_Q;
+  const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
+  const int r0 = 2 * ty;
   const T* kbase = kp + (long)g * cap * HD;
   const T* vbase = vp + (long)g * cap * HD;
-  const int kend = min(L, q0 + PQ);  // keys any row of the block may see
+  const int kend = min(L, q0 + PT_Q);  // keys any row of the block may see
   const int nchunks = (kend + AK - 1) / AK;
+  // last key of each row (padding rows past L see key 0 only: their values are never stored)
+  int klast[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) klast[i] = q0 + r0 + i < L ? q0 + r0 + i : 0;
 
   load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, 0, kend, 0);
-  for (int i = threadIdx.x; i < PQ * HD / 4; i += ATHREADS) {
+  for (int i = threadIdx.x; i < PT_Q * HD / 4; i += ATHREADS) {
     const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (q0 + r < L) v = ld4f(q + ((long)(q0 + r) * heads + h) * HD + d);
-    *reinterpret_cast<float4*>(qs + r * HD + d) = v;
+    *reinterpret_cast<float4*>(qs + r * QLD + d) = v;
   }
-  float m[ROWS], l[ROWS], acc[ROWS][VEC];
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f}, acc[2][4 * NV];
 #pragma unroll
-  for (int r = 0; r < ROWS; ++r) {
-    m[r] = -INFINITY; l[r] = 0.f;
+  for (int i = 0; i < 2; ++i)
 #pragma unroll
-    for (int i = 0; i < VEC; ++i) acc[r][i] = 0.f;
-  }
+    for (int e = 0; e < 4 * NV; ++e) acc[i][e] = 0.f;
+
   for (int c = 0; c < nchunks; ++c) {
     if (c + 1 < nchunks) load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, (c + 1) * AK, kend, (c + 1) & 1);
     else cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const T* kc = kbuf + (c & 1) * AK * kld<HD, T>();
+    const T* kc = kbuf + (c & 1) * AK * KLD;
     const T* vc = vbuf + (c & 1) * AK * HD;
+    // ---- scores: rows r0, r0 + 1 x keys tx + 16 j
+    float sc[2][4];
 #pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      const int row = warp * ROWS + r, qpos = q0 + row;
-      if (qpos < L && c * AK <= qpos)
-        chunk_update<HD, T>(qs + row * HD, kc, vc, c * AK, qpos + 1, scale, m[r], l[r], acc[r]);
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) sc[i][j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < HD; d += 4) {
+      const float4 qa = *reinterpret_cast<const float4*>(qs + r0 * QLD + d);
+      const float4 qb = *reinterpret_cast<const float4*>(qs + (r0 + 1) * QLD + d);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float4 k = ld4f(kc + (tx + 16 * j) * KLD + d);
+        sc[0][j] = fmaf(qa.x, k.x, sc[0][j]); sc[0][j] = fmaf(qa.y, k.y, sc[0][j]);
+        sc[0][j] = fmaf(qa.z, k.z, sc[0][j]); sc[0][j] = fmaf(qa.w, k.w, sc[0][j]);
+        sc[1][j] = fmaf(qb.x, k.x, sc[1][j]); sc[1][j] = fmaf(qb.y, k.y, sc[1][j]);
+        sc[1][j] = fmaf(qb.z, k.z, sc[1][j]); sc[1][j] = fmaf(qb.w, k.w, sc[1][j]);
+      }
     }
-    __syncthreads();  // the slot is refilled by the next iteration's load
+    // ---- online softmax per row over the half-warp's 64 keys
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int key = c * AK + tx + 16 * j;
+        sc[i][j] = key <= klast[i] ? sc[i][j] * scale : -INFINITY;
+        mx = fmaxf(mx, sc[i][j]);
+      }
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float mn = fmaxf(m[i], mx);  // finite: key 0 is valid for every row
+      const float corr = expf(m[i] - mn);
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float pv = expf(sc[i][j] - mn);
+        sum += pv;
+        ps[(r0 + i) * PLD + tx + 16 * j] = pv;
+      }
+#pragma unroll
+      for (int o = 8; o >= 1; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      l[i] = l[i] * corr + sum;
+      m[i] = mn;
+#pragma unroll
+      for (int e = 0; e < 4 * NV; ++e) acc[i][e] *= corr;
+    }
+    __syncthreads();  // P of the whole tile is in shared memory
+    // ---- P.V: rows r0, r0 + 1 x dimensions 4 tx + 64 n (n < NV)
+#pragma unroll 2
+    for (int k4 = 0; k4 < AK; k4 += 4) {
+      const float4 pa = *reinterpret_cast<const float4*>(ps + r0 * PLD + k4);
+      const float4 pb = *reinterpret_cast<const float4*>(ps + (r0 + 1) * PLD + k4);
+      const float pav[4] = {pa.x, pa.y, pa.z, pa.w}, pbv[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+#pragma unroll
+        for (int n = 0; n < NV; ++n) {
+          const float4 v = ld4f(vc + (k4 + kk) * HD + n * 64 + 4 * tx);
+          acc[0][4 * n] = fmaf(pav[kk], v.x, acc[0][4 * n]);
+          acc[0][4 * n + 1] = fmaf(pav[kk], v.y, acc[0][4 * n + 1]);
+          acc[0][4 * n + 2] = fmaf(pav[kk], v.z, acc[0][4 * n + 2]);
+          acc[0][4 * n + 3] = fmaf(pav[kk], v.w, acc[0][4 * n + 3]);
+          acc[1][4 * n] = fmaf(pbv[kk], v.x, acc[1][4 * n]);
+          acc[1][4 * n + 1] = fmaf(pbv[kk], v.y, acc[1][4 * n + 1]);
+          acc[1][4 * n + 2] = fmaf(pbv[kk], v.z, acc[1][4 * n + 2]);
+          acc[1][4 * n + 3] = fmaf(pbv[kk], v.w, acc[1][4 * n + 3]);
+        }
+      }
+    }
+    __syncthreads();  // the K/V slot and P are refilled by the next iteration
   }
 #pragma unroll
-  for (int r = 0; r < ROWS; ++r) {
-    const int qpos = q0 + warp * ROWS + r;
+  for (int i = 0; i < 2; ++i) {
+    const int qpos = q0 + r0 + i;
     if (qpos >= L) continue;
-    const float inv = 1.0f / l[r];
+    const float inv = 1.0f / l[i];
 #pragma unroll
-    for (int i = 0; i < VEC; ++i)
-      store_out(out, out_big, out_small, ((long)qpos * heads + h) * HD + lane * VEC + i, acc[r][i] * inv, xfmt);
+    for (int n = 0; n < NV; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        store_out(out, out_big, out_small, ((long)qpos * heads + h) * HD + n * 64 + 4 * tx + e, acc[i][4 * n + e] * inv,
+                  xfmt);
   }
 }
 
 template <int HD, typename T>
 static cudaError_t launch_prefill(const void* q, const void* kp, const void* vp, void* out, float* ob, float* os, int L,
                                   int cap, int heads, int kv_heads, float scale, cudaStream_t stream, int xfmt) {
-  dim3 grid((L + PQ - 1) / PQ, heads);
-  return launch_pdl(PDL_ATTN, prefill_attn_kernel<HD, T>, grid, dim3(ATHREADS), attn_smem_bytes<HD, T>(PQ), stream,
+  dim3 grid((L + PT_Q - 1) / PT_Q, heads);
+  return launch_pdl(PDL_ATTN, prefill_attn_kernel<HD, T>, grid, dim3(ATHREADS), prefill_smem_bytes<HD, T>(), stream,
                     static_cast<const T*>(q), static_cast<const T*>(kp), static_cast<const T*>(vp), static_cast<T*>(out),
                     ob, os, L, cap, heads, kv_heads, scale, xfmt);
 }
@@ -470,7 +515,7 @@ cudaError_t attention_decode(const void* q, const void* k_prefix, const void* v_
 template <int HD, typename T>
 static cudaError_t attn_set_smem() {
   cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel<HD, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)attn_smem_bytes<HD, T>(PQ));
+                                       (int)prefill_smem_bytes<HD, T>());
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(decode_attn_kernel<HD, T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)decode_smem_bytes<HD, T>());
