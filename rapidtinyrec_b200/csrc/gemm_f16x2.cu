@@ -372,7 +372,7 @@ cudaError_t gemm_f16x2(const TensorMap& tmW, const TensorMap& tmXh, const Tensor
   cudaGetDevice(&dev);
   // the plan counts 128-byte chunk rows: a 64-element chunk row of the pair is two
   const SplitPlan plan = tc_split_plan(tt * wt, 2 * nchunks, sms, g_tc_clusters[dev < kMaxDevices ? dev : 0],
-                                       TC_MAX_CLUSTER, ws_floats, (long)ntok * FX_WROWS, max_tickets, 0.0);
+                                       4, ws_floats, (long)ntok * FX_WROWS, max_tickets, 0.0, true);
   const int splits = plan.splits < nchunks ? plan.splits : nchunks;
   const int cs = splits % plan.cluster ? 1 : plan.cluster;
   TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}, {}, SPLIT_F16};

@@ -79,16 +79,17 @@ inline cudaError_t query_cluster_waves(const void* kernel, int threads, int smem
 //   finish         3.1 ns per split per row of the slice (64 / cluster rows)
 //   clusters       cluster_us per CTA beyond two: 0.5 us for the 3xTF32
 //                  kernels (co-scheduling a larger cluster of 11-warp CTAs on
-//                  one GPC delayed its start), 0 for the fp16-pair kernel
-//                  (8 splits in clusters of 4 measured fastest for o_proj and
-//                  q/k/v at M = 50)
+//                  one GPC delayed its start); the fp16-pair kernel takes 0
+//                  but only cluster sizes 2 and 4 (a sweep of splits x sizes
+//                  at M = 50 put 8 x 4 first for o_proj and q/k/v and 12 x 2
+//                  for down_proj; 10 x 5 and 8 x 8 were slower)
 // Both kernels take the same plan for the same tiles and K (one CTA per SM
 // in both, one wave table, 64 nominal rows), so their sums agree bit for bit.
 struct SplitPlan {
   int splits, cluster;
 };
 inline SplitPlan tc_split_plan(int tiles, int nchunks, int sms, const int* waves, int max_cs, size_t ws_floats,
-                               long tile_floats, int max_tickets, double cluster_us = 0.5) {
+                               long tile_floats, int max_tickets, double cluster_us = 0.5, bool pow2 = false) {
   static const int cap = [] {
     const char* e = getenv("RTR_TC_CLUSTER");
     const int v = e ? atoi(e) : 8;
@@ -104,7 +105,7 @@ inline SplitPlan tc_split_plan(int tiles, int nchunks, int sms, const int* waves
     const double share = (double)tiles * s / sms;
     const double t_main = fmax(0.1 * ((nchunks + s - 1) / s), stream_us / (share < 1.0 ? share : 1.0));
     for (int c = 1; c <= (cap < max_cs ? cap : max_cs); ++c) {
-      if (s % c != 0 || (c > 1 && (long)tiles * (s / c) > waves[c])) continue;
+      if (s % c != 0 || (c > 1 && (long)tiles * (s / c) > waves[c]) || (pow2 && (c & (c - 1)))) continue;
       const double t = t_main + 0.0031 * s * ((64 + c - 1) / c) + (c > 2 ? cluster_us * (c - 2) : 0.0);
       if (t < best_t - 1e-9) { best_t = t; best = SplitPlan{s, c}; }
     }
