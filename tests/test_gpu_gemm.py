@@ -91,6 +91,16 @@ def test_fp16_pair_rows_agree_bitwise_in_64_and_128_row_ctas(dev, N, K):
     assert torch.equal(_native.gemm(x[:50].contiguous(), w, 5), _native.gemm(x, w, 5)[:50])
 
 
+def test_tf32x3_persistent_lm_head_mode(dev):
+    """More weight tiles than SMs with one row tile (the LM head's shape): the
+    64-row 3xTF32 kernel runs persistent CTAs that walk several tiles."""
+    from rapidtinyrec_b200 import _native
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    N = (sms + 3) * 128
+    x, w = operands(dev, 50, N, 1536, seed=17)
+    assert rel_err(_native.gemm(x, w, 1), x, w) <= TF32X3_TOL
+
+
 def test_64_and_128_row_kernels_agree_bitwise_up_to_64_rows(dev):
     """Both promote the tensor-core accumulator every 8 chunks in the same order."""
     from rapidtinyrec_b200 import _native

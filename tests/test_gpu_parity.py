@@ -153,6 +153,21 @@ def test_tiny_generate_matches_reference_golden(tiny_engine, tiny):
     print(f'tiny: max |delta score| vs reference = {worst:.3e}')
 
 
+@pytest.mark.parametrize('gemm', ['tf32', 'ffma'])
+def test_tiny_alternate_gemm_paths_match_reference_golden(cuda, tiny, gemm, monkeypatch):
+    """The GEMM switches (RTR_GEMM=tf32: the 3xTF32 kernels; =ffma: the FP32
+    FFMA kernel) give the reference's SIDs and beam paths too."""
+    monkeypatch.setenv('RTR_GEMM', gemm)
+    eng = make_engine(tiny['cfg'], tiny['weights'], tiny['constraints'], max_prefix=128)
+    assert eng.report()['tensor_core_gemm'] == (1 if gemm == 'tf32' else 0)
+    meta, _ = load_generate_fixture('tiny_fp32')
+    items = set(tiny['items'])
+    for rec in meta['records']:
+        got = eng.generate(rec['prompt_token_ids'])
+        compare_records(got, rec)
+        check_invariants(got, tiny['cfg'], items)
+
+
 def test_tiny_step_scores_match_reference(tiny_engine):
     meta, arrays = load_generate_fixture('tiny_fp32')
     for u, rec in enumerate(meta['records'][:3]):
