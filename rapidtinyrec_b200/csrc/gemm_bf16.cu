@@ -465,8 +465,9 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
   // a 64-element bf16 chunk row is 128 bytes, as a 32-element tf32 one: the same plan
   int dev = 0;
   cudaGetDevice(&dev);
-  const SplitPlan plan = tc_split_plan(tt * wt, nchunks, sms, g_bf_clusters[dev < kMaxDevices ? dev : 0],
-                                       TC_MAX_CLUSTER, ws_floats, (long)BF_NTOK * BF_WROWS, max_tickets);
+  // the fp16-pair kernel's rule: no cost for clusters beyond two, sizes 2 and 4 only
+  const SplitPlan plan = tc_split_plan(tt * wt, nchunks, sms, g_bf_clusters[dev < kMaxDevices ? dev : 0], 4,
+                                       ws_floats, (long)BF_NTOK * BF_WROWS, max_tickets, 0.0, true);
   const int splits = plan.splits, cs = plan.cluster;
   BfParams p{C, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
   if (rope) p.rope = *rope;
