@@ -79,10 +79,10 @@ inline cudaError_t query_cluster_waves(const void* kernel, int threads, int smem
 //   finish         3.1 ns per split per row of the slice (64 / cluster rows)
 //   clusters       cluster_us per CTA beyond two: 0.5 us for the 3xTF32
 //                  kernels (co-scheduling a larger cluster of 11-warp CTAs on
-//                  one GPC delayed its start); the fp16-pair kernel takes 0
-//                  but only cluster sizes 2 and 4 (a sweep of splits x sizes
-//                  at M = 50 put 8 x 4 first for o_proj and q/k/v and 12 x 2
-//                  for down_proj; 10 x 5 and 8 x 8 were slower)
+//                  one GPC delayed its start); the fp16-pair and bf16 kernels
+//                  take 0 but only cluster sizes 2 and 4 (a sweep of splits x
+//                  sizes at M = 50 put 8 x 4 first for o_proj and q/k/v and
+//                  12 x 2 for down_proj; 10 x 5 and 8 x 8 were slower)
 // Both kernels take the same plan for the same tiles and K (one CTA per SM
 // in both, one wave table, 64 nominal rows), so their sums agree bit for bit.
 struct SplitPlan {
