@@ -127,7 +127,9 @@ __global__ void tail_max_kernel(const float* __restrict__ logits, int vocab, Bea
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
   const float* x = logits + (long)grow * vocab;
   float m = -INFINITY;
-  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) m = fmaxf(m, x[i]);
+  // unrolled with the element order kept: four loads in flight per thread
+#pragma unroll 4
+  for (long i = lo + threadIdx.x; i < hi; i += TAIL_THREADS) m = fmaxf(m, x[i]);
   m = block_max(m, red);
   if (threadIdx.x == 0) st->part[row][sp][0] = m;
 }
@@ -148,7 +150,8 @@ __global__ void tail_sum1_kernel(const float* __restrict__ logits, int vocab, Be
   const float* x = logits + (long)grow * vocab;
   const float m = row_max(st, row);
   float s = 0.f;
-  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) s += expf(x[i] - m);
+#pragma unroll 4
+  for (long i = lo + threadIdx.x; i < hi; i += TAIL_THREADS) s += expf(x[i] - m);
   s = block_sum(s, red);
   if (threadIdx.x == 0) st->part[row][sp][1] = s;
 }
@@ -167,7 +170,8 @@ __global__ void tail_sum2_kernel(const float* __restrict__ logits, int vocab, Be
   const float L1 = logf(s1);
   const float m2 = (m - m) - L1;  // max of lp1, reached at the arg-max column
   float s = 0.f;
-  for (long i = lo + threadIdx.x; i < hi; i += blockDim.x) s += expf(((x[i] - m) - L1) - m2);
+#pragma unroll 4
+  for (long i = lo + threadIdx.x; i < hi; i += TAIL_THREADS) s += expf(((x[i] - m) - L1) - m2);
   s = block_sum(s, red);
   if (threadIdx.x == 0) {
     st->part[row][sp][2] = s;
