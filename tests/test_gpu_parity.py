@@ -244,6 +244,25 @@ def test_out_of_vocab_prompt_token_reported(tiny_engine, tiny):
     assert len(rec['token_ids']) == 50
 
 
+def test_activation_beyond_the_fp16_pair_range_is_reported(cuda, tiny, monkeypatch):
+    """The fp16-pair GEMM carries activations up to 16 x 65,504: a model whose
+    residual stream exceeds that (here: the embedding scaled by 1e7) fails
+    with RTR_ERR_DEVICE instead of returning beams, and RTR_GEMM=tf32 serves
+    the same request."""
+    from rapidtinyrec_b200._native import RTR_ERR_DEVICE, NativeError
+    weights = dict(tiny['weights'])
+    key = next(k for k in weights if 'embed' in k)
+    weights[key] = weights[key] * 1e7
+    eng = make_engine(tiny['cfg'], weights, tiny['constraints'], max_prefix=128)
+    assert eng.report()['tensor_core_gemm'] == 2
+    with pytest.raises(NativeError) as e:
+        eng.generate(tiny['users'][0].prompt_token_ids)
+    assert e.value.code == RTR_ERR_DEVICE
+    monkeypatch.setenv('RTR_GEMM', 'tf32')
+    eng = make_engine(tiny['cfg'], weights, tiny['constraints'], max_prefix=128)
+    assert len(eng.generate(tiny['users'][0].prompt_token_ids)['token_ids']) == 50
+
+
 # --------------------------------------------------- full-size parity
 def full_size_case(name, n_oracle, n_props, cuda):
     from oracle.beam_cpu import beam_search
