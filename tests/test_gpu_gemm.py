@@ -101,6 +101,19 @@ def test_tf32x3_persistent_lm_head_mode(dev):
     assert rel_err(_native.gemm(x, w, 1), x, w) <= TF32X3_TOL
 
 
+def test_fp16_pair_lm_head_shape(dev):
+    """More weight tiles than SMs with one 64-row tile (the LM head's shape,
+    several waves of CTAs): within the tolerance, and the same bits as the same
+    rows inside 128-row CTAs (a two-user batch)."""
+    from rapidtinyrec_b200 import _native
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    N = (sms + 3) * 128
+    x, w = operands(dev, 100, N, 1536, seed=19)
+    c50 = _native.gemm(x[:50].contiguous(), w, 5)
+    assert rel_err(c50, x[:50], w) <= TF32X3_TOL
+    assert torch.equal(c50, _native.gemm(x, w, 5)[:50])
+
+
 def test_64_and_128_row_kernels_agree_bitwise_up_to_64_rows(dev):
     """Both promote the tensor-core accumulator every 8 chunks in the same order."""
     from rapidtinyrec_b200 import _native
