@@ -26,9 +26,10 @@ struct RopeArgs {
   int rows_per_user = 0;   // batched decode: row m belongs to user m / rows_per_user (L_dev[user])
 };
 
-// RMSNorm folded into the projection GEMMs (3xTF32 path): the norm weight is
-// folded into the packed weight's columns, the producer of the residual stream
-// (embedding, o_proj / down_proj epilogues) writes x's tf32 split and per-row
+// RMSNorm folded into the projection GEMMs (fp32 tensor-core paths): the norm
+// weight is folded into the packed weight's columns, the producer of the
+// residual stream (embedding, o_proj / down_proj epilogues) writes x's split
+// (SPLIT_F16 pair or SPLIT_TF32) and per-row
 // partial sums of squares over 128-column chunks (ss[chunk * ld + row]), and
 // the consuming GEMM scales each output row by 1 / sqrt(sum / hidden + eps).
 struct NormFold {

@@ -51,7 +51,7 @@ struct rtr_session {
   // kernel (default), or SPLIT_TF32, the 3xTF32 kernels (RTR_GEMM=tf32); every
   // activation producer writes its split in this format
   int xfmt = SPLIT_TF32;
-  // RMSNorm folded into the 3xTF32 GEMMs (fp32 tensor-core path, hidden % 128 == 0;
+  // RMSNorm folded into the GEMMs (fp32 tensor-core paths, hidden % 128 == 0;
   // RTR_NORM_FOLD=0 keeps the separate norm kernels): norm weights folded into the
   // packed q/k/v, gate/up and LM-head columns, row scales from partial sums of squares
   bool fold = false;

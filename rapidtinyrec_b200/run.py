@@ -257,7 +257,7 @@ def _folded(args, out, precision, dtype, policy):
                 'full_cohort': args.full_cohort, 'save_full_scores': args.save_full_scores,
                 'attention_layout': 'folded_query_heads', 'users': [record_of[u.cohort_index] for u in users],
                 'dtype': 'float32' if dtype == 'fp32' else 'bfloat16', 'tf32': False,
-                'numerics': ('fp32 weights and activations, 3xTF32 tensor-core projections' if dtype == 'fp32' else
+                'numerics': ('fp32 weights and activations, fp32-accurate tensor-core projections' if dtype == 'fp32' else
                              'bf16 weights, activations and KV (rounded where a bf16 torch model rounds), fp32 '
                              'accumulation, fp32 log-softmax and beam scores'),
                 'hardware': torch.cuda.get_device_name(0), 'source': inp.source,
@@ -274,6 +274,13 @@ def _folded(args, out, precision, dtype, policy):
     save(out / 'manifest.json', manifest)
     setup_started = time.perf_counter()
     engine = inp.engine()
+    if dtype == 'fp32':  # name the projection kernel the session chose (RTR_GEMM)
+        kind = {2: 'fp16-pair split operands', 1: '3xTF32 split operands', 0: 'FP32 FFMA'}
+        manifest['numerics'] = ('fp32 weights and activations, tensor-core projections on '
+                                + kind.get(engine.report()['tensor_core_gemm'], 'unknown operands')
+                                if engine.report()['tensor_core_gemm'] else
+                                'fp32 weights and activations, FP32 FFMA projections')
+        save(out / 'manifest.json', manifest)
     immutable_before = inp.immutable_inventory(engine)
     save(out / 'immutable-before.json', immutable_before)
     ids_of = {u.cohort_index: list(u.prompt_token_ids) for u in inp.users}
