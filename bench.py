@@ -124,6 +124,38 @@ class ClockSampler:
                 'samples': len(sm)}
 
 
+def physical_cores():
+    """Physical cores this process may run on (``/proc/cpuinfo`` core ids of the
+    allowed logical CPUs); logical CPUs where the core ids are not readable."""
+    try:
+        allowed = os.sched_getaffinity(0)
+    except AttributeError:
+        allowed = set(range(os.cpu_count() or 1))
+    cores, cpu, phys = set(), None, None
+    try:
+        for line in Path('/proc/cpuinfo').read_text().splitlines():
+            key, _, val = (x.strip() for x in line.partition(':'))
+            if key == 'processor':
+                cpu, phys = int(val), None
+            elif key == 'physical id':
+                phys = int(val)
+            elif key == 'core id' and cpu in allowed:
+                cores.add((phys, int(val)))
+    except (OSError, ValueError):
+        cores = set()
+    return len(cores) or len(allowed)
+
+
+def bench_config(args, wl, world, beams=50):
+    """The ``config`` object of both arms' JSON lines."""
+    cfg = wl.model
+    return {'workload': args.workload, 'model': cfg.name, 'beams': beams, 'items': wl.items,
+            'prompt_tokens': [wl.prompt_min, wl.prompt_max], 'users_per_rank': args.steps,
+            'parallelism': f'replicas{world}', 'partition': 'users round-robin, no per-step collective',
+            'l2': f'inputs larger than L2: the {gemm_weight_bytes(cfg) / 1e9:.1f} GB of weights stream from HBM '
+                  f'every forward'}
+
+
 def dist_env():
     return int(os.environ.get('RANK', 0)), int(os.environ.get('LOCAL_RANK', 0)), int(os.environ.get('WORLD_SIZE', 1))
 
@@ -164,18 +196,22 @@ def cpu_oracle_time(cfg, weights_cpu, cons, users, budget_s, threads):
 
 
 def run_reference(args):
+    """The reference algorithm on the host cores: the CPU oracle port of HF beam
+    search + the reference's processor + folded SDPA, with weights made by the
+    numpy restatement of the synthetic filler (no library of this repository is
+    loaded on this arm)."""
     rank, _, world = dist_env()
     if rank != 0:
         return
     import torch
     from rapidtinyrec_b200 import workload as wk
-    threads = os.cpu_count() or 1
+    threads = physical_cores()
     wl, _, cons, users = build_workload(args.workload, args.warmup + args.steps)
     cfg = wl.model
-    weights = wk.synth_weights(cfg, seed=wl.weight_seed, device='cpu')
-    warm = cpu_oracle_time(cfg, weights, cons, users[:min(args.warmup, 3)], 0, threads)
+    weights = wk.synth_weights(cfg, seed=wl.weight_seed, device='cpu', backend='numpy', threads=threads)
+    warm = cpu_oracle_time(cfg, weights, cons, users[:min(args.warmup, 3)], 1e9, threads)
     # bound the run: every step is one full request; cap the count to ~150 s of CPU work
-    per = warm[0] if warm else 1.0
+    per = statistics.median(warm) if warm else 1.0
     k = max(1, min(args.steps, int(150.0 / max(per, 1e-3))))
     times = cpu_oracle_time(cfg, weights, cons, users[args.warmup:args.warmup + k], 1e9, threads)
     total = sum(times)
@@ -185,10 +221,12 @@ def run_reference(args):
             'median_ms': round(1000 * statistics.median(times), 2), 'p95_ms': round(1000 * percentile(times, 0.95), 2),
             'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
             'dtype': 'f32' if cfg.dtype == 'fp32' else 'bf16',
-            'data': 'synthetic', 'config': {'workload': args.workload, 'beams': 50, 'requested_steps': args.steps},
+            'data': 'synthetic', 'config': bench_config(args, wl, world),
             'cpu_baseline': {'value': round(value, 4), 'unit': 'users/s', 'cores': threads, 'kind': 'port',
-                             'sample': f'{len(times)} users of {args.workload}, full request each (CPU oracle port of '
-                                       f'HF beam search + GpuSidConstrainedLogitsProcessor + folded SDPA)'},
+                             'sample': f'{len(times)} users of {args.workload} (of {args.steps} requested), full '
+                                       f'request each (CPU oracle port of HF beam search + '
+                                       f'GpuSidConstrainedLogitsProcessor + folded SDPA), torch on {threads} '
+                                       f'threads = physical cores'},
             'e2e': {'value': round(value, 4), 'unit': 'users/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
     print(json.dumps(line), flush=True)
 
@@ -369,12 +407,12 @@ def run_ours(args):
 
     cpu = None
     if weights_cpu is not None:
-        threads = os.cpu_count() or 1
+        threads = physical_cores()
         times = cpu_oracle_time(cfg, weights_cpu, cons, users[args.warmup:], args.cpu_budget, threads)
         cpu = {'value': round(len(times) / sum(times), 5), 'unit': 'users/s', 'cores': threads, 'kind': 'port',
                'sample': f'{len(times)} users of {args.workload} (full request each) through the CPU oracle port '
-                         f'of HF beam search + GpuSidConstrainedLogitsProcessor + folded SDPA, '
-                         f'median {1000 * statistics.median(times):.0f} ms/user'}
+                         f'of HF beam search + GpuSidConstrainedLogitsProcessor + folded SDPA, torch on {threads} '
+                         f'threads = physical cores, median {1000 * statistics.median(times):.0f} ms/user'}
 
     if rank == 0:
         n_users = args.steps * world
@@ -394,11 +432,7 @@ def run_ours(args):
             'median_ms': round(statistics.median(per_user), 3), 'p95_ms': round(percentile(per_user, 0.95), 3),
             'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None,
             'dtype': 'f32' if cfg.dtype == 'fp32' else 'bf16', 'data': 'synthetic',
-            'config': {'workload': args.workload, 'model': cfg.name, 'beams': engine.beams, 'items': wl.items,
-                       'prompt_tokens': [wl.prompt_min, wl.prompt_max], 'users_per_rank': args.steps,
-                       'parallelism': f'replicas{world}', 'partition': 'users round-robin, no per-step collective',
-                       'l2': f'inputs larger than L2: the {gemm_bytes / 1e9:.1f} GB of weights stream from HBM '
-                             f'every forward'},
+            'config': bench_config(args, wl, world, engine.beams),
             'e2e': {'value': round(n_users / e2e_total, 3), 'unit': 'users/s',
                     'median_ms': round(1000 * statistics.median(e2e_lat), 3),
                     'p95_ms': round(1000 * percentile(e2e_lat, 0.95), 3),

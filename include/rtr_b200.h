@@ -219,6 +219,18 @@ int rtr_profile_gemms(rtr_session* s, int32_t M, int32_t reps, float* ms_per_pas
 int rtr_gemm_check(int32_t device, const float* x_dev, const float* w_dev, float* c_dev, int32_t M, int32_t N,
                    int32_t K, int32_t kernel);
 
+/* Test hook (no reference counterpart; the reference's failure handling is
+ * Python exceptions): on `device`, bound every pipeline wait of the
+ * fp16-pair and bf16 tensor-core GEMMs to wait_cycles (default 2e9, ~1 s) and,
+ * with withhold_activation_copies = 1, make their activation producers issue
+ * no copy.  Those waits then run out: each CTA stops issuing, drains what it
+ * issued, frees its tensor memory, keeps the split-K tickets whole and sets the
+ * timeout bit of the session's status word, so the request fails with
+ * RTR_ERR_DEVICE and the next request runs normally.  Applies to kernels
+ * launched (or graph nodes replayed) after the call; wait_cycles >= 1000.
+ * Blocks until the setting is on the device. */
+int rtr_debug_wait_control(int32_t device, int64_t wait_cycles, int32_t withhold_activation_copies);
+
 /* Processed scores of step t (0..4) as a dense [B, V] float32 device matrix:
  * the double-normalised log-probabilities at allowed columns and -inf
  * elsewhere, i.e. GenerateBeamOutput.scores[t] (the --save-full-scores
@@ -243,21 +255,24 @@ int rtr_constraint_process(rtr_session* s, int32_t step, const int64_t* input_id
 
 /* Allocation-free rtr_constraint_process.  No counterpart in the reference.
  * For callers that must not allocate device memory per call - a plugin whose
- * host framework owns the GPU allocator, or code that runs while a stream is
- * being captured into a graph, where cudaMalloc is not permitted.  It computes
- * the same scores with the same kernels, but keeps the per-row reduction
- * scratch in a fixed static device array of the library instead of session
- * memory, and it calls no cudaMalloc, cudaFree or allocating routine.
+ * host framework owns the GPU allocator and has reserved the memory, or a
+ * serving loop whose latency budget rules out the allocator's synchronisation.
+ * It computes the same scores with the same kernels, but keeps the per-row
+ * reduction scratch in a fixed static device array of the library instead of
+ * session memory, and it calls no cudaMalloc, cudaFree or allocating routine.
  * Limits and caveats:
  *   - rows <= 256 (the array's size: 256 rows x 16 slices x 2 floats = 32 KiB,
  *     held by every GPU that loads the library until the process exits);
  *     larger requests fail with RTR_ERR_ARG;
- *   - the first call on a device looks the array's device address up once;
- *     make that first call before any stream capture;
+ *   - the first call on a device looks the array's device address up once
+ *     (cudaGetSymbolAddress) and keeps it; make that first call before any
+ *     stream capture, and do not call cudaDeviceReset on that device
+ *     afterwards (the kept address would be stale);
  *   - all calls share the one array, so calls whose work overlaps on the GPU
  *     (other streams, other sessions on the same device) race on it; nothing
  *     needs clearing between calls, because each call writes every slot it
- *     reads before reading it. */
+ *     reads before reading it;
+ *   - blocks until the scores are written. */
 int rtr_constraint_process_static(rtr_session* s, int32_t step, const int64_t* input_ids_dev,
                                   int32_t rows, int32_t cols, const float* scores_dev, float* out_dev);
 

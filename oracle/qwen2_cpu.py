@@ -48,8 +48,18 @@ def rope_cos_sin(inv_freq, position_ids, dtype):
 
 
 def rope_table(head_dim, theta, n_positions):
-    """cos/sin ``[n_positions, head_dim // 2]`` float32 - the table the CUDA path uploads."""
-    cos, sin = rope_cos_sin(rope_inv_freq(head_dim, theta), torch.arange(n_positions)[None, :], torch.float32)
+    """cos/sin ``[n_positions, head_dim // 2]`` float32 - the table the CUDA path uploads.
+
+    Built from HF's per-call computation for blocks of positions small enough
+    that torch evaluates each on one thread (every element vectorised), which is
+    how HF evaluates a prompt of up to 256 positions.
+    """
+    inv = rope_inv_freq(head_dim, theta)
+    rows = max(1, 16384 // head_dim)
+    parts = [rope_cos_sin(inv, torch.arange(i, min(i + rows, n_positions))[None, :], torch.float32)
+             for i in range(0, n_positions, rows)]
+    cos = torch.cat([c for c, _ in parts], dim=1)
+    sin = torch.cat([s for _, s in parts], dim=1)
     return cos[0, :, :head_dim // 2].contiguous(), sin[0, :, :head_dim // 2].contiguous()
 
 

@@ -24,6 +24,7 @@ EXPORTS = (
     'rtr_synth_fill_host', 'rtr_synth_fill_device', 'rtr_launch', 'rtr_wait', 'rtr_get_report',
     'rtr_profile_gemms', 'rtr_constraint_process_static', 'rtr_gemm_check',
     'rtr_session_create_batched', 'rtr_launch_batch', 'rtr_wait_batch', 'rtr_generate_batch',
+    'rtr_debug_wait_control',
 )
 
 
@@ -111,6 +112,7 @@ def load():
         'rtr_wait_batch': (P, ctypes.POINTER(ResultC)),
         'rtr_generate_batch': (P, P, P, I32, ctypes.POINTER(ResultC)),
         'rtr_constraint_process_static': (P, I32, P, I32, I32, P, P),
+        'rtr_debug_wait_control': (I32, I64, I32),
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
@@ -158,3 +160,11 @@ def gemm(x, w, kernel=0):
     torch.cuda.synchronize(x.device)
     check(load().rtr_gemm_check(x.device.index or 0, x.data_ptr(), w.data_ptr(), c.data_ptr(), M, N, K, kernel))
     return c
+
+
+DEFAULT_WAIT_CYCLES = 2_000_000_000
+
+
+def wait_control(device, wait_cycles=DEFAULT_WAIT_CYCLES, withhold_activation_copies=False):
+    """Test control of the tensor-core GEMMs' bounded pipeline waits (``rtr_debug_wait_control``)."""
+    check(load().rtr_debug_wait_control(device, int(wait_cycles), int(bool(withhold_activation_copies))))

@@ -656,7 +656,9 @@ cudaError_t constraint_process(const DevTables& tb, int step, const int64_t* ids
 // loads the library, for the life of the process) instead of memory the
 // session allocated.  Host code must not pass `g_static_proc_scratch`
 // itself to a kernel - on the host that name is only a stand-in - so its
-// device address is looked up once per device with cudaGetSymbolAddress.
+// device address is looked up once per device with cudaGetSymbolAddress, on
+// the first call with that device current, and kept (a cudaDeviceReset of the
+// device afterwards would leave the kept address stale).
 static __device__ __align__(256) float g_static_proc_scratch[STATIC_PROC_MAX_ROWS * PROC_SPLITS * 2];
 
 static std::mutex g_static_proc_mutex;

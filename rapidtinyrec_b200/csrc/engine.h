@@ -85,6 +85,11 @@ cudaError_t pack_weight_tiles_f16x2(const float* src, int N, int K, void* dst, c
 bool make_tmap_f16(TensorMap* out, const void* base, long rows, long cols, long ld, int box_rows);
 bool make_tmap_packed_f16x2(TensorMap* out, const void* packed, int N, int K);
 cudaError_t gemm_f16x2_init();
+// Test control of the fp16-pair and bf16 GEMMs on the current device: the
+// bound of their pipeline waits (cycles) and a switch that makes their
+// activation producers issue no copy (so those waits run out).
+cudaError_t gemm_f16x2_wait_control(long long wait_cycles, int withhold_x);
+cudaError_t gemm_bf16_wait_control(long long wait_cycles, int withhold_x);
 cudaError_t gemm_f16x2(const TensorMap& tmW, const TensorMap& tmXh, const TensorMap& tmXl, float* C, float* C_big,
                        float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                        size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,

@@ -188,6 +188,10 @@ RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int row0, int row
   __syncthreads();
 }
 
+// Bound of the pipeline waits and the test switch that withholds the
+// activation copies (rtr_debug_wait_control); one copy per device.
+static __device__ WaitControl g_bf_wait = {kWaitCycles, 0, 0};
+
 __global__ void __launch_bounds__(BF_THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, BfParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -203,10 +207,12 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 1) + 1;
   __shared__ int go;                        // this cluster finishes the tile
+  __shared__ int issued[2];                 // stages issued by the W and X producers (abort path)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * BF_NTOK;
   const int n0 = blockIdx.y * BF_WROWS;
+  const long long lim = g_bf_wait.wait_cycles;
   const int nchunks = (p.K + BF_KC - 1) / BF_KC;
   const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
   const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
@@ -231,7 +237,8 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  int w_issued = 0, x_issued = 0, mma_groups = 0;
+  int w_issued = 0, x_issued = 0;
+  uint32_t last_bar = 0, last_par = 0;  // MMA thread: barrier and phase of its last commit
   float acc[BF_NTOK];  // live only in the promoter warps
 
   if (warp == 0) {
@@ -239,7 +246,7 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
       // weights do not depend on the previous kernel: no griddepcontrol.wait
       for (int q = 0; q < nstages; ++q) {
         const int s = q % BF_STAGES;
-        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / BF_STAGES) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / BF_STAGES) & 1) ^ 1, abort_flag, lim)) break;
         const int nc = nloc - q * BF_CPS < BF_CPS ? nloc - q * BF_CPS : BF_CPS;
         const uint32_t fb = smem_addr(&s_full[s]);
         mbar_expect_tx(fb, nc * BF_WC_BYTES);
@@ -261,7 +268,7 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
         for (int b = 0; b < 2; ++b) {
           const int j = 2 * jj + b;  // promotion group
           if (j * BF_GSTAGES >= nstages) break;
-          if (j >= 2 && !mbar_wait(smem_addr(&d_empty[b]), (jj - 1) & 1, abort_flag)) {
+          if (j >= 2 && !mbar_wait(smem_addr(&d_empty[b]), (jj - 1) & 1, abort_flag, lim)) {
             ok = false;
             break;
           }
@@ -270,7 +277,7 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
           for (int u = 0; u < BF_GSTAGES; ++u) {
             const int q = j * BF_GSTAGES + u, s = b * BF_GSTAGES + u;
             if (q >= nstages) break;
-            if (!mbar_wait(smem_addr(&s_full[s]), jj & 1, abort_flag)) {
+            if (!mbar_wait(smem_addr(&s_full[s]), jj & 1, abort_flag, lim)) {
               ok = false;
               break;
             }
@@ -285,20 +292,23 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
                 mma_f16_ss(d, ad + 2 * kk, bd + 2 * kk, idesc, (u | c | kk) ? 1u : 0u);
             }
             mma_commit(smem_addr(&s_empty[s]));
+            last_bar = smem_addr(&s_empty[s]);
+            last_par = jj & 1;
           }
           if (!ok) break;
           mma_commit(smem_addr(&d_full[b]));
-          mma_groups = j + 1;
+          last_bar = smem_addr(&d_full[b]);
+          last_par = jj & 1;
         }
       }
     }
     __syncwarp();
   } else if (warp == 2) {
     pdl_wait();
-    if (lane == 0) {
+    if (lane == 0 && !g_bf_wait.withhold_x) {
       for (int q = 0; q < nstages; ++q) {
         const int s = q % BF_STAGES;
-        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / BF_STAGES) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / BF_STAGES) & 1) ^ 1, abort_flag, lim)) break;
         const int nc = nloc - q * BF_CPS < BF_CPS ? nloc - q * BF_CPS : BF_CPS;
         const uint32_t fb = smem_addr(&s_full[s]);
         mbar_expect_tx(fb, nc * BF_XC_BYTES);
@@ -315,7 +325,7 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     for (int g = 0; g < ngroups; ++g) {
       const int b = g & 1;
-      if (!mbar_wait(smem_addr(&d_full[b]), (g >> 1) & 1, abort_flag)) break;
+      if (!mbar_wait(smem_addr(&d_full[b]), (g >> 1) & 1, abort_flag, lim)) break;
       tc_fence_after();
       const uint32_t d = tmem + lane_base + b * BF_D_COLS;
 #pragma unroll
@@ -332,20 +342,23 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
     }
   }
   pdl_launch_dependents();
+  if (warp == 0 && lane == 0) issued[0] = w_issued;
+  if (warp == 2 && lane == 0) issued[1] = x_issued;
+  __syncthreads();  // every role is done waiting: the abort flag is final
 
   // drain on abort: issued copies and MMAs must land before smem/TMEM go away
-  if (*abort_flag) {
-    if (threadIdx.x == 0) atomicOr(p.status, RTR_DEV_TIMEOUT);
-    // (a stage whose other producer gave up never completes: the drain then
-    // waits out its bound, which only delays the exit of an aborted CTA)
-    if (warp == 0 && lane == 0)
-      for (int q = 0; q < w_issued; ++q) mbar_drain(smem_addr(&s_full[q % BF_STAGES]), (q / BF_STAGES) & 1);
-    if (warp == 2 && lane == 0)
-      for (int q = 0; q < x_issued; ++q) mbar_drain(smem_addr(&s_full[q % BF_STAGES]), (q / BF_STAGES) & 1);
-    if (warp == 1 && lane == 0 && mma_groups > 0) {
-      const int g = mma_groups - 1;
-      mbar_drain(smem_addr(&d_full[g & 1]), (g >> 1) & 1);
+  const bool aborted = *abort_flag != 0;
+  if (aborted) {
+    if (threadIdx.x == 0) {
+      atomicOr(p.status, RTR_DEV_TIMEOUT);
+      // a stage's full barrier takes one arrival from each producer: stand in
+      // for the one that stopped earlier, then wait for the issued copies
+      const int wi = issued[0], xi = issued[1];
+      ring_stand_in(s_full, BF_STAGES, xi, wi);
+      ring_stand_in(s_full, BF_STAGES, wi, xi);
+      drain_ring(s_full, BF_STAGES, wi > xi ? wi : xi);
     }
+    if (warp == 1 && lane == 0 && last_bar) mbar_drain(last_bar, last_par);  // all MMAs issued
   }
   tc_fence_before();
   __syncthreads();
@@ -353,8 +366,14 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, BF_TMEM_COLS);
   }
-  if (*abort_flag) return;
-  pdl_wait();  // the epilogue reads and writes memory of earlier kernels
+  pdl_wait();  // the split-K workspace and the epilogue touch memory of earlier kernels
+  if (aborted) {
+    if (p.splits > 1) {
+      int r0, r1;
+      splitk_claim(p, smem_addr(red_bar), &go, 0, blockIdx.y * gridDim.x + blockIdx.x, r0, r1, true);
+    }
+    return;
+  }
 
   const bool have = warp >= 4;
   const int quarter = warp & 3;
@@ -437,6 +456,11 @@ bool make_tmap_packed_bf16(TensorMap* out, const void* packed, int N, int K) {
 }
 
 static int g_bf_clusters[kMaxDevices][TC_MAX_CLUSTER + 1];
+
+cudaError_t gemm_bf16_wait_control(long long wait_cycles, int withhold_x) {
+  const WaitControl c{wait_cycles, withhold_x, 0};
+  return cudaMemcpyToSymbol(g_bf_wait, &c, sizeof(c));
+}
 
 cudaError_t gemm_bf16_init() {
   cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BF_SMEM_BYTES);

@@ -123,3 +123,12 @@ extern "C" int rtr_gemm_check(int32_t device, const float* x_dev, const float* w
                               int32_t N, int32_t K, int32_t kernel) {
   return rtr::gemm_check_impl(device, x_dev, w_dev, c_dev, M, N, K, kernel);
 }
+
+extern "C" int rtr_debug_wait_control(int32_t device, int64_t wait_cycles, int32_t withhold_activation_copies) {
+  if (wait_cycles < 1000 || withhold_activation_copies < 0 || withhold_activation_copies > 1) return RTR_ERR_ARG;
+  if (cudaSetDevice(device) != cudaSuccess) return RTR_ERR_CUDA;
+  if (rtr::gemm_f16x2_wait_control(wait_cycles, withhold_activation_copies) != cudaSuccess ||
+      rtr::gemm_bf16_wait_control(wait_cycles, withhold_activation_copies) != cudaSuccess)
+    return RTR_ERR_CUDA;
+  return RTR_OK;
+}

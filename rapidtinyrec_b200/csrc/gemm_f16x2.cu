@@ -69,6 +69,10 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// Bound of the pipeline waits and the test switch that withholds the
+// activation copies (rtr_debug_wait_control); one copy per device.
+static __device__ WaitControl g_fx_wait = {kWaitCycles, 0, 0};
+
 template <int NTOK>
 __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
     gemm_f16x2_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmXh,
@@ -88,10 +92,12 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 1);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 1) + 1;
   __shared__ int go;                        // this cluster finishes the tile
+  __shared__ int issued[2];                 // copies issued by the W and X producers (abort path)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tok0 = blockIdx.x * NTOK;
   const int n0 = blockIdx.y * FX_WROWS;
+  const long long lim = g_fx_wait.wait_cycles;
   const int nchunks = (p.K + FX_KC - 1) / FX_KC;
   const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
   const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
@@ -116,7 +122,8 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  int w_issued = 0, x_issued = 0, mma_groups = 0;
+  int w_issued = 0, x_issued = 0;
+  uint32_t last_bar = 0, last_par = 0;  // MMA thread: barrier and phase of its last commit
   float acc[64];  // live only in the promoter warps
 
   if (warp == 0) {
@@ -125,7 +132,7 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
       // weights do not depend on the previous kernel: no griddepcontrol.wait
       for (int q = 0; q < nloc; ++q) {
         const int s = q % STAGES;
-        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / STAGES) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / STAGES) & 1) ^ 1, abort_flag, lim)) break;
         const uint32_t fb = smem_addr(&s_full[s]);
         mbar_expect_tx(fb, FX_W_BYTES);
         // packed block of (tile, chunk): 256 rows of 128 bytes, contiguous
@@ -143,14 +150,14 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
       bool ok = true;
       for (int j = 0; ok && j < ngroups; ++j) {  // one promotion group
         const int b = j & 1;
-        if (j >= 2 && !mbar_wait(smem_addr(&d_empty[b]), ((j >> 1) - 1) & 1, abort_flag)) break;
+        if (j >= 2 && !mbar_wait(smem_addr(&d_empty[b]), ((j >> 1) - 1) & 1, abort_flag, lim)) break;
         const uint32_t d = tmem + b * Cfg::D_COLS;
 #pragma unroll
         for (int u = 0; u < FX_PROMOTE; ++u) {
           const int q = j * FX_PROMOTE + u;
           if (q < nloc) {
             const int s = q % STAGES;
-            if (!mbar_wait(smem_addr(&s_full[s]), (q / STAGES) & 1, abort_flag)) {
+            if (!mbar_wait(smem_addr(&s_full[s]), (q / STAGES) & 1, abort_flag, lim)) {
               ok = false;
             } else {
               tc_fence_after();
@@ -163,23 +170,26 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
                 mma_f16_ss(d + NTOK, al + 2 * kk, bx + 2 * kk, id_x, 1u);
               }
               mma_commit(smem_addr(&s_empty[s]));
+              last_bar = smem_addr(&s_empty[s]);
+              last_par = (q / STAGES) & 1;
             }
           }
           if (!ok) break;
         }
         if (!ok) break;
         mma_commit(smem_addr(&d_full[b]));
-        mma_groups = j + 1;
+        last_bar = smem_addr(&d_full[b]);
+        last_par = (j >> 1) & 1;
       }
     }
     __syncwarp();
   } else if (warp == 2) {
     // ------------------------------------------- activation producer (TMA)
     pdl_wait();
-    if (lane == 0) {
+    if (lane == 0 && !g_fx_wait.withhold_x) {
       for (int q = 0; q < nloc; ++q) {
         const int s = q % STAGES;
-        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / STAGES) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / STAGES) & 1) ^ 1, abort_flag, lim)) break;
         const uint32_t fb = smem_addr(&s_full[s]);
         uint8_t* st = xring + s * Cfg::X_BYTES;
         mbar_expect_tx(fb, Cfg::X_BYTES);
@@ -203,7 +213,7 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     for (int g = 0; g < ngroups; ++g) {
       const int b = g & 1;
-      if (!mbar_wait(smem_addr(&d_full[b]), (g >> 1) & 1, abort_flag)) break;
+      if (!mbar_wait(smem_addr(&d_full[b]), (g >> 1) & 1, abort_flag, lim)) break;
       tc_fence_after();
       const uint32_t d = tmem + lane_base + b * Cfg::D_COLS + half * 64;
 #pragma unroll
@@ -225,20 +235,23 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
     }
   }
   pdl_launch_dependents();
+  if (warp == 0 && lane == 0) issued[0] = w_issued;
+  if (warp == 2 && lane == 0) issued[1] = x_issued;
+  __syncthreads();  // every role is done waiting: the abort flag is final
 
   // drain on abort: issued copies and MMAs must land before smem/TMEM go away
-  if (*abort_flag) {
-    if (threadIdx.x == 0) atomicOr(p.status, RTR_DEV_TIMEOUT);
-    // (a stage whose other producer gave up never completes: the drain then
-    // waits out its bound, which only delays the exit of an aborted CTA)
-    if (warp == 0 && lane == 0)
-      for (int q = 0; q < w_issued; ++q) mbar_drain(smem_addr(&s_full[q % STAGES]), (q / STAGES) & 1);
-    if (warp == 2 && lane == 0)
-      for (int q = 0; q < x_issued; ++q) mbar_drain(smem_addr(&s_full[q % STAGES]), (q / STAGES) & 1);
-    if (warp == 1 && lane == 0 && mma_groups > 0) {
-      const int g = mma_groups - 1;
-      mbar_drain(smem_addr(&d_full[g & 1]), (g >> 1) & 1);
+  const bool aborted = *abort_flag != 0;
+  if (aborted) {
+    if (threadIdx.x == 0) {
+      atomicOr(p.status, RTR_DEV_TIMEOUT);
+      // a stage's full barrier takes one arrival from each producer: stand in
+      // for the one that stopped earlier, then wait for the issued copies
+      const int wi = issued[0], xi = issued[1];
+      ring_stand_in(s_full, STAGES, xi, wi);
+      ring_stand_in(s_full, STAGES, wi, xi);
+      drain_ring(s_full, STAGES, wi > xi ? wi : xi);
     }
+    if (warp == 1 && lane == 0 && last_bar) mbar_drain(last_bar, last_par);  // all MMAs issued
   }
   tc_fence_before();
   __syncthreads();
@@ -246,8 +259,15 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
-  if (*abort_flag) return;
   pdl_wait();  // the split-K workspace and the epilogue touch memory of earlier kernels
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  if (aborted) {
+    if (p.splits > 1) {
+      int r0, r1;
+      splitk_claim(p, smem_addr(red_bar), &go, 0, tile, r0, r1, true);
+    }
+    return;
+  }
 
   const bool have = warp >= 4;
   const int quarter = warp & 3, half = (warp - 4) >> 2;
@@ -257,7 +277,6 @@ __global__ void __launch_bounds__(FxCfg<NTOK>::THREADS, 1)
   float4* red4 = reinterpret_cast<float4*>(smem);  // the rings are free now
   if (p.splits > 1) {
     // Partial tiles are tile-contiguous: ws[(split * tiles + tile)][row][128].
-    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
     const long tstride = (long)gridDim.x * gridDim.y * (NTOK * FX_WROWS);
     if (have && n < p.N) {
       float* w = p.ws + blockIdx.z * tstride + (long)tile * (NTOK * FX_WROWS) + (half * 64) * FX_WROWS +
@@ -338,6 +357,11 @@ bool make_tmap_f16(TensorMap* out, const void* base, long rows, long cols, long 
 bool make_tmap_packed_f16x2(TensorMap* out, const void* packed, int N, int K) {
   const long rows = (long)packed_weight_elems_f16x2(N, K) / FX_KC;
   return make_tmap_f16(out, packed, rows, FX_KC, FX_KC, 2 * FX_WROWS);
+}
+
+cudaError_t gemm_f16x2_wait_control(long long wait_cycles, int withhold_x) {
+  const WaitControl c{wait_cycles, withhold_x, 0};
+  return cudaMemcpyToSymbol(g_fx_wait, &c, sizeof(c));
 }
 
 cudaError_t gemm_f16x2_init() {

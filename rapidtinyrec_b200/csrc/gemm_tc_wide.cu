@@ -110,7 +110,8 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
   const uint32_t tmem = *tmem_slot;
   const uint32_t tmem_a = tmem + TW_D_COLS;
 
-  int w_issued = 0, x_issued = 0, mma_groups = 0;
+  int w_issued = 0, x_issued = 0;
+  uint32_t last_bar = 0, last_par = 0;  // MMA thread: barrier and phase of its last commit
   float acc[64];  // live only in the promoter warps
 
   if (warp == 0) {
@@ -158,10 +159,13 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
             }
           }
           mma_commit(smem_addr(&s_empty[s]));
+          last_bar = smem_addr(&s_empty[s]);
+          last_par = (u / TW_STAGES) & 1;
         }
         if (!ok) break;
         mma_commit(smem_addr(d_full));
-        mma_groups = j + 1;
+        last_bar = smem_addr(d_full);
+        last_par = j & 1;
       }
     }
     __syncwarp();
@@ -254,15 +258,15 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
     }
   }
   pdl_launch_dependents();
+  __syncthreads();  // every role is done waiting: the abort flag is final
 
   // drain on abort: issued copies and MMAs must land before smem/TMEM go away
-  if (*abort_flag) {
+  const bool aborted = *abort_flag != 0;
+  if (aborted) {
     if (threadIdx.x == 0) atomicOr(p.status, RTR_DEV_TIMEOUT);
-    if (warp == 0 && lane == 0)
-      for (int i = 0; i < w_issued; ++i) mbar_drain(smem_addr(&w_full[i % TW_WSTAGES]), (i / TW_WSTAGES) & 1);
-    if (warp == 14 && lane == 0)
-      for (int q = 0; q < x_issued; ++q) mbar_drain(smem_addr(&x_full[q % TW_STAGES]), (q / TW_STAGES) & 1);
-    if (warp == 1 && lane == 0 && mma_groups > 0) mbar_drain(smem_addr(d_full), (mma_groups - 1) & 1);
+    if (warp == 0 && lane == 0) drain_ring(w_full, TW_WSTAGES, w_issued);
+    if (warp == 14 && lane == 0) drain_ring(x_full, TW_STAGES, x_issued);
+    if (warp == 1 && lane == 0 && last_bar) mbar_drain(last_bar, last_par);  // all MMAs issued
   }
   tc_fence_before();
   __syncthreads();
@@ -270,7 +274,14 @@ __global__ void __launch_bounds__(TW_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, TW_TMEM_COLS);
   }
-  if (*abort_flag) return;
+  if (aborted) {
+    if (p.splits > 1) {
+      pdl_wait();  // the tickets are shared with earlier kernels
+      int r0, r1;
+      splitk_claim(p, smem_addr(red_bar), &go, 0, blockIdx.y * gridDim.x + blockIdx.x, r0, r1, true);
+    }
+    return;
+  }
 
   const bool have = warp >= 6 && warp <= 13;
   const int quarter = warp & 3, half = (warp - 6) >> 2;

@@ -885,8 +885,13 @@ static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t 
 static int check_result(rtr_session* s, const rtr_result* out, int u = 0) {
   const DevResult& r = s->hres[u];
   const uint32_t st = r.status;
-  if (st & (RTR_DEV_BAD_TOKEN | RTR_DEV_BAD_PARENT | RTR_DEV_BAD_LENGTH | RTR_DEV_TOO_MANY_CAND | RTR_DEV_NAN_SCORE |
-            RTR_DEV_TIMEOUT))
+  if (st & RTR_DEV_TIMEOUT) {
+    // the aborted GEMMs keep their split-K tickets whole; re-arm them anyway so
+    // no count left by an interrupted launch can reach the next request
+    CUDA_TRY(s, cudaMemsetAsync(s->tickets, 0, kTickets * sizeof(int), s->stream));
+    return fail(s, RTR_ERR_DEVICE, "a bounded pipeline wait ran out (status 0x" + std::to_string(st) + ")");
+  }
+  if (st & (RTR_DEV_BAD_TOKEN | RTR_DEV_BAD_PARENT | RTR_DEV_BAD_LENGTH | RTR_DEV_TOO_MANY_CAND | RTR_DEV_NAN_SCORE))
     return fail(s, RTR_ERR_DEVICE, "device bound check failed (status 0x" + std::to_string(st) + ")");
   if (st & RTR_DEV_NOT_STOPPED)
     return fail(s, RTR_ERR_DEVICE, "beam search would continue after 5 steps (catalog grammar is not 3 SID tokens + newline + EOS)");

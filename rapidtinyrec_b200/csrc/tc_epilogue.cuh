@@ -270,8 +270,15 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
 // would get) and running the epilogue on that slice.  Returns whether this
 // CTA finishes rows [r0, r1).  `red_bar` (count = cluster size) and `*go` (0)
 // were set before the start-up cluster barrier.
+//
+// A CTA that aborted (a pipeline wait ran out; the status word says so) still
+// takes its ticket and arrives on every peer with `skip` set: the ticket count
+// stays whole for the next launch, and the CTA stays resident until every
+// peer's remote store and arrive on it has happened.  It never finishes rows,
+// and when it holds the last ticket no CTA of its cluster does.
 template <class P>
-RTR_DEVICE bool splitk_claim(const P& p, uint32_t red_bar, int* go, int rows, int tile, int& r0, int& r1) {
+RTR_DEVICE bool splitk_claim(const P& p, uint32_t red_bar, int* go, int rows, int tile, int& r0, int& r1,
+                             bool skip = false) {
   const uint32_t cs = cluster_ncta();
   if (threadIdx.x == 0) {
     int* tk = p.tickets + tile;
@@ -280,12 +287,13 @@ RTR_DEVICE bool splitk_claim(const P& p, uint32_t red_bar, int* go, int rows, in
       *tk = 0;  // re-arm for the next launch / graph replay
       __threadfence();
     }
+    const bool fin = last && !skip;
     if (cs == 1) {
-      *go = last;
+      *go = fin;
     } else {
       const uint32_t goa = smem_addr(go);
       for (uint32_t r = 0; r < cs; ++r) {
-        if (last) st_cluster_u32(cluster_map(goa, r), 1u);
+        if (fin) st_cluster_u32(cluster_map(goa, r), 1u);
         mbar_arrive_remote(cluster_map(red_bar, r));
       }
       // every CTA of the cluster has arrived: no remote access to this CTA follows
@@ -296,7 +304,7 @@ RTR_DEVICE bool splitk_claim(const P& p, uint32_t red_bar, int* go, int rows, in
     }
   }
   __syncthreads();
-  if (!*reinterpret_cast<volatile int*>(go)) return false;
+  if (skip || !*reinterpret_cast<volatile int*>(go)) return false;
   __threadfence();
   const int r = (int)cluster_rank();
   r0 = r * rows / (int)cs;

@@ -36,16 +36,27 @@ RTR_DEVICE bool mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: false when the CTA aborted or ~1 s passed (then abort is set).
-RTR_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+// Bounded wait: false when the CTA aborted or `limit` cycles passed (then
+// abort is set).
+RTR_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, long long limit = kWaitCycles) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try(bar, parity)) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) { *abort_flag = 1; return false; }
+    if (clock64() - t0 > limit) { *abort_flag = 1; return false; }
   }
   return true;
 }
+
+// Pipeline-wait control of the default tensor-core GEMMs (fp16 pairs, bf16),
+// one copy per device: `wait_cycles` bounds every pipeline wait and
+// `withhold_x` makes the activation producer issue no copy, so a test can make
+// a bounded wait run out without any fault.  Defaults: kWaitCycles, 0.
+struct WaitControl {
+  long long wait_cycles;
+  int withhold_x;
+  int pad;
+};
 // ------------------------------------------------- thread-block clusters
 RTR_DEVICE uint32_t cluster_ncta() {
   uint32_t n;
@@ -96,6 +107,24 @@ RTR_DEVICE bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
 RTR_DEVICE void mbar_drain(uint32_t bar, uint32_t parity) {
   const long long t0 = clock64();
   while (!mbar_try(bar, parity) && clock64() - t0 < kWaitCycles) {}
+}
+
+// After an abort, one thread: wait until the copies issued into a ring of
+// `stages` full barriers have landed.  Only the last `stages` loads can be in
+// flight (a slot is reissued after its previous phase completed), and only
+// their phases are still open: an older phase's parity names a later one.
+RTR_DEVICE void drain_ring(const uint64_t* full, int stages, int issued) {
+  for (int q = issued > stages ? issued - stages : 0; q < issued; ++q)
+    mbar_drain(smem_addr(&full[q % stages]), (q / stages) & 1);
+}
+
+// After an abort, one thread of a ring whose full barrier takes one arrival
+// from each of two producers: arrive for the stages that only the other
+// producer issued (q in [mine, theirs)), so those phases complete once the
+// issued copies land.  Before the abort both producers issued every q below
+// min(mine, theirs) + stages in order, so each such stage is open at q.
+RTR_DEVICE void ring_stand_in(const uint64_t* full, int stages, int mine, int theirs) {
+  for (int q = mine; q < theirs; ++q) mbar_arrive(smem_addr(&full[q % stages]));
 }
 
 RTR_DEVICE void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {

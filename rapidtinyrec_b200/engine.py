@@ -32,8 +32,14 @@ def rope_table(head_dim: int, theta: float, n_positions: int, dtype=None):
     pos = torch.arange(n_positions)[None, None, :].float()
     freqs = (inv[None, :, None].float() @ pos).transpose(1, 2)
     emb = torch.cat((freqs, freqs), dim=-1)
-    return (emb.cos()[0, :, :head_dim // 2].contiguous().numpy(),
-            emb.sin()[0, :, :head_dim // 2].contiguous().numpy())
+    # cos/sin in blocks below torch's parallel grain (32,768 elements) so every
+    # element takes the vectorised path, as a single-threaded HF call does; a
+    # thread split of the whole table could leave scalar tails with other bits.
+    rows = max(1, 16384 // head_dim)
+    cos = torch.cat([emb[:, i:i + rows].cos() for i in range(0, n_positions, rows)], dim=1)
+    sin = torch.cat([emb[:, i:i + rows].sin() for i in range(0, n_positions, rows)], dim=1)
+    return (cos[0, :, :head_dim // 2].contiguous().numpy(),
+            sin[0, :, :head_dim // 2].contiguous().numpy())
 
 
 def weight_order(cfg: ModelConfig):

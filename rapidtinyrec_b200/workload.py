@@ -83,25 +83,40 @@ def synth_values_numpy(seed: int, tid: int, n: int, scale: float, offset: float,
     return k * step + np.float32(offset)
 
 
-def synth_weights(cfg: ModelConfig, seed: int = 0, device: str = 'cpu', backend: str = 'native'):
+def _numpy_fill(dst: np.ndarray, seed: int, tid: int, scale: float, offset: float, pool, chunk: int = 1 << 22):
+    """:func:`synth_values_numpy` over ``dst`` (flat float32) in chunks on a thread pool
+    (numpy's ufuncs release the GIL on large arrays)."""
+    def one(start):
+        n = min(chunk, dst.size - start)
+        dst[start:start + n] = synth_values_numpy(seed, tid, n, scale, offset, start=start)
+    list(pool.map(one, range(0, dst.size, chunk)))
+
+
+def synth_weights(cfg: ModelConfig, seed: int = 0, device: str = 'cpu', backend: str = 'native',
+                  threads: int = 1):
     """All weights as float32 torch tensors (HF names).
 
     ``backend='native'``: on ``device='cuda'`` the CUDA filler writes straight
     into HBM, on the host the multi-threaded native filler runs.
-    ``backend='numpy'``: :func:`synth_values_numpy` (slow; small models only).
-    All three are bit-identical.
+    ``backend='numpy'``: :func:`synth_values_numpy` in chunks on ``threads``
+    host threads (no native library involved).  All three are bit-identical.
     """
+    import concurrent.futures
     import torch
     out = {}
+    pool = concurrent.futures.ThreadPoolExecutor(max_workers=max(1, threads)) if backend == 'numpy' else None
     for tid, (name, shape, scale, offset) in enumerate(tensor_specs(cfg)):
         if backend == 'numpy':
-            n = int(np.prod(shape))
-            t = torch.from_numpy(synth_values_numpy(seed, tid, n, scale, offset).reshape(shape)).to(device)
+            flat = np.empty(int(np.prod(shape)), dtype=np.float32)
+            _numpy_fill(flat, seed, tid, scale, offset, pool)
+            t = torch.from_numpy(flat.reshape(shape)).to(device)
         else:
             from . import _native
             t = torch.empty(shape, dtype=torch.float32, device=device)
             _native.synth_fill(t, seed, tid, scale, offset)
         out[name] = t
+    if pool is not None:
+        pool.shutdown()
     if cfg.tied:
         out['lm_head.weight'] = out['model.embed_tokens.weight']
     return out

@@ -1,9 +1,12 @@
 """Generate golden vectors by running the reference implementation itself.
 
-Run in a container where the reference checkout is present (it is read, never
-modified), e.g.::
+Run where a checkout of the reference is present (it is read, never modified);
+its location comes from ``--reference`` or the ``RTR_REFERENCE`` environment
+variable::
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <checkout>
+    python tests/golden/make_golden.py --reference <checkout> --cohort qwen1.5b-fp32 \
+        --shard 0/2 --parts <dir>        # one of two processes; then --merge
 
 It imports ``rapidtinyrec`` from that checkout and records, for the CPU:
 
@@ -23,6 +26,15 @@ Models: the two CPU models of the reference's own tests
 (``tests/test_decoding.py:37-41`` seed 42 with the ``catalog()`` grammar;
 ``tests/test_inference_precision.py:174-185`` seed 50111 with the 4x4x4
 grammar, FP32 and BF16) and the tiny synthetic workload (all 8 users).
+
+``--cohort WORKLOAD`` runs the same reference ``generate`` on the full-size
+synthetic workloads (the 1.5B-shaped FP32 and BF16 cohorts, the 7B-shaped BF16
+model) and writes ``cohort_<workload>.npz``: per user the ranked token ids,
+beam indices, sequence and transition log-probabilities, plus fingerprints of
+the weights and prompts the records were made from.  BF16 follows the
+reference's ``bf16-experimental`` opt-in on the CPU: the whole model cast to
+bfloat16, HF's FP32 normalisation and beam scores.  The work splits into
+``--shard i/n`` processes whose part files ``--merge`` joins.
 """
 from __future__ import annotations
 
@@ -213,19 +225,163 @@ def torch_init_weights(cfg, seed):
     return {k: v.detach().clone() for k, v in model.state_dict().items()}
 
 
-def main():
-    ap = argparse.ArgumentParser(description=__doc__)
-    ap.add_argument('--reference', type=Path, default=Path('/root/reference'))
-    args = ap.parse_args()
-    sys.path.insert(0, str(args.reference))
+def prompts_fingerprint(prompts):
+    h = hashlib.sha256()
+    for p in prompts:
+        h.update(np.asarray(p, dtype=np.int32).tobytes())
+        h.update(b'|')
+    return h.hexdigest()
+
+
+def cohort_model(cfg, seed):
+    """The workload's synthetic weights in a ``Qwen2ForCausalLM`` of the run's dtype.
+
+    BF16 models are built tensor by tensor (fp32 values rounded to bfloat16, as
+    ``model.to(torch.bfloat16)`` rounds them) so the 7B model never holds an
+    fp32 copy of every weight at once.
+    """
+    from transformers import Qwen2Config, Qwen2ForCausalLM
+    from rapidtinyrec_b200 import _native
+    dtype = torch.bfloat16 if cfg.dtype == 'bf16' else torch.float32
+    hf_cfg = Qwen2Config(vocab_size=cfg.vocab, hidden_size=cfg.hidden, intermediate_size=cfg.intermediate,
+                         num_hidden_layers=cfg.layers, num_attention_heads=cfg.heads,
+                         num_key_value_heads=cfg.kv_heads, rope_theta=cfg.rope_theta, rms_norm_eps=cfg.rms_eps,
+                         tie_word_embeddings=cfg.tied, max_position_embeddings=4096,
+                         bos_token_id=1, eos_token_id=cfg.eos, pad_token_id=cfg.eos)
+    old = torch.get_default_dtype()
+    torch.set_default_dtype(dtype)
+    try:
+        model = Qwen2ForCausalLM(hf_cfg)
+    finally:
+        torch.set_default_dtype(old)
+    params = dict(model.named_parameters())
+    full, probe = hashlib.sha256(), hashlib.sha256()
+    with torch.no_grad():
+        for tid, (name, shape, scale, offset) in enumerate(workload.tensor_specs(cfg)):
+            t = torch.empty(shape, dtype=torch.float32)
+            _native.synth_fill(t, seed, tid, scale, offset)
+            a = t.reshape(-1).numpy()
+            full.update(name.encode())
+            full.update(a.tobytes())
+            probe.update(name.encode())
+            probe.update(a[:4096].tobytes())
+            params[name].copy_(t.to(dtype))
+            del t
+        if cfg.tied:
+            assert model.lm_head.weight.data_ptr() == model.model.embed_tokens.weight.data_ptr()
+    model = model.to(dtype).eval()
+    model.config._attn_implementation = 'sdpa'
+    return model, full.hexdigest(), probe.hexdigest()
+
+
+COHORT_FIELDS = ('token_ids', 'beam_indices', 'sequence_logp', 'transition_logp')
+
+
+def run_cohort_part(name, users_sel, parts, ref):
+    """Reference ``generate`` for the selected cohort indices; one part file per user."""
+    import time
+    wl = configs.workload(name)
+    cfg = wl.model
+    items = workload.catalog_items(wl)
+    cons = workload.constraint_dict(cfg, items)
+    prompts = [u.prompt_token_ids for u in workload.users(wl, items, count=max(users_sel) + 1)]
+    tables = ref.GpuSidConstraintTables(cons, cfg.root, cfg.newline, cfg.eos, 'cpu')
+    parts.mkdir(parents=True, exist_ok=True)
+    todo = [u for u in users_sel if not (parts / f'{name}_{u:05d}.json').exists()]
+    if not todo:
+        return
+    t0 = time.perf_counter()
+    model, full, probe = cohort_model(cfg, wl.weight_seed)
+    (parts / f'{name}_weights.json').write_text(json.dumps({'weights_sha256': full, 'weights_probe_sha256': probe}))
+    print(f'{name}: model ready in {time.perf_counter() - t0:.0f} s, {len(todo)} users to run', flush=True)
+    for u in todo:
+        t = time.perf_counter()
+        record, _ = run_reference_generate(model, cfg, tables, prompts[u], ref)
+        record = {k: record[k] for k in ('prompt_tokens', 'score_dtypes', *COHORT_FIELDS)}
+        record['cohort_index'] = u
+        record['elapsed_s'] = time.perf_counter() - t
+        tmp = parts / f'{name}_{u:05d}.json.tmp'
+        tmp.write_text(json.dumps(record))
+        tmp.replace(parts / f'{name}_{u:05d}.json')
+        print(f'{name} user {u} L={record["prompt_tokens"]} {record["elapsed_s"]:.1f} s', flush=True)
+
+
+def merge_cohort(name, indices, parts):
+    """Join the part files of the cohort users ``indices`` into ``cohort_<name>.npz``."""
+    wl = configs.workload(name)
+    items = workload.catalog_items(wl)
+    everyone = workload.users(wl, items, count=max(indices) + 1)
+    prompts = [everyone[u].prompt_token_ids for u in indices]
+    recs = [json.loads((parts / f'{name}_{u:05d}.json').read_text()) for u in indices]
+    fps = json.loads((parts / f'{name}_weights.json').read_text())
+    assert all(r['cohort_index'] == u and r['prompt_tokens'] == len(p) for u, r, p in zip(indices, recs, prompts))
+    assert all(r['score_dtypes'] == ['torch.float32'] * 5 for r in recs)
+    arrays = {
+        'cohort_index': np.array(indices, dtype=np.int32),
+        'prompt_tokens': np.array([r['prompt_tokens'] for r in recs], dtype=np.int32),
+        'token_ids': np.array([r['token_ids'] for r in recs], dtype=np.int32),
+        'beam_indices': np.array([r['beam_indices'] for r in recs], dtype=np.int16),
+        'sequence_logp': np.array([r['sequence_logp'] for r in recs], dtype=np.float32),
+        'transition_logp': np.array([r['transition_logp'] for r in recs], dtype=np.float32),
+        'elapsed_s': np.array([r['elapsed_s'] for r in recs], dtype=np.float32),
+    }
+    meta = {'workload': name, 'users': len(indices), 'dtype': wl.model.dtype,
+            'weights': f'synthetic seed {wl.weight_seed}', **fps,
+            'prompts_sha256': prompts_fingerprint(prompts),
+            'driver': 'HF generate (beam 50, max_new_tokens=8, length_penalty=0) under the reference\'s '
+                      'PrefillOnce + GpuSidConstrainedLogitsProcessor + fold_decode_attention(True), CPU',
+            'versions': {'torch': torch.__version__, 'transformers': __import__('transformers').__version__},
+            'threads': torch.get_num_threads()}
+    arrays['meta'] = np.array(json.dumps(meta))
+    np.savez_compressed(HERE / f'cohort_{name}.npz', **arrays)
+    print('wrote', HERE / f'cohort_{name}.npz', flush=True)
+
+
+def load_reference(path):
+    sys.path.insert(0, str(path))
     from rapidtinyrec import gpu_constraints, shared_prefill, folded_attention
-    ref = argparse.Namespace(GpuSidConstraintTables=gpu_constraints.GpuSidConstraintTables,
-                             GpuSidConstrainedLogitsProcessor=gpu_constraints.GpuSidConstrainedLogitsProcessor,
-                             PrefillOnce=shared_prefill.PrefillOnce,
-                             fold_decode_attention=folded_attention.fold_decode_attention)
-    torch.set_num_threads(4)
+    return argparse.Namespace(GpuSidConstraintTables=gpu_constraints.GpuSidConstraintTables,
+                              GpuSidConstrainedLogitsProcessor=gpu_constraints.GpuSidConstrainedLogitsProcessor,
+                              PrefillOnce=shared_prefill.PrefillOnce,
+                              fold_decode_attention=folded_attention.fold_decode_attention)
+
+
+def main():
+    import os
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--reference', type=Path, default=os.environ.get('RTR_REFERENCE'),
+                    help='checkout of the reference (default: $RTR_REFERENCE)')
+    ap.add_argument('--cohort', default=None, help='full-size workload to record (e.g. qwen1.5b-fp32)')
+    ap.add_argument('--users', type=int, default=None, help='cohort users 0..N-1 (default: the whole cohort)')
+    ap.add_argument('--indices', default=None, help='comma-separated cohort users instead of --users')
+    ap.add_argument('--shard', default='0/1', help='i/n: this process runs users u with u %% n == i')
+    ap.add_argument('--parts', type=Path, default=None, help='folder for per-user part files')
+    ap.add_argument('--merge', action='store_true', help='join the part files into cohort_<workload>.npz')
+    ap.add_argument('--threads', type=int, default=4)
+    args = ap.parse_args()
+    torch.set_num_threads(args.threads)
     warnings.simplefilter('ignore')
 
+    if args.cohort:
+        if args.indices:
+            indices = [int(x) for x in args.indices.split(',')]
+        else:
+            indices = list(range(args.users or configs.workload(args.cohort).users))
+        if args.parts is None:
+            ap.error('--cohort needs --parts')
+        if args.merge:
+            merge_cohort(args.cohort, indices, args.parts)
+            return
+        if args.reference is None:
+            ap.error('give --reference or set RTR_REFERENCE')
+        i, n = (int(x) for x in args.shard.split('/'))
+        run_cohort_part(args.cohort, [u for k, u in enumerate(indices) if k % n == i], args.parts,
+                        load_reference(args.reference))
+        return
+
+    if args.reference is None:
+        ap.error('give --reference or set RTR_REFERENCE')
+    ref = load_reference(args.reference)
     wl = configs.workload('tiny')
     items = workload.catalog_items(wl)
     tiny_constraints = workload.constraint_dict(wl.model, items)

@@ -1,9 +1,9 @@
 """The allocation-free processor entry point, through the C ABI.
 
 rtr_constraint_process_static serves callers that may not allocate device
-memory per call (a plugin under a host framework's allocator, or work issued
-while a stream is captured into a graph): it keeps its reduction scratch in a
-static device array of the library.  Its scores must match
+memory per call (a plugin under a host framework's allocator that has reserved
+the GPU's memory): it keeps its reduction scratch in a static device array of
+the library.  Its scores must match
 rtr_constraint_process - the entry point that uses session-allocated scratch -
 within the processor tolerance, call after call, since every call reuses the
 same array.  The file sorts last so a failure here comes after every other
@@ -64,6 +64,28 @@ def test_static_scratch_processor_matches_session_scratch(tiny):
         assert int(finite_g.sum()) > 0
         assert float((got[finite_g] - want[finite_w]).abs().max()) <= PROCESSOR_TOL, call
         assert torch.equal(got[~finite_g], want[~finite_w])  # -inf outside the allowed columns
+
+
+def test_static_scratch_processor_allocates_nothing(tiny):
+    """Free device memory is the same before and after repeated calls."""
+    if not torch.cuda.is_available():
+        pytest.fail('CUDA device required')
+    from rapidtinyrec_b200 import _native
+    lib = _native.load()
+    eng = _engine(tiny)
+    dev = torch.device('cuda:0')
+    z = np.load(GOLDEN / 'processor_tiny.npz')
+    scores = torch.randn((50, eng.cfg.vocab), generator=torch.Generator().manual_seed(3)).to(dev)
+    ids = torch.from_numpy(z['input_0'].astype(np.int64)).to(dev)
+    out = torch.empty_like(scores)
+    assert _call(lib, eng, 'rtr_constraint_process_static', 0, ids, scores, out) == _native.RTR_OK  # set-up call
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(dev)
+    for _ in range(5):
+        assert _call(lib, eng, 'rtr_constraint_process_static', 0, ids, scores, out) == _native.RTR_OK
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(dev)
+    assert free1 == free0, (free0, free1)
 
 
 def test_static_scratch_processor_rejects_rows_beyond_its_array(tiny):
