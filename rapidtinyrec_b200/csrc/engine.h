@@ -162,6 +162,20 @@ cudaError_t attention_decode(const void* q, const void* k_prefix, const void* v_
                              int head_dim, float scale, uint32_t* status, bool bf16, cudaStream_t stream,
                              const DecodeUsers& du = DecodeUsers{}, int xfmt = 0);
 cudaError_t attention_init();
+// Folded decode attention (attn_decode.cu): the rows of KV group g are its
+// (beam, head) pairs; a cluster of 8 CTAs splits the prefix keys, staged by
+// TMA through `arena`, a 2-D map over the prefix arena with rows of head_dim
+// elements, boxes of 32 rows x 128 bytes, 128-byte swizzle.  krow0 / vrow0:
+// the arena rows of the layer's K / V of group 0 of user 0; user_rows: arena
+// rows per user.  Same arguments and results as attention_decode otherwise.
+cudaError_t attention_decode_folded(const TensorMap& arena, long krow0, long vrow0, long user_rows, const void* q,
+                                    const void* k_suffix, const void* v_suffix, const int32_t* anc,
+                                    const int32_t* L_dev, int t, void* out, float* out_big, float* out_small,
+                                    int beams, int prefix_cap, int heads, int kv_heads, int head_dim, float scale,
+                                    uint32_t* status, bool bf16, cudaStream_t stream, const DecodeUsers& du,
+                                    int xfmt);
+cudaError_t attention_folded_init();
+bool attention_folded_supported(int heads, int kv_heads, int head_dim, bool bf16);
 
 // ---- constraints + beam step (beam.cu) ----
 struct DevTables {

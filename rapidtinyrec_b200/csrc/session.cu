@@ -82,6 +82,8 @@ struct rtr_session {
   uint8_t* tvalid = nullptr;
   // KV and activations
   float *kv_prefix = nullptr, *kv_suffix = nullptr;
+  TensorMap arena_map{};     // TMA map over the prefix arena (folded decode attention)
+  bool folded_attn = false;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
   // tf32 split (big = tf32(v), small = v - big) of the GEMM activation operands
   float *h_big = nullptr, *h_small = nullptr, *attn_big = nullptr, *attn_small = nullptr;
@@ -216,6 +218,7 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
   CREATE_TRY(gemm_tc_init());
   CREATE_TRY(gemm_tc_wide_init());
   CREATE_TRY(attention_init());
+  CREATE_TRY(attention_folded_init());
   CREATE_TRY(gemm_bf16_init());
   CREATE_TRY(gemm_f16x2_init());
   bool tf32 = false;
@@ -282,6 +285,16 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
   s->prefix_user = (long)c.layers * 2 * kvd * cap;
   CREATE_TRY(dev_alloc(s, &s->kv_prefix, (size_t)s->prefix_user * U));
   CREATE_TRY(dev_alloc(s, &s->kv_suffix, (size_t)c.layers * 2 * 4 * B * U * kvd));
+  {
+    // decode attention: the per-head kernel of attention.cu, or with
+    // RTR_ATTN=folded the folded cluster kernel (TMA over the arena; measured
+    // slower on B200: 2.46 against 2.38 ms per 1.5B decode step)
+    const char* e = getenv("RTR_ATTN");
+    const long arena_rows = s->prefix_user * U / D;
+    s->folded_attn = e && strcmp(e, "folded") == 0 && attention_folded_supported(c.heads, c.kv_heads, D, s->bf16) &&
+                     (s->bf16 ? make_tmap_bf16(&s->arena_map, s->kv_prefix, arena_rows, D, D, 32)
+                              : make_tmap_f32(&s->arena_map, s->kv_prefix, arena_rows, D, D, 32));
+  }
   CREATE_TRY(dev_alloc(s, &s->x, M * H));
   CREATE_TRY(dev_alloc(s, &s->h, M * H));
   CREATE_TRY(dev_alloc(s, &s->qkv, M * qkvd));
@@ -670,6 +683,25 @@ static cudaError_t gemm16(rtr_session* s, const float* X, const void* Wp, void* 
                    s->d_status, s->sms, s->stream, s->pdl, rope);
 }
 
+// Decode attention of one layer: the per-head kernel, or the folded cluster
+// kernel (RTR_ATTN=folded).
+static cudaError_t decode_attention(rtr_session* s, const void* kp, const void* vp, const void* ks, const void* vs,
+                                    int t, float* ob, float* os, float scale, const DecodeUsers& du) {
+  const auto& c = s->cfg;
+  const int D = c.head_dim;
+  if (s->folded_attn) {
+    const long esz = s->bf16 ? 2 : 4;
+    const char* base = reinterpret_cast<const char*>(s->kv_prefix);
+    const long krow0 = (long)(reinterpret_cast<const char*>(kp) - base) / esz / D;
+    const long vrow0 = (long)(reinterpret_cast<const char*>(vp) - base) / esz / D;
+    return attention_decode_folded(s->arena_map, krow0, vrow0, s->prefix_user / D, s->q, ks, vs,
+                                   &s->beam->anc[0][0], s->d_L, t, s->attn, ob, os, beams_of(s), c.max_prefix,
+                                   c.heads, c.kv_heads, D, scale, s->d_status, s->bf16, s->stream, du, s->xfmt);
+  }
+  return attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, ob, os, beams_of(s),
+                          c.max_prefix, c.heads, c.kv_heads, D, scale, s->d_status, s->bf16, s->stream, du, s->xfmt);
+}
+
 // The forward of the bf16 mode: the same launches as the fp32 forward with
 // bf16 activations, KV and weights (the reference's bf16-experimental model).
 static cudaError_t forward_bf16(rtr_session* s, int t) {
@@ -706,8 +738,7 @@ static cudaError_t forward_bf16(rtr_session* s, int t) {
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, nullptr, nullptr, M, cap, c.heads, c.kv_heads, D, scale, true,
                                 st));
     else
-      FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, nullptr, nullptr, B,
-                               cap, c.heads, c.kv_heads, D, scale, s->d_status, true, st, du));
+      FWD_TRY(decode_attention(s, kp, vp, ks, vs, t, nullptr, nullptr, scale, du));
     FWD_TRY(gemm16(s, s->attn, w.po, s->x, H, nullptr, M, H, qd, EPI_RESID));
     FWD_TRY(rms_norm_rows_bf16(s->x, w.n_post, s->h, M, H, c.rms_eps, st));
     FWD_TRY(gemm16(s, s->h, w.pgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
@@ -762,9 +793,7 @@ static cudaError_t forward(rtr_session* s, int t) {
         FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
                                   scale, false, st, s->xfmt));
       } else {
-        FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
-                                 s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st, du,
-                                 s->xfmt));
+        FWD_TRY(decode_attention(s, kp, vp, ks, vs, t, s->attn_big, s->attn_small, scale, du));
       }
       FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID, nullptr, &out));
       FWD_TRY(gemm(s, s->x, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU, nullptr, &in));
@@ -803,9 +832,7 @@ static cudaError_t forward(rtr_session* s, int t) {
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
                                 scale, false, st, s->xfmt));
     } else {
-      FWD_TRY(attention_decode(s->q, kp, vp, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn, s->attn_big,
-                               s->attn_small, B, cap, c.heads, c.kv_heads, D, scale, s->d_status, false, st, du,
-                               s->xfmt));
+      FWD_TRY(decode_attention(s, kp, vp, ks, vs, t, s->attn_big, s->attn_small, scale, du));
     }
     FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID));
     FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st, s->xfmt));

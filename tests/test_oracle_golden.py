@@ -119,3 +119,49 @@ def test_output_invariants_on_golden(tiny):
                 acc = np.float32(acc + np.float32(v))
             assert acc == np.float32(seq)
         assert rec['sequence_logp'] == sorted(rec['sequence_logp'], reverse=True)
+
+
+# ------------------------------------------------ full-size cohort records
+COHORTS = sorted(p.stem[len('cohort_'):] for p in GOLDEN.glob('cohort_*.npz'))
+
+
+@pytest.mark.parametrize('name', COHORTS)
+def test_cohort_fixture_matches_this_workload_and_holds_the_output_invariants(name):
+    """The reference's full-size records were made from exactly the weights and
+    prompts this repository generates, and satisfy the reference's own audit
+    invariants (audit_decode_pilot.py:37-48): 50 distinct catalog SIDs ending
+    in newline + EOS, finite scores, sequence score = sequential FP32 sum of the
+    five transitions, ranks in score order."""
+    from rapidtinyrec_b200 import configs, workload
+    z = np.load(GOLDEN / f'cohort_{name}.npz')
+    meta = json.loads(str(z['meta']))
+    wl = configs.workload(name)
+    cfg = wl.model
+    idx = [int(u) for u in z['cohort_index']] if 'cohort_index' in z.files else list(range(meta['users']))
+    items = workload.catalog_items(wl)
+    everyone = workload.users(wl, items, count=max(idx) + 1)
+    h = hashlib.sha256()
+    for u in idx:
+        h.update(np.asarray(everyone[u].prompt_token_ids, dtype=np.int32).tobytes())
+        h.update(b'|')
+    assert h.hexdigest() == meta['prompts_sha256']
+    probe = hashlib.sha256()
+    for tid, (tname, shape, scale, offset) in enumerate(workload.tensor_specs(cfg)):
+        probe.update(tname.encode())
+        probe.update(workload.synth_values_numpy(wl.weight_seed, tid, min(4096, int(np.prod(shape))), scale,
+                                                 offset).tobytes())
+    assert probe.hexdigest() == meta['weights_probe_sha256']
+    iset = set(items)
+    toks, seq, trans = z['token_ids'], z['sequence_logp'], z['transition_logp']
+    assert toks.shape == (len(idx), 50, 5) and list(z['prompt_tokens']) == [everyone[u].prompt_tokens for u in idx]
+    for r in range(len(idx)):
+        sids = [tuple(int(x) for x in t) for t in toks[r]]
+        assert len(set(sids)) == 50
+        assert all(s[:3] in iset and s[3] == cfg.newline and s[4] == cfg.eos for s in sids)
+        assert np.all(np.isfinite(trans[r]))
+        for b in range(50):
+            acc = np.float32(0)
+            for v in trans[r, b]:
+                acc = np.float32(acc + v)
+            assert acc == seq[r, b]
+        assert np.all(np.diff(seq[r]) <= 0)
