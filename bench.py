@@ -195,6 +195,38 @@ def cpu_oracle_time(cfg, weights_cpu, cons, users, budget_s, threads):
     return times
 
 
+def decode_step_roofline(engine, cfg, users, ids_dev, stream, peak):
+    """Device time of decode steps 1-4 inside requests (CUDA events around each
+    step on the session's stream) against the bytes a step must move: every
+    weight once (layers, LM head, final norm) plus the K/V it reads (the shared
+    prefix and the beams' suffix rows) and writes (50 new rows)."""
+    import torch
+    b = 4 if cfg.dtype == 'fp32' else 2
+    kv_token = 2 * cfg.kv_heads * cfg.head_dim * cfg.layers * b
+    times, nbytes = [], []
+    for i, u in enumerate(users):
+        L = u.prompt_tokens
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        engine._check(engine.lib.rtr_prefill(engine.handle, ids_dev[i].data_ptr(), L, 1))
+        ev[0].record(stream)
+        for t in range(1, 5):
+            engine.decode_step(t)
+            ev[t].record(stream)
+        engine.read_results()
+        torch.cuda.synchronize()
+        for t in range(1, 5):
+            times.append(ev[t - 1].elapsed_time(ev[t]))
+            nbytes.append(cfg.weight_bytes_per_step() + kv_token * (L + engine.beams * (t - 1)) +
+                          kv_token * engine.beams)
+    ms = statistics.median(times)
+    byt = statistics.median(nbytes)
+    achieved = byt / (ms / 1000.0) / 1e9
+    return {'bound': 'hbm', 'ms_per_step': round(ms, 4), 'bytes_per_step': int(byt), 'achieved': round(achieved, 1),
+            'peak': peak, 'unit': 'GB/s', 'frac': round(achieved / peak, 4),
+            'steps_timed': len(times), 'note': 'median decode step 1-4 inside requests (weights + prefix/suffix K/V '
+                                               'read + new K/V written) / CUDA-event step time'}
+
+
 def run_reference(args):
     """The reference algorithm on the host cores: the CPU oracle port of HF beam
     search + the reference's processor + folded SDPA, with weights made by the
@@ -389,6 +421,8 @@ def run_ours(args):
 
     # ---- roofline of the dominant kernel: the decode projection GEMMs (M = beams)
     gemm_ms = engine.profile_gemms(engine.beams, reps=5)
+    step_roof = decode_step_roofline(engine, cfg, [users[i] for i in timed][:6], [ids_dev[i] for i in timed][:6],
+                                     stream, measured_peaks()[0])
     gemm_bytes = gemm_weight_bytes(cfg)
     peak, peak_kind = measured_peaks()
 
@@ -449,6 +483,7 @@ def run_ours(args):
                              else None,
                          'bytes_per_pass': gemm_bytes, 'ms_per_pass': round(gemm_ms, 4),
                          'gemm_tflops': round(gemm_flops / (gemm_ms / 1000.0) / 1e12, 2)},
+            'decode_step_roofline': step_roof,
             'gpu_launches': int(launches),
             'concurrent': concurrent,
             'batched': batched,

@@ -179,6 +179,42 @@ __global__ void tail_sum2_kernel(const float* __restrict__ logits, int vocab, Be
   }
 }
 
+// The second log-softmax pass when the LM head left per-tile (max, sum exp)
+// partials: every CTA of a row first folds the row's partials in tile order
+// into the row max m and the first sum s1 = sum_t s_t exp(m_t - m) (the same
+// bits in each of the row's CTAs), then sums its slice of the second pass.
+__global__ void tail_lse_sum2_kernel(const float* __restrict__ logits, int vocab, BeamState* st, int rows_per_user,
+                                     const float2* __restrict__ lse) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float red[33];
+  st += blockIdx.x / rows_per_user;  // batched decode: each user's rows feed its own state
+  const int grow = blockIdx.x, row = blockIdx.x % rows_per_user, sp = blockIdx.y;
+  const int ntiles = (vocab + 127) / 128;
+  const float2* part = lse + (long)grow * ntiles;
+  float m = -INFINITY;
+  for (int t = threadIdx.x; t < ntiles; t += TAIL_THREADS) m = fmaxf(m, part[t].x);
+  m = block_max(m, red);
+  float s1 = 0.f;
+  for (int t = threadIdx.x; t < ntiles; t += TAIL_THREADS) {
+    const float2 v = part[t];
+    s1 += v.y * expf(v.x - m);
+  }
+  s1 = block_sum(s1, red);
+  const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
+  const float* x = logits + (long)grow * vocab;
+  const float L1 = logf(s1);
+  const float m2 = (m - m) - L1;  // max of lp1, reached at the arg-max column
+  float s = 0.f;
+#pragma unroll 4
+  for (long i = lo + threadIdx.x; i < hi; i += TAIL_THREADS) s += expf(((x[i] - m) - L1) - m2);
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) {
+    st->part[row][sp][2] = s;
+    if (sp == 0) { st->row_stats[row][0] = m; st->row_stats[row][1] = L1; st->row_stats[row][2] = m2; }
+  }
+}
+
 // ---------------------------------------------------- select + update
 __device__ __forceinline__ uint64_t cand_key(float acc, uint32_t flat) {
   return ((uint64_t)float_key(acc) << 32) | (uint64_t)(~flat);
@@ -458,11 +494,18 @@ cudaError_t beam_init() {
 }
 
 cudaError_t beam_step(BeamState* st, const float* logits, int rows, int vocab, int beams, int step,
-                      const DevTables& tb, uint32_t* status, cudaStream_t stream, int users) {
+                      const DevTables& tb, uint32_t* status, cudaStream_t stream, int users, const float2* lse) {
   dim3 grid(rows * users, TAIL_SPLITS);
-  cudaError_t e = launch_pdl(PDL_TAIL, tail_max_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
-  if (e == cudaSuccess) e = launch_pdl(PDL_TAIL, tail_sum1_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
-  if (e == cudaSuccess) e = launch_pdl(PDL_TAIL, tail_sum2_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
+  cudaError_t e = cudaSuccess;
+  if (lse) {
+    e = launch_pdl(PDL_TAIL, tail_lse_sum2_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows, lse);
+  } else {
+    e = launch_pdl(PDL_TAIL, tail_max_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
+    if (e == cudaSuccess)
+      e = launch_pdl(PDL_TAIL, tail_sum1_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
+    if (e == cudaSuccess)
+      e = launch_pdl(PDL_TAIL, tail_sum2_kernel, grid, dim3(TAIL_THREADS), 0, stream, logits, vocab, st, rows);
+  }
   const int width = lookup_width_of(tb, step);
   const size_t need = (size_t)beams * width * sizeof(uint64_t);
   if (e == cudaSuccess)

@@ -93,7 +93,7 @@ cudaError_t gemm_bf16_wait_control(long long wait_cycles, int withhold_x);
 cudaError_t gemm_f16x2(const TensorMap& tmW, const TensorMap& tmXh, const TensorMap& tmXl, float* C, float* C_big,
                        float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                        size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
-                       bool pdl, const RopeArgs* rope = nullptr, const NormFold* fold = nullptr);
+                       bool pdl, const RopeArgs* rope = nullptr, const NormFold* fold = nullptr, float2* lse = nullptr, int lse_ld = 0);
 
 // ---- bf16 tensor-core GEMM (gemm_bf16.cu): the bf16 mode ----
 // X: bf16 activations [rows][K]; weights packed once into bf16 tile blocks.
@@ -230,8 +230,12 @@ cudaError_t beam_reset(BeamState* st, const int32_t* ids_dev, const int32_t* L_d
                        cudaStream_t stream);
 // Full step tail on logits [rows, V] (rows = 1 at step 0, otherwise beams).
 // `users` consecutive beam states, each with `rows` logits rows (1 at step 0, else beams)
+// With `lse` (the LM head's per-128-column-tile (max, sum exp) partials,
+// [row][ceil(vocab / 128)]) the tail reads the logits once: two launches
+// instead of four.
 cudaError_t beam_step(BeamState* st, const float* logits, int rows, int vocab, int beams, int step,
-                      const DevTables& tb, uint32_t* status, cudaStream_t stream, int users = 1);
+                      const DevTables& tb, uint32_t* status, cudaStream_t stream, int users = 1,
+                      const float2* lse = nullptr);
 cudaError_t beam_finalize(const BeamState* st, int beams, DevResult* res, const uint32_t* status,
                           cudaStream_t stream, int users = 1);
 cudaError_t beam_dense_scores(const BeamState* st, int step, int beams, int vocab, float* out,

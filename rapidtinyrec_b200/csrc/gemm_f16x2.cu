@@ -377,8 +377,9 @@ cudaError_t gemm_f16x2_init() {
 cudaError_t gemm_f16x2(const TensorMap& tmW, const TensorMap& tmXh, const TensorMap& tmXl, float* C, float* C_big,
                        float* C_small, int ldc, const float* bias, int M, int N, int K, int epi, float* ws,
                        size_t ws_floats, int* tickets, int max_tickets, uint32_t* status, int sms, cudaStream_t stream,
-                       bool pdl, const RopeArgs* rope, const NormFold* fold) {
+                       bool pdl, const RopeArgs* rope, const NormFold* fold, float2* lse, int lse_ld) {
   if (epi == EPI_SWIGLU && (!C_big || !C_small)) return cudaErrorInvalidValue;
+  if (lse && (epi != EPI_STORE || lse_ld < (N + FX_WROWS - 1) / FX_WROWS)) return cudaErrorInvalidValue;
   if (epi == EPI_ROPE) {
     if (!rope || !bias || (rope->head_dim != 64 && rope->head_dim != 128) ||
         N != (rope->heads + 2 * rope->kv_heads) * rope->head_dim || (reinterpret_cast<uintptr_t>(bias) & 15))
@@ -402,6 +403,8 @@ cudaError_t gemm_f16x2(const TensorMap& tmW, const TensorMap& tmXh, const Tensor
   TcParams p{C, C_big, C_small, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}, {}, SPLIT_F16};
   if (rope) p.rope = *rope;
   if (fold) p.fold = *fold;
+  p.lse = lse;
+  p.lse_ld = lse_ld;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tt, wt, splits);
   cfg.blockDim = dim3(wide ? FxCfg<128>::THREADS : FxCfg<64>::THREADS);

@@ -83,6 +83,8 @@ struct rtr_session {
   // KV and activations
   float *kv_prefix = nullptr, *kv_suffix = nullptr;
   TensorMap arena_map{};     // TMA map over the prefix arena (folded decode attention)
+  float2* lse = nullptr;     // LM head's per-tile (max, sum exp) partials: [tiles][B * max_users]
+  bool lse_tail = false;     // decode step tails read the logits once (fp16-pair LM head)
   bool folded_attn = false;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
   // tf32 split (big = tf32(v), small = v - big) of the GEMM activation operands
@@ -316,6 +318,13 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
     CREATE_TRY(dev_alloc(s, &s->ss, (H / 128) * M));
   }
   CREATE_TRY(dev_alloc(s, &s->logits, B * U * V));
+  {
+    // the fp16-pair LM head leaves the first log-softmax's partials (RTR_TAIL=passes:
+    // three passes over the logits instead)
+    const char* e = getenv("RTR_TAIL");
+    s->lse_tail = s->use_tc && s->xfmt == SPLIT_F16 && !(e && strcmp(e, "passes") == 0);
+    if (s->lse_tail) CREATE_TRY(dev_alloc(s, &s->lse, (size_t)((V + 127) / 128) * B * U));
+  }
   long max_n = qkvd;
   if (H > max_n) max_n = H;
   if (2 * I > max_n) max_n = 2 * I;
@@ -636,7 +645,7 @@ int rtr_load_constraints(rtr_session* s, const rtr_constraint_tables* t) {
 // kernel (RTR_GEMM=ffma).
 static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W, float* C, int ldc,
                         const float* bias, int M, int N, int K, int epi, const RopeArgs* rope = nullptr,
-                        const NormFold* fold = nullptr) {
+                        const NormFold* fold = nullptr, float2* lse = nullptr) {
   if (s->use_tc) {
     auto sp = s->split_of.find(A);
     if (sp == s->split_of.end()) return cudaErrorInvalidValue;
@@ -654,7 +663,8 @@ static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W,
     }
     if (s->xfmt == SPLIT_F16)
       return gemm_f16x2(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws, s->ws_floats,
-                        s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope, fold);
+                        s->tickets, kTickets, s->d_status, s->sms, s->stream, s->pdl, rope, fold, lse,
+                        (s->cfg.vocab + 127) / 128);
     // more than 64 rows (the prefill): one 128-row MMA per instruction instead of two 64-row ones
     if (M > 64 && s->tc_wide)
       return gemm_tc_wide(w->second, xb->second, xs->second, C, cb, cs, ldc, bias, M, N, K, epi, s->ws,
@@ -803,7 +813,8 @@ static cudaError_t forward(rtr_session* s, int t) {
       FWD_TRY(rms_norm_rows(s->x + (size_t)(M - 1) * H, s->norm_final, s->h, nullptr, nullptr, 1, H, c.rms_eps, st));
       FWD_TRY(gemv_f32(s->h, s->lm_head, s->logits, V, H, st));
     } else {
-      FWD_TRY(gemm(s, s->x, H, s->lm_head, s->logits, V, nullptr, M, V, H, EPI_STORE, nullptr, &in));
+      FWD_TRY(gemm(s, s->x, H, s->lm_head, s->logits, V, nullptr, M, V, H, EPI_STORE, nullptr, &in,
+                   s->lse_tail ? s->lse : nullptr));
     }
     return cudaSuccess;
   }
@@ -844,7 +855,8 @@ static cudaError_t forward(rtr_session* s, int t) {
     FWD_TRY(gemv_f32(s->h, s->lm_head, s->logits, V, H, st));
   } else {
     FWD_TRY(rms_norm_rows(s->x, s->norm_final, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st, s->xfmt));
-    FWD_TRY(gemm(s, s->h, H, s->lm_head, s->logits, V, nullptr, M, V, H, EPI_STORE));
+    FWD_TRY(gemm(s, s->h, H, s->lm_head, s->logits, V, nullptr, M, V, H, EPI_STORE, nullptr, nullptr,
+                 s->lse_tail ? s->lse : nullptr));
   }
   return cudaSuccess;
 }
@@ -852,7 +864,7 @@ static cudaError_t forward(rtr_session* s, int t) {
 static cudaError_t decode_and_tail(rtr_session* s, int t) {
   FWD_TRY(forward(s, t));
   return beam_step(s->beam, s->logits, beams_of(s), s->cfg.vocab, beams_of(s), t, s->tb, s->d_status, s->stream,
-                   s->step_users);
+                   s->step_users, s->lse_tail ? s->lse : nullptr);
 }
 
 static cudaError_t finalize_and_copy(rtr_session* s) {
@@ -877,7 +889,8 @@ static int64_t forward_kernels(const rtr_session* s, bool prefill) {
   if (s->fold) return 1 + 5 * (int64_t)s->cfg.layers + (prefill ? 2 : 1);
   return 1 + (s->use_tc ? 7 : 8) * (int64_t)s->cfg.layers + 2;
 }
-static constexpr int64_t kTailKernels = 4;
+static constexpr int64_t kTailKernels = 4;   // step 0 (the prefill's GEMV LM head)
+static int64_t decode_tail_kernels(const rtr_session* s) { return s->lse_tail ? 2 : kTailKernels; }
 
 static int check_prompt(rtr_session* s, const int32_t* ids, int32_t L) {
   if (!ids) return fail(s, RTR_ERR_ARG, "null ids");
@@ -950,7 +963,7 @@ int rtr_decode_step(rtr_session* s, int32_t t) {
   if (s->steps_done != t - 1) return fail(s, RTR_ERR_STATE, "decode steps must follow prefill in order");
   CUDA_TRY(s, cudaSetDevice(s->device));
   CUDA_TRY(s, decode_and_tail(s, t));
-  s->launches += forward_kernels(s, false) + kTailKernels;
+  s->launches += forward_kernels(s, false) + decode_tail_kernels(s);
   s->steps_done = t;
   return RTR_OK;
 }
@@ -1073,7 +1086,8 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   out->kernel_launches = s->launches;
   // beam_reset + NSTEPS x (forward + step tail) + beam_finalize
   out->launches_per_request =
-      1 + forward_kernels(s, true) + (NSTEPS - 1) * forward_kernels(s, false) + NSTEPS * kTailKernels + 1;
+      1 + forward_kernels(s, true) + (NSTEPS - 1) * forward_kernels(s, false) + kTailKernels +
+      (NSTEPS - 1) * decode_tail_kernels(s) + 1;
   out->graph_kernel_nodes = s->graph_kernels;
   out->prefix_bytes_written = (int64_t)c.layers * 2 * kvd * s->L * (int64_t)sizeof(float);
   out->prefix_bytes_reordered = 0;

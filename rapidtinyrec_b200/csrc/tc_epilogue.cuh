@@ -20,6 +20,8 @@ struct TcParams {
   RopeArgs rope;    // EPI_ROPE only
   NormFold fold;    // ss_in: scale rows by their RMS factor; ss_out: EPI_RESID partials
   int xfmt;         // split written for the next GEMM: SPLIT_TF32 or SPLIT_F16
+  float2* lse = nullptr;  // EPI_STORE (LM head): per row and 128-column tile, (max, sum exp(x - max))
+  int lse_ld = 0;         // tiles per row of the partials (row stride)
 };
 
 
@@ -259,6 +261,46 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
     if (p.epi == EPI_BIAS) v = f4add(v, *reinterpret_cast<const float4*>(p.bias + col));
     else if (p.epi == EPI_RESID) v = f4add(*c, v);
     *c = v;
+  }
+  if (p.lse && p.epi == EPI_STORE) {
+    // LM head: every row's (max, sum of exp(x - max)) over the tile's columns,
+    // for the first log-softmax (the step tail then reads the logits once).
+    // Warp w takes rows w, w + W, ... eight at a time (lane = float4 column),
+    // so the eight shuffle trees of a group overlap instead of queueing.  The
+    // hardware exponential: these partials only set the row's normaliser,
+    // whose sum over the vocabulary averages their rounding.
+    constexpr int NW = THREADS / 32, G = 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int j0 = warp; j0 < rows; j0 += NW * G) {
+      float4 v[G];
+      float mx[G], e[G];
+#pragma unroll
+      for (int r = 0; r < G; ++r) {
+        const int j = j0 + r * NW;
+        const bool ok = j < rows && lane < cols4;
+        v[r] = ok ? row_scale(red4[j * ld4 + lane], j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        mx[r] = fmaxf(fmaxf(v[r].x, v[r].y), fmaxf(v[r].z, v[r].w));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < G; ++r) mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], o));
+#pragma unroll
+      for (int r = 0; r < G; ++r)
+        e[r] = lane < cols4 ? (__expf(v[r].x - mx[r]) + __expf(v[r].y - mx[r])) +
+                                  (__expf(v[r].z - mx[r]) + __expf(v[r].w - mx[r]))
+                            : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < G; ++r) e[r] += __shfl_xor_sync(0xffffffffu, e[r], o);
+      if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < G; ++r) {
+          const int j = j0 + r * NW;
+          if (j < rows) p.lse[(long)(tok0 + j) * p.lse_ld + (n0 >> 7)] = make_float2(mx[r], e[r]);
+        }
+    }
   }
 }
 

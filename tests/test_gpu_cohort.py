@@ -231,14 +231,23 @@ def bf16_cohort(name):
 
 
 def test_bf16_cohort_against_the_reference_bf16_run():
+    """Measured on B200: every rank list changes (as the reference's own BF16
+    run changes all 500 against its TF32 control), 9,307 of 25,000 positions
+    match, the same top item for 451 users, top-50 overlap 47.9 mean / 43 min,
+    |delta| of shared SIDs 0.039 median / 0.24 max.  Bounds leave a margin."""
     s = bf16_cohort('qwen1.5b-bf16')
     assert s['users'] == 500
-    assert s['min_top50_overlap'] >= 25
-    assert s['abs_delta_shared_sids']['max'] <= 0.5
+    assert s['min_top50_overlap'] >= 40 and s['mean_top50_overlap'] >= 46
+    assert s['same_top1_users'] >= 425
+    assert s['abs_delta_shared_sids']['max'] <= 0.4 and s['abs_delta_shared_sids']['median'] <= 0.08
 
 
 def test_7b_bf16_long_prefix_against_the_reference_bf16_run():
+    """Five users including the longest prompt (1,024 tokens) and the shortest
+    (600).  Measured: the same top item for all five, overlap 47-48, |delta|
+    0.088 median / 0.45 max."""
     s = bf16_cohort('qwen7b-bf16')
     assert max(u['prompt_tokens'] for u in s['per_user']) == 1024
-    assert s['min_top50_overlap'] >= 25
-    assert s['abs_delta_shared_sids']['max'] <= 0.5
+    assert s['min_top50_overlap'] >= 44
+    assert s['same_top1_users'] >= 4
+    assert s['abs_delta_shared_sids']['max'] <= 0.7

@@ -219,9 +219,10 @@ def test_report_counts_match_the_captured_graph(tiny_engine, tiny):
         decode, prefill = 1 + 5 * cfg.layers + 1, 1 + 5 * cfg.layers + 2
     else:
         decode = prefill = 1 + 7 * cfg.layers + 2  # embed, 7 per layer (RoPE fused), final norm, LM head
-    tail = 4                                  # max, two sums, beam selection
+    tail0 = 4   # step 0 after the prefill's GEMV: max, two sums, beam selection
+    tail = 2    # decode steps: the LM head leaves the first pass's partials; second sum, selection
     assert rep['graph_kernel_nodes'] == 4 * (decode + tail) + 1   # decode steps 1-4, finalize
-    assert rep['launches_per_request'] == 1 + prefill + tail + rep['graph_kernel_nodes']
+    assert rep['launches_per_request'] == 1 + prefill + tail0 + rep['graph_kernel_nodes']
     assert rep['tensor_core_gemm'] == 2 and rep['norm_fold'] == 1
 
 
