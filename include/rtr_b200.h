@@ -197,6 +197,9 @@ typedef struct {
   int64_t tensor_core_gemm;       /* 2: tcgen05 fp16-pair projections (fp32
                                      default), 1: tcgen05 3xTF32, 0: FFMA      */
   int64_t norm_fold;              /* 1: RMSNorms folded into the GEMMs         */
+  int64_t decode_attention;       /* 0: per-head kernel (default), 1: tensor-
+                                     core folded kernel (RTR_ATTN=tc), 2: folded
+                                     FFMA cluster kernel (RTR_ATTN=folded)     */
 } rtr_report;
 int rtr_get_report(const rtr_session* s, rtr_report* out);
 

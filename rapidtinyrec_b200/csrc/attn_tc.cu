@@ -1,0 +1,546 @@
+// Decode attention on the 5th-generation tensor cores, fp32-accurate through
+// fp16 pairs (the scheme of the projection GEMM, gemm_f16x2.cu).
+//
+// The reference folds the query heads that share a KV head into rows
+// (rapidtinyrec/folded_attention.py:16-31).  Here the rows of KV group g are
+// its (beam, head) pairs, 128 to a tile (the MMA's M), and a thread-block
+// cluster of 8 CTAs covers one (user, group, row tile):
+//
+//   ranks 0..6  one 64-key chunk of the shared prefix each (prompts of up to
+//               448 tokens), staged by TMA from the pair copies the prefill's
+//               q/k/v epilogue wrote (K as [key][dim], V transposed as
+//               [dim][key], hi and lo fp16 planes, 128-byte swizzle);
+//   rank 7      every beam's own suffix keys (at most 4, found through the
+//               ancestry table: the direct-reorder parent gather without
+//               moving bytes), on the FMA pipe.
+//
+// A prefix rank, thread = row (TMEM lane):
+//   q (fp32) -> pair planes in shared memory (the A operand);
+//   S  = q_hi.[k_hi; k_lo]^T (N = 128) + q_lo.k_hi^T (N = 64)   tcgen05 kind::f16
+//   softmax of the row over the chunk in registers (tcgen05.ld), P -> pair planes;
+//   O  = p_hi.[v_hi; v_lo] (N = 2 head_dim) + p_lo.v_hi (N = head_dim);
+//   partial (m, l, O) of the row into shared memory.
+// The dropped q_lo.k_lo and p_lo.v_lo terms are 2^-22 relative.  The 8 ranks'
+// partials meet through distributed shared memory: rank r finishes rows
+// 16 r .. 16 r + 15, summing the ranks in rank order (the same bits every run).
+// Every wait is bounded; a wait that runs out sets RTR_DEV_TIMEOUT.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "common.cuh"
+#include "engine.h"
+#include "tcgen05.cuh"
+
+namespace rtr {
+
+constexpr int AT_ROWS = 128;      // MMA M: (beam, head) rows of a tile
+constexpr int AT_KEYS = 64;       // keys per chunk (one 128-byte row of fp16)
+constexpr int AT_CLUSTER = 8;     // 7 prefix chunks + the suffix rank
+constexpr int AT_THREADS = 512;   // thread = (row, quarter of its keys / dimensions)
+constexpr int AT_MAX_PREFIX = (AT_CLUSTER - 1) * AT_KEYS;
+
+template <int HD> struct AtCfg {
+  static constexpr int NC = HD / 64;                     // 128-byte chunks of a q / k row
+  static constexpr int Q_BYTES = 2 * NC * AT_ROWS * 128; // hi / lo planes
+  static constexpr int K_BYTES = NC * 2 * AT_KEYS * 128; // per dim chunk: [k_hi 64 keys; k_lo 64 keys]
+  static constexpr int V_BYTES = 2 * HD * 128;           // [v_hi^T HD rows; v_lo^T HD rows] x 64 keys
+  static constexpr int P_BYTES = 2 * AT_ROWS * 128;      // p_hi, p_lo planes
+  static constexpr int Q_OFF = 0, K_OFF = Q_BYTES, V_OFF = K_OFF + K_BYTES, P_OFF = V_OFF + V_BYTES;
+  static constexpr int PRE_BYTES = P_OFF + P_BYTES;      // the prefix ranks' operands
+  // (m, l) per row, barriers, then [4][128] partials, [4][80] suffix rows, [16][128] partial dots
+  static constexpr int TAIL_BYTES = AT_ROWS * 8 + 64 + (4 * AT_ROWS + 4 * 80 + 16 * AT_ROWS) * 4;
+  static constexpr int S_COLS = 2 * AT_KEYS;             // [hh | cross]
+  static constexpr int O_COLS = 2 * HD;
+  static constexpr int TMEM_COLS = S_COLS + O_COLS <= 256 ? 256 : 512;
+  static_assert(AT_ROWS * (HD + 4) * 4 <= Q_BYTES + K_BYTES, "the partial O tile fits where q and k were");
+};
+
+// Beams a 128-row tile touches for hpg query heads per KV head.
+__host__ __device__ constexpr int at_tile_beams(int hpg) { return (AT_ROWS - 1) / hpg + 2; }
+// The suffix rank's staging: the tile's q rows ([128][HD + 4] fp32) and the
+// K and V rows of 4 slots of its beams ([4][beams][HD + 4] fp32 each; the
+// padding spreads rows of different beams over the banks).
+template <int HD> constexpr int at_suffix_bytes(int hpg) {
+  return (AT_ROWS * (HD + 4) + 2 * 4 * at_tile_beams(hpg) * (HD + 4)) * 4;
+}
+// Offset of the (m, l) array and the barriers: after the larger of the two uses.
+template <int HD> constexpr int at_tail_off(int hpg) {
+  const int a = AtCfg<HD>::PRE_BYTES, b = at_suffix_bytes<HD>(hpg);
+  return ((a > b ? a : b) + 1023) / 1024 * 1024;
+}
+
+RTR_DEVICE float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+RTR_DEVICE float2 ld_cluster_f32x2_tc(uint32_t addr) {
+  float2 v;
+  asm("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr));
+  return v;
+}
+RTR_DEVICE void cluster_barrier_tc() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Row r of a 128-byte-row operand in the 128-byte swizzle: 16-byte unit u of
+// the row sits at unit u ^ (r % 8) (what TMA writes for a 1024-aligned box).
+RTR_DEVICE uint8_t* sw_unit(uint8_t* plane, int r, int u) { return plane + r * 128 + ((u ^ (r & 7)) << 4); }
+
+// Eight fp32 values as fp16 pairs (pair_split: x / 16 = hi + lo / 2048) into
+// unit u of row r of the hi and lo planes.
+RTR_DEVICE void put_pairs8(uint8_t* hi_plane, uint8_t* lo_plane, int r, int u, const float* x, float pre) {
+  __align__(16) __half hi[8];
+  __align__(16) __half lo[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float xs = x[e] * pre;
+    hi[e] = __float2half_rn(xs);
+    lo[e] = __float2half_rn((xs - __half2float(hi[e])) * kPairLo);
+  }
+  *reinterpret_cast<uint4*>(sw_unit(hi_plane, r, u)) = *reinterpret_cast<const uint4*>(hi);
+  *reinterpret_cast<uint4*>(sw_unit(lo_plane, r, u)) = *reinterpret_cast<const uint4*>(lo);
+}
+
+template <int HD>
+__global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS, 1) decode_attn_tc_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, long krow0, long kplane,
+    long kuser, long vrow0, long vplane, long vuser, int pair_cap, const float* __restrict__ q,
+    const float* __restrict__ ksuf, const float* __restrict__ vsuf, const int32_t* __restrict__ anc,
+    const int32_t* __restrict__ L_dev, float* __restrict__ out, float* __restrict__ out_big,
+    float* __restrict__ out_small, int beams, int cap, int heads, int kv_heads, int t, float scale,
+    uint32_t* __restrict__ status, int anc_user_stride, int xfmt, int tail_off) {
+  using C = AtCfg<HD>;
+  extern __shared__ __align__(1024) uint8_t at_smem_raw[];
+  uint8_t* smem = at_smem_raw + ((1024u - (smem_addr(at_smem_raw) & 1023u)) & 1023u);
+  uint8_t* qs = smem + C::Q_OFF;
+  uint8_t* ks = smem + C::K_OFF;
+  uint8_t* vs = smem + C::V_OFF;
+  uint8_t* ps = smem + C::P_OFF;
+  float* ml = reinterpret_cast<float*>(smem + tail_off);
+  // [128][HD + 4] after the S product (q and k are consumed); the padding
+  // spreads the row-per-thread stores over the banks
+  constexpr int OLD = HD + 4;
+  float* opart = reinterpret_cast<float*>(qs);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + tail_off + AT_ROWS * 8);
+  uint64_t* kv_full = bars;       // K and V chunk landed (TMA)
+  uint64_t* s_done = bars + 1;    // S product done
+  uint64_t* o_done = bars + 2;    // O product done
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3) + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // thread = (row, quarter): warps w and w + 4, w + 8, w + 12 share TMEM lanes
+  // 32 (w % 4) .., each takes a quarter of the row's keys or dimensions
+  const int lq = warp & 3, qt = warp >> 2, r = lq * 32 + lane;
+  const int rank = (int)cluster_rank();
+  const bool suffix_rank = rank == AT_CLUSTER - 1;
+  const int hpg = heads / kv_heads;
+  const int nrows = beams * hpg;
+  const int ug = blockIdx.z, u = ug / kv_heads, g = ug % kv_heads;
+  const int rt0 = blockIdx.y * AT_ROWS;
+  const int r0 = u * beams, rows_all = gridDim.z / kv_heads * beams;
+  anc += (long)u * anc_user_stride;
+  float* red = reinterpret_cast<float*>(smem + tail_off + AT_ROWS * 8 + 64);  // [4][128] per-quarter partials
+
+  if (tid == 0) {
+    mbar_init(smem_addr(kv_full), 1);
+    mbar_init(smem_addr(s_done), 1);
+    mbar_init(smem_addr(o_done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  if (warp == 0) tmem_alloc(smem_addr(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t s_tmem = tmem, o_tmem = tmem + C::S_COLS;
+  const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+  pdl_launch_dependents();
+  pdl_wait();  // q, the suffix rows and the pair copies come from earlier kernels
+
+  int L = L_dev[u];
+  if (L < 1 || L > cap || L > AT_MAX_PREFIX) {  // no valid prefix: attend to the suffix only
+    if (tid == 0 && rank == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
+    L = 0;
+  }
+  const int key0 = rank * AT_KEYS;
+  const int nk = suffix_rank ? 0 : (L - key0 < 0 ? 0 : (L - key0 < AT_KEYS ? L - key0 : AT_KEYS));
+
+  float m = -INFINITY, l = 0.f;
+  bool issued_s = false, issued_o = false;
+  if (nk > 0) {
+    if (tid == 0) {
+      // K chunk: per 64-dim chunk c, [k_hi 64 keys; k_lo 64 keys]; V^T: [v_hi^T; v_lo^T]
+      const uint32_t bar = smem_addr(kv_full);
+      mbar_expect_tx(bar, C::K_BYTES + C::V_BYTES);
+      const long kr = krow0 + (long)u * kuser + (long)g * pair_cap + key0;
+      const long vr = vrow0 + (long)u * vuser + (long)g * HD;
+#pragma unroll
+      for (int c = 0; c < C::NC; ++c) {
+        tma_load_2d(smem_addr(ks + c * 2 * AT_KEYS * 128), &kmap, c * 64, (int)kr, bar);
+        tma_load_2d(smem_addr(ks + c * 2 * AT_KEYS * 128 + AT_KEYS * 128), &kmap, c * 64, (int)(kr + kplane), bar);
+      }
+      tma_load_2d(smem_addr(vs), &vmap, key0, (int)vr, bar);
+      tma_load_2d(smem_addr(vs + HD * 128), &vmap, key0, (int)(vr + vplane), bar);
+    }
+    // the tile's q rows -> pair planes (A operand), zeros past the group's rows:
+    // a warp reads whole rows (coalesced), a thread four values
+#pragma unroll
+    for (int i = tid; i < AT_ROWS * (HD / 4); i += AT_THREADS) {
+      const int rr = i / (HD / 4), c4 = i % (HD / 4), rh = rt0 + rr;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (rh < nrows) {
+        const int bb = rh / hpg, hh = g * hpg + rh % hpg;
+        v = *reinterpret_cast<const float4*>(q + ((long)(r0 + bb) * heads + hh) * HD + 4 * c4);
+      }
+      __align__(8) __half hi[4];
+      __align__(8) __half lo[4];
+      pair_split(v.x, hi[0], lo[0]); pair_split(v.y, hi[1], lo[1]);
+      pair_split(v.z, hi[2], lo[2]); pair_split(v.w, hi[3], lo[3]);
+      const int c = (4 * c4) >> 6, un = ((4 * c4) & 63) >> 3, half8 = (c4 & 1) * 8;
+      *reinterpret_cast<uint2*>(sw_unit(qs + c * AT_ROWS * 128, rr, un) + half8) = *reinterpret_cast<const uint2*>(hi);
+      *reinterpret_cast<uint2*>(sw_unit(qs + (C::NC + c) * AT_ROWS * 128, rr, un) + half8) =
+          *reinterpret_cast<const uint2*>(lo);
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 32) {
+      // S = q_hi.[k_hi; k_lo]^T + q_lo.k_hi^T over head_dim in steps of 16
+      if (mbar_wait(smem_addr(kv_full), 0, abort_flag)) {
+        tc_fence_after();
+        constexpr uint32_t id_cat = idesc_f16(AT_ROWS, 2 * AT_KEYS), id_one = idesc_f16(AT_ROWS, AT_KEYS);
+#pragma unroll
+        for (int c = 0; c < C::NC; ++c) {
+          const uint64_t qh = sw128_desc(smem_addr(qs + c * AT_ROWS * 128));
+          const uint64_t ql = sw128_desc(smem_addr(qs + (C::NC + c) * AT_ROWS * 128));
+          const uint64_t kk = sw128_desc(smem_addr(ks + c * 2 * AT_KEYS * 128));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            mma_f16_ss(s_tmem, qh + 2 * k, kk + 2 * k, id_cat, (c | k) ? 1u : 0u);
+            mma_f16_ss(s_tmem + AT_KEYS, ql + 2 * k, kk + 2 * k, id_one, 1u);
+          }
+        }
+        mma_commit(smem_addr(s_done));
+        issued_s = true;
+      }
+    }
+    const bool s_ok = mbar_wait(smem_addr(s_done), 0, abort_flag);
+    if (__syncthreads_or(!s_ok) == 0) {
+      tc_fence_after();
+      // softmax of row r over the chunk, keys 16 qt .. 16 qt + 15 in this
+      // thread: s = 256 (hh + cross / 2048) * scale
+      constexpr int KQ = AT_KEYS / 4;
+      float sv[KQ];
+      {
+        uint32_t hh[16], cr[16];
+        tmem_ld16(s_tmem + lane_base + qt * KQ, hh);
+        tmem_ld16(s_tmem + lane_base + AT_KEYS + qt * KQ, cr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < KQ; ++j) {
+          const float raw = __uint_as_float(hh[j]) + __uint_as_float(cr[j]) * (1.0f / kPairLo);
+          sv[j] = qt * KQ + j < nk ? raw * (kPairScale * kPairScale) * scale : -INFINITY;
+        }
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < KQ; ++j) mx = fmaxf(mx, sv[j]);
+      red[qt * AT_ROWS + r] = mx;
+      __syncthreads();
+      m = fmaxf(fmaxf(red[r], red[AT_ROWS + r]), fmaxf(red[2 * AT_ROWS + r], red[3 * AT_ROWS + r]));
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < KQ; ++j) {
+        sv[j] = __expf(sv[j] - m);  // the hardware exponential: ~2 ulp, the pair's own precision
+        sum += sv[j];
+      }
+#pragma unroll
+      for (int un = 0; un < KQ / 8; ++un) put_pairs8(ps, ps + AT_ROWS * 128, r, qt * (KQ / 8) + un, sv + un * 8, 1.0f);
+      __syncthreads();  // every max is read before the sums reuse the array
+      red[qt * AT_ROWS + r] = sum;
+      fence_proxy_async();
+      tc_fence_before();
+      __syncthreads();
+      l = (red[r] + red[AT_ROWS + r]) + (red[2 * AT_ROWS + r] + red[3 * AT_ROWS + r]);
+      if (tid == 32) {
+        // O = p_hi.[v_hi; v_lo] + p_lo.v_hi over the chunk's keys in steps of 16
+        tc_fence_after();
+        constexpr uint32_t id_cat = idesc_f16(AT_ROWS, 2 * HD), id_one = idesc_f16(AT_ROWS, HD);
+        const uint64_t ph = sw128_desc(smem_addr(ps)), pl = sw128_desc(smem_addr(ps + AT_ROWS * 128));
+        const uint64_t vv = sw128_desc(smem_addr(vs));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          mma_f16_ss(o_tmem, ph + 2 * k, vv + 2 * k, id_cat, k ? 1u : 0u);
+          mma_f16_ss(o_tmem + HD, pl + 2 * k, vv + 2 * k, id_one, 1u);
+        }
+        mma_commit(smem_addr(o_done));
+        issued_o = true;
+      }
+      const bool o_ok = mbar_wait(smem_addr(o_done), 0, abort_flag);
+      if (__syncthreads_or(!o_ok) == 0) {
+        tc_fence_after();
+        // partial O of row r (unnormalised), dimensions qt HD / 4 ..: 16 (hh + cross / 2048)
+        constexpr int DQ = HD / 4;
+#pragma unroll
+        for (int cb = 0; cb < DQ; cb += 16) {
+          uint32_t hh[16], cr[16];
+          tmem_ld16(o_tmem + lane_base + qt * DQ + cb, hh);
+          tmem_ld16(o_tmem + lane_base + HD + qt * DQ + cb, cr);
+          tmem_ld_wait();
+          float* orow = opart + r * OLD + qt * DQ + cb;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4) {
+            float4 o4;
+            o4.x = (__uint_as_float(hh[j]) + __uint_as_float(cr[j]) * (1.0f / kPairLo)) * kPairScale;
+            o4.y = (__uint_as_float(hh[j + 1]) + __uint_as_float(cr[j + 1]) * (1.0f / kPairLo)) * kPairScale;
+            o4.z = (__uint_as_float(hh[j + 2]) + __uint_as_float(cr[j + 2]) * (1.0f / kPairLo)) * kPairScale;
+            o4.w = (__uint_as_float(hh[j + 3]) + __uint_as_float(cr[j + 3]) * (1.0f / kPairLo)) * kPairScale;
+            *reinterpret_cast<float4*>(orow + j) = o4;
+          }
+        }
+      }
+    }
+    if (*abort_flag) {
+      // a wait ran out: record it; issued copies and products finish before the memory goes away
+      if (tid == 0) {
+        atomicOr(status, RTR_DEV_TIMEOUT);
+        mbar_drain(smem_addr(kv_full), 0);
+      }
+      if (tid == 32) {
+        if (issued_s) mbar_drain(smem_addr(s_done), 0);
+        if (issued_o) mbar_drain(smem_addr(o_done), 0);
+      }
+      m = -INFINITY;
+      l = 0.f;
+    }
+  } else if (suffix_rank) {
+    // every row's t suffix keys of its beam on the FMA pipe, from q rows and
+    // the beams' K / V rows staged in shared memory (rows padded to HD + 4
+    // floats so the float4 reads of consecutive rows spread over the banks)
+    constexpr int QLD = HD + 4;
+    const int bfirst = rt0 / hpg, nb = at_tile_beams(hpg);
+    float* sq = reinterpret_cast<float*>(smem);   // [128][QLD]
+    float* sk = sq + AT_ROWS * QLD;               // [4][nb][QLD]
+    float* sv = sk + 4 * nb * QLD;
+    int* srows = reinterpret_cast<int*>(red + 4 * AT_ROWS);  // [4][nb <= 80] K / V row of (slot, beam)
+    // q rows first: they do not wait for the ancestry rows
+    for (int i = tid; i < AT_ROWS * (HD / 4); i += AT_THREADS) {
+      const int rr = i / (HD / 4), d = (i % (HD / 4)) * 4, rh = rt0 + rr;
+      const bool ok = rh < nrows;
+      const int bb = ok ? rh / hpg : 0, hh = g * hpg + (ok ? rh % hpg : 0);
+      cp_async16(sq + rr * QLD + d, q + ((long)(r0 + bb) * heads + hh) * HD + d, ok);
+    }
+    for (int i = tid; i < t * nb; i += AT_THREADS) {
+      const int sl = i / nb, bb = bfirst + i % nb;
+      int row = bb < beams ? bb : 0;
+      if (bb < beams && sl != t - 1) {
+        row = anc[bb * 4 + sl];
+        if (row < 0 || row >= beams) {
+          atomicOr(status, RTR_DEV_BAD_PARENT);
+          row = bb;
+        }
+      }
+      srows[i] = row;
+    }
+    __syncthreads();
+    for (int i = tid; i < t * nb * (HD / 4); i += AT_THREADS) {
+      const int sl = i / (nb * (HD / 4)), bi = (i / (HD / 4)) % nb, d = (i % (HD / 4)) * 4;
+      const bool ok = bfirst + bi < beams;
+      const long off = (((long)sl * rows_all + r0 + srows[sl * nb + bi]) * kv_heads + g) * HD + d;
+      cp_async16(sk + (sl * nb + bi) * QLD + d, ksuf + off, ok);
+      cp_async16(sv + (sl * nb + bi) * QLD + d, vsuf + off, ok);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    // thread (r, qt) takes a quarter of the dimensions of row r; the quarter
+    // dot products meet in shared memory
+    constexpr int DQ = HD / 4;
+    const int rho = rt0 + r;
+    const int bi = (rho < nrows ? rho / hpg : bfirst) - bfirst;
+    float dots[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int d0 = qt * DQ; d0 < qt * DQ + DQ; d0 += 4) {
+      const float4 qv = *reinterpret_cast<const float4*>(sq + r * QLD + d0);
+#pragma unroll
+      for (int sl = 0; sl < 4; ++sl) {
+        if (sl < t) {
+          const float4 kv = *reinterpret_cast<const float4*>(sk + (sl * nb + bi) * QLD + d0);
+          dots[sl] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, dots[sl]))));
+        }
+      }
+    }
+    float* sdot = red + 4 * AT_ROWS + 4 * 80;  // [4 quarters][4 slots][128]: past srows
+#pragma unroll
+    for (int sl = 0; sl < 4; ++sl) sdot[(qt * 4 + sl) * AT_ROWS + r] = dots[sl];
+    __syncthreads();  // every q row is read and every partial dot written
+    float pr[4];
+#pragma unroll
+    for (int sl = 0; sl < 4; ++sl) {
+      const float dsum = (sdot[sl * AT_ROWS + r] + sdot[(4 + sl) * AT_ROWS + r]) +
+                         (sdot[(8 + sl) * AT_ROWS + r] + sdot[(12 + sl) * AT_ROWS + r]);
+      dots[sl] = sl < t ? dsum * scale : -INFINITY;
+      m = fmaxf(m, dots[sl]);
+    }
+#pragma unroll
+    for (int sl = 0; sl < 4; ++sl) {
+      pr[sl] = sl < t ? __expf(dots[sl] - m) : 0.f;
+      l += pr[sl];
+    }
+#pragma unroll
+    for (int d0 = qt * DQ; d0 < qt * DQ + DQ; d0 += 4) {
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int sl = 0; sl < 4; ++sl) {
+        if (sl < t) {
+          const float4 vv = *reinterpret_cast<const float4*>(sv + (sl * nb + bi) * QLD + d0);
+          o.x = fmaf(pr[sl], vv.x, o.x); o.y = fmaf(pr[sl], vv.y, o.y);
+          o.z = fmaf(pr[sl], vv.z, o.z); o.w = fmaf(pr[sl], vv.w, o.w);
+        }
+      }
+      *reinterpret_cast<float4*>(opart + r * OLD + d0) = o;  // row r's own q slots, read above
+    }
+  } else {
+    // no key of the prefix falls to this rank
+    for (int d0 = qt * (HD / 4); d0 < (qt + 1) * (HD / 4); d0 += 4)
+      *reinterpret_cast<float4*>(opart + r * OLD + d0) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (qt == 0) {
+    ml[2 * r] = m;
+    ml[2 * r + 1] = l;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  cluster_barrier_tc();
+  {
+    // rank k finishes rows 16 k .. 16 k + 15: 32 threads per row, HD / 32 dims each
+    constexpr int DPT = HD / 32;
+    const int rr = 16 * rank + (tid >> 5), d0 = lane * DPT;
+    const uint32_t ml_a = smem_addr(ml + 2 * rr), o_a = smem_addr(opart + rr * OLD + d0);
+    // only ranks that hold keys are read: the first ceil(L / 64) and the suffix rank
+    const int nfull = (L + AT_KEYS - 1) / AT_KEYS;
+    float2 mine = make_float2(-INFINITY, 0.f);
+    if (lane < AT_CLUSTER && (lane < nfull || lane == AT_CLUSTER - 1))
+      mine = ld_cluster_f32x2_tc(cluster_map(ml_a, lane));
+    float2 mlj[AT_CLUSTER];
+    float oj[AT_CLUSTER][DPT];
+#pragma unroll
+    for (int j = 0; j < AT_CLUSTER; ++j) {
+      mlj[j].x = __shfl_sync(0xffffffffu, mine.x, j);
+      mlj[j].y = __shfl_sync(0xffffffffu, mine.y, j);
+#pragma unroll
+      for (int e = 0; e < DPT; ++e) oj[j][e] = 0.f;
+      if (j < nfull || j == AT_CLUSTER - 1) {
+        if constexpr (DPT == 4) {
+          const float4 v = ld_cluster_f32x4(cluster_map(o_a, j));
+          oj[j][0] = v.x; oj[j][1] = v.y; oj[j][2] = v.z; oj[j][3] = v.w;
+        } else {
+          const float2 v = ld_cluster_f32x2_tc(cluster_map(o_a, j));
+          oj[j][0] = v.x; oj[j][1] = v.y;
+        }
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < AT_CLUSTER; ++j) M = fmaxf(M, mlj[j].x);
+    float Ls = 0.f;
+    float o[DPT];
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) o[e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < AT_CLUSTER; ++j) {  // rank order
+      const float w = expf(mlj[j].x - M);   // 0 for a rank without keys (m = -inf)
+      Ls = fmaf(w, mlj[j].y, Ls);
+#pragma unroll
+      for (int e = 0; e < DPT; ++e) o[e] = fmaf(w, oj[j][e], o[e]);
+    }
+    const int rh = rt0 + rr;
+    if (rh < nrows) {
+      const int bb = rh / hpg, hh = g * hpg + rh % hpg;
+      const float inv = 1.0f / Ls;
+      const long base = ((long)(r0 + bb) * heads + hh) * HD + d0;
+      if constexpr (DPT == 4) {
+        const float4 v = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
+        *reinterpret_cast<float4*>(out + base) = v;
+        if (out_big) store_split4(out_big, out_small, base, v, xfmt);
+      } else {
+#pragma unroll
+        for (int e = 0; e < DPT; ++e) store_split(out, out_big, out_small, base + e, o[e] * inv, xfmt);
+      }
+    }
+  }
+  cluster_barrier_tc();  // no CTA leaves while a peer still reads its shared memory
+}
+
+// Largest dynamic shared memory a CTA may take (227 KB) minus the alignment slack.
+constexpr int AT_SMEM_MAX = 227 * 1024 - 1024;
+
+static int at_smem_bytes(int head_dim, int hpg) {
+  const int off = head_dim == 128 ? at_tail_off<128>(hpg) : at_tail_off<64>(hpg);
+  return off + (head_dim == 128 ? AtCfg<128>::TAIL_BYTES : AtCfg<64>::TAIL_BYTES);
+}
+
+bool attention_tc_supported(int heads, int kv_heads, int head_dim, int max_prefix) {
+  return kv_heads >= 1 && heads % kv_heads == 0 && (head_dim == 64 || head_dim == 128) &&
+         max_prefix <= AT_MAX_PREFIX && at_tile_beams(heads / kv_heads) <= 80 &&
+         at_smem_bytes(head_dim, heads / kv_heads) <= AT_SMEM_MAX;
+}
+
+template <int HD>
+static cudaError_t launch_tc(const AttnPairs& ap, const float* q, const float* ks, const float* vs,
+                             const int32_t* anc, const int32_t* L_dev, int t, float* out, float* ob, float* os,
+                             int beams, int cap, int heads, int kv_heads, float scale, uint32_t* status,
+                             cudaStream_t stream, const DecodeUsers& du, int xfmt) {
+  const int hpg = heads / kv_heads;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(AT_CLUSTER, (beams * hpg + AT_ROWS - 1) / AT_ROWS, du.users * kv_heads);
+  cfg.blockDim = dim3(AT_THREADS);
+  const int tail_off = at_tail_off<HD>(hpg);
+  cfg.dynamicSmemBytes = 1024 + tail_off + AtCfg<HD>::TAIL_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_on(PDL_ATTN) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, decode_attn_tc_kernel<HD>, *reinterpret_cast<const CUtensorMap*>(&ap.kmap),
+                            *reinterpret_cast<const CUtensorMap*>(&ap.vmap), ap.krow0, ap.kplane, ap.kuser, ap.vrow0,
+                            ap.vplane, ap.vuser, ap.pair_cap, q, ks, vs, anc, L_dev, out, ob, os, beams, cap, heads,
+                            kv_heads, t, scale, status, du.anc_user_stride, xfmt, tail_off);
+}
+
+cudaError_t attention_decode_tc(const AttnPairs& ap, const float* q, const float* k_suffix, const float* v_suffix,
+                                const int32_t* anc, const int32_t* L_dev, int t, float* out, float* out_big,
+                                float* out_small, int beams, int prefix_cap, int heads, int kv_heads, int head_dim,
+                                float scale, uint32_t* status, cudaStream_t stream, const DecodeUsers& du, int xfmt) {
+  if (t < 1 || t > 4 || beams > MAX_BEAMS || du.users < 1 ||
+      !attention_tc_supported(heads, kv_heads, head_dim, prefix_cap))
+    return cudaErrorInvalidValue;
+  if (head_dim == 128)
+    return launch_tc<128>(ap, q, k_suffix, v_suffix, anc, L_dev, t, out, out_big, out_small, beams, prefix_cap, heads,
+                          kv_heads, scale, status, stream, du, xfmt);
+  return launch_tc<64>(ap, q, k_suffix, v_suffix, anc, L_dev, t, out, out_big, out_small, beams, prefix_cap, heads,
+                       kv_heads, scale, status, stream, du, xfmt);
+}
+
+cudaError_t attention_tc_init() {
+  // the most a supported launch takes (the suffix staging grows as hpg falls)
+  cudaError_t e = cudaFuncSetAttribute(decode_attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       AT_SMEM_MAX + 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AT_SMEM_MAX + 1024);
+  return e;
+}
+
+}  // namespace rtr

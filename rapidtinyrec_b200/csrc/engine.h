@@ -24,6 +24,15 @@ struct RopeArgs {
   int slot;                // < 0: prefill (row m at position m); else decode suffix slot
   const int32_t* L_dev;    // decode: prefix length (position = *L_dev + slot)
   int rows_per_user = 0;   // batched decode: row m belongs to user m / rows_per_user (L_dev[user])
+  // prefill only, when set: the prefix K and V also as fp16 pairs for the
+  // tensor-core decode attention (the layer's group-0 bases): K as
+  // [group][pair_cap][head_dim] hi / lo planes, V transposed as
+  // [group][head_dim][pair_cap] hi / lo planes
+  void* kpair_hi = nullptr;
+  void* kpair_lo = nullptr;
+  void* vtpair_hi = nullptr;
+  void* vtpair_lo = nullptr;
+  int pair_cap = 0;
 };
 
 // RMSNorm folded into the projection GEMMs (fp32 tensor-core paths): the norm
@@ -175,6 +184,24 @@ cudaError_t attention_decode_folded(const TensorMap& arena, long krow0, long vro
                                     uint32_t* status, bool bf16, cudaStream_t stream, const DecodeUsers& du,
                                     int xfmt);
 cudaError_t attention_folded_init();
+
+// Tensor-core decode attention (attn_tc.cu): the prefix K and V as fp16 pairs
+// (written by the prefill's q/k/v epilogue), K [row][head_dim] and V
+// transposed [row][pair_cap], each with a hi plane and, `*plane` rows
+// further, a lo plane.  krow0 / vrow0: the rows of the layer's group 0 of user
+// 0; kuser / vuser: rows per user; groups are pair_cap (K) or head_dim (V)
+// rows apart.  Prompts of up to 448 tokens, fp32 mode.
+struct AttnPairs {
+  TensorMap kmap, vmap;
+  long krow0, kplane, kuser, vrow0, vplane, vuser;
+  int pair_cap;
+};
+bool attention_tc_supported(int heads, int kv_heads, int head_dim, int max_prefix);
+cudaError_t attention_decode_tc(const AttnPairs& ap, const float* q, const float* k_suffix, const float* v_suffix,
+                                const int32_t* anc, const int32_t* L_dev, int t, float* out, float* out_big,
+                                float* out_small, int beams, int prefix_cap, int heads, int kv_heads, int head_dim,
+                                float scale, uint32_t* status, cudaStream_t stream, const DecodeUsers& du, int xfmt);
+cudaError_t attention_tc_init();
 bool attention_folded_supported(int heads, int kv_heads, int head_dim, bool bf16);
 
 // ---- constraints + beam step (beam.cu) ----

@@ -64,11 +64,6 @@ template <int NTOK> struct FxCfg {
   static_assert(TMEM_COLS <= 512, "tensor memory");
 };
 
-// Instruction descriptor, kind::f16 with fp16 A and B: D f32, both K-major.
-__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
-  return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-
 // Bound of the pipeline waits and the test switch that withholds the
 // activation copies (rtr_debug_wait_control); one copy per device.
 static __device__ WaitControl g_fx_wait = {kWaitCycles, 0, 0};

@@ -83,6 +83,10 @@ struct rtr_session {
   // KV and activations
   float *kv_prefix = nullptr, *kv_suffix = nullptr;
   TensorMap arena_map{};     // TMA map over the prefix arena (folded decode attention)
+  // tensor-core decode attention: the prefix K / V as fp16 pairs, written by the prefill
+  bool tc_attn = false;
+  __half* kvpair = nullptr;  // [K hi][K lo][V^T hi][V^T lo] planes
+  AttnPairs pairs{};
   float2* lse = nullptr;     // LM head's per-tile (max, sum exp) partials: [tiles][B * max_users]
   bool lse_tail = false;     // decode step tails read the logits once (fp16-pair LM head)
   bool folded_attn = false;
@@ -221,6 +225,7 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
   CREATE_TRY(gemm_tc_wide_init());
   CREATE_TRY(attention_init());
   CREATE_TRY(attention_folded_init());
+  CREATE_TRY(attention_tc_init());
   CREATE_TRY(gemm_bf16_init());
   CREATE_TRY(gemm_f16x2_init());
   bool tf32 = false;
@@ -288,11 +293,31 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
   CREATE_TRY(dev_alloc(s, &s->kv_prefix, (size_t)s->prefix_user * U));
   CREATE_TRY(dev_alloc(s, &s->kv_suffix, (size_t)c.layers * 2 * 4 * B * U * kvd));
   {
-    // decode attention: the per-head kernel of attention.cu, or with
-    // RTR_ATTN=folded the folded cluster kernel (TMA over the arena; measured
-    // slower on B200: 2.46 against 2.38 ms per 1.5B decode step)
+    // decode attention: the per-head kernel of attention.cu; RTR_ATTN=tc the
+    // tensor-core kernel of attn_tc.cu (fp32 mode, prompts of up to 448
+    // tokens), RTR_ATTN=folded the folded FFMA cluster kernel of
+    // attn_decode.cu.  Both folded kernels read each KV group's prefix once
+    // per 128 (beam, head) rows; on B200 neither beats the per-head kernel
+    // inside a decode step (2.45 and 2.46 against 2.43 ms at 1.5B).
     const char* e = getenv("RTR_ATTN");
     const long arena_rows = s->prefix_user * U / D;
+    s->tc_attn = e && strcmp(e, "tc") == 0 && s->use_tc && !s->bf16 &&
+                 attention_tc_supported(c.heads, c.kv_heads, D, cap);
+    if (s->tc_attn) {
+      const int pc = (cap + 63) / 64 * 64;
+      const long plane = (long)U * c.layers * c.kv_heads * pc * D;  // halfs per plane (K and V^T alike)
+      CREATE_TRY(dev_alloc(s, &s->kvpair, (size_t)4 * plane));
+      CREATE_TRY(cudaMemset(s->kvpair, 0, (size_t)4 * plane * sizeof(__half)));
+      AttnPairs& ap = s->pairs;
+      ap.pair_cap = pc;
+      ap.kplane = plane / D;                            // K rows per plane
+      ap.kuser = (long)c.layers * c.kv_heads * pc;
+      ap.vplane = plane / pc;                           // V^T rows per plane
+      ap.vuser = (long)c.layers * c.kv_heads * D;
+      if (!make_tmap_f16(&ap.kmap, s->kvpair, 2 * ap.kplane, D, D, 64) ||
+          !make_tmap_f16(&ap.vmap, s->kvpair + 2 * plane, 2 * ap.vplane, pc, pc, D))
+        return fail(nullptr, RTR_ERR_CUDA, "tensor map of the K / V pair copies");
+    }
     s->folded_attn = e && strcmp(e, "folded") == 0 && attention_folded_supported(c.heads, c.kv_heads, D, s->bf16) &&
                      (s->bf16 ? make_tmap_bf16(&s->arena_map, s->kv_prefix, arena_rows, D, D, 32)
                               : make_tmap_f32(&s->arena_map, s->kv_prefix, arena_rows, D, D, 32));
@@ -693,12 +718,37 @@ static cudaError_t gemm16(rtr_session* s, const float* X, const void* Wp, void* 
                    s->d_status, s->sms, s->stream, s->pdl, rope);
 }
 
-// Decode attention of one layer: the per-head kernel, or the folded cluster
-// kernel (RTR_ATTN=folded).
-static cudaError_t decode_attention(rtr_session* s, const void* kp, const void* vp, const void* ks, const void* vs,
-                                    int t, float* ob, float* os, float scale, const DecodeUsers& du) {
+// The prefill of user cur_user also writes layer l's K / V as fp16 pairs for
+// the tensor-core decode attention.
+static void set_pair_copies(const rtr_session* s, RopeArgs& ra, int l) {
+  if (!s->tc_attn) return;
+  const auto& c = s->cfg;
+  const AttnPairs& ap = s->pairs;
+  const long lg = ((long)s->cur_user * c.layers + l) * c.kv_heads;
+  const long plane = ap.kplane * c.head_dim;
+  __half* k = s->kvpair + lg * ap.pair_cap * c.head_dim;
+  __half* v = s->kvpair + 2 * plane + lg * c.head_dim * ap.pair_cap;
+  ra.kpair_hi = k;
+  ra.kpair_lo = k + plane;
+  ra.vtpair_hi = v;
+  ra.vtpair_lo = v + plane;
+  ra.pair_cap = ap.pair_cap;
+}
+
+// Decode attention of layer l: the per-head kernel, the tensor-core kernel
+// (RTR_ATTN=tc) or the folded cluster kernel (RTR_ATTN=folded).
+static cudaError_t decode_attention(rtr_session* s, int l, const void* kp, const void* vp, const void* ks,
+                                    const void* vs, int t, float* ob, float* os, float scale, const DecodeUsers& du) {
   const auto& c = s->cfg;
   const int D = c.head_dim;
+  if (s->tc_attn) {
+    AttnPairs ap = s->pairs;
+    ap.krow0 = (long)l * c.kv_heads * ap.pair_cap;
+    ap.vrow0 = (long)l * c.kv_heads * D;
+    return attention_decode_tc(ap, s->q, static_cast<const float*>(ks), static_cast<const float*>(vs),
+                               &s->beam->anc[0][0], s->d_L, t, s->attn, ob, os, beams_of(s), c.max_prefix, c.heads,
+                               c.kv_heads, D, scale, s->d_status, s->stream, du, s->xfmt);
+  }
   if (s->folded_attn) {
     const long esz = s->bf16 ? 2 : 4;
     const char* base = reinterpret_cast<const char*>(s->kv_prefix);
@@ -748,7 +798,7 @@ static cudaError_t forward_bf16(rtr_session* s, int t) {
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, nullptr, nullptr, M, cap, c.heads, c.kv_heads, D, scale, true,
                                 st));
     else
-      FWD_TRY(decode_attention(s, kp, vp, ks, vs, t, nullptr, nullptr, scale, du));
+      FWD_TRY(decode_attention(s, l, kp, vp, ks, vs, t, nullptr, nullptr, scale, du));
     FWD_TRY(gemm16(s, s->attn, w.po, s->x, H, nullptr, M, H, qd, EPI_RESID));
     FWD_TRY(rms_norm_rows_bf16(s->x, w.n_post, s->h, M, H, c.rms_eps, st));
     FWD_TRY(gemm16(s, s->h, w.pgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU));
@@ -796,14 +846,15 @@ static cudaError_t forward(rtr_session* s, int t) {
       float* ks = s->kv_suffix + (size_t)l * 2 * 4 * RB * kvd;
       float* vs = ks + (size_t)4 * RB * kvd;
       const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * n * kvd;
-      const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
-                        t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L, B};
+      RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
+                  t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L, B};
+      if (t == 0) set_pair_copies(s, ra, l);
       FWD_TRY(gemm(s, s->x, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra, &in));
       if (t == 0) {
         FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
                                   scale, false, st, s->xfmt));
       } else {
-        FWD_TRY(decode_attention(s, kp, vp, ks, vs, t, s->attn_big, s->attn_small, scale, du));
+        FWD_TRY(decode_attention(s, l, kp, vp, ks, vs, t, s->attn_big, s->attn_small, scale, du));
       }
       FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID, nullptr, &out));
       FWD_TRY(gemm(s, s->x, H, w.wgu, s->act, I, nullptr, M, 2 * I, H, EPI_SWIGLU, nullptr, &in));
@@ -830,8 +881,9 @@ static cudaError_t forward(rtr_session* s, int t) {
     const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * n * kvd;
     if (s->use_tc) {
       // q/k/v projection with RoPE and the cache write fused into its epilogue
-      const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
-                        t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L, B};
+      RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
+                  t == 0 ? kp : ks + slot, t == 0 ? vp : vs + slot, cap, t == 0 ? -1 : t - 1, s->d_L, B};
+      if (t == 0) set_pair_copies(s, ra, l);
       FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra));
     } else {
       FWD_TRY(gemm(s, s->h, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_BIAS));
@@ -843,7 +895,7 @@ static cudaError_t forward(rtr_session* s, int t) {
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
                                 scale, false, st, s->xfmt));
     } else {
-      FWD_TRY(decode_attention(s, kp, vp, ks, vs, t, s->attn_big, s->attn_small, scale, du));
+      FWD_TRY(decode_attention(s, l, kp, vp, ks, vs, t, s->attn_big, s->attn_small, scale, du));
     }
     FWD_TRY(gemm(s, s->attn, qd, w.wo, s->x, H, nullptr, M, H, qd, EPI_RESID));
     FWD_TRY(rms_norm_rows(s->x, w.n_post, s->h, s->h_big, s->h_small, M, H, c.rms_eps, st, s->xfmt));
@@ -1099,6 +1151,7 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   out->d2h_bytes_per_request = (int64_t)sizeof(DevResult);
   out->tensor_core_gemm = s->use_tc ? (s->xfmt == SPLIT_F16 ? 2 : 1) : 0;
   out->norm_fold = s->fold ? 1 : 0;
+  out->decode_attention = s->tc_attn ? 1 : s->folded_attn ? 2 : 0;
   return RTR_OK;
 }
 

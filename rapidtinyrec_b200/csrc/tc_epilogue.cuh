@@ -115,6 +115,8 @@ inline SplitPlan tc_split_plan(int tiles, int nchunks, int sms, const int* waves
   return best;
 }
 
+constexpr int FTILE_COLS = 128;  // output columns of a tensor-core GEMM tile
+
 // Split-K sum, run by every thread of a CTA finishing a tile: rows
 // [row0, row0 + rows) of the partial tiles summed in split order into the same
 // rows of a [NTOK][128] shared tile (float4 slots, four splits of loads in
@@ -229,8 +231,40 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
         const int g = is_k ? h - r.heads : h - r.heads - r.kv_heads;
         float* cache = is_k ? r.k_dst : r.v_dst;
         dst = r.slot < 0 ? cache + ((long)g * r.prefix_cap + m) * D + d : cache + ((long)m * r.kv_heads + g) * D + d;
+        if (r.slot < 0 && r.kpair_hi) {
+          // the same K / V values as fp16 pairs for the tensor-core decode attention
+          __align__(8) __half hi[4];
+          __align__(8) __half lo[4];
+          pair_split(v.x, hi[0], lo[0]); pair_split(v.y, hi[1], lo[1]);
+          pair_split(v.z, hi[2], lo[2]); pair_split(v.w, hi[3], lo[3]);
+          if (is_k) {  // V is written transposed below
+            const long o = ((long)g * r.pair_cap + m) * D + d;
+            *reinterpret_cast<uint2*>(static_cast<__half*>(r.kpair_hi) + o) = *reinterpret_cast<const uint2*>(hi);
+            *reinterpret_cast<uint2*>(static_cast<__half*>(r.kpair_lo) + o) = *reinterpret_cast<const uint2*>(lo);
+          }
+        }
       }
       *reinterpret_cast<float4*>(dst) = v;
+    }
+    if (r.slot < 0 && r.vtpair_hi && n0 + FTILE_COLS > (r.heads + r.kv_heads) * D) {
+      // the tile's V columns as fp16 pairs, transposed ([group][dim][token]):
+      // consecutive threads take consecutive tokens of a column, so the stores
+      // of a warp are contiguous
+      const float* red = reinterpret_cast<const float*>(red4);
+      for (int q = threadIdx.x; q < rows * cols4 * 4; q += THREADS) {
+        const int c = q / rows, j = q % rows;
+        const int col = n0 + c, h = col / D, d = col % D;
+        if (h < r.heads + r.kv_heads) continue;
+        const int g = h - r.heads - r.kv_heads;
+        float v = red[j * ld4 * 4 + c];
+        if (scaled) v *= rsc[j];
+        v += p.bias[col];
+        __half hi, lo;
+        pair_split(v, hi, lo);
+        const long o = ((long)g * D + d) * r.pair_cap + tok0 + j;
+        static_cast<__half*>(r.vtpair_hi)[o] = hi;
+        static_cast<__half*>(r.vtpair_lo)[o] = lo;
+      }
     }
     return;
   }

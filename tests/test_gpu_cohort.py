@@ -199,6 +199,23 @@ def test_folded_decode_attention_on_the_primary_cohort(monkeypatch):
     assert stats['same_rank_list'] >= 62
 
 
+def test_tensor_core_decode_attention_on_the_primary_cohort(monkeypatch):
+    """RTR_ATTN=tc (the tensor-core cluster kernel) on the first 64 users of
+    the primary cohort: the same bar as the default kernel."""
+    monkeypatch.setenv('RTR_ATTN', 'tc')
+    name = 'qwen1.5b-fp32'
+    meta, indices, refs = load_cohort(name)
+    eng, cfg, items, users = cohort_engine(name, indices, meta)
+    assert eng.report()['decode_attention'] == 1
+    stats = {'swaps': 0, 'max_swap_gap': 0.0, 'moved_parents': 0, 'identical': 0, 'same_rank_list': 0}
+    for u, ref in zip(users[:64], refs[:64]):
+        got = eng.generate(u.prompt_token_ids)
+        check_invariants(got, cfg, items)
+        fp32_compare(got, ref, stats)
+    eng.close()
+    assert stats['same_rank_list'] >= 62
+
+
 def bf16_cohort(name):
     meta, indices, refs = load_cohort(name)
     eng, cfg, items, users = cohort_engine(name, indices, meta)

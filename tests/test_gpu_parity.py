@@ -173,6 +173,19 @@ def test_tiny_folded_decode_attention_matches_reference_golden(cuda, tiny, monke
     rows, keys split over 8 CTAs, TMA staging) in place of the per-head one."""
     monkeypatch.setenv('RTR_ATTN', 'folded')
     eng = make_engine(tiny['cfg'], tiny['weights'], tiny['constraints'], max_prefix=128)
+    assert eng.report()['decode_attention'] == 2
+    meta, _ = load_generate_fixture('tiny_fp32')
+    for rec in meta['records'][:4]:
+        compare_records(eng.generate(rec['prompt_token_ids']), rec)
+
+
+def test_tiny_tensor_core_decode_attention_matches_reference_golden(cuda, tiny, monkeypatch):
+    """RTR_ATTN=tc: the tensor-core kernel (query heads of a KV group as 128
+    rows, prefix keys in 64-key chunks over a cluster of 8 CTAs, QK^T and P.V
+    as fp16-pair tcgen05 products, the suffix keys on the FMA pipe)."""
+    monkeypatch.setenv('RTR_ATTN', 'tc')
+    eng = make_engine(tiny['cfg'], tiny['weights'], tiny['constraints'], max_prefix=128)
+    assert eng.report()['decode_attention'] == 1
     meta, _ = load_generate_fixture('tiny_fp32')
     for rec in meta['records'][:4]:
         compare_records(eng.generate(rec['prompt_token_ids']), rec)
