@@ -974,6 +974,12 @@ static int stage_prefill(rtr_session* s, const int32_t* ids, int32_t L, int32_t 
   return RTR_OK;
 }
 
+static std::string status_hex(uint32_t st) {
+  char b[16];
+  snprintf(b, sizeof b, "0x%x", st);
+  return b;
+}
+
 static int check_result(rtr_session* s, const rtr_result* out, int u = 0) {
   const DevResult& r = s->hres[u];
   const uint32_t st = r.status;
@@ -981,10 +987,10 @@ static int check_result(rtr_session* s, const rtr_result* out, int u = 0) {
     // the aborted GEMMs keep their split-K tickets whole; re-arm them anyway so
     // no count left by an interrupted launch can reach the next request
     CUDA_TRY(s, cudaMemsetAsync(s->tickets, 0, kTickets * sizeof(int), s->stream));
-    return fail(s, RTR_ERR_DEVICE, "a bounded pipeline wait ran out (status 0x" + std::to_string(st) + ")");
+    return fail(s, RTR_ERR_DEVICE, "a bounded pipeline wait ran out (status " + status_hex(st) + ")");
   }
   if (st & (RTR_DEV_BAD_TOKEN | RTR_DEV_BAD_PARENT | RTR_DEV_BAD_LENGTH | RTR_DEV_TOO_MANY_CAND | RTR_DEV_NAN_SCORE))
-    return fail(s, RTR_ERR_DEVICE, "device bound check failed (status 0x" + std::to_string(st) + ")");
+    return fail(s, RTR_ERR_DEVICE, "device bound check failed (status " + status_hex(st) + ")");
   if (st & RTR_DEV_NOT_STOPPED)
     return fail(s, RTR_ERR_DEVICE, "beam search would continue after 5 steps (catalog grammar is not 3 SID tokens + newline + EOS)");
   if (st & RTR_DEV_STOPPED_EARLY)
