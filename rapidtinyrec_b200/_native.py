@@ -59,7 +59,7 @@ class ReportC(ctypes.Structure):
         'requests', 'kernel_launches', 'launches_per_request', 'graph_kernel_nodes', 'prefix_bytes_written',
         'prefix_bytes_reordered', 'suffix_bytes_written', 'suffix_bytes_gathered', 'weight_bytes',
         'device_bytes', 'h2d_bytes_per_request', 'd2h_bytes_per_request', 'tensor_core_gemm', 'norm_fold',
-        'decode_attention')]
+        'decode_attention', 'prefill_attention')]
 
     def as_dict(self):
         return {name: int(getattr(self, name)) for name, _ in self._fields_}

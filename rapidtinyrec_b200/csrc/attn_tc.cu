@@ -103,6 +103,35 @@ RTR_DEVICE void put_pairs8(uint8_t* hi_plane, uint8_t* lo_plane, int r, int u, c
   *reinterpret_cast<uint4*>(sw_unit(lo_plane, r, u)) = *reinterpret_cast<const uint4*>(lo);
 }
 
+// A tile's 128 q rows (fp32) -> fp16 pair planes in the 128-byte swizzle (the
+// A operand of S = q.k^T).  Tile row rr reads q[qrow(rr) * HD ..] (qrow < 0:
+// zeros); a warp reads whole rows, and every thread issues all of its loads
+// before it converts and stores any, so the tile costs one L2 round trip.
+template <int HD, typename RowOf>
+RTR_DEVICE void load_q_pairs(uint8_t* qs, const float* __restrict__ q, RowOf qrow) {
+  constexpr int NC = HD / 64, PER = AT_ROWS * (HD / 4) / AT_THREADS;
+  static_assert(AT_ROWS * (HD / 4) % AT_THREADS == 0, "whole float4s per thread");
+  float4 v[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = threadIdx.x + k * AT_THREADS, rr = i / (HD / 4), c4 = i % (HD / 4);
+    const long row = qrow(rr);
+    v[k] = row >= 0 ? *reinterpret_cast<const float4*>(q + row * HD + 4 * c4) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int i = threadIdx.x + k * AT_THREADS, rr = i / (HD / 4), c4 = i % (HD / 4);
+    __align__(8) __half hi[4];
+    __align__(8) __half lo[4];
+    pair_split(v[k].x, hi[0], lo[0]); pair_split(v[k].y, hi[1], lo[1]);
+    pair_split(v[k].z, hi[2], lo[2]); pair_split(v[k].w, hi[3], lo[3]);
+    const int c = (4 * c4) >> 6, un = ((4 * c4) & 63) >> 3, half8 = (c4 & 1) * 8;
+    *reinterpret_cast<uint2*>(sw_unit(qs + c * AT_ROWS * 128, rr, un) + half8) = *reinterpret_cast<const uint2*>(hi);
+    *reinterpret_cast<uint2*>(sw_unit(qs + (NC + c) * AT_ROWS * 128, rr, un) + half8) =
+        *reinterpret_cast<const uint2*>(lo);
+  }
+}
+
 template <int HD>
 __global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS, 1) decode_attn_tc_kernel(
     const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, long krow0, long kplane,
@@ -188,25 +217,11 @@ __global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS,
       tma_load_2d(smem_addr(vs), &vmap, key0, (int)vr, bar);
       tma_load_2d(smem_addr(vs + HD * 128), &vmap, key0, (int)(vr + vplane), bar);
     }
-    // the tile's q rows -> pair planes (A operand), zeros past the group's rows:
-    // a warp reads whole rows (coalesced), a thread four values
-#pragma unroll
-    for (int i = tid; i < AT_ROWS * (HD / 4); i += AT_THREADS) {
-      const int rr = i / (HD / 4), c4 = i % (HD / 4), rh = rt0 + rr;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (rh < nrows) {
-        const int bb = rh / hpg, hh = g * hpg + rh % hpg;
-        v = *reinterpret_cast<const float4*>(q + ((long)(r0 + bb) * heads + hh) * HD + 4 * c4);
-      }
-      __align__(8) __half hi[4];
-      __align__(8) __half lo[4];
-      pair_split(v.x, hi[0], lo[0]); pair_split(v.y, hi[1], lo[1]);
-      pair_split(v.z, hi[2], lo[2]); pair_split(v.w, hi[3], lo[3]);
-      const int c = (4 * c4) >> 6, un = ((4 * c4) & 63) >> 3, half8 = (c4 & 1) * 8;
-      *reinterpret_cast<uint2*>(sw_unit(qs + c * AT_ROWS * 128, rr, un) + half8) = *reinterpret_cast<const uint2*>(hi);
-      *reinterpret_cast<uint2*>(sw_unit(qs + (C::NC + c) * AT_ROWS * 128, rr, un) + half8) =
-          *reinterpret_cast<const uint2*>(lo);
-    }
+    // the tile's q rows -> pair planes (A operand), zeros past the group's rows
+    load_q_pairs<HD>(qs, q, [&](int rr) -> long {
+      const int rh = rt0 + rr;
+      return rh < nrows ? (long)(r0 + rh / hpg) * heads + g * hpg + rh % hpg : -1;
+    });
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
@@ -482,6 +497,290 @@ __global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS,
   cluster_barrier_tc();  // no CTA leaves while a peer still reads its shared memory
 }
 
+// ------------------------------------------------------------------ prefill
+// Causal prefill attention of one prompt on the tensor cores, from the same
+// pair copies of K and V^T (written by the q/k/v epilogue of the same layer)
+// and the same fp16-pair products as the decode kernel above.  A CTA owns 128
+// rows of KV group g, row rho = token * hpg + head-in-group (the reference's
+// folded layout, rapidtinyrec/folded_attention.py:16-31, applied to the
+// prompt), and walks the keys 0 .. last token of its rows in 64-key chunks
+// with an online softmax (the causal SDPA of the reference's prefill,
+// rapidtinyrec/benchmark_inference.py:134):
+//   K chunks double-buffered, loaded two chunks ahead; V^T single-buffered,
+//   loaded while the next chunk's scores are computed;
+//   S(c + 1) issued as soon as S(c) has landed (two S buffers in TMEM), so the
+//   tensor core computes it while the threads run the softmax of chunk c;
+//   O(c) = P(c).V(c) into TMEM, folded into the fp32 running output in
+//   registers with the softmax rescale: o = o * exp(m_old - m_new) + O(c).
+// Thread = (row, quarter): 16 keys of the chunk, HD / 4 output dimensions.
+// Every wait is bounded; a wait that runs out sets RTR_DEV_TIMEOUT, the CTA
+// drains what it issued and writes nothing.
+template <int HD> struct PtCfg {
+  static constexpr int NC = HD / 64;
+  static constexpr int Q_BYTES = 2 * NC * AT_ROWS * 128;
+  static constexpr int K_BYTES = NC * 2 * AT_KEYS * 128;  // one chunk
+  static constexpr int V_BYTES = 2 * HD * 128;
+  static constexpr int P_BYTES = 2 * AT_ROWS * 128;
+  static constexpr int Q_OFF = 0, K_OFF = Q_BYTES, V_OFF = K_OFF + 2 * K_BYTES, P_OFF = V_OFF + V_BYTES;
+  static constexpr int TAIL_OFF = P_OFF + P_BYTES;
+  static constexpr int TAIL_BYTES = 64 + 2 * 4 * AT_ROWS * 4;  // barriers, [2][4][128] row partials
+  static constexpr int SMEM = 1024 + TAIL_OFF + TAIL_BYTES;
+  static constexpr int S_COLS = 2 * AT_KEYS;              // one S buffer: [hh | cross]
+  static constexpr int O_COLS = 2 * HD;
+  static constexpr int TMEM_COLS = 512;                   // 2 S buffers + O
+  static_assert(2 * S_COLS + O_COLS <= TMEM_COLS, "tensor memory");
+};
+
+template <int HD>
+__global__ void __launch_bounds__(AT_THREADS, 1) prefill_attn_tc_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, long krow, long kplane,
+    long vrow, long vplane, int pair_cap, const float* __restrict__ q, float* __restrict__ out,
+    float* __restrict__ out_big, float* __restrict__ out_small, int L, int heads, int kv_heads, float scale,
+    uint32_t* __restrict__ status, int xfmt) {
+  using C = PtCfg<HD>;
+  extern __shared__ __align__(1024) uint8_t pt_smem_raw[];
+  uint8_t* smem = pt_smem_raw + ((1024u - (smem_addr(pt_smem_raw) & 1023u)) & 1023u);
+  uint8_t* qs = smem + C::Q_OFF;
+  uint8_t* kb = smem + C::K_OFF;  // [2] chunks
+  uint8_t* vs = smem + C::V_OFF;
+  uint8_t* ps = smem + C::P_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::TAIL_OFF);
+  uint64_t* k_full = bars;      // [2]
+  uint64_t* v_full = bars + 2;
+  uint64_t* s_done = bars + 3;  // [2]
+  uint64_t* o_done = bars + 5;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 6);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6) + 1;
+  float* red = reinterpret_cast<float*>(smem + C::TAIL_OFF + 64);  // [2][4][128]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lq = warp & 3, qt = warp >> 2, r = lq * 32 + lane;
+  const int hpg = heads / kv_heads, nrows = L * hpg;
+  const int g = blockIdx.y, rt0 = blockIdx.x * AT_ROWS;
+  const int last_tok = min(L - 1, (rt0 + AT_ROWS - 1) / hpg);
+  const int nch = last_tok / AT_KEYS + 1;
+  const int rho = rt0 + r;
+  const int tok = rho < nrows ? rho / hpg : 0;  // padding rows see key 0 only; never stored
+  const long kr0 = krow + (long)g * pair_cap;  // the group's key 0 (hi plane)
+  const long vr0 = vrow + (long)g * HD;        // the group's dimension 0 (V^T, hi plane)
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&k_full[i]), 1);
+      mbar_init(smem_addr(&s_done[i]), 1);
+    }
+    mbar_init(smem_addr(v_full), 1);
+    mbar_init(smem_addr(o_done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  if (warp == 0) tmem_alloc(smem_addr(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t o_tmem = tmem + 2 * C::S_COLS;
+  const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+  pdl_launch_dependents();
+  pdl_wait();  // q and the pair copies come from the q/k/v projection
+
+  auto load_k = [&](int c) {
+    const uint32_t bar = smem_addr(&k_full[c & 1]);
+    uint8_t* dst = kb + (c & 1) * C::K_BYTES;
+    mbar_expect_tx(bar, C::K_BYTES);
+    const long row = kr0 + (long)c * AT_KEYS;
+#pragma unroll
+    for (int cc = 0; cc < C::NC; ++cc) {
+      tma_load_2d(smem_addr(dst + cc * 2 * AT_KEYS * 128), &kmap, cc * 64, (int)row, bar);
+      tma_load_2d(smem_addr(dst + cc * 2 * AT_KEYS * 128 + AT_KEYS * 128), &kmap, cc * 64, (int)(row + kplane), bar);
+    }
+  };
+  auto load_v = [&](int c) {
+    const uint32_t bar = smem_addr(v_full);
+    mbar_expect_tx(bar, C::V_BYTES);
+    tma_load_2d(smem_addr(vs), &vmap, c * AT_KEYS, (int)vr0, bar);
+    tma_load_2d(smem_addr(vs + HD * 128), &vmap, c * AT_KEYS, (int)(vr0 + vplane), bar);
+  };
+  // S(c) = q_hi.[k_hi; k_lo]^T + q_lo.k_hi^T into S buffer c % 2
+  auto issue_s = [&](int c) -> bool {
+    if (!mbar_wait(smem_addr(&k_full[c & 1]), (c >> 1) & 1, abort_flag)) return false;
+    tc_fence_after();
+    constexpr uint32_t id_cat = idesc_f16(AT_ROWS, 2 * AT_KEYS), id_one = idesc_f16(AT_ROWS, AT_KEYS);
+    const uint32_t st = tmem + (c & 1) * C::S_COLS;
+    const uint8_t* kc = kb + (c & 1) * C::K_BYTES;
+#pragma unroll
+    for (int cc = 0; cc < C::NC; ++cc) {
+      const uint64_t qh = sw128_desc(smem_addr(qs + cc * AT_ROWS * 128));
+      const uint64_t ql = sw128_desc(smem_addr(qs + (C::NC + cc) * AT_ROWS * 128));
+      const uint64_t kk = sw128_desc(smem_addr(kc + cc * 2 * AT_KEYS * 128));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        mma_f16_ss(st, qh + 2 * k, kk + 2 * k, id_cat, (cc | k) ? 1u : 0u);
+        mma_f16_ss(st + AT_KEYS, ql + 2 * k, kk + 2 * k, id_one, 1u);
+      }
+    }
+    mma_commit(smem_addr(&s_done[c & 1]));
+    return true;
+  };
+
+  int k_issued = 0, v_issued = 0, s_issued = 0, o_issued = 0;  // tid 0: copies; tid 32: products
+  if (tid == 0) {
+    load_k(0);
+    k_issued = 1;
+    if (nch > 1) {
+      load_k(1);
+      k_issued = 2;
+    }
+    load_v(0);
+    v_issued = 1;
+  }
+  // the tile's q rows -> pair planes (A operand), zeros past the prompt's rows
+  load_q_pairs<HD>(qs, q, [&](int rr) -> long {
+    const int rh = rt0 + rr;
+    return rh < nrows ? (long)(rh / hpg) * heads + g * hpg + rh % hpg : -1;
+  });
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 32 && issue_s(0)) s_issued = 1;
+
+  constexpr int KQ = AT_KEYS / 4, DQ = HD / 4;
+  float o[DQ];
+#pragma unroll
+  for (int e = 0; e < DQ; ++e) o[e] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  bool ok = true;
+  for (int c = 0; c < nch; ++c) {
+    ok = mbar_wait(smem_addr(&s_done[c & 1]), (c >> 1) & 1, abort_flag);
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    if (tid == 32 && c + 1 < nch && issue_s(c + 1)) s_issued = c + 2;  // overlaps this chunk's softmax
+    if (tid == 0 && c + 2 < nch) {
+      load_k(c + 2);  // S(c) has read its buffer
+      k_issued = c + 3;
+    }
+    // softmax of row r over the chunk, keys 16 qt .. 16 qt + 15 in this thread
+    float sv[KQ];
+    {
+      uint32_t hh[16], cr[16];
+      const uint32_t st = tmem + (c & 1) * C::S_COLS + lane_base + qt * KQ;
+      tmem_ld16(st, hh);
+      tmem_ld16(st + AT_KEYS, cr);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < KQ; ++j) {
+        const float raw = __uint_as_float(hh[j]) + __uint_as_float(cr[j]) * (1.0f / kPairLo);
+        sv[j] = c * AT_KEYS + qt * KQ + j <= tok ? raw * (kPairScale * kPairScale) * scale : -INFINITY;
+      }
+    }
+    float* rm = red + (c & 1) * 4 * AT_ROWS;  // alternating halves: one barrier per use
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < KQ; ++j) mx = fmaxf(mx, sv[j]);
+    rm[qt * AT_ROWS + r] = mx;
+    __syncthreads();
+    const float mn = fmaxf(m, fmaxf(fmaxf(rm[r], rm[AT_ROWS + r]), fmaxf(rm[2 * AT_ROWS + r], rm[3 * AT_ROWS + r])));
+    const float alpha = __expf(m - mn);  // 0 on the first chunk (m = -inf); mn is finite: key 0 is every row's
+    m = mn;
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < KQ; ++j) {
+      sv[j] = __expf(sv[j] - mn);
+      sum += sv[j];
+    }
+#pragma unroll
+    for (int un = 0; un < KQ / 8; ++un) put_pairs8(ps, ps + AT_ROWS * 128, r, qt * (KQ / 8) + un, sv + un * 8, 1.0f);
+    float* rs = red + ((c + 1) & 1) * 4 * AT_ROWS;
+    rs[qt * AT_ROWS + r] = sum;
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    l = l * alpha + ((rs[r] + rs[AT_ROWS + r]) + (rs[2 * AT_ROWS + r] + rs[3 * AT_ROWS + r]));
+    if (tid == 32) {
+      // O(c) = p_hi.[v_hi; v_lo] + p_lo.v_hi over the chunk's keys
+      if (mbar_wait(smem_addr(v_full), c & 1, abort_flag)) {
+        tc_fence_after();
+        constexpr uint32_t id_cat = idesc_f16(AT_ROWS, 2 * HD), id_one = idesc_f16(AT_ROWS, HD);
+        const uint64_t ph = sw128_desc(smem_addr(ps)), pl = sw128_desc(smem_addr(ps + AT_ROWS * 128));
+        const uint64_t vv = sw128_desc(smem_addr(vs));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          mma_f16_ss(o_tmem, ph + 2 * k, vv + 2 * k, id_cat, k ? 1u : 0u);
+          mma_f16_ss(o_tmem + HD, pl + 2 * k, vv + 2 * k, id_one, 1u);
+        }
+        mma_commit(smem_addr(o_done));
+        o_issued = c + 1;
+      }
+    }
+    ok = mbar_wait(smem_addr(o_done), c & 1, abort_flag);
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    if (tid == 0 && c + 1 < nch) {
+      load_v(c + 1);  // O(c) has read the buffer
+      v_issued = c + 2;
+    }
+#pragma unroll
+    for (int cb = 0; cb < DQ; cb += 16) {
+      uint32_t hh[16], cr[16];
+      tmem_ld16(o_tmem + lane_base + qt * DQ + cb, hh);
+      tmem_ld16(o_tmem + lane_base + HD + qt * DQ + cb, cr);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        o[cb + j] = fmaf(o[cb + j], alpha,
+                         (__uint_as_float(hh[j]) + __uint_as_float(cr[j]) * (1.0f / kPairLo)) * kPairScale);
+    }
+    tc_fence_before();
+    __syncthreads();  // O(c) and S(c) are read: the next products may overwrite them
+  }
+  if (!ok) {
+    // a wait ran out: record it; issued copies and products land before the memory goes away
+    if (tid == 0) {
+      atomicOr(status, RTR_DEV_TIMEOUT);
+      for (int c = k_issued > 2 ? k_issued - 2 : 0; c < k_issued; ++c) mbar_drain(smem_addr(&k_full[c & 1]), (c >> 1) & 1);
+      if (v_issued) mbar_drain(smem_addr(v_full), (v_issued - 1) & 1);
+    }
+    if (tid == 32) {
+      for (int c = s_issued > 2 ? s_issued - 2 : 0; c < s_issued; ++c) mbar_drain(smem_addr(&s_done[c & 1]), (c >> 1) & 1);
+      if (o_issued) mbar_drain(smem_addr(o_done), (o_issued - 1) & 1);
+    }
+  } else {
+    // normalised rows through a shared tile ([128][HD + 4] over the free
+    // operand buffers), then a warp stores whole rows (coalesced)
+    constexpr int OLD = HD + 4;
+    static_assert(AT_ROWS * OLD * 4 <= C::TAIL_OFF, "output tile fits in the operand buffers");
+    float* ot = reinterpret_cast<float*>(smem);
+    const float inv = 1.0f / l;
+#pragma unroll
+    for (int e = 0; e < DQ; e += 4)
+      *reinterpret_cast<float4*>(ot + r * OLD + qt * DQ + e) =
+          make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
+    __syncthreads();
+    for (int i = tid; i < AT_ROWS * (HD / 4); i += AT_THREADS) {
+      const int rr = i / (HD / 4), c4 = i % (HD / 4), rh = rt0 + rr;
+      if (rh >= nrows) continue;
+      const long base = ((long)(rh / hpg) * heads + g * hpg + rh % hpg) * HD + 4 * c4;
+      const float4 v = *reinterpret_cast<const float4*>(ot + rr * OLD + 4 * c4);
+      *reinterpret_cast<float4*>(out + base) = v;
+      if (out_big) store_split4(out_big, out_small, base, v, xfmt);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 // Largest dynamic shared memory a CTA may take (227 KB) minus the alignment slack.
 constexpr int AT_SMEM_MAX = 227 * 1024 - 1024;
 
@@ -533,6 +832,42 @@ cudaError_t attention_decode_tc(const AttnPairs& ap, const float* q, const float
                        kv_heads, scale, status, stream, du, xfmt);
 }
 
+bool attention_prefill_tc_supported(int heads, int kv_heads, int head_dim) {
+  return kv_heads >= 1 && heads % kv_heads == 0 && (head_dim == 64 || head_dim == 128);
+}
+
+template <int HD>
+static cudaError_t launch_prefill_tc(const AttnPairs& ap, int user, const float* q, float* out, float* ob, float* os,
+                                     int L, int heads, int kv_heads, float scale, uint32_t* status, cudaStream_t stream,
+                                     int xfmt) {
+  const int hpg = heads / kv_heads;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((L * hpg + AT_ROWS - 1) / AT_ROWS, kv_heads);
+  cfg.blockDim = dim3(AT_THREADS);
+  cfg.dynamicSmemBytes = PtCfg<HD>::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_on(PDL_ATTN) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prefill_attn_tc_kernel<HD>, *reinterpret_cast<const CUtensorMap*>(&ap.kmap),
+                            *reinterpret_cast<const CUtensorMap*>(&ap.vmap), ap.krow0 + (long)user * ap.kuser,
+                            ap.kplane, ap.vrow0 + (long)user * ap.vuser, ap.vplane, ap.pair_cap, q, out, ob, os, L,
+                            heads, kv_heads, scale, status, xfmt);
+}
+
+cudaError_t attention_prefill_tc(const AttnPairs& ap, int user, const float* q, float* out, float* out_big,
+                                 float* out_small, int L, int heads, int kv_heads, int head_dim, float scale,
+                                 uint32_t* status, cudaStream_t stream, int xfmt) {
+  if (L < 1 || L > ap.pair_cap || !attention_prefill_tc_supported(heads, kv_heads, head_dim))
+    return cudaErrorInvalidValue;
+  if (head_dim == 128)
+    return launch_prefill_tc<128>(ap, user, q, out, out_big, out_small, L, heads, kv_heads, scale, status, stream,
+                                  xfmt);
+  return launch_prefill_tc<64>(ap, user, q, out, out_big, out_small, L, heads, kv_heads, scale, status, stream, xfmt);
+}
+
 cudaError_t attention_tc_init() {
   // the most a supported launch takes (the suffix staging grows as hpg falls)
   cudaError_t e = cudaFuncSetAttribute(decode_attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -540,6 +875,12 @@ cudaError_t attention_tc_init() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(decode_attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              AT_SMEM_MAX + 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill_attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PtCfg<128>::SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill_attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PtCfg<64>::SMEM);
   return e;
 }
 

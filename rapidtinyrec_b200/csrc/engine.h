@@ -202,6 +202,13 @@ cudaError_t attention_decode_tc(const AttnPairs& ap, const float* q, const float
                                 float* out_small, int beams, int prefix_cap, int heads, int kv_heads, int head_dim,
                                 float scale, uint32_t* status, cudaStream_t stream, const DecodeUsers& du, int xfmt);
 cudaError_t attention_tc_init();
+// Causal prefill attention of user `user`'s prompt (L tokens) on the tensor
+// cores, from the pair copies the layer's q/k/v epilogue wrote (ap.krow0 /
+// ap.vrow0 set to the layer, as for attention_decode_tc); fp32 mode.
+bool attention_prefill_tc_supported(int heads, int kv_heads, int head_dim);
+cudaError_t attention_prefill_tc(const AttnPairs& ap, int user, const float* q, float* out, float* out_big,
+                                 float* out_small, int L, int heads, int kv_heads, int head_dim, float scale,
+                                 uint32_t* status, cudaStream_t stream, int xfmt);
 bool attention_folded_supported(int heads, int kv_heads, int head_dim, bool bf16);
 
 // ---- constraints + beam step (beam.cu) ----

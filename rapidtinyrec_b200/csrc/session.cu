@@ -85,6 +85,7 @@ struct rtr_session {
   TensorMap arena_map{};     // TMA map over the prefix arena (folded decode attention)
   // tensor-core decode attention: the prefix K / V as fp16 pairs, written by the prefill
   bool tc_attn = false;
+  bool tc_prefill = false;  // prefill attention on the tensor cores (attn_tc.cu)
   __half* kvpair = nullptr;  // [K hi][K lo][V^T hi][V^T lo] planes
   AttnPairs pairs{};
   float2* lse = nullptr;     // LM head's per-tile (max, sum exp) partials: [tiles][B * max_users]
@@ -303,7 +304,13 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
     const long arena_rows = s->prefix_user * U / D;
     s->tc_attn = e && strcmp(e, "tc") == 0 && s->use_tc && !s->bf16 &&
                  attention_tc_supported(c.heads, c.kv_heads, D, cap);
-    if (s->tc_attn) {
+    // prefill attention: the tensor-core kernel of attn_tc.cu in fp32 mode
+    // with the tensor-core projections (their q/k/v epilogue writes the pair
+    // copies it reads), unless RTR_PREFILL_ATTN=ffma asks for the FFMA kernel
+    const char* pe = getenv("RTR_PREFILL_ATTN");
+    s->tc_prefill = !(pe && strcmp(pe, "ffma") == 0) && s->use_tc && !s->bf16 &&
+                    attention_prefill_tc_supported(c.heads, c.kv_heads, D);
+    if (s->tc_attn || s->tc_prefill) {
       const int pc = (cap + 63) / 64 * 64;
       const long plane = (long)U * c.layers * c.kv_heads * pc * D;  // halfs per plane (K and V^T alike)
       CREATE_TRY(dev_alloc(s, &s->kvpair, (size_t)4 * plane));
@@ -721,7 +728,7 @@ static cudaError_t gemm16(rtr_session* s, const float* X, const void* Wp, void* 
 // The prefill of user cur_user also writes layer l's K / V as fp16 pairs for
 // the tensor-core decode attention.
 static void set_pair_copies(const rtr_session* s, RopeArgs& ra, int l) {
-  if (!s->tc_attn) return;
+  if (!s->tc_attn && !s->tc_prefill) return;
   const auto& c = s->cfg;
   const AttnPairs& ap = s->pairs;
   const long lg = ((long)s->cur_user * c.layers + l) * c.kv_heads;
@@ -733,6 +740,22 @@ static void set_pair_copies(const rtr_session* s, RopeArgs& ra, int l) {
   ra.vtpair_hi = v;
   ra.vtpair_lo = v + plane;
   ra.pair_cap = ap.pair_cap;
+}
+
+// Prefill attention of layer l over the M prompt rows of user cur_user: the
+// tensor-core kernel (from the pair copies the q/k/v epilogue just wrote) or
+// the FFMA kernel of attention.cu.
+static cudaError_t prefill_attention(rtr_session* s, int l, const float* kp, const float* vp, int M, float scale) {
+  const auto& c = s->cfg;
+  if (s->tc_prefill) {
+    AttnPairs ap = s->pairs;
+    ap.krow0 = (long)l * c.kv_heads * ap.pair_cap;
+    ap.vrow0 = (long)l * c.kv_heads * c.head_dim;
+    return attention_prefill_tc(ap, s->cur_user, s->q, s->attn, s->attn_big, s->attn_small, M, c.heads, c.kv_heads,
+                                c.head_dim, scale, s->d_status, s->stream, s->xfmt);
+  }
+  return attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, c.max_prefix, c.heads, c.kv_heads,
+                           c.head_dim, scale, false, s->stream, s->xfmt);
 }
 
 // Decode attention of layer l: the per-head kernel, the tensor-core kernel
@@ -851,8 +874,7 @@ static cudaError_t forward(rtr_session* s, int t) {
       if (t == 0) set_pair_copies(s, ra, l);
       FWD_TRY(gemm(s, s->x, H, w.wqkv, s->qkv, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra, &in));
       if (t == 0) {
-        FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
-                                  scale, false, st, s->xfmt));
+        FWD_TRY(prefill_attention(s, l, kp, vp, M, scale));
       } else {
         FWD_TRY(decode_attention(s, l, kp, vp, ks, vs, t, s->attn_big, s->attn_small, scale, du));
       }
@@ -892,8 +914,7 @@ static cudaError_t forward(rtr_session* s, int t) {
                       s->d_status, st));
     }
     if (t == 0) {
-      FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, s->attn_big, s->attn_small, M, cap, c.heads, c.kv_heads, D,
-                                scale, false, st, s->xfmt));
+      FWD_TRY(prefill_attention(s, l, kp, vp, M, scale));
     } else {
       FWD_TRY(decode_attention(s, l, kp, vp, ks, vs, t, s->attn_big, s->attn_small, scale, du));
     }
@@ -1158,6 +1179,7 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   out->tensor_core_gemm = s->use_tc ? (s->xfmt == SPLIT_F16 ? 2 : 1) : 0;
   out->norm_fold = s->fold ? 1 : 0;
   out->decode_attention = s->tc_attn ? 1 : s->folded_attn ? 2 : 0;
+  out->prefill_attention = s->tc_prefill ? 1 : 0;
   return RTR_OK;
 }
 

@@ -179,6 +179,17 @@ def test_tiny_folded_decode_attention_matches_reference_golden(cuda, tiny, monke
         compare_records(eng.generate(rec['prompt_token_ids']), rec)
 
 
+def test_tiny_ffma_prefill_attention_matches_reference_golden(cuda, tiny, monkeypatch):
+    """RTR_PREFILL_ATTN=ffma: the FFMA prefill attention kernel in place of the
+    tensor-core one (the fp32 default); the decode path is unchanged."""
+    monkeypatch.setenv('RTR_PREFILL_ATTN', 'ffma')
+    eng = make_engine(tiny['cfg'], tiny['weights'], tiny['constraints'], max_prefix=128)
+    assert eng.report()['prefill_attention'] == 0
+    meta, _ = load_generate_fixture('tiny_fp32')
+    for rec in meta['records'][:4]:
+        compare_records(eng.generate(rec['prompt_token_ids']), rec)
+
+
 def test_tiny_tensor_core_decode_attention_matches_reference_golden(cuda, tiny, monkeypatch):
     """RTR_ATTN=tc: the tensor-core kernel (query heads of a KV group as 128
     rows, prefix keys in 64-key chunks over a cluster of 8 CTAs, QK^T and P.V
@@ -279,6 +290,7 @@ def test_activation_beyond_the_fp16_pair_range_is_reported(cuda, tiny, monkeypat
     weights[key] = weights[key] * 1e7
     eng = make_engine(tiny['cfg'], weights, tiny['constraints'], max_prefix=128)
     assert eng.report()['tensor_core_gemm'] == 2
+    assert eng.report()['prefill_attention'] == 1
     with pytest.raises(NativeError) as e:
         eng.generate(tiny['users'][0].prompt_token_ids)
     assert e.value.code == RTR_ERR_DEVICE
