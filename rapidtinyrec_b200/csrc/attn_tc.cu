@@ -583,7 +583,6 @@ __global__ void __launch_bounds__(AT_THREADS, 1) prefill_attn_tc_kernel(
   const uint32_t tmem = *tmem_slot;
   const uint32_t o_tmem = tmem + 2 * C::S_COLS;
   const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
-  pdl_launch_dependents();
   pdl_wait();  // q and the pair copies come from the q/k/v projection
 
   auto load_k = [&](int c) {
@@ -645,6 +644,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) prefill_attn_tc_kernel(
   tc_fence_before();
   __syncthreads();
   if (tid == 32 && issue_s(0)) s_issued = 1;
+  pdl_launch_dependents();
 
   constexpr int KQ = AT_KEYS / 4, DQ = HD / 4;
   float o[DQ];
