@@ -270,9 +270,8 @@ int rtr_constraint_process(rtr_session* s, int32_t step, const int64_t* input_id
  *     held by every GPU that loads the library until the process exits);
  *     larger requests fail with RTR_ERR_ARG;
  *   - the first call on a device looks the array's device address up once
- *     (cudaGetSymbolAddress) and keeps it; make that first call before any
- *     stream capture, and do not call cudaDeviceReset on that device
- *     afterwards (the kept address would be stale);
+ *     (cudaGetSymbolAddress) and keeps it; do not call cudaDeviceReset on
+ *     that device afterwards (the kept address would be stale);
  *   - all calls share the one array, so calls whose work overlaps on the GPU
  *     (other streams, other sessions on the same device) race on it; nothing
  *     needs clearing between calls, because each call writes every slot it
