@@ -201,7 +201,7 @@ typedef struct {
                                      core folded kernel (RTR_ATTN=tc), 2: folded
                                      FFMA cluster kernel (RTR_ATTN=folded)     */
   int64_t prefill_attention;      /* 0: FFMA kernel, 1: tensor-core kernel
-                                     (fp32 default; RTR_PREFILL_ATTN=ffma)     */
+                                     (default; RTR_PREFILL_ATTN=ffma)          */
 } rtr_report;
 int rtr_get_report(const rtr_session* s, rtr_report* out);
 

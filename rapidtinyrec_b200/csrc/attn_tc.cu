@@ -25,6 +25,7 @@
 // 16 r .. 16 r + 15, summing the ranks in rank order (the same bits every run).
 // Every wait is bounded; a wait that runs out sets RTR_DEV_TIMEOUT.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
 
@@ -781,6 +782,285 @@ __global__ void __launch_bounds__(AT_THREADS, 1) prefill_attn_tc_kernel(
   }
 }
 
+// The bf16 mode's prefill attention: the structure of prefill_attn_tc_kernel
+// with bf16 operands, K read by TMA straight from the prefix arena and V from
+// the transposed copy the bf16 q/k/v epilogue writes.  S = q.k^T is one bf16
+// product (fp32 accumulation of exact bf16 products, as the FFMA kernel's fp32
+// arithmetic on the same bf16 inputs); P is carried as a bf16 pair
+// (p_hi + p_lo, 16 significant bits) into O = p_hi.v + p_lo.v; the output is
+// rounded to bf16 once, as the FFMA kernel stores it.
+template <int HD> struct PbCfg {
+  static constexpr int NC = HD / 64;
+  static constexpr int Q_BYTES = NC * AT_ROWS * 128;
+  static constexpr int K_BYTES = NC * AT_KEYS * 128;  // one chunk
+  static constexpr int V_BYTES = HD * 128;
+  static constexpr int P_BYTES = 2 * AT_ROWS * 128;
+  static constexpr int Q_OFF = 0, K_OFF = Q_BYTES, V_OFF = K_OFF + 2 * K_BYTES, P_OFF = V_OFF + V_BYTES;
+  static constexpr int TAIL_OFF = P_OFF + P_BYTES;
+  static constexpr int TAIL_BYTES = 64 + 2 * 4 * AT_ROWS * 4;
+  static constexpr int SMEM = 1024 + TAIL_OFF + TAIL_BYTES;
+  static constexpr int S_COLS = AT_KEYS;
+  static constexpr int TMEM_COLS = 256;
+  static_assert(2 * S_COLS + HD <= TMEM_COLS, "tensor memory");
+  static_assert(AT_ROWS * (HD + 4) * 4 <= TAIL_OFF, "output tile fits in the operand buffers");
+};
+
+// Eight fp32 values as bf16 pairs (hi = bf16(x), lo = bf16(x - hi)) into unit
+// u of row r of the hi and lo planes.
+RTR_DEVICE void put_bf16_pairs8(uint8_t* hi_plane, uint8_t* lo_plane, int r, int u, const float* x) {
+  __align__(16) __nv_bfloat16 hi[8];
+  __align__(16) __nv_bfloat16 lo[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    hi[e] = __float2bfloat16_rn(x[e]);
+    lo[e] = __float2bfloat16_rn(x[e] - __bfloat162float(hi[e]));
+  }
+  *reinterpret_cast<uint4*>(sw_unit(hi_plane, r, u)) = *reinterpret_cast<const uint4*>(hi);
+  *reinterpret_cast<uint4*>(sw_unit(lo_plane, r, u)) = *reinterpret_cast<const uint4*>(lo);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(AT_THREADS, 1) prefill_attn_tc_bf16_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, long krow, int cap, long vrow,
+    int pair_cap, const __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ out, int L, int heads,
+    int kv_heads, float scale, uint32_t* __restrict__ status) {
+  using C = PbCfg<HD>;
+  extern __shared__ __align__(1024) uint8_t pb_smem_raw[];
+  uint8_t* smem = pb_smem_raw + ((1024u - (smem_addr(pb_smem_raw) & 1023u)) & 1023u);
+  uint8_t* qs = smem + C::Q_OFF;
+  uint8_t* kb = smem + C::K_OFF;
+  uint8_t* vs = smem + C::V_OFF;
+  uint8_t* ps = smem + C::P_OFF;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::TAIL_OFF);
+  uint64_t* k_full = bars;      // [2]
+  uint64_t* v_full = bars + 2;
+  uint64_t* s_done = bars + 3;  // [2]
+  uint64_t* o_done = bars + 5;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 6);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6) + 1;
+  float* red = reinterpret_cast<float*>(smem + C::TAIL_OFF + 64);  // [2][4][128]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lq = warp & 3, qt = warp >> 2, r = lq * 32 + lane;
+  const int hpg = heads / kv_heads, nrows = L * hpg;
+  const int g = blockIdx.y, rt0 = blockIdx.x * AT_ROWS;
+  const int last_tok = min(L - 1, (rt0 + AT_ROWS - 1) / hpg);
+  const int nch = last_tok / AT_KEYS + 1;
+  const int rho = rt0 + r;
+  const int tok = rho < nrows ? rho / hpg : 0;  // padding rows see key 0 only; never stored
+  const long kr0 = krow + (long)g * cap;        // the group's key 0 in the arena's K plane
+  const long vr0 = vrow + (long)g * HD;         // the group's dimension 0 in the V^T copy
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&k_full[i]), 1);
+      mbar_init(smem_addr(&s_done[i]), 1);
+    }
+    mbar_init(smem_addr(v_full), 1);
+    mbar_init(smem_addr(o_done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  if (warp == 0) tmem_alloc(smem_addr(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t o_tmem = tmem + 2 * C::S_COLS;
+  const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+  pdl_wait();  // q, the arena rows and the V^T copy come from the q/k/v projection
+
+  auto load_k = [&](int c) {
+    const uint32_t bar = smem_addr(&k_full[c & 1]);
+    uint8_t* dst = kb + (c & 1) * C::K_BYTES;
+    mbar_expect_tx(bar, C::K_BYTES);
+#pragma unroll
+    for (int cc = 0; cc < C::NC; ++cc)
+      tma_load_2d(smem_addr(dst + cc * AT_KEYS * 128), &kmap, cc * 64, (int)(kr0 + (long)c * AT_KEYS), bar);
+  };
+  auto load_v = [&](int c) {
+    const uint32_t bar = smem_addr(v_full);
+    mbar_expect_tx(bar, C::V_BYTES);
+    tma_load_2d(smem_addr(vs), &vmap, c * AT_KEYS, (int)vr0, bar);
+  };
+  auto issue_s = [&](int c) -> bool {
+    if (!mbar_wait(smem_addr(&k_full[c & 1]), (c >> 1) & 1, abort_flag)) return false;
+    tc_fence_after();
+    constexpr uint32_t id = idesc_bf16(AT_ROWS, AT_KEYS);
+    const uint32_t st = tmem + (c & 1) * C::S_COLS;
+    const uint8_t* kc = kb + (c & 1) * C::K_BYTES;
+#pragma unroll
+    for (int cc = 0; cc < C::NC; ++cc) {
+      const uint64_t qd = sw128_desc(smem_addr(qs + cc * AT_ROWS * 128));
+      const uint64_t kd = sw128_desc(smem_addr(kc + cc * AT_KEYS * 128));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) mma_f16_ss(st, qd + 2 * k, kd + 2 * k, id, (cc | k) ? 1u : 0u);
+    }
+    mma_commit(smem_addr(&s_done[c & 1]));
+    return true;
+  };
+
+  int k_issued = 0, v_issued = 0, s_issued = 0, o_issued = 0;
+  if (tid == 0) {
+    load_k(0);
+    k_issued = 1;
+    if (nch > 1) {
+      load_k(1);
+      k_issued = 2;
+    }
+    load_v(0);
+    v_issued = 1;
+  }
+  {
+    // the tile's q rows (bf16) -> the A operand, zeros past the prompt's rows:
+    // every 16-byte load in flight before any store
+    constexpr int UPR = HD / 8, PER = AT_ROWS * UPR / AT_THREADS;
+    static_assert(AT_ROWS * UPR % AT_THREADS == 0, "whole units per thread");
+    uint4 v[PER];
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = tid + k * AT_THREADS, rr = i / UPR, u8 = i % UPR, rh = rt0 + rr;
+      v[k] = rh < nrows ? *reinterpret_cast<const uint4*>(q + ((long)(rh / hpg) * heads + g * hpg + rh % hpg) * HD + 8 * u8)
+                        : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int i = tid + k * AT_THREADS, rr = i / UPR, u8 = i % UPR;
+      *reinterpret_cast<uint4*>(sw_unit(qs + (u8 >> 3) * AT_ROWS * 128, rr, u8 & 7)) = v[k];
+    }
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 32 && issue_s(0)) s_issued = 1;
+  pdl_launch_dependents();
+
+  constexpr int KQ = AT_KEYS / 4, DQ = HD / 4;
+  float o[DQ];
+#pragma unroll
+  for (int e = 0; e < DQ; ++e) o[e] = 0.f;
+  float m = -INFINITY, l = 0.f;
+  bool ok = true;
+  for (int c = 0; c < nch; ++c) {
+    ok = mbar_wait(smem_addr(&s_done[c & 1]), (c >> 1) & 1, abort_flag);
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    if (tid == 32 && c + 1 < nch && issue_s(c + 1)) s_issued = c + 2;
+    if (tid == 0 && c + 2 < nch) {
+      load_k(c + 2);
+      k_issued = c + 3;
+    }
+    float sv[KQ];
+    {
+      uint32_t sr[16];
+      tmem_ld16(tmem + (c & 1) * C::S_COLS + lane_base + qt * KQ, sr);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < KQ; ++j)
+        sv[j] = c * AT_KEYS + qt * KQ + j <= tok ? __uint_as_float(sr[j]) * scale : -INFINITY;
+    }
+    float* rm = red + (c & 1) * 4 * AT_ROWS;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < KQ; ++j) mx = fmaxf(mx, sv[j]);
+    rm[qt * AT_ROWS + r] = mx;
+    __syncthreads();
+    const float mn = fmaxf(m, fmaxf(fmaxf(rm[r], rm[AT_ROWS + r]), fmaxf(rm[2 * AT_ROWS + r], rm[3 * AT_ROWS + r])));
+    const float alpha = __expf(m - mn);
+    m = mn;
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < KQ; ++j) {
+      sv[j] = __expf(sv[j] - mn);
+      sum += sv[j];
+    }
+#pragma unroll
+    for (int un = 0; un < KQ / 8; ++un) put_bf16_pairs8(ps, ps + AT_ROWS * 128, r, qt * (KQ / 8) + un, sv + un * 8);
+    float* rs = red + ((c + 1) & 1) * 4 * AT_ROWS;
+    rs[qt * AT_ROWS + r] = sum;
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    l = l * alpha + ((rs[r] + rs[AT_ROWS + r]) + (rs[2 * AT_ROWS + r] + rs[3 * AT_ROWS + r]));
+    if (tid == 32) {
+      if (mbar_wait(smem_addr(v_full), c & 1, abort_flag)) {
+        tc_fence_after();
+        constexpr uint32_t id = idesc_bf16(AT_ROWS, HD);
+        const uint64_t ph = sw128_desc(smem_addr(ps)), pl = sw128_desc(smem_addr(ps + AT_ROWS * 128));
+        const uint64_t vv = sw128_desc(smem_addr(vs));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          mma_f16_ss(o_tmem, ph + 2 * k, vv + 2 * k, id, k ? 1u : 0u);
+          mma_f16_ss(o_tmem, pl + 2 * k, vv + 2 * k, id, 1u);
+        }
+        mma_commit(smem_addr(o_done));
+        o_issued = c + 1;
+      }
+    }
+    ok = mbar_wait(smem_addr(o_done), c & 1, abort_flag);
+    if (__syncthreads_or(!ok)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    if (tid == 0 && c + 1 < nch) {
+      load_v(c + 1);
+      v_issued = c + 2;
+    }
+#pragma unroll
+    for (int cb = 0; cb < DQ; cb += 16) {
+      uint32_t ov[16];
+      tmem_ld16(o_tmem + lane_base + qt * DQ + cb, ov);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[cb + j] = fmaf(o[cb + j], alpha, __uint_as_float(ov[j]));
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  if (!ok) {
+    if (tid == 0) {
+      atomicOr(status, RTR_DEV_TIMEOUT);
+      for (int c = k_issued > 2 ? k_issued - 2 : 0; c < k_issued; ++c) mbar_drain(smem_addr(&k_full[c & 1]), (c >> 1) & 1);
+      if (v_issued) mbar_drain(smem_addr(v_full), (v_issued - 1) & 1);
+    }
+    if (tid == 32) {
+      for (int c = s_issued > 2 ? s_issued - 2 : 0; c < s_issued; ++c) mbar_drain(smem_addr(&s_done[c & 1]), (c >> 1) & 1);
+      if (o_issued) mbar_drain(smem_addr(o_done), (o_issued - 1) & 1);
+    }
+  } else {
+    constexpr int OLD = HD + 4;
+    float* ot = reinterpret_cast<float*>(smem);
+    const float inv = 1.0f / l;
+#pragma unroll
+    for (int e = 0; e < DQ; e += 4)
+      *reinterpret_cast<float4*>(ot + r * OLD + qt * DQ + e) =
+          make_float4(o[e] * inv, o[e + 1] * inv, o[e + 2] * inv, o[e + 3] * inv);
+    __syncthreads();
+    for (int i = tid; i < AT_ROWS * (HD / 4); i += AT_THREADS) {
+      const int rr = i / (HD / 4), c4 = i % (HD / 4), rh = rt0 + rr;
+      if (rh >= nrows) continue;
+      const float4 v = *reinterpret_cast<const float4*>(ot + rr * OLD + 4 * c4);
+      const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+      uint2 u;
+      u.x = *reinterpret_cast<const uint32_t*>(&a);
+      u.y = *reinterpret_cast<const uint32_t*>(&b);
+      *reinterpret_cast<uint2*>(out + ((long)(rh / hpg) * heads + g * hpg + rh % hpg) * HD + 4 * c4) = u;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 // Largest dynamic shared memory a CTA may take (227 KB) minus the alignment slack.
 constexpr int AT_SMEM_MAX = 227 * 1024 - 1024;
 
@@ -868,6 +1148,40 @@ cudaError_t attention_prefill_tc(const AttnPairs& ap, int user, const float* q, 
   return launch_prefill_tc<64>(ap, user, q, out, out_big, out_small, L, heads, kv_heads, scale, status, stream, xfmt);
 }
 
+template <int HD>
+static cudaError_t launch_prefill_tc_bf16(const BfPrefillMaps& mp, int user, int layer, const void* q, void* out,
+                                          int L, int heads, int kv_heads, int cap, float scale, uint32_t* status,
+                                          cudaStream_t stream, int layers) {
+  const int hpg = heads / kv_heads;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((L * hpg + AT_ROWS - 1) / AT_ROWS, kv_heads);
+  cfg.blockDim = dim3(AT_THREADS);
+  cfg.dynamicSmemBytes = PbCfg<HD>::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_on(PDL_ATTN) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const long ul = (long)user * layers + layer;
+  const long krow = ul * 2 * kv_heads * cap;        // the arena's K plane of (user, layer)
+  const long vrow = ul * kv_heads * HD;             // the V^T copy of (user, layer)
+  return cudaLaunchKernelEx(&cfg, prefill_attn_tc_bf16_kernel<HD>, *reinterpret_cast<const CUtensorMap*>(&mp.kmap),
+                            *reinterpret_cast<const CUtensorMap*>(&mp.vmap), krow, cap, vrow, mp.pair_cap,
+                            static_cast<const __nv_bfloat16*>(q), static_cast<__nv_bfloat16*>(out), L, heads, kv_heads,
+                            scale, status);
+}
+
+cudaError_t attention_prefill_tc_bf16(const BfPrefillMaps& mp, int user, int layer, int layers, const void* q,
+                                      void* out, int L, int heads, int kv_heads, int head_dim, int cap, float scale,
+                                      uint32_t* status, cudaStream_t stream) {
+  if (L < 1 || L > cap || L > mp.pair_cap || !attention_prefill_tc_supported(heads, kv_heads, head_dim))
+    return cudaErrorInvalidValue;
+  if (head_dim == 128)
+    return launch_prefill_tc_bf16<128>(mp, user, layer, q, out, L, heads, kv_heads, cap, scale, status, stream, layers);
+  return launch_prefill_tc_bf16<64>(mp, user, layer, q, out, L, heads, kv_heads, cap, scale, status, stream, layers);
+}
+
 cudaError_t attention_tc_init() {
   // the most a supported launch takes (the suffix staging grows as hpg falls)
   cudaError_t e = cudaFuncSetAttribute(decode_attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -881,6 +1195,12 @@ cudaError_t attention_tc_init() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(prefill_attn_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              PtCfg<64>::SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill_attn_tc_bf16_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PbCfg<128>::SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(prefill_attn_tc_bf16_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PbCfg<64>::SMEM);
   return e;
 }
 

@@ -209,6 +209,17 @@ bool attention_prefill_tc_supported(int heads, int kv_heads, int head_dim);
 cudaError_t attention_prefill_tc(const AttnPairs& ap, int user, const float* q, float* out, float* out_big,
                                  float* out_small, int L, int heads, int kv_heads, int head_dim, float scale,
                                  uint32_t* status, cudaStream_t stream, int xfmt);
+// The bf16 mode's tensor-core prefill attention: K by TMA from the bf16 prefix
+// arena (kmap: the arena as [rows][head_dim], 64-row boxes), V from the
+// transposed copy the bf16 q/k/v epilogue writes ([user][layer][group][dim]
+// [pair_cap], vmap: head_dim-row boxes).
+struct BfPrefillMaps {
+  TensorMap kmap, vmap;
+  int pair_cap;
+};
+cudaError_t attention_prefill_tc_bf16(const BfPrefillMaps& mp, int user, int layer, int layers, const void* q,
+                                      void* out, int L, int heads, int kv_heads, int head_dim, int cap, float scale,
+                                      uint32_t* status, cudaStream_t stream);
 bool attention_folded_supported(int heads, int kv_heads, int head_dim, bool bf16);
 
 // ---- constraints + beam step (beam.cu) ----

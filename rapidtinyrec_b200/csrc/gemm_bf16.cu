@@ -136,6 +136,20 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
       }
       st_bf4(dst, v);
     }
+    if (r.slot < 0 && r.vtpair_hi && n0 + FTILE_COLS > (r.heads + r.kv_heads) * D) {
+      // prefill: the tile's V columns also transposed ([group][dim][token],
+      // the same bf16 values) for the tensor-core prefill attention; a warp
+      // takes consecutive tokens of a column, so its stores are contiguous
+      const float* red = reinterpret_cast<const float*>(red4);
+      for (int q = threadIdx.x; q < rows * cols4 * 4; q += BF_THREADS) {
+        const int c = q / rows, j = q % rows;
+        const int col = n0 + c, h = col / D, d = col % D;
+        if (h < r.heads + r.kv_heads) continue;
+        const int g = h - r.heads - r.kv_heads;
+        bfp(r.vtpair_hi)[((long)g * D + d) * r.pair_cap + tok0 + j] =
+            __float2bfloat16_rn(red[j * ld4 * 4 + c] + p.bias[col]);
+      }
+    }
     return;
   }
   for (int q = threadIdx.x; q < rows * 32; q += BF_THREADS) {

@@ -86,6 +86,8 @@ struct rtr_session {
   // tensor-core decode attention: the prefix K / V as fp16 pairs, written by the prefill
   bool tc_attn = false;
   bool tc_prefill = false;  // prefill attention on the tensor cores (attn_tc.cu)
+  uint16_t* vt_bf16 = nullptr;  // bf16 mode: V transposed per (user, layer, group) for it
+  BfPrefillMaps pbmaps = {};
   __half* kvpair = nullptr;  // [K hi][K lo][V^T hi][V^T lo] planes
   AttnPairs pairs{};
   float2* lse = nullptr;     // LM head's per-tile (max, sum exp) partials: [tiles][B * max_users]
@@ -304,13 +306,24 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
     const long arena_rows = s->prefix_user * U / D;
     s->tc_attn = e && strcmp(e, "tc") == 0 && s->use_tc && !s->bf16 &&
                  attention_tc_supported(c.heads, c.kv_heads, D, cap);
-    // prefill attention: the tensor-core kernel of attn_tc.cu in fp32 mode
-    // with the tensor-core projections (their q/k/v epilogue writes the pair
-    // copies it reads), unless RTR_PREFILL_ATTN=ffma asks for the FFMA kernel
+    // prefill attention: the tensor-core kernels of attn_tc.cu (fp32 mode with
+    // the tensor-core projections, whose q/k/v epilogue writes the pair copies
+    // they read; the bf16 mode), unless RTR_PREFILL_ATTN=ffma asks for the
+    // FFMA kernel
     const char* pe = getenv("RTR_PREFILL_ATTN");
-    s->tc_prefill = !(pe && strcmp(pe, "ffma") == 0) && s->use_tc && !s->bf16 &&
+    s->tc_prefill = !(pe && strcmp(pe, "ffma") == 0) && (s->bf16 || s->use_tc) &&
                     attention_prefill_tc_supported(c.heads, c.kv_heads, D);
-    if (s->tc_attn || s->tc_prefill) {
+    if (s->tc_prefill && s->bf16) {
+      const int pc = (cap + 63) / 64 * 64;
+      const long vt_rows = (long)U * c.layers * c.kv_heads * D;
+      CREATE_TRY(dev_alloc(s, &s->vt_bf16, (size_t)vt_rows * pc));
+      CREATE_TRY(cudaMemset(s->vt_bf16, 0, (size_t)vt_rows * pc * sizeof(uint16_t)));
+      s->pbmaps.pair_cap = pc;
+      if (!make_tmap_bf16(&s->pbmaps.kmap, s->kv_prefix, arena_rows, D, D, 64) ||
+          !make_tmap_bf16(&s->pbmaps.vmap, s->vt_bf16, vt_rows, pc, pc, D))
+        return fail(nullptr, RTR_ERR_CUDA, "tensor map of the bf16 prefix arena / V copy");
+    }
+    if (s->tc_attn || (s->tc_prefill && !s->bf16)) {
       const int pc = (cap + 63) / 64 * 64;
       const long plane = (long)U * c.layers * c.kv_heads * pc * D;  // halfs per plane (K and V^T alike)
       CREATE_TRY(dev_alloc(s, &s->kvpair, (size_t)4 * plane));
@@ -728,7 +741,7 @@ static cudaError_t gemm16(rtr_session* s, const float* X, const void* Wp, void* 
 // The prefill of user cur_user also writes layer l's K / V as fp16 pairs for
 // the tensor-core decode attention.
 static void set_pair_copies(const rtr_session* s, RopeArgs& ra, int l) {
-  if (!s->tc_attn && !s->tc_prefill) return;
+  if (s->bf16 || (!s->tc_attn && !s->tc_prefill)) return;
   const auto& c = s->cfg;
   const AttnPairs& ap = s->pairs;
   const long lg = ((long)s->cur_user * c.layers + l) * c.kv_heads;
@@ -813,11 +826,18 @@ static cudaError_t forward_bf16(rtr_session* s, int t) {
     uint16_t* vs = ks + (size_t)4 * RB * kvd;
     const size_t slot = t == 0 ? 0 : (size_t)(t - 1) * B * n * kvd;
     FWD_TRY(rms_norm_rows_bf16(s->x, w.n_in, s->h, M, H, c.rms_eps, st));
-    const RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
-                      reinterpret_cast<float*>(t == 0 ? kp : ks + slot),
-                      reinterpret_cast<float*>(t == 0 ? vp : vs + slot), cap, t == 0 ? -1 : t - 1, s->d_L, B};
+    RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
+                reinterpret_cast<float*>(t == 0 ? kp : ks + slot),
+                reinterpret_cast<float*>(t == 0 ? vp : vs + slot), cap, t == 0 ? -1 : t - 1, s->d_L, B};
+    if (t == 0 && s->tc_prefill) {  // the epilogue also writes V transposed for the prefill attention
+      ra.vtpair_hi = s->vt_bf16 + (((long)s->cur_user * c.layers + l) * c.kv_heads) * D * s->pbmaps.pair_cap;
+      ra.pair_cap = s->pbmaps.pair_cap;
+    }
     FWD_TRY(gemm16(s, s->h, w.pqkv, nullptr, qkvd, w.bqkv, M, qkvd, H, EPI_ROPE, &ra));
-    if (t == 0)
+    if (t == 0 && s->tc_prefill)
+      FWD_TRY(attention_prefill_tc_bf16(s->pbmaps, s->cur_user, l, c.layers, s->q, s->attn, M, c.heads, c.kv_heads, D,
+                                        cap, scale, s->d_status, st));
+    else if (t == 0)
       FWD_TRY(attention_prefill(s->q, kp, vp, s->attn, nullptr, nullptr, M, cap, c.heads, c.kv_heads, D, scale, true,
                                 st));
     else

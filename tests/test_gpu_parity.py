@@ -388,6 +388,15 @@ def test_tiny_bf16_against_the_bf16_oracle(cuda):
     assert max(s['max_abs_delta'] for s in stats) <= 0.5
 
 
+def test_tiny_bf16_ffma_prefill_attention_against_the_bf16_oracle(cuda, monkeypatch):
+    """RTR_PREFILL_ATTN=ffma keeps the bf16 mode's FFMA prefill attention
+    (the default is the tensor-core kernel)."""
+    monkeypatch.setenv('RTR_PREFILL_ATTN', 'ffma')
+    stats = bf16_case('tiny', 8, cuda, weight_backend='numpy')
+    assert min(s['overlap'] for s in stats) >= 25
+    assert max(s['max_abs_delta'] for s in stats) <= 0.5
+
+
 def test_1p5b_bf16_against_the_bf16_oracle(cuda):
     stats = bf16_case('qwen1.5b-bf16', 1, cuda)
     assert min(s['overlap'] for s in stats) >= 25
