@@ -197,9 +197,10 @@ typedef struct {
   int64_t tensor_core_gemm;       /* 2: tcgen05 fp16-pair projections (fp32
                                      default), 1: tcgen05 3xTF32, 0: FFMA      */
   int64_t norm_fold;              /* 1: RMSNorms folded into the GEMMs         */
-  int64_t decode_attention;       /* 0: per-head kernel (default), 1: tensor-
-                                     core folded kernel (RTR_ATTN=tc), 2: folded
-                                     FFMA cluster kernel (RTR_ATTN=folded)     */
+  int64_t decode_attention;       /* 0: per-head kernel (fp32 default,
+                                     RTR_ATTN=rows), 1: tensor-core folded
+                                     kernel (bf16 default, fp32 RTR_ATTN=tc),
+                                     2: folded FFMA kernel (RTR_ATTN=folded)   */
   int64_t prefill_attention;      /* 0: FFMA kernel, 1: tensor-core kernel
                                      (default; RTR_PREFILL_ATTN=ffma)          */
 } rtr_report;

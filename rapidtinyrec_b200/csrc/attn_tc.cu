@@ -1061,6 +1061,444 @@ __global__ void __launch_bounds__(AT_THREADS, 1) prefill_attn_tc_bf16_kernel(
   }
 }
 
+// The bf16 mode's decode attention on the tensor cores, for long prefixes
+// too: the cluster layout of decode_attn_tc_kernel (rows = a KV group's
+// (beam, head) pairs, 128 to a tile; ranks 0..6 the prefix, rank 7 the beams'
+// suffix keys on the FMA pipe; the partial (m, l, O) of the 8 ranks combined
+// through distributed shared memory in rank order), with every prefix rank
+// walking chunks rank, rank + 7, rank + 14, .. with an online softmax, so
+// prompts of any length the arena holds are served.  K comes by TMA straight
+// from the bf16 prefix arena, V from the transposed copy of the prefill; S is
+// one bf16 product, P a bf16 pair, the output rounded to bf16 once.
+template <int HD> struct DbCfg {
+  static constexpr int NC = HD / 64;
+  static constexpr int Q_BYTES = NC * AT_ROWS * 128;
+  static constexpr int K_BYTES = NC * AT_KEYS * 128;
+  static constexpr int V_BYTES = HD * 128;
+  static constexpr int P_BYTES = 2 * AT_ROWS * 128;
+  static constexpr int Q_OFF = 0, K_OFF = Q_BYTES, V_OFF = K_OFF + 2 * K_BYTES, P_OFF = V_OFF + V_BYTES;
+  static constexpr int PRE_BYTES = P_OFF + P_BYTES;
+  static constexpr int OLD = HD + 4;                     // partial O rows (fp32), over Q / K / V
+  static constexpr int SLD = HD + 8;                     // suffix staging rows (bf16)
+  static constexpr int S_COLS = AT_KEYS;
+  static constexpr int TMEM_COLS = 256;
+  // (m, l) per row, barriers, [2][4][128] row partials, [4][80] suffix rows, [16][128] partial dots
+  static constexpr int TAIL_BYTES = AT_ROWS * 8 + 64 + (2 * 4 * AT_ROWS + 4 * 80 + 16 * AT_ROWS) * 4;
+  static_assert(AT_ROWS * OLD * 4 <= P_OFF, "the partial O tile fits over q, k and v");
+  static_assert(2 * S_COLS + HD <= TMEM_COLS, "tensor memory");
+};
+template <int HD> constexpr int db_suffix_bytes(int hpg) {
+  return (AT_ROWS * DbCfg<HD>::SLD + 2 * 4 * at_tile_beams(hpg) * DbCfg<HD>::SLD) * 2;
+}
+template <int HD> constexpr int db_tail_off(int hpg) {
+  const int a = DbCfg<HD>::PRE_BYTES, b = db_suffix_bytes<HD>(hpg);
+  return ((a > b ? a : b) + 1023) / 1024 * 1024;
+}
+
+RTR_DEVICE float4 bf4_to_f4(uint2 u) {
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+template <int HD>
+__global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS, 1) decode_attn_tc_bf16_kernel(
+    const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, long krow, long kuser,
+    long vrow, long vuser, int cap, const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ ksuf,
+    const __nv_bfloat16* __restrict__ vsuf, const int32_t* __restrict__ anc, const int32_t* __restrict__ L_dev,
+    __nv_bfloat16* __restrict__ out, int beams, int heads, int kv_heads, int t, float scale,
+    uint32_t* __restrict__ status, int anc_user_stride, int tail_off) {
+  using C = DbCfg<HD>;
+  constexpr int OLD = C::OLD, SLD = C::SLD;
+  extern __shared__ __align__(1024) uint8_t db_smem_raw[];
+  uint8_t* smem = db_smem_raw + ((1024u - (smem_addr(db_smem_raw) & 1023u)) & 1023u);
+  uint8_t* qs = smem + C::Q_OFF;
+  uint8_t* kb = smem + C::K_OFF;  // [2] chunks
+  uint8_t* vs = smem + C::V_OFF;
+  uint8_t* ps = smem + C::P_OFF;
+  float* opart = reinterpret_cast<float*>(smem);  // [128][OLD] after the last product
+  float* ml = reinterpret_cast<float*>(smem + tail_off);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + tail_off + AT_ROWS * 8);
+  uint64_t* k_full = bars;      // [2]
+  uint64_t* v_full = bars + 2;
+  uint64_t* s_done = bars + 3;  // [2]
+  uint64_t* o_done = bars + 5;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 6);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6) + 1;
+  float* red = reinterpret_cast<float*>(smem + tail_off + AT_ROWS * 8 + 64);  // [2][4][128]
+  int* srows = reinterpret_cast<int*>(red + 2 * 4 * AT_ROWS);                // [4][nb <= 80]
+  float* sdot = reinterpret_cast<float*>(srows + 4 * 80);                    // [16][128]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lq = warp & 3, qt = warp >> 2, r = lq * 32 + lane;
+  const int rank = (int)cluster_rank();
+  const bool suffix_rank = rank == AT_CLUSTER - 1;
+  const int hpg = heads / kv_heads;
+  const int nrows = beams * hpg;
+  const int ug = blockIdx.z, u = ug / kv_heads, g = ug % kv_heads;
+  const int rt0 = blockIdx.y * AT_ROWS;
+  const int r0 = u * beams, rows_all = gridDim.z / kv_heads * beams;
+  anc += (long)u * anc_user_stride;
+  const long kr0 = krow + (long)u * kuser + (long)g * cap;
+  const long vr0 = vrow + (long)u * vuser + (long)g * HD;
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_addr(&k_full[i]), 1);
+      mbar_init(smem_addr(&s_done[i]), 1);
+    }
+    mbar_init(smem_addr(v_full), 1);
+    mbar_init(smem_addr(o_done), 1);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  if (warp == 0) tmem_alloc(smem_addr(tmem_slot), C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t o_tmem = tmem + 2 * C::S_COLS;
+  const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+  pdl_launch_dependents();
+  pdl_wait();  // q, the suffix rows and the prefix copies come from earlier kernels
+
+  int L = L_dev[u];
+  if (L < 1 || L > cap) {  // no valid prefix: attend to the suffix only
+    if (tid == 0 && rank == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
+    L = 0;
+  }
+  const int nch_all = (L + AT_KEYS - 1) / AT_KEYS;
+  const int nmine = suffix_rank || rank >= nch_all ? 0 : (nch_all - rank + AT_CLUSTER - 2) / (AT_CLUSTER - 1);
+
+  float m = -INFINITY, l = 0.f;
+  if (nmine > 0) {
+    auto chunk = [&](int i) { return rank + i * (AT_CLUSTER - 1); };
+    auto load_k = [&](int i) {
+      const uint32_t bar = smem_addr(&k_full[i & 1]);
+      uint8_t* dst = kb + (i & 1) * C::K_BYTES;
+      mbar_expect_tx(bar, C::K_BYTES);
+#pragma unroll
+      for (int cc = 0; cc < C::NC; ++cc)
+        tma_load_2d(smem_addr(dst + cc * AT_KEYS * 128), &kmap, cc * 64, (int)(kr0 + (long)chunk(i) * AT_KEYS), bar);
+    };
+    auto load_v = [&](int i) {
+      const uint32_t bar = smem_addr(v_full);
+      mbar_expect_tx(bar, C::V_BYTES);
+      tma_load_2d(smem_addr(vs), &vmap, chunk(i) * AT_KEYS, (int)vr0, bar);
+    };
+    auto issue_s = [&](int i) -> bool {
+      if (!mbar_wait(smem_addr(&k_full[i & 1]), (i >> 1) & 1, abort_flag)) return false;
+      tc_fence_after();
+      constexpr uint32_t id = idesc_bf16(AT_ROWS, AT_KEYS);
+      const uint32_t st = tmem + (i & 1) * C::S_COLS;
+      const uint8_t* kc = kb + (i & 1) * C::K_BYTES;
+#pragma unroll
+      for (int cc = 0; cc < C::NC; ++cc) {
+        const uint64_t qd = sw128_desc(smem_addr(qs + cc * AT_ROWS * 128));
+        const uint64_t kd = sw128_desc(smem_addr(kc + cc * AT_KEYS * 128));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) mma_f16_ss(st, qd + 2 * k, kd + 2 * k, id, (cc | k) ? 1u : 0u);
+      }
+      mma_commit(smem_addr(&s_done[i & 1]));
+      return true;
+    };
+    int k_issued = 0, v_issued = 0, s_issued = 0, o_issued = 0;
+    if (tid == 0) {
+      load_k(0);
+      k_issued = 1;
+      if (nmine > 1) {
+        load_k(1);
+        k_issued = 2;
+      }
+      load_v(0);
+      v_issued = 1;
+    }
+    {
+      // the tile's q rows (bf16) -> the A operand, zeros past the group's rows
+      constexpr int UPR = HD / 8, PER = AT_ROWS * UPR / AT_THREADS;
+      uint4 v[PER];
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int i = tid + k * AT_THREADS, rr = i / UPR, u8 = i % UPR, rh = rt0 + rr;
+        v[k] = rh < nrows ? *reinterpret_cast<const uint4*>(q + ((long)(r0 + rh / hpg) * heads + g * hpg + rh % hpg) * HD + 8 * u8)
+                          : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int i = tid + k * AT_THREADS, rr = i / UPR, u8 = i % UPR;
+        *reinterpret_cast<uint4*>(sw_unit(qs + (u8 >> 3) * AT_ROWS * 128, rr, u8 & 7)) = v[k];
+      }
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 32 && issue_s(0)) s_issued = 1;
+
+    constexpr int KQ = AT_KEYS / 4, DQ = HD / 4;
+    float o[DQ];
+#pragma unroll
+    for (int e = 0; e < DQ; ++e) o[e] = 0.f;
+    bool ok = true;
+    for (int i = 0; i < nmine; ++i) {
+      ok = mbar_wait(smem_addr(&s_done[i & 1]), (i >> 1) & 1, abort_flag);
+      if (__syncthreads_or(!ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (tid == 32 && i + 1 < nmine && issue_s(i + 1)) s_issued = i + 2;
+      if (tid == 0 && i + 2 < nmine) {
+        load_k(i + 2);
+        k_issued = i + 3;
+      }
+      float sv[KQ];
+      {
+        uint32_t sr[16];
+        tmem_ld16(tmem + (i & 1) * C::S_COLS + lane_base + qt * KQ, sr);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < KQ; ++j)
+          sv[j] = chunk(i) * AT_KEYS + qt * KQ + j < L ? __uint_as_float(sr[j]) * scale : -INFINITY;
+      }
+      float* rm = red + (i & 1) * 4 * AT_ROWS;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < KQ; ++j) mx = fmaxf(mx, sv[j]);
+      rm[qt * AT_ROWS + r] = mx;
+      __syncthreads();
+      // finite: the rank's first chunk holds key rank * 64 < L for every row
+      const float mn = fmaxf(m, fmaxf(fmaxf(rm[r], rm[AT_ROWS + r]), fmaxf(rm[2 * AT_ROWS + r], rm[3 * AT_ROWS + r])));
+      const float alpha = __expf(m - mn);
+      m = mn;
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < KQ; ++j) {
+        sv[j] = __expf(sv[j] - mn);
+        sum += sv[j];
+      }
+#pragma unroll
+      for (int un = 0; un < KQ / 8; ++un) put_bf16_pairs8(ps, ps + AT_ROWS * 128, r, qt * (KQ / 8) + un, sv + un * 8);
+      float* rs = red + ((i + 1) & 1) * 4 * AT_ROWS;
+      rs[qt * AT_ROWS + r] = sum;
+      fence_proxy_async();
+      tc_fence_before();
+      __syncthreads();
+      l = l * alpha + ((rs[r] + rs[AT_ROWS + r]) + (rs[2 * AT_ROWS + r] + rs[3 * AT_ROWS + r]));
+      if (tid == 32) {
+        if (mbar_wait(smem_addr(v_full), i & 1, abort_flag)) {
+          tc_fence_after();
+          constexpr uint32_t id = idesc_bf16(AT_ROWS, HD);
+          const uint64_t ph = sw128_desc(smem_addr(ps)), pl = sw128_desc(smem_addr(ps + AT_ROWS * 128));
+          const uint64_t vv = sw128_desc(smem_addr(vs));
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            mma_f16_ss(o_tmem, ph + 2 * k, vv + 2 * k, id, k ? 1u : 0u);
+            mma_f16_ss(o_tmem, pl + 2 * k, vv + 2 * k, id, 1u);
+          }
+          mma_commit(smem_addr(o_done));
+          o_issued = i + 1;
+        }
+      }
+      ok = mbar_wait(smem_addr(o_done), i & 1, abort_flag);
+      if (__syncthreads_or(!ok)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (tid == 0 && i + 1 < nmine) {
+        load_v(i + 1);
+        v_issued = i + 2;
+      }
+#pragma unroll
+      for (int cb = 0; cb < DQ; cb += 16) {
+        uint32_t ov[16];
+        tmem_ld16(o_tmem + lane_base + qt * DQ + cb, ov);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[cb + j] = fmaf(o[cb + j], alpha, __uint_as_float(ov[j]));
+      }
+      tc_fence_before();
+      __syncthreads();  // S(i), O(i), the K / V buffers and q are read
+    }
+    if (!ok) {
+      if (tid == 0) {
+        atomicOr(status, RTR_DEV_TIMEOUT);
+        for (int i = k_issued > 2 ? k_issued - 2 : 0; i < k_issued; ++i)
+          mbar_drain(smem_addr(&k_full[i & 1]), (i >> 1) & 1);
+        if (v_issued) mbar_drain(smem_addr(v_full), (v_issued - 1) & 1);
+      }
+      if (tid == 32) {
+        for (int i = s_issued > 2 ? s_issued - 2 : 0; i < s_issued; ++i)
+          mbar_drain(smem_addr(&s_done[i & 1]), (i >> 1) & 1);
+        if (o_issued) mbar_drain(smem_addr(o_done), (o_issued - 1) & 1);
+      }
+      __syncthreads();
+      m = -INFINITY;
+      l = 0.f;
+    } else {
+#pragma unroll
+      for (int e = 0; e < DQ; e += 4)
+        *reinterpret_cast<float4*>(opart + r * OLD + qt * DQ + e) = make_float4(o[e], o[e + 1], o[e + 2], o[e + 3]);
+    }
+  } else if (suffix_rank) {
+    // every row's t suffix keys of its beam on the FMA pipe, from bf16 q rows
+    // and the beams' K / V rows staged in shared memory
+    const int bfirst = rt0 / hpg, nb = at_tile_beams(hpg);
+    __nv_bfloat16* sq = reinterpret_cast<__nv_bfloat16*>(smem);  // [128][SLD]
+    __nv_bfloat16* sk = sq + AT_ROWS * SLD;                      // [4][nb][SLD]
+    __nv_bfloat16* sv = sk + 4 * nb * SLD;
+    for (int i = tid; i < AT_ROWS * (HD / 8); i += AT_THREADS) {
+      const int rr = i / (HD / 8), d = (i % (HD / 8)) * 8, rh = rt0 + rr;
+      const bool okr = rh < nrows;
+      const int bb = okr ? rh / hpg : 0, hh = g * hpg + (okr ? rh % hpg : 0);
+      cp_async16(sq + rr * SLD + d, q + ((long)(r0 + bb) * heads + hh) * HD + d, okr);
+    }
+    for (int i = tid; i < t * nb; i += AT_THREADS) {
+      const int sl = i / nb, bb = bfirst + i % nb;
+      int row = bb < beams ? bb : 0;
+      if (bb < beams && sl != t - 1) {
+        row = anc[bb * 4 + sl];
+        if (row < 0 || row >= beams) {
+          atomicOr(status, RTR_DEV_BAD_PARENT);
+          row = bb;
+        }
+      }
+      srows[i] = row;
+    }
+    __syncthreads();
+    for (int i = tid; i < t * nb * (HD / 8); i += AT_THREADS) {
+      const int sl = i / (nb * (HD / 8)), bi = (i / (HD / 8)) % nb, d = (i % (HD / 8)) * 8;
+      const bool okb = bfirst + bi < beams;
+      const long off = (((long)sl * rows_all + r0 + srows[sl * nb + bi]) * kv_heads + g) * HD + d;
+      cp_async16(sk + (sl * nb + bi) * SLD + d, ksuf + off, okb);
+      cp_async16(sv + (sl * nb + bi) * SLD + d, vsuf + off, okb);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    constexpr int DQ = HD / 4;
+    const int rho = rt0 + r;
+    const int bi = (rho < nrows ? rho / hpg : bfirst) - bfirst;
+    float dots[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int d0 = qt * DQ; d0 < qt * DQ + DQ; d0 += 4) {
+      const float4 qv = bf4_to_f4(*reinterpret_cast<const uint2*>(sq + r * SLD + d0));
+#pragma unroll
+      for (int sl = 0; sl < 4; ++sl) {
+        if (sl < t) {
+          const float4 kv = bf4_to_f4(*reinterpret_cast<const uint2*>(sk + (sl * nb + bi) * SLD + d0));
+          dots[sl] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, dots[sl]))));
+        }
+      }
+    }
+#pragma unroll
+    for (int sl = 0; sl < 4; ++sl) sdot[(qt * 4 + sl) * AT_ROWS + r] = dots[sl];
+    __syncthreads();
+    float pr[4];
+#pragma unroll
+    for (int sl = 0; sl < 4; ++sl) {
+      const float dsum = (sdot[sl * AT_ROWS + r] + sdot[(4 + sl) * AT_ROWS + r]) +
+                         (sdot[(8 + sl) * AT_ROWS + r] + sdot[(12 + sl) * AT_ROWS + r]);
+      dots[sl] = sl < t ? dsum * scale : -INFINITY;
+      m = fmaxf(m, dots[sl]);
+    }
+#pragma unroll
+    for (int sl = 0; sl < 4; ++sl) {
+      pr[sl] = sl < t ? __expf(dots[sl] - m) : 0.f;
+      l += pr[sl];
+    }
+    float4 ov[DQ / 4];
+#pragma unroll
+    for (int e = 0; e < DQ / 4; ++e) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int sl = 0; sl < 4; ++sl) {
+        if (sl < t) {
+          const float4 vv = bf4_to_f4(*reinterpret_cast<const uint2*>(sv + (sl * nb + bi) * SLD + qt * DQ + 4 * e));
+          acc.x = fmaf(pr[sl], vv.x, acc.x); acc.y = fmaf(pr[sl], vv.y, acc.y);
+          acc.z = fmaf(pr[sl], vv.z, acc.z); acc.w = fmaf(pr[sl], vv.w, acc.w);
+        }
+      }
+      ov[e] = acc;
+    }
+    __syncthreads();  // the staged rows are read: opart overlays them
+#pragma unroll
+    for (int e = 0; e < DQ / 4; ++e) *reinterpret_cast<float4*>(opart + r * OLD + qt * DQ + 4 * e) = ov[e];
+  }
+  if (qt == 0) {
+    ml[2 * r] = m;
+    ml[2 * r + 1] = l;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  cluster_barrier_tc();
+  {
+    // rank k finishes rows 16 k .. 16 k + 15: 32 threads per row, HD / 32 dims each
+    constexpr int DPT = HD / 32;
+    const int rr = 16 * rank + (tid >> 5), d0 = lane * DPT;
+    const uint32_t ml_a = smem_addr(ml + 2 * rr), o_a = smem_addr(opart + rr * OLD + d0);
+    const int nfull = nch_all < AT_CLUSTER - 1 ? nch_all : AT_CLUSTER - 1;  // prefix ranks holding keys
+    float2 mine = make_float2(-INFINITY, 0.f);
+    if (lane < AT_CLUSTER && (lane < nfull || lane == AT_CLUSTER - 1))
+      mine = ld_cluster_f32x2_tc(cluster_map(ml_a, lane));
+    float2 mlj[AT_CLUSTER];
+    float oj[AT_CLUSTER][DPT];
+#pragma unroll
+    for (int j = 0; j < AT_CLUSTER; ++j) {
+      mlj[j].x = __shfl_sync(0xffffffffu, mine.x, j);
+      mlj[j].y = __shfl_sync(0xffffffffu, mine.y, j);
+#pragma unroll
+      for (int e = 0; e < DPT; ++e) oj[j][e] = 0.f;
+      if ((j < nfull || j == AT_CLUSTER - 1) && mlj[j].y > 0.f) {
+        if constexpr (DPT == 4) {
+          const float4 v = ld_cluster_f32x4(cluster_map(o_a, j));
+          oj[j][0] = v.x; oj[j][1] = v.y; oj[j][2] = v.z; oj[j][3] = v.w;
+        } else {
+          const float2 v = ld_cluster_f32x2_tc(cluster_map(o_a, j));
+          oj[j][0] = v.x; oj[j][1] = v.y;
+        }
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < AT_CLUSTER; ++j) M = fmaxf(M, mlj[j].x);
+    float Ls = 0.f;
+    float o[DPT];
+#pragma unroll
+    for (int e = 0; e < DPT; ++e) o[e] = 0.f;
+#pragma unroll
+    for (int j = 0; j < AT_CLUSTER; ++j) {  // rank order
+      const float w = mlj[j].y > 0.f ? expf(mlj[j].x - M) : 0.f;
+      Ls = fmaf(w, mlj[j].y, Ls);
+#pragma unroll
+      for (int e = 0; e < DPT; ++e) o[e] = fmaf(w, oj[j][e], o[e]);
+    }
+    const int rh = rt0 + rr;
+    if (rh < nrows) {
+      const int bb = rh / hpg, hh = g * hpg + rh % hpg;
+      const float inv = 1.0f / Ls;
+      __nv_bfloat16* dst = out + ((long)(r0 + bb) * heads + hh) * HD + d0;
+      if constexpr (DPT == 4) {
+        const __nv_bfloat162 a = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
+        const __nv_bfloat162 b = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
+        uint2 w;
+        w.x = *reinterpret_cast<const uint32_t*>(&a);
+        w.y = *reinterpret_cast<const uint32_t*>(&b);
+        *reinterpret_cast<uint2*>(dst) = w;
+      } else {
+        *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
+      }
+    }
+  }
+  cluster_barrier_tc();  // no CTA leaves while a peer still reads its shared memory
+}
+
 // Largest dynamic shared memory a CTA may take (227 KB) minus the alignment slack.
 constexpr int AT_SMEM_MAX = 227 * 1024 - 1024;
 
@@ -1182,6 +1620,55 @@ cudaError_t attention_prefill_tc_bf16(const BfPrefillMaps& mp, int user, int lay
   return launch_prefill_tc_bf16<64>(mp, user, layer, q, out, L, heads, kv_heads, cap, scale, status, stream, layers);
 }
 
+bool attention_decode_tc_bf16_supported(int heads, int kv_heads, int head_dim) {
+  if (kv_heads < 1 || heads % kv_heads || (head_dim != 64 && head_dim != 128)) return false;
+  const int hpg = heads / kv_heads;
+  if (at_tile_beams(hpg) > 80) return false;
+  const int off = head_dim == 128 ? db_tail_off<128>(hpg) : db_tail_off<64>(hpg);
+  return off + (head_dim == 128 ? DbCfg<128>::TAIL_BYTES : DbCfg<64>::TAIL_BYTES) <= AT_SMEM_MAX;
+}
+
+template <int HD>
+static cudaError_t launch_decode_tc_bf16(const BfPrefillMaps& mp, int layer, int layers, const void* q, const void* ks,
+                                         const void* vs, const int32_t* anc, const int32_t* L_dev, int t, void* out,
+                                         int beams, int cap, int heads, int kv_heads, float scale, uint32_t* status,
+                                         cudaStream_t stream, const DecodeUsers& du) {
+  const int hpg = heads / kv_heads;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(AT_CLUSTER, (beams * hpg + AT_ROWS - 1) / AT_ROWS, du.users * kv_heads);
+  cfg.blockDim = dim3(AT_THREADS);
+  const int tail_off = db_tail_off<HD>(hpg);
+  cfg.dynamicSmemBytes = 1024 + tail_off + DbCfg<HD>::TAIL_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_on(PDL_ATTN) ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const long krow = (long)layer * 2 * kv_heads * cap, kuser = (long)layers * 2 * kv_heads * cap;
+  const long vrow = (long)layer * kv_heads * HD, vuser = (long)layers * kv_heads * HD;
+  return cudaLaunchKernelEx(&cfg, decode_attn_tc_bf16_kernel<HD>, *reinterpret_cast<const CUtensorMap*>(&mp.kmap),
+                            *reinterpret_cast<const CUtensorMap*>(&mp.vmap), krow, kuser, vrow, vuser, cap,
+                            static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(ks),
+                            static_cast<const __nv_bfloat16*>(vs), anc, L_dev, static_cast<__nv_bfloat16*>(out),
+                            beams, heads, kv_heads, t, scale, status, du.anc_user_stride, tail_off);
+}
+
+cudaError_t attention_decode_tc_bf16(const BfPrefillMaps& mp, int layer, int layers, const void* q,
+                                     const void* k_suffix, const void* v_suffix, const int32_t* anc,
+                                     const int32_t* L_dev, int t, void* out, int beams, int prefix_cap, int heads,
+                                     int kv_heads, int head_dim, float scale, uint32_t* status, cudaStream_t stream,
+                                     const DecodeUsers& du) {
+  if (t < 1 || t > 4 || beams > MAX_BEAMS || du.users < 1 || prefix_cap > mp.pair_cap ||
+      !attention_decode_tc_bf16_supported(heads, kv_heads, head_dim))
+    return cudaErrorInvalidValue;
+  if (head_dim == 128)
+    return launch_decode_tc_bf16<128>(mp, layer, layers, q, k_suffix, v_suffix, anc, L_dev, t, out, beams, prefix_cap,
+                                      heads, kv_heads, scale, status, stream, du);
+  return launch_decode_tc_bf16<64>(mp, layer, layers, q, k_suffix, v_suffix, anc, L_dev, t, out, beams, prefix_cap,
+                                   heads, kv_heads, scale, status, stream, du);
+}
+
 cudaError_t attention_tc_init() {
   // the most a supported launch takes (the suffix staging grows as hpg falls)
   cudaError_t e = cudaFuncSetAttribute(decode_attn_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1201,6 +1688,12 @@ cudaError_t attention_tc_init() {
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(prefill_attn_tc_bf16_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              PbCfg<64>::SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_tc_bf16_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AT_SMEM_MAX + 1024);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(decode_attn_tc_bf16_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             AT_SMEM_MAX + 1024);
   return e;
 }
 

@@ -220,6 +220,14 @@ struct BfPrefillMaps {
 cudaError_t attention_prefill_tc_bf16(const BfPrefillMaps& mp, int user, int layer, int layers, const void* q,
                                       void* out, int L, int heads, int kv_heads, int head_dim, int cap, float scale,
                                       uint32_t* status, cudaStream_t stream);
+// The bf16 mode's decode attention on the tensor cores (any prefix the arena
+// holds; the same arena map and V copy as the prefill kernel).
+bool attention_decode_tc_bf16_supported(int heads, int kv_heads, int head_dim);
+cudaError_t attention_decode_tc_bf16(const BfPrefillMaps& mp, int layer, int layers, const void* q,
+                                     const void* k_suffix, const void* v_suffix, const int32_t* anc,
+                                     const int32_t* L_dev, int t, void* out, int beams, int prefix_cap, int heads,
+                                     int kv_heads, int head_dim, float scale, uint32_t* status, cudaStream_t stream,
+                                     const DecodeUsers& du);
 bool attention_folded_supported(int heads, int kv_heads, int head_dim, bool bf16);
 
 // ---- constraints + beam step (beam.cu) ----

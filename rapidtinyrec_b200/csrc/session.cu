@@ -86,7 +86,8 @@ struct rtr_session {
   // tensor-core decode attention: the prefix K / V as fp16 pairs, written by the prefill
   bool tc_attn = false;
   bool tc_prefill = false;  // prefill attention on the tensor cores (attn_tc.cu)
-  uint16_t* vt_bf16 = nullptr;  // bf16 mode: V transposed per (user, layer, group) for it
+  uint16_t* vt_bf16 = nullptr;  // bf16 mode: V transposed per (user, layer, group) for the tensor-core attention
+  bool tc_attn_bf16 = false;    // bf16 mode: decode attention on the tensor cores (attn_tc.cu)
   BfPrefillMaps pbmaps = {};
   __half* kvpair = nullptr;  // [K hi][K lo][V^T hi][V^T lo] planes
   AttnPairs pairs{};
@@ -313,7 +314,11 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
     const char* pe = getenv("RTR_PREFILL_ATTN");
     s->tc_prefill = !(pe && strcmp(pe, "ffma") == 0) && (s->bf16 || s->use_tc) &&
                     attention_prefill_tc_supported(c.heads, c.kv_heads, D);
-    if (s->tc_prefill && s->bf16) {
+    // the bf16 decode attention: the tensor-core kernel unless RTR_ATTN=rows or
+    // =folded names another one; it reads the prefix arena and V copy below
+    s->tc_attn_bf16 = s->bf16 && !(e && (strcmp(e, "rows") == 0 || strcmp(e, "folded") == 0)) &&
+                      attention_decode_tc_bf16_supported(c.heads, c.kv_heads, D);
+    if (s->bf16 && (s->tc_prefill || s->tc_attn_bf16)) {
       const int pc = (cap + 63) / 64 * 64;
       const long vt_rows = (long)U * c.layers * c.kv_heads * D;
       CREATE_TRY(dev_alloc(s, &s->vt_bf16, (size_t)vt_rows * pc));
@@ -777,6 +782,10 @@ static cudaError_t decode_attention(rtr_session* s, int l, const void* kp, const
                                     const void* vs, int t, float* ob, float* os, float scale, const DecodeUsers& du) {
   const auto& c = s->cfg;
   const int D = c.head_dim;
+  if (s->tc_attn_bf16)
+    return attention_decode_tc_bf16(s->pbmaps, l, c.layers, s->q, ks, vs, &s->beam->anc[0][0], s->d_L, t, s->attn,
+                                    beams_of(s), c.max_prefix, c.heads, c.kv_heads, D, scale, s->d_status, s->stream,
+                                    du);
   if (s->tc_attn) {
     AttnPairs ap = s->pairs;
     ap.krow0 = (long)l * c.kv_heads * ap.pair_cap;
@@ -829,7 +838,7 @@ static cudaError_t forward_bf16(rtr_session* s, int t) {
     RopeArgs ra{s->rope_cos, s->rope_sin, s->rope_positions, c.heads, c.kv_heads, D, s->q,
                 reinterpret_cast<float*>(t == 0 ? kp : ks + slot),
                 reinterpret_cast<float*>(t == 0 ? vp : vs + slot), cap, t == 0 ? -1 : t - 1, s->d_L, B};
-    if (t == 0 && s->tc_prefill) {  // the epilogue also writes V transposed for the prefill attention
+    if (t == 0 && s->vt_bf16) {  // the epilogue also writes V transposed for the tensor-core attention
       ra.vtpair_hi = s->vt_bf16 + (((long)s->cur_user * c.layers + l) * c.kv_heads) * D * s->pbmaps.pair_cap;
       ra.pair_cap = s->pbmaps.pair_cap;
     }
@@ -1198,7 +1207,7 @@ int rtr_get_report(const rtr_session* s, rtr_report* out) {
   out->d2h_bytes_per_request = (int64_t)sizeof(DevResult);
   out->tensor_core_gemm = s->use_tc ? (s->xfmt == SPLIT_F16 ? 2 : 1) : 0;
   out->norm_fold = s->fold ? 1 : 0;
-  out->decode_attention = s->tc_attn ? 1 : s->folded_attn ? 2 : 0;
+  out->decode_attention = s->tc_attn || s->tc_attn_bf16 ? 1 : s->folded_attn ? 2 : 0;
   out->prefill_attention = s->tc_prefill ? 1 : 0;
   return RTR_OK;
 }

@@ -7,6 +7,7 @@ Bars (from the reference's own acceptance rules):
   score equals the sequential FP32 sum of the five transitions.
 """
 import json
+import os
 
 import numpy as np
 import pytest
@@ -364,6 +365,10 @@ def bf16_case(name, n_users, cuda, weight_backend='native'):
     else:
         weights = workload.synth_weights(cfg, seed=wl.weight_seed, device='cuda')
     eng = make_engine(cfg, weights, cons, max_prefix=max(u.prompt_tokens for u in users))
+    rep = eng.report()
+    want_attn = 0 if os.environ.get('RTR_ATTN') == 'rows' else 1
+    assert rep['decode_attention'] == want_attn and rep['prefill_attention'] == (
+        0 if os.environ.get('RTR_PREFILL_ATTN') == 'ffma' else 1)
     cpu_w = {k: v.cpu() for k, v in weights.items()}
     del weights
     torch.cuda.empty_cache()
@@ -392,6 +397,15 @@ def test_tiny_bf16_ffma_prefill_attention_against_the_bf16_oracle(cuda, monkeypa
     """RTR_PREFILL_ATTN=ffma keeps the bf16 mode's FFMA prefill attention
     (the default is the tensor-core kernel)."""
     monkeypatch.setenv('RTR_PREFILL_ATTN', 'ffma')
+    stats = bf16_case('tiny', 8, cuda, weight_backend='numpy')
+    assert min(s['overlap'] for s in stats) >= 25
+    assert max(s['max_abs_delta'] for s in stats) <= 0.5
+
+
+def test_tiny_bf16_per_head_decode_attention_against_the_bf16_oracle(cuda, monkeypatch):
+    """RTR_ATTN=rows keeps the bf16 mode's per-head decode attention (the
+    default is the tensor-core cluster kernel)."""
+    monkeypatch.setenv('RTR_ATTN', 'rows')
     stats = bf16_case('tiny', 8, cuda, weight_backend='numpy')
     assert min(s['overlap'] for s in stats) >= 25
     assert max(s['max_abs_delta'] for s in stats) <= 0.5
