@@ -131,18 +131,21 @@ RTR_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory")
 RTR_DEVICE void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }
 
 // Programmatic dependent launch (PDL) policy per kernel class.  RTR_PDL is a
-// comma-separated list of classes launched with PDL ("gemm", "norm", "rope",
-// "attn", "embed", "gemv", "tail"), "0" for none, "all" for every class.
-// Read once per process.  The default leaves RMSNorm and RoPE on plain
-// launches: measured on the 1.5B decode, PDL on RMSNorm cost 1.9 ms per
-// request (4 ms with 64-thread norm CTAs that fit beside a GEMM CTA, so SM
-// co-residency is not the cause), on RoPE 0.2 ms, while the GEMM, attention,
-// embedding, GEMV and beam-tail launches each gained.
+// comma-separated list of classes launched with PDL ("gemm", "norm" (fp32
+// RMSNorm), "rope", "attn", "embed", "gemv", "tail", "rms16" (the bf16 mode's
+// RMSNorm)), "0" for none, "all" for every class.  Read once per process.
+// The default leaves the fp32 RMSNorm and RoPE on plain launches: measured on
+// the 1.5B decode, PDL on RMSNorm cost 1.9 ms per request (4 ms with 64-thread
+// norm CTAs that fit beside a GEMM CTA, so SM co-residency is not the cause),
+// on RoPE 0.2 ms, while the GEMM, attention, embedding, GEMV and beam-tail
+// launches each gained.
 enum PdlClass : unsigned {
   PDL_GEMM = 1u, PDL_NORM = 2u, PDL_ROPE = 4u, PDL_ATTN = 8u, PDL_EMBED = 16u, PDL_GEMV = 32u, PDL_TAIL = 64u,
-  PDL_ALL = 127u
+  PDL_NORM16 = 128u, PDL_ALL = 255u
 };
-constexpr unsigned kPdlDefault = PDL_GEMM | PDL_ATTN | PDL_EMBED | PDL_GEMV | PDL_TAIL;
+// The bf16 mode's RMSNorm (between its GEMMs) gains from it: decode steps
+// 2.09 -> 2.01 ms at 1.5B, 4.06 -> 3.99 ms at 7B (A/B on one box).
+constexpr unsigned kPdlDefault = PDL_GEMM | PDL_ATTN | PDL_EMBED | PDL_GEMV | PDL_TAIL | PDL_NORM16;
 inline unsigned pdl_mask() {
   static const unsigned mask = [] {
     const char* e = getenv("RTR_PDL");
@@ -150,7 +153,7 @@ inline unsigned pdl_mask() {
     if (strcmp(e, "all") == 0) return (unsigned)PDL_ALL;
     static const struct { const char* name; unsigned bit; } names[] = {
         {"gemm", PDL_GEMM}, {"norm", PDL_NORM}, {"rope", PDL_ROPE}, {"attn", PDL_ATTN},
-        {"embed", PDL_EMBED}, {"gemv", PDL_GEMV}, {"tail", PDL_TAIL}};
+        {"embed", PDL_EMBED}, {"gemv", PDL_GEMV}, {"tail", PDL_TAIL}, {"rms16", PDL_NORM16}};
     unsigned m = 0;
     for (const auto& n : names)
       if (strstr(e, n.name)) m |= n.bit;

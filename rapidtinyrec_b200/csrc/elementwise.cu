@@ -157,7 +157,7 @@ __global__ void rms_norm_bf16_kernel(const __nv_bfloat16* x, const float* w, __n
 
 cudaError_t rms_norm_rows_bf16(const void* x, const float* w, void* h, int M, int hidden, float eps,
                                cudaStream_t stream) {
-  return launch_pdl(PDL_NORM, rms_norm_bf16_kernel, dim3(M), dim3(256), 0, stream,
+  return launch_pdl(PDL_NORM16, rms_norm_bf16_kernel, dim3(M), dim3(256), 0, stream,
                     static_cast<const __nv_bfloat16*>(x), w, static_cast<__nv_bfloat16*>(h), hidden, eps);
 }
 
