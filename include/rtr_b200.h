@@ -225,6 +225,18 @@ int rtr_profile_gemms(rtr_session* s, int32_t M, int32_t reps, float* ms_per_pas
 int rtr_gemm_check(int32_t device, const float* x_dev, const float* w_dev, float* c_dev, int32_t M, int32_t N,
                    int32_t K, int32_t kernel);
 
+/* Test hook (no reference counterpart): causal prefill attention of one layer
+ * of one user, out[L, heads, D] = softmax(q k^T / sqrt(D), causal) v with the
+ * query heads of KV group g = h / (heads / kv_heads) reading k, v [g] (fp32,
+ * row-major, device pointers; k and v [kv_heads, L, D]) through one kernel:
+ * 0 the FFMA kernel, 1 the tensor-core fp16-pair kernel, 2 the bf16 FFMA
+ * kernel and 3 the bf16 tensor-core kernel (2 and 3: q, k, v rounded to bf16
+ * first, out holds the bf16 results).  head_dim 64 or 128.  Builds the arena
+ * and copies the kernel reads; scratch is allocated per call; blocks until
+ * done. */
+int rtr_attention_check(int32_t device, const float* q_dev, const float* k_dev, const float* v_dev, float* out_dev,
+                        int32_t L, int32_t heads, int32_t kv_heads, int32_t head_dim, int32_t kernel);
+
 /* Test hook (no reference counterpart; the reference's failure handling is
  * Python exceptions): on `device`, bound every pipeline wait of the
  * fp16-pair and bf16 tensor-core GEMMs to wait_cycles (default 2e9, ~1 s) and,

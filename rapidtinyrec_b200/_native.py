@@ -24,7 +24,7 @@ EXPORTS = (
     'rtr_synth_fill_host', 'rtr_synth_fill_device', 'rtr_launch', 'rtr_wait', 'rtr_get_report',
     'rtr_profile_gemms', 'rtr_constraint_process_static', 'rtr_gemm_check',
     'rtr_session_create_batched', 'rtr_launch_batch', 'rtr_wait_batch', 'rtr_generate_batch',
-    'rtr_debug_wait_control',
+    'rtr_debug_wait_control', 'rtr_attention_check',
 )
 
 
@@ -114,6 +114,7 @@ def load():
         'rtr_generate_batch': (P, P, P, I32, ctypes.POINTER(ResultC)),
         'rtr_constraint_process_static': (P, I32, P, I32, I32, P, P),
         'rtr_debug_wait_control': (I32, I64, I32),
+        'rtr_attention_check': (I32, P, P, P, P, I32, I32, I32, I32, I32),
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
@@ -161,6 +162,21 @@ def gemm(x, w, kernel=0):
     torch.cuda.synchronize(x.device)
     check(load().rtr_gemm_check(x.device.index or 0, x.data_ptr(), w.data_ptr(), c.data_ptr(), M, N, K, kernel))
     return c
+
+
+def attention(q, k, v, kernel):
+    """Causal prefill attention of one layer through one kernel
+    (``rtr_attention_check``): q [L, heads, D], k and v [kv_heads, L, D], fp32
+    CUDA tensors; 0 FFMA, 1 tensor-core fp16 pairs, 2 bf16 FFMA, 3 bf16 tensor
+    core."""
+    import torch
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    L, heads, D = q.shape
+    out = torch.empty_like(q)
+    torch.cuda.synchronize(q.device)
+    check(load().rtr_attention_check(q.device.index or 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                     L, heads, k.shape[0], D, kernel))
+    return out
 
 
 DEFAULT_WAIT_CYCLES = 2_000_000_000
