@@ -1,28 +1,38 @@
-// Decode attention on the 5th-generation tensor cores, fp32-accurate through
-// fp16 pairs (the scheme of the projection GEMM, gemm_f16x2.cu).
+// Attention on the 5th-generation tensor cores: the decode and prefill
+// attention of the fp32 mode, fp32-accurate through fp16 pairs (the scheme of
+// the projection GEMM, gemm_f16x2.cu), and of the bf16 mode with bf16
+// operands.
 //
 // The reference folds the query heads that share a KV head into rows
 // (rapidtinyrec/folded_attention.py:16-31).  Here the rows of KV group g are
-// its (beam, head) pairs, 128 to a tile (the MMA's M), and a thread-block
-// cluster of 8 CTAs covers one (user, group, row tile):
+// its (beam, head) pairs in decode and its (token, head) pairs in prefill,
+// 128 to a tile (the MMA's M).  K and V come by TMA in 64-key chunks (the
+// 128-byte swizzle): in fp32 from the fp16-pair copies the prefill's q/k/v
+// epilogue writes (K as [key][dim], V transposed as [dim][key], hi and lo
+// planes), in bf16 K straight from the prefix arena and V from a transposed
+// bf16 copy.  Per chunk, a thread per (row, quarter of the keys / dims):
+//   S = q.k^T in TMEM (fp32: q_hi.[k_hi; k_lo]^T (N = 128) + q_lo.k_hi^T
+//       (N = 64); bf16: one product);
+//   the row's softmax over the chunk from tcgen05.ld, P back to shared memory
+//       as a pair (fp16 or bf16 hi / lo);
+//   O = P.V in TMEM (fp32: p_hi.[v_hi; v_lo] (N = 2 head_dim) + p_lo.v_hi;
+//       bf16: p_hi.v + p_lo.v).
+// The dropped lo.lo terms are 2^-22 relative (fp16 pairs).
 //
-//   ranks 0..6  one 64-key chunk of the shared prefix each (prompts of up to
-//               448 tokens), staged by TMA from the pair copies the prefill's
-//               q/k/v epilogue wrote (K as [key][dim], V transposed as
-//               [dim][key], hi and lo fp16 planes, 128-byte swizzle);
-//   rank 7      every beam's own suffix keys (at most 4, found through the
-//               ancestry table: the direct-reorder parent gather without
-//               moving bytes), on the FMA pipe.
-//
-// A prefix rank, thread = row (TMEM lane):
-//   q (fp32) -> pair planes in shared memory (the A operand);
-//   S  = q_hi.[k_hi; k_lo]^T (N = 128) + q_lo.k_hi^T (N = 64)   tcgen05 kind::f16
-//   softmax of the row over the chunk in registers (tcgen05.ld), P -> pair planes;
-//   O  = p_hi.[v_hi; v_lo] (N = 2 head_dim) + p_lo.v_hi (N = head_dim);
-//   partial (m, l, O) of the row into shared memory.
-// The dropped q_lo.k_lo and p_lo.v_lo terms are 2^-22 relative.  The 8 ranks'
-// partials meet through distributed shared memory: rank r finishes rows
-// 16 r .. 16 r + 15, summing the ranks in rank order (the same bits every run).
+//   decode_attn_tc_kernel (fp32, RTR_ATTN=tc): a thread-block cluster of 8
+//       CTAs per (user, group, row tile): ranks 0..6 one 64-key chunk of the
+//       shared prefix each (prompts of up to 448 tokens), rank 7 every beam's
+//       own suffix keys (at most 4, found through the ancestry table: the
+//       direct-reorder parent gather without moving bytes) on the FMA pipe;
+//       the 8 partial (m, l, O) meet through distributed shared memory, rank
+//       r finishing rows 16 r .. 16 r + 15 in rank order (the same bits every
+//       run);
+//   decode_attn_tc_bf16_kernel (bf16 default): the same cluster, prefix rank
+//       r walking chunks r, r + 7, .. with an online softmax (any prompt the
+//       arena holds);
+//   prefill_attn_tc_kernel / _bf16_kernel (defaults): one CTA per tile walks
+//       the causal key range with an online softmax, the next chunk's scores
+//       computed while the threads run the current softmax.
 // Every wait is bounded; a wait that runs out sets RTR_DEV_TIMEOUT.
 #include <cuda.h>
 #include <cuda_bf16.h>
