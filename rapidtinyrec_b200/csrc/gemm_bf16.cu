@@ -169,13 +169,43 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
 }
 
 // Split-K sum (a CTA finishing a tile): rows [row0, row0 + rows) of the
-// partials summed in split order into the same rows of a [64][128] shared tile.
+// partials summed in split order into the same rows of a [64][128] shared
+// tile.  Each round of loads is one L2 round trip, so the sum takes whichever
+// order needs fewer rounds: every split (up to KS_MAX) of two float4 slots per
+// thread at once, or every slot two splits at a time.
 RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int row0, int rows, int cols4, int tile, long tstride) {
   constexpr int SLOTS = (BF_NTOK * BF_WROWS / 4 + BF_THREADS - 1) / BF_THREADS;
   const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (BF_NTOK * BF_WROWS)) + row0 * 32;
   red4 += row0 * 32;
   const long zs = tstride >> 2;
   const int nslots = rows * (BF_WROWS / 4);
+  const int active = (nslots + BF_THREADS - 1) / BF_THREADS;  // slots a thread holds
+  if (p.splits <= KS_MAX && (active + 1) / 2 < (p.splits + 1) / 2) {
+    constexpr int PS = 2;
+#pragma unroll 1
+    for (int u0 = 0; u0 < SLOTS && u0 * BF_THREADS < nslots; u0 += PS) {
+      float4 v[PS][KS_MAX];
+#pragma unroll
+      for (int u = 0; u < PS; ++u)
+#pragma unroll
+        for (int z = 0; z < KS_MAX; ++z) {
+          const int q = threadIdx.x + (u0 + u) * BF_THREADS;
+          const bool ok = u0 + u < SLOTS && z < p.splits && q < nslots && (q & 31) < cols4;
+          v[u][z] = ok ? __ldcg(base + z * zs + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int u = 0; u < PS; ++u) {
+        const int q = threadIdx.x + (u0 + u) * BF_THREADS;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int z = 0; z < KS_MAX; ++z)
+          if (z < p.splits) acc = f4add(acc, v[u][z]);  // split order
+        if (u0 + u < SLOTS && q < nslots) red4[q] = acc;
+      }
+    }
+    __syncthreads();
+    return;
+  }
   float4 s[SLOTS];
 #pragma unroll
   for (int u = 0; u < SLOTS; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -192,7 +222,8 @@ RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int row0, int row
 #pragma unroll
     for (int dz = 0; dz < 2; ++dz)
 #pragma unroll
-      for (int u = 0; u < SLOTS; ++u) s[u] = f4add(s[u], v[dz][u]);
+      for (int u = 0; u < SLOTS; ++u)
+        if (z + dz < p.splits) s[u] = f4add(s[u], v[dz][u]);  // split order
   }
 #pragma unroll
   for (int u = 0; u < SLOTS; ++u) {

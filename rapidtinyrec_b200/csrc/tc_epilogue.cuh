@@ -119,22 +119,54 @@ constexpr int FTILE_COLS = 128;  // output columns of a tensor-core GEMM tile
 
 // Split-K sum, run by every thread of a CTA finishing a tile: rows
 // [row0, row0 + rows) of the partial tiles summed in split order into the same
-// rows of a [NTOK][128] shared tile (float4 slots, four splits of loads in
-// flight per slot).
+// rows of a [NTOK][128] shared tile.  Each round of loads is one L2 round trip,
+// so the sum takes whichever order needs fewer rounds: every split (up to
+// KS_MAX) of two float4 slots per thread in flight at once - a decode slice
+// (13 or 25 rows, 8 or 12 splits) then takes 1-2 rounds instead of 2-6 - or
+// groups of G slots four splits at a time (prefill slices: many slots, few
+// splits).
+constexpr int KS_MAX = 12;
 template <int THREADS, int NTOK>
 RTR_DEVICE void splitk_sum(const TcParams& p, float4* red4, int row0, int rows, int cols4, int tile, long tstride) {
   constexpr int SLOTS = (NTOK * 128 / 4 + THREADS - 1) / THREADS;
+  constexpr int G = SLOTS < 6 ? SLOTS : 3;
   const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (NTOK * 128)) + row0 * 32;
   red4 += row0 * 32;
   const long zs = tstride >> 2;
   const int nslots = rows * 32;
+  const int active = (nslots + THREADS - 1) / THREADS;  // slots a thread holds
+  if (NTOK == 64 && p.splits <= KS_MAX && (active + 1) / 2 < (active + G - 1) / G * ((p.splits + 3) / 4)) {
+    constexpr int PS = 2;  // slots in flight per thread (registers: 2 x 12 float4)
+#pragma unroll 1
+    for (int u0 = 0; u0 < SLOTS && u0 * THREADS < nslots; u0 += PS) {
+      float4 v[PS][KS_MAX];
+#pragma unroll
+      for (int u = 0; u < PS; ++u)
+#pragma unroll
+        for (int z = 0; z < KS_MAX; ++z) {
+          const int q = threadIdx.x + (u0 + u) * THREADS;
+          const bool ok = u0 + u < SLOTS && z < p.splits && q < nslots && (q & 31) < cols4;
+          v[u][z] = ok ? __ldcg(base + z * zs + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int u = 0; u < PS; ++u) {
+        const int q = threadIdx.x + (u0 + u) * THREADS;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int z = 0; z < KS_MAX; ++z)
+          if (z < p.splits) acc = f4add(acc, v[u][z]);  // split order
+        if (u0 + u < SLOTS && q < nslots) red4[q] = acc;
+      }
+    }
+    __syncthreads();
+    return;
+  }
   // slots in groups of G keep four splits of loads in flight without running out of registers
-  constexpr int G = SLOTS < 6 ? SLOTS : 3;
 #pragma unroll 1
   for (int u0 = 0; u0 < SLOTS && u0 * THREADS < nslots; u0 += G) {
-    float4 s[G];
+    float4 acc[G];
 #pragma unroll
-    for (int u = 0; u < G; ++u) s[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int u = 0; u < G; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int z = 0; z < p.splits; z += 4) {
       float4 v[4][G];
 #pragma unroll
@@ -148,12 +180,13 @@ RTR_DEVICE void splitk_sum(const TcParams& p, float4* red4, int row0, int rows, 
 #pragma unroll
       for (int dz = 0; dz < 4; ++dz)
 #pragma unroll
-        for (int u = 0; u < G; ++u) s[u] = f4add(s[u], v[dz][u]);  // split order (zero adds are exact)
+        for (int u = 0; u < G; ++u)
+          if (z + dz < p.splits) acc[u] = f4add(acc[u], v[dz][u]);  // split order
     }
 #pragma unroll
     for (int u = 0; u < G; ++u) {
       const int q = threadIdx.x + (u0 + u) * THREADS;
-      if (u0 + u < SLOTS && q < nslots) red4[q] = s[u];
+      if (u0 + u < SLOTS && q < nslots) red4[q] = acc[u];
     }
   }
   __syncthreads();
