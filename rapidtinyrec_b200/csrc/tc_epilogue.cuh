@@ -199,12 +199,23 @@ template <int THREADS>
 RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, int tok0, int n0, int rows, int cols4) {
   // RMSNorm folded into this GEMM: row scale 1 / sqrt(mean(x^2) + eps) from
   // the producer's partial sums of squares, summed in chunk order
+  // (a row's partials are all loaded before the first is added: one L2
+  // round trip, not one per chunk)
   __shared__ float rsc[128];
   const bool scaled = p.fold.ss_in != nullptr;
   if (scaled) {
+    constexpr int PB = 16;  // partials in flight per round (hidden <= 2048: one round)
     for (int j = threadIdx.x; j < rows; j += THREADS) {
+      const float* src = p.fold.ss_in + tok0 + j;
       float ss = 0.f;
-      for (int t = 0; t < p.fold.parts; ++t) ss += p.fold.ss_in[(long)t * p.fold.ld + tok0 + j];
+      for (int t0 = 0; t0 < p.fold.parts; t0 += PB) {
+        float v[PB];
+#pragma unroll
+        for (int t = 0; t < PB; ++t) v[t] = t0 + t < p.fold.parts ? src[(long)(t0 + t) * p.fold.ld] : 0.f;
+#pragma unroll
+        for (int t = 0; t < PB; ++t)
+          if (t0 + t < p.fold.parts) ss += v[t];  // chunk order
+      }
       rsc[j] = 1.0f / sqrtf(ss / (float)p.fold.hidden + p.fold.eps);
     }
     __syncthreads();
@@ -235,49 +246,76 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
     const RopeArgs& r = p.rope;
     const int D = r.head_dim, half = D >> 1;
 
-    for (int q = threadIdx.x; q < rows * 32; q += THREADS) {
-      const int j = q >> 5, c4 = q & 31;
-      if (c4 >= cols4) continue;
-      const int col = n0 + c4 * 4, m = tok0 + j;
-      const int h = col / D, d = col % D;
-      float4 v = f4add(row_scale(red4[j * ld4 + c4], j), *reinterpret_cast<const float4*>(p.bias + col));
-      if (h < r.heads + r.kv_heads) {
+    // QB iterations per thread at a time, their global loads in two rounds:
+    // the bias columns and the row's position, then the RoPE table rows
+    constexpr int QB = 2;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q0 = threadIdx.x; q0 < rows * 32; q0 += QB * THREADS) {
+      float4 bv[QB], bp[QB], cs[QB], sn[QB];
+      int pos[QB];
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
+        const bool ok = q < rows * 32 && c4 < cols4;
+        const int col = n0 + c4 * 4, m = tok0 + j, h = col / D, d = col % D;
+        const bool rot = ok && h < r.heads + r.kv_heads;
         const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
-        const float4 pv =
-            f4add(row_scale(red4[j * ld4 + pc4], j), *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4));
+        bv[k] = ok ? *reinterpret_cast<const float4*>(p.bias + col) : zero;
+        bp[k] = rot ? *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4) : zero;
         // decode: position L + slot, L of the row's user in a batched step
-        int pos = r.slot < 0 ? m : r.L_dev[r.rows_per_user ? m / r.rows_per_user : 0] + r.slot;
-        if (pos < 0 || pos >= r.positions) {
-          atomicOr(p.status, RTR_DEV_BAD_LENGTH);
-          pos = 0;
-        }
-        const float4 cs = *reinterpret_cast<const float4*>(r.cos_t + (long)pos * half + (d % half));
-        const float4 sn = *reinterpret_cast<const float4*>(r.sin_t + (long)pos * half + (d % half));
-        v = d < half ? f4add_rn(f4mul(v, cs), f4mul(f4neg(pv), sn))   // x1 cos - x2 sin
-                     : f4add_rn(f4mul(v, cs), f4mul(pv, sn));          // x2 cos + x1 sin
+        pos[k] = !rot ? 0 : r.slot < 0 ? m : r.L_dev[r.rows_per_user ? m / r.rows_per_user : 0] + r.slot;
       }
-      float* dst;
-      if (h < r.heads) {
-        dst = r.q_out + ((long)m * r.heads + h) * D + d;
-      } else {
-        const bool is_k = h < r.heads + r.kv_heads;
-        const int g = is_k ? h - r.heads : h - r.heads - r.kv_heads;
-        float* cache = is_k ? r.k_dst : r.v_dst;
-        dst = r.slot < 0 ? cache + ((long)g * r.prefix_cap + m) * D + d : cache + ((long)m * r.kv_heads + g) * D + d;
-        if (r.slot < 0 && r.kpair_hi) {
-          // the same K / V values as fp16 pairs for the tensor-core decode attention
-          __align__(8) __half hi[4];
-          __align__(8) __half lo[4];
-          pair_split(v.x, hi[0], lo[0]); pair_split(v.y, hi[1], lo[1]);
-          pair_split(v.z, hi[2], lo[2]); pair_split(v.w, hi[3], lo[3]);
-          if (is_k) {  // V is written transposed below
-            const long o = ((long)g * r.pair_cap + m) * D + d;
-            *reinterpret_cast<uint2*>(static_cast<__half*>(r.kpair_hi) + o) = *reinterpret_cast<const uint2*>(hi);
-            *reinterpret_cast<uint2*>(static_cast<__half*>(r.kpair_lo) + o) = *reinterpret_cast<const uint2*>(lo);
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
+        const bool ok = q < rows * 32 && c4 < cols4;
+        const int col = n0 + c4 * 4, h = col / D, d = col % D;
+        cs[k] = sn[k] = zero;
+        if (ok && h < r.heads + r.kv_heads) {
+          if (pos[k] < 0 || pos[k] >= r.positions) {
+            atomicOr(p.status, RTR_DEV_BAD_LENGTH);
+            pos[k] = 0;
+          }
+          cs[k] = *reinterpret_cast<const float4*>(r.cos_t + (long)pos[k] * half + (d % half));
+          sn[k] = *reinterpret_cast<const float4*>(r.sin_t + (long)pos[k] * half + (d % half));
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
+        if (q >= rows * 32 || c4 >= cols4) continue;
+        const int col = n0 + c4 * 4, m = tok0 + j;
+        const int h = col / D, d = col % D;
+        float4 v = f4add(row_scale(red4[j * ld4 + c4], j), bv[k]);
+        if (h < r.heads + r.kv_heads) {
+          const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
+          const float4 pv = f4add(row_scale(red4[j * ld4 + pc4], j), bp[k]);
+          v = d < half ? f4add_rn(f4mul(v, cs[k]), f4mul(f4neg(pv), sn[k]))   // x1 cos - x2 sin
+                       : f4add_rn(f4mul(v, cs[k]), f4mul(pv, sn[k]));          // x2 cos + x1 sin
+        }
+        float* dst;
+        if (h < r.heads) {
+          dst = r.q_out + ((long)m * r.heads + h) * D + d;
+        } else {
+          const bool is_k = h < r.heads + r.kv_heads;
+          const int g = is_k ? h - r.heads : h - r.heads - r.kv_heads;
+          float* cache = is_k ? r.k_dst : r.v_dst;
+          dst = r.slot < 0 ? cache + ((long)g * r.prefix_cap + m) * D + d : cache + ((long)m * r.kv_heads + g) * D + d;
+          if (r.slot < 0 && r.kpair_hi) {
+            // the same K / V values as fp16 pairs for the tensor-core attention
+            __align__(8) __half hi[4];
+            __align__(8) __half lo[4];
+            pair_split(v.x, hi[0], lo[0]); pair_split(v.y, hi[1], lo[1]);
+            pair_split(v.z, hi[2], lo[2]); pair_split(v.w, hi[3], lo[3]);
+            if (is_k) {  // V is written transposed below
+              const long o = ((long)g * r.pair_cap + m) * D + d;
+              *reinterpret_cast<uint2*>(static_cast<__half*>(r.kpair_hi) + o) = *reinterpret_cast<const uint2*>(hi);
+              *reinterpret_cast<uint2*>(static_cast<__half*>(r.kpair_lo) + o) = *reinterpret_cast<const uint2*>(lo);
+            }
           }
         }
+        *reinterpret_cast<float4*>(dst) = v;
       }
-      *reinterpret_cast<float4*>(dst) = v;
     }
     if (r.slot < 0 && r.vtpair_hi && n0 + FTILE_COLS > (r.heads + r.kv_heads) * D) {
       // the tile's V columns as fp16 pairs, transposed ([group][dim][token]):
@@ -302,20 +340,35 @@ RTR_DEVICE void tile_epilogue(const TcParams& p, const float4* red4, int ld4, in
     return;
   }
   if (p.epi == EPI_RESID && p.fold.ss_out) {
-    // x += y, its tf32 split, and the row's sum of squares over this 128-column
-    // tile (a warp holds one row: lane = float4 column)
-    for (int q = threadIdx.x; q < rows * 32; q += THREADS) {
-      const int j = q >> 5, c4 = q & 31;
-      const bool ok = c4 < cols4;
-      const long o = (long)(tok0 + j) * p.ldc + n0 + c4 * 4;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (ok) {
-        v = f4add(*reinterpret_cast<const float4*>(p.C + o), red4[j * ld4 + c4]);
-        *reinterpret_cast<float4*>(p.C + o) = v;
-        store_split4(p.C_big, p.C_small, o, v, p.xfmt);
+    // x += y, its split, and the row's sum of squares over this 128-column
+    // tile (a warp holds one row: lane = float4 column); every residual value
+    // of the thread is loaded before the first is used
+    constexpr int QB = 4;  // iterations per thread whose residual loads are in flight together
+    for (int q0 = threadIdx.x; q0 < rows * 32; q0 += QB * THREADS) {
+      float4 x[QB];
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
+        x[k] = q < rows * 32 && c4 < cols4
+                   ? *reinterpret_cast<const float4*>(p.C + (long)(tok0 + j) * p.ldc + n0 + c4 * 4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      const float sq = warp_sum((v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w));
-      if (c4 == 0) p.fold.ss_out[(long)(n0 >> 7) * p.fold.ld + tok0 + j] = sq;
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
+        if (q < rows * 32) {  // whole warps: rows * 32 is a multiple of 32
+          const bool ok = c4 < cols4;
+          const long o = (long)(tok0 + j) * p.ldc + n0 + c4 * 4;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (ok) {
+            v = f4add(x[k], red4[j * ld4 + c4]);
+            *reinterpret_cast<float4*>(p.C + o) = v;
+            store_split4(p.C_big, p.C_small, o, v, p.xfmt);
+          }
+          const float sq = warp_sum((v.x * v.x + v.y * v.y) + (v.z * v.z + v.w * v.w));
+          if (c4 == 0) p.fold.ss_out[(long)(n0 >> 7) * p.fold.ld + tok0 + j] = sq;
+        }
+      }
     }
     return;
   }
