@@ -118,6 +118,26 @@ __host__ __device__ int lookup_width_of(const DevTables& tb, int step) {
 int lookup_width(const DevTables& tb, int step) { return lookup_width_of(tb, step); }
 
 // -------------------------------------------------- vocabulary passes
+// f(x[i]) for the thread's elements i = lo + tid + k * TAIL_THREADS of a row
+// slice, in that order (the order of the plain loop, so the same bits), TB at
+// a time with every load of a batch issued before the first is used: a slice
+// of ~9,500 columns costs three L2 round trips instead of ten.
+template <typename F>
+RTR_DEVICE void for_slice(const float* __restrict__ x, long lo, long hi, F f) {
+  constexpr int TB = 16;
+  for (long i0 = lo + threadIdx.x; i0 < hi; i0 += (long)TB * TAIL_THREADS) {
+    float v[TB];
+#pragma unroll
+    for (int k = 0; k < TB; ++k) {
+      const long i = i0 + (long)k * TAIL_THREADS;
+      v[k] = i < hi ? x[i] : 0.f;
+    }
+#pragma unroll
+    for (int k = 0; k < TB; ++k)
+      if (i0 + (long)k * TAIL_THREADS < hi) f(v[k]);
+  }
+}
+
 __global__ void tail_max_kernel(const float* __restrict__ logits, int vocab, BeamState* st, int rows_per_user) {
   pdl_launch_dependents();
   pdl_wait();
@@ -127,9 +147,7 @@ __global__ void tail_max_kernel(const float* __restrict__ logits, int vocab, Bea
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
   const float* x = logits + (long)grow * vocab;
   float m = -INFINITY;
-  // unrolled with the element order kept: four loads in flight per thread
-#pragma unroll 4
-  for (long i = lo + threadIdx.x; i < hi; i += TAIL_THREADS) m = fmaxf(m, x[i]);
+  for_slice(x, lo, hi, [&](float v) { m = fmaxf(m, v); });
   m = block_max(m, red);
   if (threadIdx.x == 0) st->part[row][sp][0] = m;
 }
@@ -150,8 +168,7 @@ __global__ void tail_sum1_kernel(const float* __restrict__ logits, int vocab, Be
   const float* x = logits + (long)grow * vocab;
   const float m = row_max(st, row);
   float s = 0.f;
-#pragma unroll 4
-  for (long i = lo + threadIdx.x; i < hi; i += TAIL_THREADS) s += expf(x[i] - m);
+  for_slice(x, lo, hi, [&](float v) { s += expf(v - m); });
   s = block_sum(s, red);
   if (threadIdx.x == 0) st->part[row][sp][1] = s;
 }
@@ -170,8 +187,7 @@ __global__ void tail_sum2_kernel(const float* __restrict__ logits, int vocab, Be
   const float L1 = logf(s1);
   const float m2 = (m - m) - L1;  // max of lp1, reached at the arg-max column
   float s = 0.f;
-#pragma unroll 4
-  for (long i = lo + threadIdx.x; i < hi; i += TAIL_THREADS) s += expf(((x[i] - m) - L1) - m2);
+  for_slice(x, lo, hi, [&](float v) { s += expf(((v - m) - L1) - m2); });
   s = block_sum(s, red);
   if (threadIdx.x == 0) {
     st->part[row][sp][2] = s;
@@ -192,22 +208,30 @@ __global__ void tail_lse_sum2_kernel(const float* __restrict__ logits, int vocab
   const int grow = blockIdx.x, row = blockIdx.x % rows_per_user, sp = blockIdx.y;
   const int ntiles = (vocab + 127) / 128;
   const float2* part = lse + (long)grow * ntiles;
+  // the thread's partials are loaded once, all in flight, and kept for both folds
+  constexpr int PB = 8;  // ntiles <= PB * TAIL_THREADS (vocab <= 262,144)
+  float2 pv[PB];
+#pragma unroll
+  for (int k = 0; k < PB; ++k) {
+    const int t = threadIdx.x + k * TAIL_THREADS;
+    pv[k] = t < ntiles ? part[t] : make_float2(-INFINITY, 0.f);
+  }
   float m = -INFINITY;
-  for (int t = threadIdx.x; t < ntiles; t += TAIL_THREADS) m = fmaxf(m, part[t].x);
+#pragma unroll
+  for (int k = 0; k < PB; ++k)
+    if (threadIdx.x + k * TAIL_THREADS < ntiles) m = fmaxf(m, pv[k].x);
   m = block_max(m, red);
   float s1 = 0.f;
-  for (int t = threadIdx.x; t < ntiles; t += TAIL_THREADS) {
-    const float2 v = part[t];
-    s1 += v.y * expf(v.x - m);
-  }
+#pragma unroll
+  for (int k = 0; k < PB; ++k)
+    if (threadIdx.x + k * TAIL_THREADS < ntiles) s1 += pv[k].y * expf(pv[k].x - m);
   s1 = block_sum(s1, red);
   const long lo = (long)vocab * sp / TAIL_SPLITS, hi = (long)vocab * (sp + 1) / TAIL_SPLITS;
   const float* x = logits + (long)grow * vocab;
   const float L1 = logf(s1);
   const float m2 = (m - m) - L1;  // max of lp1, reached at the arg-max column
   float s = 0.f;
-#pragma unroll 4
-  for (long i = lo + threadIdx.x; i < hi; i += TAIL_THREADS) s += expf(((x[i] - m) - L1) - m2);
+  for_slice(x, lo, hi, [&](float v) { s += expf(((v - m) - L1) - m2); });
   s = block_sum(s, red);
   if (threadIdx.x == 0) {
     st->part[row][sp][2] = s;
@@ -334,17 +358,39 @@ __global__ void __launch_bounds__(SEL_THREADS) beam_select_kernel(BeamState* st,
       if ((k & mk) == pf) atomicAdd(&sh.hist[(k >> shift) & 255], 1u);
     }
     __syncthreads();
-    if (tid == 0) {
-      unsigned above = 0;
-      int d = 255;
-      for (; d > 0; --d) {
-        if (above + sh.hist[d] >= (unsigned)sh.krem) break;
-        above += sh.hist[d];
+    if (tid < 32) {
+      // the digit holding the krem-th largest key: the highest d whose bins
+      // 255 .. d hold at least krem keys (bin 0 at the latest).  Lane l sums
+      // bins 255 - 8 l .. 248 - 8 l, a warp scan orders the lanes, and the
+      // first lane that reaches krem walks its own eight bins.
+      const int lane = tid;
+      const unsigned krem = (unsigned)sh.krem;
+      unsigned c[8], tot = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        c[e] = sh.hist[255 - 8 * lane - e];
+        tot += c[e];
       }
-      sh.krem -= (int)above;
-      sh.prefix = pf | ((uint64_t)d << shift);
-      sh.mask = mk | (0xFFull << shift);
-      if ((int)sh.hist[d] == sh.krem) sh.done = 1;
+      unsigned incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const unsigned ball = __ballot_sync(0xffffffffu, incl >= krem);
+      const int first = ball ? __ffs(ball) - 1 : 31;
+      if (lane == first) {
+        unsigned above = incl - tot;
+        int d = 255 - 8 * lane;
+        for (int e = 0; e < 7 && d > 0; ++e, --d) {
+          if (above + c[e] >= krem) break;
+          above += c[e];
+        }
+        sh.krem -= (int)above;
+        sh.prefix = pf | ((uint64_t)d << shift);
+        sh.mask = mk | (0xFFull << shift);
+        if ((int)sh.hist[d] == sh.krem) sh.done = 1;
+      }
     }
     __syncthreads();
   }
