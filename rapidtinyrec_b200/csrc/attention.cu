@@ -295,6 +295,7 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   constexpr int AD4 = HD / 4 / AWARPS;  // float4 columns per warp in phase A
   static_assert(DBEAMS == 8 && AWARPS == 8 && AK == 64, "tiling assumes 8 beams, 8 warps, 64-key chunks");
   pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) unsigned char asmem[];
   T* kbuf = reinterpret_cast<T*>(asmem);
   T* vbuf = kbuf + 2 * AK * kld<HD, T>();
@@ -310,9 +311,6 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   const int b0 = (blockIdx.y % gpu) * DBEAMS, r0 = u * beams, rows = users * beams;
   anc += (long)u * anc_user_stride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // The prompt length and the prefix K / V were written by the request's
-  // prefill, which completed before its decode steps began: the first prefix
-  // chunk is requested before waiting for this step's q / k / v projection.
   int L = L_dev[u];
   if (L < 1 || L > cap) {  // the prefill recorded no valid prefix: attend to the suffix only
     if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
@@ -321,9 +319,6 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   const T* kbase = kp + u * prefix_user_stride + (long)g * cap * HD;
   const T* vbase = vp + u * prefix_user_stride + (long)g * cap * HD;
   const int nchunks = (L + AK - 1) / AK;
-  if (nchunks > 0) load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, 0, L, 0);
-  else cp_async_commit();
-  pdl_wait();  // q, the suffix rows and the ancestry come from this step's kernels
 
   // the suffix rows of the 8 beams (slot s < t - 1: row anc[b][s]; slot t - 1: row b)
   for (int i = threadIdx.x; i < DBEAMS * 4 * (HD / E); i += ATHREADS) {
@@ -340,6 +335,8 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
     cp_async16(sufv + (bb * 4 + sl) * HD + d, vsuf + off, true);
   }
   cp_async_commit();
+  if (nchunks > 0) load_kv_chunk<HD, T>(kbuf, vbuf, kbase, vbase, 0, L, 0);
+  else cp_async_commit();
   for (int i = threadIdx.x; i < DBEAMS * HD / 4; i += ATHREADS) {
     const int r = i / (HD / 4), d = (i % (HD / 4)) * 4;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);

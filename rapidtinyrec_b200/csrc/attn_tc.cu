@@ -1172,10 +1172,8 @@ __global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS,
   const uint32_t o_tmem = tmem + 2 * C::S_COLS;
   const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
   pdl_launch_dependents();
+  pdl_wait();  // q, the suffix rows and the prefix copies come from earlier kernels
 
-  // The prompt length, the prefix arena and the V copy were written by the
-  // request's prefill, which completed before its decode steps began: the
-  // first chunks are requested before waiting for this step's q / k / v.
   int L = L_dev[u];
   if (L < 1 || L > cap) {  // no valid prefix: attend to the suffix only
     if (tid == 0 && rank == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
@@ -1183,35 +1181,23 @@ __global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS,
   }
   const int nch_all = (L + AT_KEYS - 1) / AT_KEYS;
   const int nmine = suffix_rank || rank >= nch_all ? 0 : (nch_all - rank + AT_CLUSTER - 2) / (AT_CLUSTER - 1);
-  auto chunk = [&](int i) { return rank + i * (AT_CLUSTER - 1); };
-  auto load_k = [&](int i) {
-    const uint32_t bar = smem_addr(&k_full[i & 1]);
-    uint8_t* dst = kb + (i & 1) * C::K_BYTES;
-    mbar_expect_tx(bar, C::K_BYTES);
-#pragma unroll
-    for (int cc = 0; cc < C::NC; ++cc)
-      tma_load_2d(smem_addr(dst + cc * AT_KEYS * 128), &kmap, cc * 64, (int)(kr0 + (long)chunk(i) * AT_KEYS), bar);
-  };
-  auto load_v = [&](int i) {
-    const uint32_t bar = smem_addr(v_full);
-    mbar_expect_tx(bar, C::V_BYTES);
-    tma_load_2d(smem_addr(vs), &vmap, chunk(i) * AT_KEYS, (int)vr0, bar);
-  };
-  int k_issued = 0, v_issued = 0, s_issued = 0, o_issued = 0;
-  if (nmine > 0 && tid == 0) {
-    load_k(0);
-    k_issued = 1;
-    if (nmine > 1) {
-      load_k(1);
-      k_issued = 2;
-    }
-    load_v(0);
-    v_issued = 1;
-  }
-  pdl_wait();  // q, the suffix rows and the ancestry come from this step's kernels
 
   float m = -INFINITY, l = 0.f;
   if (nmine > 0) {
+    auto chunk = [&](int i) { return rank + i * (AT_CLUSTER - 1); };
+    auto load_k = [&](int i) {
+      const uint32_t bar = smem_addr(&k_full[i & 1]);
+      uint8_t* dst = kb + (i & 1) * C::K_BYTES;
+      mbar_expect_tx(bar, C::K_BYTES);
+#pragma unroll
+      for (int cc = 0; cc < C::NC; ++cc)
+        tma_load_2d(smem_addr(dst + cc * AT_KEYS * 128), &kmap, cc * 64, (int)(kr0 + (long)chunk(i) * AT_KEYS), bar);
+    };
+    auto load_v = [&](int i) {
+      const uint32_t bar = smem_addr(v_full);
+      mbar_expect_tx(bar, C::V_BYTES);
+      tma_load_2d(smem_addr(vs), &vmap, chunk(i) * AT_KEYS, (int)vr0, bar);
+    };
     auto issue_s = [&](int i) -> bool {
       if (!mbar_wait(smem_addr(&k_full[i & 1]), (i >> 1) & 1, abort_flag)) return false;
       tc_fence_after();
@@ -1228,6 +1214,17 @@ __global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS,
       mma_commit(smem_addr(&s_done[i & 1]));
       return true;
     };
+    int k_issued = 0, v_issued = 0, s_issued = 0, o_issued = 0;
+    if (tid == 0) {
+      load_k(0);
+      k_issued = 1;
+      if (nmine > 1) {
+        load_k(1);
+        k_issued = 2;
+      }
+      load_v(0);
+      v_issued = 1;
+    }
     {
       // the tile's q rows (bf16) -> the A operand, zeros past the group's rows
       constexpr int UPR = HD / 8, PER = AT_ROWS * UPR / AT_THREADS;
