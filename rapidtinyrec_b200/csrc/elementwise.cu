@@ -125,39 +125,61 @@ cudaError_t embed_rows_bf16(const int32_t* ids, int ids_stride, int M, const voi
 // Qwen2RMSNorm on a bf16 model (modeling_qwen2.py:258-263): the variance in
 // fp32, then weight * bf16(x * rsqrt(var + eps)) rounded to bf16; w holds the
 // bf16 norm weights as fp32.
-__global__ void rms_norm_bf16_kernel(const __nv_bfloat16* x, const float* w, __nv_bfloat16* h, int hidden, float eps) {
+// One CTA (256 threads) per row.  The weights (constants) are loaded before
+// the wait for the previous kernel and the row stays in registers, so the
+// only dependent global round trips are the row's load and the store; the
+// sum of squares runs in the same order for every hidden size.
+constexpr int NORM16_THREADS = 256, NORM16_PAIRS = 8;  // hidden <= 2 * 8 * 256 = 4096
+__global__ void __launch_bounds__(NORM16_THREADS)
+    rms_norm_bf16_kernel(const __nv_bfloat16* x, const float* w, __nv_bfloat16* h, int hidden, float eps) {
+  const int npair = hidden / 2;
+  float2 wv[NORM16_PAIRS];
+#pragma unroll
+  for (int t = 0; t < NORM16_PAIRS; ++t) {
+    const int i = threadIdx.x + t * NORM16_THREADS;
+    wv[t] = i < npair ? make_float2(w[2 * i], w[2 * i + 1]) : make_float2(0.f, 0.f);
+  }
   pdl_launch_dependents();
   pdl_wait();
   const int m = blockIdx.x;
   const __nv_bfloat162* xr = reinterpret_cast<const __nv_bfloat162*>(x + (long)m * hidden);
+  float2 xv[NORM16_PAIRS];
+#pragma unroll
+  for (int t = 0; t < NORM16_PAIRS; ++t) {
+    const int i = threadIdx.x + t * NORM16_THREADS;
+    xv[t] = i < npair ? __bfloat1622float2(xr[i]) : make_float2(0.f, 0.f);
+  }
   float ss = 0.f;
-  for (int i = threadIdx.x; i < hidden / 2; i += blockDim.x) {
-    const float2 v = __bfloat1622float2(xr[i]);
-    ss = fmaf(v.x, v.x, ss);
-    ss = fmaf(v.y, v.y, ss);
+#pragma unroll
+  for (int t = 0; t < NORM16_PAIRS; ++t) {
+    if (threadIdx.x + t * NORM16_THREADS < npair) {
+      ss = fmaf(xv[t].x, xv[t].x, ss);
+      ss = fmaf(xv[t].y, xv[t].y, ss);
+    }
   }
   __shared__ float red[32];
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    float v = threadIdx.x < (NORM16_THREADS >> 5) ? red[threadIdx.x] : 0.f;
     v = warp_sum(v);
     if (threadIdx.x == 0) red[0] = v;
   }
   __syncthreads();
   const float r = 1.0f / sqrtf(red[0] / (float)hidden + eps);
   __nv_bfloat162* hr = reinterpret_cast<__nv_bfloat162*>(h + (long)m * hidden);
-  for (int i = threadIdx.x; i < hidden / 2; i += blockDim.x) {
-    const float2 v = __bfloat1622float2(xr[i]);
-    const float a = bf16_round(v.x * r), b = bf16_round(v.y * r);
-    hr[i] = __floats2bfloat162_rn(w[2 * i] * a, w[2 * i + 1] * b);
+#pragma unroll
+  for (int t = 0; t < NORM16_PAIRS; ++t) {
+    const int i = threadIdx.x + t * NORM16_THREADS;
+    if (i < npair) hr[i] = __floats2bfloat162_rn(wv[t].x * bf16_round(xv[t].x * r), wv[t].y * bf16_round(xv[t].y * r));
   }
 }
 
 cudaError_t rms_norm_rows_bf16(const void* x, const float* w, void* h, int M, int hidden, float eps,
                                cudaStream_t stream) {
-  return launch_pdl(PDL_NORM16, rms_norm_bf16_kernel, dim3(M), dim3(256), 0, stream,
+  if (hidden % 2 || hidden > 2 * NORM16_PAIRS * NORM16_THREADS) return cudaErrorInvalidValue;
+  return launch_pdl(PDL_NORM16, rms_norm_bf16_kernel, dim3(M), dim3(NORM16_THREADS), 0, stream,
                     static_cast<const __nv_bfloat16*>(x), w, static_cast<__nv_bfloat16*>(h), hidden, eps);
 }
 
