@@ -105,36 +105,65 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
     const RopeArgs& r = p.rope;
     const int D = r.head_dim, half = D >> 1;
 
-    for (int q = threadIdx.x; q < rows * 32; q += BF_THREADS) {
-      const int j = q >> 5, c4 = q & 31;
-      if (c4 >= cols4) continue;
-      const int col = n0 + c4 * 4, m = tok0 + j;
-      const int h = col / D, d = col % D;
-      float4 v = rbf4(f4add(red4[j * ld4 + c4], *reinterpret_cast<const float4*>(p.bias + col)));
-      if (h < r.heads + r.kv_heads) {
+    // QB iterations per thread at a time, their global loads in two rounds:
+    // the bias columns and the row's position, then the RoPE table rows
+    constexpr int QB = 2;
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q0 = threadIdx.x; q0 < rows * 32; q0 += QB * BF_THREADS) {
+      float4 bv[QB], bp[QB], cs[QB], sn[QB];
+      int pos[QB];
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        const bool ok = q < rows * 32 && c4 < cols4;
+        const int col = n0 + c4 * 4, m = tok0 + j, h = col / D, d = col % D;
+        const bool rot = ok && h < r.heads + r.kv_heads;
         const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
-        const float4 pv = rbf4(f4add(red4[j * ld4 + pc4], *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4)));
+        bv[k] = ok ? *reinterpret_cast<const float4*>(p.bias + col) : zero;
+        bp[k] = rot ? *reinterpret_cast<const float4*>(p.bias + n0 + pc4 * 4) : zero;
         // decode: position L + slot, L of the row's user in a batched step
-        int pos = r.slot < 0 ? m : r.L_dev[r.rows_per_user ? m / r.rows_per_user : 0] + r.slot;
-        if (pos < 0 || pos >= r.positions) {
-          atomicOr(p.status, RTR_DEV_BAD_LENGTH);
-          pos = 0;
+        pos[k] = !rot ? 0 : r.slot < 0 ? m : r.L_dev[r.rows_per_user ? m / r.rows_per_user : 0] + r.slot;
+      }
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        const bool ok = q < rows * 32 && c4 < cols4;
+        const int col = n0 + c4 * 4, h = col / D, d = col % D;
+        cs[k] = sn[k] = zero;
+        if (ok && h < r.heads + r.kv_heads) {
+          if (pos[k] < 0 || pos[k] >= r.positions) {
+            atomicOr(p.status, RTR_DEV_BAD_LENGTH);
+            pos[k] = 0;
+          }
+          cs[k] = *reinterpret_cast<const float4*>(r.cos_t + (long)pos[k] * half + (d % half));
+          sn[k] = *reinterpret_cast<const float4*>(r.sin_t + (long)pos[k] * half + (d % half));
         }
-        const float4 cs = *reinterpret_cast<const float4*>(r.cos_t + (long)pos * half + (d % half));
-        const float4 sn = *reinterpret_cast<const float4*>(r.sin_t + (long)pos * half + (d % half));
-        // q * cos + rotate_half(q) * sin, each product and the sum rounded to bf16
-        v = d < half ? bf_add4(bf_mul4(v, cs), bf_mul4(f4neg(pv), sn)) : bf_add4(bf_mul4(v, cs), bf_mul4(pv, sn));
       }
-      __nv_bfloat16* dst;
-      if (h < r.heads) {
-        dst = bfp(r.q_out) + ((long)m * r.heads + h) * D + d;
-      } else {
-        const bool is_k = h < r.heads + r.kv_heads;
-        const int g = is_k ? h - r.heads : h - r.heads - r.kv_heads;
-        __nv_bfloat16* cache = bfp(is_k ? r.k_dst : r.v_dst);
-        dst = r.slot < 0 ? cache + ((long)g * r.prefix_cap + m) * D + d : cache + ((long)m * r.kv_heads + g) * D + d;
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        if (q >= rows * 32 || c4 >= cols4) continue;
+        const int col = n0 + c4 * 4, m = tok0 + j;
+        const int h = col / D, d = col % D;
+        float4 v = rbf4(f4add(red4[j * ld4 + c4], bv[k]));
+        if (h < r.heads + r.kv_heads) {
+          const int pc4 = d < half ? c4 + half / 4 : c4 - half / 4;
+          const float4 pv = rbf4(f4add(red4[j * ld4 + pc4], bp[k]));
+          // q * cos + rotate_half(q) * sin, each product and the sum rounded to bf16
+          v = d < half ? bf_add4(bf_mul4(v, cs[k]), bf_mul4(f4neg(pv), sn[k]))
+                       : bf_add4(bf_mul4(v, cs[k]), bf_mul4(pv, sn[k]));
+        }
+        __nv_bfloat16* dst;
+        if (h < r.heads) {
+          dst = bfp(r.q_out) + ((long)m * r.heads + h) * D + d;
+        } else {
+          const bool is_k = h < r.heads + r.kv_heads;
+          const int g = is_k ? h - r.heads : h - r.heads - r.kv_heads;
+          __nv_bfloat16* cache = bfp(is_k ? r.k_dst : r.v_dst);
+          dst = r.slot < 0 ? cache + ((long)g * r.prefix_cap + m) * D + d : cache + ((long)m * r.kv_heads + g) * D + d;
+        }
+        st_bf4(dst, v);
       }
-      st_bf4(dst, v);
     }
     if (r.slot < 0 && r.vtpair_hi && n0 + FTILE_COLS > (r.heads + r.kv_heads) * D) {
       // prefill: the tile's V columns also transposed ([group][dim][token],
@@ -148,6 +177,26 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
         const int g = h - r.heads - r.kv_heads;
         bfp(r.vtpair_hi)[((long)g * D + d) * r.pair_cap + tok0 + j] =
             __float2bfloat16_rn(red[j * ld4 * 4 + c] + p.bias[col]);
+      }
+    }
+    return;
+  }
+  if (p.epi == EPI_RESID) {
+    // x = bf16(x + bf16(y)); QB iterations' residual loads in flight together
+    constexpr int QB = 4;
+    for (int q0 = threadIdx.x; q0 < rows * 32; q0 += QB * BF_THREADS) {
+      float4 x[QB];
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        x[k] = q < rows * 32 && c4 < cols4 ? ld_bf4(bfp(p.C) + (long)(tok0 + j) * p.ldc + n0 + c4 * 4)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int k = 0; k < QB; ++k) {
+        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        if (q < rows * 32 && c4 < cols4)
+          st_bf4(bfp(p.C) + (long)(tok0 + j) * p.ldc + n0 + c4 * 4, f4add(x[k], rbf4(red4[j * ld4 + c4])));
       }
     }
     return;
