@@ -115,7 +115,8 @@ cudaError_t pack_weight_tiles_bf16(const float* src, int N, int K, void* dst, cu
 bool make_tmap_packed_bf16(TensorMap* out, const void* packed, int N, int K);
 cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int ldc, const float* bias, int M, int N,
                       int K, int epi, float* ws, size_t ws_floats, int* tickets, int max_tickets, uint32_t* status,
-                      int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr);
+                      int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr,
+                      float2* lse = nullptr, int lse_ld = 0);
 
 // ---- element-wise (elementwise.cu) ----
 // x = table[ids]; with x_big/x_small (optional) also x's GEMM split (format

@@ -63,6 +63,8 @@ struct BfParams {
   int* tickets;
   uint32_t* status;
   RopeArgs rope;           // EPI_ROPE: q_out / k_dst / v_dst are bf16
+  float2* lse = nullptr;   // EPI_STORE (LM head): per row and 128-column tile, (max, sum exp(x - max))
+  int lse_ld = 0;          // tiles per row of the partials (row stride)
 };
 
 RTR_DEVICE float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
@@ -213,6 +215,45 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
       st_bf4(bfp(p.C) + o, f4add(v, *reinterpret_cast<const float4*>(p.bias + col)));
     } else {  // EPI_RESID: x = bf16(x + bf16(y))
       st_bf4(bfp(p.C) + o, f4add(ld_bf4(bfp(p.C) + o), rbf4(v)));
+    }
+  }
+  if (p.lse && p.epi == EPI_STORE) {
+    // LM head: every row's (max, sum of exp(x - max)) over the tile's bf16
+    // logits, for the first log-softmax (the step tail then reads the logits
+    // once).  Warp w takes rows w, w + 8, ... eight at a time (lane = float4
+    // column).  The hardware exponential: these partials only set the row's
+    // normaliser, whose sum over the vocabulary averages their rounding.
+    constexpr int NW = BF_THREADS / 32, G = 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int j0 = warp; j0 < rows; j0 += NW * G) {
+      float4 v[G];
+      float mx[G], e[G];
+#pragma unroll
+      for (int r = 0; r < G; ++r) {
+        const int j = j0 + r * NW;
+        const bool ok = j < rows && lane < cols4;
+        v[r] = ok ? rbf4(red4[j * ld4 + lane]) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        mx[r] = fmaxf(fmaxf(v[r].x, v[r].y), fmaxf(v[r].z, v[r].w));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < G; ++r) mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], o));
+#pragma unroll
+      for (int r = 0; r < G; ++r)
+        e[r] = lane < cols4 ? (__expf(v[r].x - mx[r]) + __expf(v[r].y - mx[r])) +
+                                  (__expf(v[r].z - mx[r]) + __expf(v[r].w - mx[r]))
+                            : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int r = 0; r < G; ++r) e[r] += __shfl_xor_sync(0xffffffffu, e[r], o);
+      if (lane == 0)
+#pragma unroll
+        for (int r = 0; r < G; ++r) {
+          const int j = j0 + r * NW;
+          if (j < rows) p.lse[(long)(tok0 + j) * p.lse_ld + (n0 >> 7)] = make_float2(mx[r], e[r]);
+        }
     }
   }
 }
@@ -568,7 +609,8 @@ cudaError_t gemm_bf16_init() {
 
 cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int ldc, const float* bias, int M, int N,
                       int K, int epi, float* ws, size_t ws_floats, int* tickets, int max_tickets, uint32_t* status,
-                      int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope) {
+                      int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope, float2* lse, int lse_ld) {
+  if (lse && (epi != EPI_STORE || lse_ld < (N + BF_WROWS - 1) / BF_WROWS)) return cudaErrorInvalidValue;
   if (epi == EPI_ROPE) {
     if (!rope || !bias || (rope->head_dim != 64 && rope->head_dim != 128) ||
         N != (rope->heads + 2 * rope->kv_heads) * rope->head_dim || (reinterpret_cast<uintptr_t>(bias) & 15))
@@ -589,6 +631,8 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
   const int splits = plan.splits, cs = plan.cluster;
   BfParams p{C, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
   if (rope) p.rope = *rope;
+  p.lse = lse;
+  p.lse_ld = lse_ld;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tt, wt, splits);
   cfg.blockDim = dim3(BF_THREADS);

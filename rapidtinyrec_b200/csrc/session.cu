@@ -92,7 +92,7 @@ struct rtr_session {
   __half* kvpair = nullptr;  // [K hi][K lo][V^T hi][V^T lo] planes
   AttnPairs pairs{};
   float2* lse = nullptr;     // LM head's per-tile (max, sum exp) partials: [tiles][B * max_users]
-  bool lse_tail = false;     // decode step tails read the logits once (fp16-pair LM head)
+  bool lse_tail = false;     // decode step tails read the logits once (fp16-pair or bf16 LM head)
   bool folded_attn = false;
   float *x = nullptr, *h = nullptr, *qkv = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr;
   // tf32 split (big = tf32(v), small = v - big) of the GEMM activation operands
@@ -369,10 +369,10 @@ int rtr_session_create_batched(const rtr_model_config* cfg, int device, int32_t 
   }
   CREATE_TRY(dev_alloc(s, &s->logits, B * U * V));
   {
-    // the fp16-pair LM head leaves the first log-softmax's partials (RTR_TAIL=passes:
-    // three passes over the logits instead)
+    // the fp16-pair and bf16 LM heads leave the first log-softmax's partials
+    // (RTR_TAIL=passes: three passes over the logits instead)
     const char* e = getenv("RTR_TAIL");
-    s->lse_tail = s->use_tc && s->xfmt == SPLIT_F16 && !(e && strcmp(e, "passes") == 0);
+    s->lse_tail = s->use_tc && (s->xfmt == SPLIT_F16 || s->bf16) && !(e && strcmp(e, "passes") == 0);
     if (s->lse_tail) CREATE_TRY(dev_alloc(s, &s->lse, (size_t)((V + 127) / 128) * B * U));
   }
   long max_n = qkvd;
@@ -735,12 +735,12 @@ static cudaError_t gemm(rtr_session* s, const float* A, int lda, const float* W,
 // bf16 mode: projection GEMM of the bf16 activation buffer X (its TMA map)
 // against a packed bf16 weight.
 static cudaError_t gemm16(rtr_session* s, const float* X, const void* Wp, void* C, int ldc, const float* bias, int M,
-                          int N, int K, int epi, const RopeArgs* rope = nullptr) {
+                          int N, int K, int epi, const RopeArgs* rope = nullptr, float2* lse = nullptr) {
   auto x = s->tmaps.find({X, 64});
   auto w = s->tmaps.find({Wp, 128});
   if (x == s->tmaps.end() || w == s->tmaps.end()) return cudaErrorInvalidValue;
   return gemm_bf16(w->second, x->second, C, ldc, bias, M, N, K, epi, s->ws, s->ws_floats, s->tickets, kTickets,
-                   s->d_status, s->sms, s->stream, s->pdl, rope);
+                   s->d_status, s->sms, s->stream, s->pdl, rope, lse, (s->cfg.vocab + 127) / 128);
 }
 
 // The prefill of user cur_user also writes layer l's K / V as fp16 pairs for
@@ -862,7 +862,8 @@ static cudaError_t forward_bf16(rtr_session* s, int t) {
     FWD_TRY(gemm16(s, s->h, s->lm_packed_bf, s->logits, V, nullptr, 1, V, H, EPI_STORE));
   } else {
     FWD_TRY(rms_norm_rows_bf16(s->x, s->norm_final, s->h, M, H, c.rms_eps, st));
-    FWD_TRY(gemm16(s, s->h, s->lm_packed_bf, s->logits, V, nullptr, M, V, H, EPI_STORE));
+    FWD_TRY(gemm16(s, s->h, s->lm_packed_bf, s->logits, V, nullptr, M, V, H, EPI_STORE, nullptr,
+                   s->lse_tail ? s->lse : nullptr));
   }
   return cudaSuccess;
 }
