@@ -116,7 +116,7 @@ bool make_tmap_packed_bf16(TensorMap* out, const void* packed, int N, int K);
 cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int ldc, const float* bias, int M, int N,
                       int K, int epi, float* ws, size_t ws_floats, int* tickets, int max_tickets, uint32_t* status,
                       int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope = nullptr,
-                      float2* lse = nullptr, int lse_ld = 0);
+                      float2* lse = nullptr, int lse_ld = 0, bool allow_wide = true);
 
 // ---- element-wise (elementwise.cu) ----
 // x = table[ids]; with x_big/x_small (optional) also x's GEMM split (format

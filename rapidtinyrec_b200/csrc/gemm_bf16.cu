@@ -88,11 +88,12 @@ RTR_DEVICE float4 bf_add4(float4 a, float4 b) { return rbf4(make_float4(a.x + b.
 
 // Epilogue from a [rows][ld4 float4] shared tile of fp32 sums, every thread of
 // the CTA, 4 columns at a time.
+template <int THREADS>
 RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4, int tok0, int n0, int rows,
                                  int cols4) {
   if (p.epi == EPI_SWIGLU) {
     // packed rows: 32 q + [0,16) gate, 32 q + [16,32) up of intermediate 16 q + [0,16)
-    for (int q = threadIdx.x; q < rows * 16; q += BF_THREADS) {
+    for (int q = threadIdx.x; q < rows * 16; q += THREADS) {
       const int j = q >> 4, blk = (q >> 2) & 3, g4 = q & 3;
       const int c4 = blk * 8 + g4;
       if (c4 + 4 >= cols4) continue;
@@ -111,12 +112,12 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
     // the bias columns and the row's position, then the RoPE table rows
     constexpr int QB = 2;
     const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q0 = threadIdx.x; q0 < rows * 32; q0 += QB * BF_THREADS) {
+    for (int q0 = threadIdx.x; q0 < rows * 32; q0 += QB * THREADS) {
       float4 bv[QB], bp[QB], cs[QB], sn[QB];
       int pos[QB];
 #pragma unroll
       for (int k = 0; k < QB; ++k) {
-        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
         const bool ok = q < rows * 32 && c4 < cols4;
         const int col = n0 + c4 * 4, m = tok0 + j, h = col / D, d = col % D;
         const bool rot = ok && h < r.heads + r.kv_heads;
@@ -128,7 +129,7 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
       }
 #pragma unroll
       for (int k = 0; k < QB; ++k) {
-        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
         const bool ok = q < rows * 32 && c4 < cols4;
         const int col = n0 + c4 * 4, h = col / D, d = col % D;
         cs[k] = sn[k] = zero;
@@ -143,7 +144,7 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
       }
 #pragma unroll
       for (int k = 0; k < QB; ++k) {
-        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
         if (q >= rows * 32 || c4 >= cols4) continue;
         const int col = n0 + c4 * 4, m = tok0 + j;
         const int h = col / D, d = col % D;
@@ -172,7 +173,7 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
       // the same bf16 values) for the tensor-core prefill attention; a warp
       // takes consecutive tokens of a column, so its stores are contiguous
       const float* red = reinterpret_cast<const float*>(red4);
-      for (int q = threadIdx.x; q < rows * cols4 * 4; q += BF_THREADS) {
+      for (int q = threadIdx.x; q < rows * cols4 * 4; q += THREADS) {
         const int c = q / rows, j = q % rows;
         const int col = n0 + c, h = col / D, d = col % D;
         if (h < r.heads + r.kv_heads) continue;
@@ -186,24 +187,24 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
   if (p.epi == EPI_RESID) {
     // x = bf16(x + bf16(y)); QB iterations' residual loads in flight together
     constexpr int QB = 4;
-    for (int q0 = threadIdx.x; q0 < rows * 32; q0 += QB * BF_THREADS) {
+    for (int q0 = threadIdx.x; q0 < rows * 32; q0 += QB * THREADS) {
       float4 x[QB];
 #pragma unroll
       for (int k = 0; k < QB; ++k) {
-        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
         x[k] = q < rows * 32 && c4 < cols4 ? ld_bf4(bfp(p.C) + (long)(tok0 + j) * p.ldc + n0 + c4 * 4)
                                            : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int k = 0; k < QB; ++k) {
-        const int q = q0 + k * BF_THREADS, j = q >> 5, c4 = q & 31;
+        const int q = q0 + k * THREADS, j = q >> 5, c4 = q & 31;
         if (q < rows * 32 && c4 < cols4)
           st_bf4(bfp(p.C) + (long)(tok0 + j) * p.ldc + n0 + c4 * 4, f4add(x[k], rbf4(red4[j * ld4 + c4])));
       }
     }
     return;
   }
-  for (int q = threadIdx.x; q < rows * 32; q += BF_THREADS) {
+  for (int q = threadIdx.x; q < rows * 32; q += THREADS) {
     const int j = q >> 5, c4 = q & 31;
     if (c4 >= cols4) continue;
     const int col = n0 + c4 * 4;
@@ -223,7 +224,7 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
     // once).  Warp w takes rows w, w + 8, ... eight at a time (lane = float4
     // column).  The hardware exponential: these partials only set the row's
     // normaliser, whose sum over the vocabulary averages their rounding.
-    constexpr int NW = BF_THREADS / 32, G = 8;
+    constexpr int NW = THREADS / 32, G = 8;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int j0 = warp; j0 < rows; j0 += NW * G) {
       float4 v[G];
@@ -263,29 +264,30 @@ RTR_DEVICE void bf_tile_epilogue(const BfParams& p, const float4* red4, int ld4,
 // tile.  Each round of loads is one L2 round trip, so the sum takes whichever
 // order needs fewer rounds: every split (up to KS_MAX) of two float4 slots per
 // thread at once, or every slot two splits at a time.
+template <int THREADS, int NTOK>
 RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int row0, int rows, int cols4, int tile, long tstride) {
-  constexpr int SLOTS = (BF_NTOK * BF_WROWS / 4 + BF_THREADS - 1) / BF_THREADS;
-  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (BF_NTOK * BF_WROWS)) + row0 * 32;
+  constexpr int SLOTS = (NTOK * BF_WROWS / 4 + THREADS - 1) / THREADS;
+  const float4* base = reinterpret_cast<const float4*>(p.ws + (long)tile * (NTOK * BF_WROWS)) + row0 * 32;
   red4 += row0 * 32;
   const long zs = tstride >> 2;
   const int nslots = rows * (BF_WROWS / 4);
-  const int active = (nslots + BF_THREADS - 1) / BF_THREADS;  // slots a thread holds
+  const int active = (nslots + THREADS - 1) / THREADS;  // slots a thread holds
   if (p.splits <= KS_MAX && (active + 1) / 2 < (p.splits + 1) / 2) {
     constexpr int PS = 2;
 #pragma unroll 1
-    for (int u0 = 0; u0 < SLOTS && u0 * BF_THREADS < nslots; u0 += PS) {
+    for (int u0 = 0; u0 < SLOTS && u0 * THREADS < nslots; u0 += PS) {
       float4 v[PS][KS_MAX];
 #pragma unroll
       for (int u = 0; u < PS; ++u)
 #pragma unroll
         for (int z = 0; z < KS_MAX; ++z) {
-          const int q = threadIdx.x + (u0 + u) * BF_THREADS;
+          const int q = threadIdx.x + (u0 + u) * THREADS;
           const bool ok = u0 + u < SLOTS && z < p.splits && q < nslots && (q & 31) < cols4;
           v[u][z] = ok ? __ldcg(base + z * zs + q) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
       for (int u = 0; u < PS; ++u) {
-        const int q = threadIdx.x + (u0 + u) * BF_THREADS;
+        const int q = threadIdx.x + (u0 + u) * THREADS;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int z = 0; z < KS_MAX; ++z)
@@ -305,7 +307,7 @@ RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int row0, int row
     for (int dz = 0; dz < 2; ++dz)
 #pragma unroll
       for (int u = 0; u < SLOTS; ++u) {
-        const int q = threadIdx.x + u * BF_THREADS;
+        const int q = threadIdx.x + u * THREADS;
         const bool ok = z + dz < p.splits && q < nslots && (q & 31) < cols4;
         v[dz][u] = ok ? __ldcg(base + (z + dz) * zs + q) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
@@ -317,7 +319,7 @@ RTR_DEVICE void bf_splitk_sum(const BfParams& p, float4* red4, int row0, int row
   }
 #pragma unroll
   for (int u = 0; u < SLOTS; ++u) {
-    const int q = threadIdx.x + u * BF_THREADS;
+    const int q = threadIdx.x + u * THREADS;
     if (q < nslots) red4[q] = s[u];
   }
   __syncthreads();
@@ -529,8 +531,8 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
     __syncthreads();
     int r0 = 0, r1 = 0;
     if (!splitk_claim(p, smem_addr(red_bar), &go, rows, tile, r0, r1)) return;
-    bf_splitk_sum(p, red4, r0, r1 - r0, cols4, tile, tstride);
-    bf_tile_epilogue(p, red4 + r0 * 32, BF_WROWS / 4, tok0 + r0, n0, r1 - r0, cols4);
+    bf_splitk_sum<BF_THREADS, BF_NTOK>(p, red4, r0, r1 - r0, cols4, tile, tstride);
+    bf_tile_epilogue<BF_THREADS>(p, red4 + r0 * 32, BF_WROWS / 4, tok0 + r0, n0, r1 - r0, cols4);
     return;
   }
   if (have && n < p.N) {
@@ -540,7 +542,236 @@ __global__ void __launch_bounds__(BF_THREADS, 1)
       if (j < rows) red[j * BF_RLD] = acc[j];
   }
   __syncthreads();
-  bf_tile_epilogue(p, red4, BF_RLD / 4, tok0, n0, rows, cols4);
+  bf_tile_epilogue<BF_THREADS>(p, red4, BF_RLD / 4, tok0, n0, rows, cols4);
+}
+
+// ------------------------------------------------------- 128-row variant
+// More than 64 activation rows (the prefill, batched decode): a CTA owns 128
+// weight rows x 128 activation rows, so a weight tile is read once per 128
+// rows and each MMA is N = 128.  Stages of one chunk (16 KB of W + 16 KB of
+// X, 6 deep), runtime stage indices; warps 4..11 promote (lane quarter x
+// 64-row half).  The same promotion groups (4 chunks) and split-K plan as
+// the 64-row kernel for the same tiles.
+constexpr int BW_NTOK = 128;
+constexpr int BW_PROMOTERS = 8;
+constexpr int BW_THREADS = 128 + 32 * BW_PROMOTERS;   // 12 warps
+constexpr int BW_STAGES = 6;
+constexpr int BW_XC_BYTES = BW_NTOK * 128;
+constexpr int BW_D_COLS = BW_NTOK;
+constexpr int BW_TMEM_COLS = 2 * BW_D_COLS;           // 256: double-buffered accumulator
+constexpr int BW_NBARS = 2 * BW_STAGES + 5;
+constexpr int BW_RING_BYTES = BW_STAGES * (BF_WC_BYTES + BW_XC_BYTES);
+constexpr int BW_SMEM_BYTES = BW_RING_BYTES + 1024 + 8 * BW_NBARS + 16;
+static_assert(BW_NTOK * BF_RLD * 4 <= BW_RING_BYTES, "epilogue tile fits in the rings");
+
+__global__ void __launch_bounds__(BW_THREADS, 1)
+    gemm_bf16_wide_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+                          BfParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* wring = smem;
+  uint8_t* xring = smem + BW_STAGES * BF_WC_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(xring + BW_STAGES * BW_XC_BYTES);
+  uint64_t* s_full = bars;                  // [BW_STAGES] W and X of the stage landed (2 arrivals + bytes)
+  uint64_t* s_empty = s_full + BW_STAGES;   // [BW_STAGES] the stage's MMAs are done
+  uint64_t* d_full = s_empty + BW_STAGES;   // [2]
+  uint64_t* d_empty = d_full + 2;           // [2]
+  uint64_t* red_bar = d_empty + 2;          // split-K finish: every CTA of the cluster arrived
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(red_bar + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(red_bar + 1) + 1;
+  __shared__ int go;                        // this cluster finishes the tile
+  __shared__ int issued[2];                 // chunks issued by the W and X producers (abort path)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tok0 = blockIdx.x * BW_NTOK;
+  const int n0 = blockIdx.y * BF_WROWS;
+  const long long lim = g_bf_wait.wait_cycles;
+  const int nchunks = (p.K + BF_KC - 1) / BF_KC;
+  const int c0 = (int)((long)blockIdx.z * nchunks / p.splits);
+  const int c1 = (int)((long)(blockIdx.z + 1) * nchunks / p.splits);
+  const int nloc = c1 - c0;
+  const int ngroups = (nloc + BF_PROMOTE - 1) / BF_PROMOTE;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < BW_STAGES; ++s) { mbar_init(smem_addr(&s_full[s]), 2); mbar_init(smem_addr(&s_empty[s]), 1); }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_addr(&d_full[b]), 1);
+      mbar_init(smem_addr(&d_empty[b]), BW_PROMOTERS);
+    }
+    mbar_init(smem_addr(red_bar), cluster_ncta());
+    go = 0;
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) tmem_alloc(smem_addr(tmem_slot), BW_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  if (cluster_ncta() > 1) cluster_sync_all();  // peers' barriers are initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int w_issued = 0, x_issued = 0;
+  uint32_t last_bar = 0, last_par = 0;  // MMA thread: barrier and phase of its last commit
+  float acc[64];  // live only in the promoter warps
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // weights do not depend on the previous kernel: no griddepcontrol.wait
+      for (int q = 0; q < nloc; ++q) {
+        const int s = q % BW_STAGES;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / BW_STAGES) & 1) ^ 1, abort_flag, lim)) break;
+        const uint32_t fb = smem_addr(&s_full[s]);
+        mbar_expect_tx(fb, BF_WC_BYTES);
+        tma_load_2d(smem_addr(wring + s * BF_WC_BYTES), &tmW, 0, (blockIdx.y * nchunks + c0 + q) * BF_WROWS, fb);
+        w_issued = q + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BF_WROWS, BW_NTOK);
+      const uint64_t ad0 = sw128_desc(smem_addr(wring)), bd0 = sw128_desc(smem_addr(xring));
+      bool ok = true;
+      for (int j = 0; ok && j < ngroups; ++j) {  // one promotion group
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(smem_addr(&d_empty[b]), ((j >> 1) - 1) & 1, abort_flag, lim)) break;
+        const uint32_t d = tmem + b * BW_D_COLS;
+#pragma unroll
+        for (int u = 0; u < BF_PROMOTE; ++u) {
+          const int q = j * BF_PROMOTE + u;
+          if (q >= nloc) break;
+          const int s = q % BW_STAGES;
+          if (!mbar_wait(smem_addr(&s_full[s]), (q / BW_STAGES) & 1, abort_flag, lim)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = ad0 + (uint64_t)((s * BF_WC_BYTES) >> 4);
+          const uint64_t bd = bd0 + (uint64_t)((s * BW_XC_BYTES) >> 4);
+#pragma unroll
+          for (int kk = 0; kk < BF_KC / 16; ++kk)  // 16 bf16 = 32 bytes along K
+            mma_f16_ss(d, ad + 2 * kk, bd + 2 * kk, idesc, (u | kk) ? 1u : 0u);
+          mma_commit(smem_addr(&s_empty[s]));
+          last_bar = smem_addr(&s_empty[s]);
+          last_par = (q / BW_STAGES) & 1;
+        }
+        if (!ok) break;
+        mma_commit(smem_addr(&d_full[b]));
+        last_bar = smem_addr(&d_full[b]);
+        last_par = (j >> 1) & 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    pdl_wait();
+    if (lane == 0 && !g_bf_wait.withhold_x) {
+      for (int q = 0; q < nloc; ++q) {
+        const int s = q % BW_STAGES;
+        if (!mbar_wait(smem_addr(&s_empty[s]), ((q / BW_STAGES) & 1) ^ 1, abort_flag, lim)) break;
+        const uint32_t fb = smem_addr(&s_full[s]);
+        uint8_t* st = xring + s * BW_XC_BYTES;
+        mbar_expect_tx(fb, BW_XC_BYTES);
+        const int kx = (c0 + q) * BF_KC;
+#pragma unroll
+        for (int h = 0; h < BW_NTOK / 64; ++h)  // 64-row boxes
+          tma_load_2d(smem_addr(st + h * 64 * 128), &tmX, kx, tok0 + h * 64, fb);
+        x_issued = q + 1;
+      }
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------- warps 4..11: promote (lane quarter = warp % 4, 64-row half)
+    const int half = (warp - 4) >> 2;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    for (int g = 0; g < ngroups; ++g) {
+      const int b = g & 1;
+      if (!mbar_wait(smem_addr(&d_full[b]), (g >> 1) & 1, abort_flag, lim)) break;
+      tc_fence_after();
+      const uint32_t d = tmem + lane_base + b * BW_D_COLS + half * 64;
+#pragma unroll
+      for (int cb = 0; cb < 64; cb += 32) {
+        uint32_t r[32];
+        tmem_ld32(d + cb, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[cb + j] += __uint_as_float(r[j]);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&d_empty[b]));
+    }
+  }
+  pdl_launch_dependents();
+  if (warp == 0 && lane == 0) issued[0] = w_issued;
+  if (warp == 2 && lane == 0) issued[1] = x_issued;
+  __syncthreads();  // every role is done waiting: the abort flag is final
+
+  // drain on abort: issued copies and MMAs must land before smem/TMEM go away
+  const bool aborted = *abort_flag != 0;
+  if (aborted) {
+    if (threadIdx.x == 0) {
+      atomicOr(p.status, RTR_DEV_TIMEOUT);
+      // a stage's full barrier takes one arrival from each producer: stand in
+      // for the one that stopped earlier, then wait for the issued copies
+      const int wi = issued[0], xi = issued[1];
+      ring_stand_in(s_full, BW_STAGES, xi, wi);
+      ring_stand_in(s_full, BW_STAGES, wi, xi);
+      drain_ring(s_full, BW_STAGES, wi > xi ? wi : xi);
+    }
+    if (warp == 1 && lane == 0 && last_bar) mbar_drain(last_bar, last_par);  // all MMAs issued
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BW_TMEM_COLS);
+  }
+  pdl_wait();  // the split-K workspace and the epilogue touch memory of earlier kernels
+  const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+  if (aborted) {
+    if (p.splits > 1) {
+      int r0, r1;
+      splitk_claim(p, smem_addr(red_bar), &go, 0, tile, r0, r1, true);
+    }
+    return;
+  }
+
+  const bool have = warp >= 4;
+  const int quarter = warp & 3, half = (warp - 4) >> 2;
+  const int n = n0 + quarter * 32 + lane;  // weight row of this thread
+  const int rows = p.M - tok0 < BW_NTOK ? p.M - tok0 : BW_NTOK;
+  const int cols4 = (p.N - n0 < BF_WROWS ? p.N - n0 : BF_WROWS) >> 2;
+  float4* red4 = reinterpret_cast<float4*>(smem);  // the rings are free now
+  if (p.splits > 1) {
+    // partial tiles are tile-contiguous: ws[(split * tiles + tile)][row][128]
+    const long tstride = (long)gridDim.x * gridDim.y * (BW_NTOK * BF_WROWS);
+    if (have && n < p.N) {
+      float* w = p.ws + blockIdx.z * tstride + (long)tile * (BW_NTOK * BF_WROWS) + (half * 64) * BF_WROWS +
+                 quarter * 32 + lane;
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (half * 64 + j < rows) __stcg(w + j * BF_WROWS, acc[j]);
+    }
+    __threadfence();
+    __syncthreads();
+    int r0 = 0, r1 = 0;
+    if (!splitk_claim(p, smem_addr(red_bar), &go, rows, tile, r0, r1)) return;
+    bf_splitk_sum<BW_THREADS, BW_NTOK>(p, red4, r0, r1 - r0, cols4, tile, tstride);
+    bf_tile_epilogue<BW_THREADS>(p, red4 + r0 * 32, BF_WROWS / 4, tok0 + r0, n0, r1 - r0, cols4);
+    return;
+  }
+  if (have && n < p.N) {
+    float* red = reinterpret_cast<float*>(smem) + (half * 64) * BF_RLD + quarter * 32 + lane;
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+      if (half * 64 + j < rows) red[j * BF_RLD] = acc[j];
+  }
+  __syncthreads();
+  bf_tile_epilogue<BW_THREADS>(p, red4, BF_RLD / 4, tok0, n0, rows, cols4);
 }
 
 // ---------------------------------------------------------------- host side
@@ -600,6 +831,8 @@ cudaError_t gemm_bf16_wait_control(long long wait_cycles, int withhold_x) {
 cudaError_t gemm_bf16_init() {
   cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BF_SMEM_BYTES);
   if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(gemm_bf16_wide_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BW_SMEM_BYTES);
+  if (e != cudaSuccess) return e;
   int dev = 0;
   if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
   if (dev >= kMaxDevices) return cudaErrorInvalidDevice;
@@ -609,7 +842,8 @@ cudaError_t gemm_bf16_init() {
 
 cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int ldc, const float* bias, int M, int N,
                       int K, int epi, float* ws, size_t ws_floats, int* tickets, int max_tickets, uint32_t* status,
-                      int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope, float2* lse, int lse_ld) {
+                      int sms, cudaStream_t stream, bool pdl, const RopeArgs* rope, float2* lse, int lse_ld,
+                      bool allow_wide) {
   if (lse && (epi != EPI_STORE || lse_ld < (N + BF_WROWS - 1) / BF_WROWS)) return cudaErrorInvalidValue;
   if (epi == EPI_ROPE) {
     if (!rope || !bias || (rope->head_dim != 64 && rope->head_dim != 128) ||
@@ -620,14 +854,18 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
   }
   if (epi == EPI_BIAS && (!bias || (reinterpret_cast<uintptr_t>(bias) & 15))) return cudaErrorInvalidValue;
   if (K % 8) return cudaErrorInvalidValue;  // TMA rows of the activations: 16-byte multiples
-  const int tt = (M + BF_NTOK - 1) / BF_NTOK, wt = (N + BF_WROWS - 1) / BF_WROWS;
+  // more than 64 rows: 128-row CTAs (the same split plan and promotion order
+  // as 64-row CTAs for the same tiles)
+  const bool wide = allow_wide && M > BF_NTOK;
+  const int ntok = wide ? BW_NTOK : BF_NTOK;
+  const int tt = (M + ntok - 1) / ntok, wt = (N + BF_WROWS - 1) / BF_WROWS;
   const int nchunks = (K + BF_KC - 1) / BF_KC;
   // a 64-element bf16 chunk row is 128 bytes, as a 32-element tf32 one: the same plan
   int dev = 0;
   cudaGetDevice(&dev);
   // the fp16-pair kernel's rule: no cost for clusters beyond two, sizes 2 and 4 only
   const SplitPlan plan = tc_split_plan(tt * wt, nchunks, sms, g_bf_clusters[dev < kMaxDevices ? dev : 0], 4,
-                                       ws_floats, (long)BF_NTOK * BF_WROWS, max_tickets, 0.0, true);
+                                       ws_floats, (long)ntok * BF_WROWS, max_tickets, 0.0, true);
   const int splits = plan.splits, cs = plan.cluster;
   BfParams p{C, bias, M, N, K, ldc, epi, splits, ws, tickets, status, {}};
   if (rope) p.rope = *rope;
@@ -635,8 +873,8 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
   p.lse_ld = lse_ld;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tt, wt, splits);
-  cfg.blockDim = dim3(BF_THREADS);
-  cfg.dynamicSmemBytes = BF_SMEM_BYTES;
+  cfg.blockDim = dim3(wide ? BW_THREADS : BF_THREADS);
+  cfg.dynamicSmemBytes = wide ? BW_SMEM_BYTES : BF_SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -647,8 +885,9 @@ cudaError_t gemm_bf16(const TensorMap& tmW, const TensorMap& tmX, void* C, int l
   attr[1].val.clusterDim.z = cs;
   cfg.attrs = attr;
   cfg.numAttrs = cs > 1 ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, gemm_bf16_kernel, *reinterpret_cast<const CUtensorMap*>(&tmW),
-                            *reinterpret_cast<const CUtensorMap*>(&tmX), p);
+  const CUtensorMap& w = *reinterpret_cast<const CUtensorMap*>(&tmW);
+  const CUtensorMap& x = *reinterpret_cast<const CUtensorMap*>(&tmX);
+  return wide ? cudaLaunchKernelEx(&cfg, gemm_bf16_wide_kernel, w, x, p) : cudaLaunchKernelEx(&cfg, gemm_bf16_kernel, w, x, p);
 }
 
 }  // namespace rtr

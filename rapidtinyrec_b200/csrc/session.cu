@@ -740,7 +740,7 @@ static cudaError_t gemm16(rtr_session* s, const float* X, const void* Wp, void* 
   auto w = s->tmaps.find({Wp, 128});
   if (x == s->tmaps.end() || w == s->tmaps.end()) return cudaErrorInvalidValue;
   return gemm_bf16(w->second, x->second, C, ldc, bias, M, N, K, epi, s->ws, s->ws_floats, s->tickets, kTickets,
-                   s->d_status, s->sms, s->stream, s->pdl, rope, lse, (s->cfg.vocab + 127) / 128);
+                   s->d_status, s->sms, s->stream, s->pdl, rope, lse, (s->cfg.vocab + 127) / 128, s->tc_wide);
 }
 
 // The prefill of user cur_user also writes layer l's K / V as fp16 pairs for

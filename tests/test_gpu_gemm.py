@@ -122,7 +122,8 @@ def test_64_and_128_row_kernels_agree_bitwise_up_to_64_rows(dev):
 
 
 @pytest.mark.parametrize('M,N,K', [(50, 256, 64), (50, 256, 192), (50, 256, 1536), (50, 256, 8960),
-                                   (50, 17920, 1536), (50, 1536, 8960), (237, 2048, 1536)])
+                                   (50, 17920, 1536), (50, 1536, 8960), (237, 2048, 1536), (100, 1536, 8960),
+                                   (300, 17920, 1536), (766, 3584, 3584)])
 def test_bf16_kernel_within_one_bf16_ulp_of_the_rounded_product(dev, M, N, K):
     from rapidtinyrec_b200 import _native
     x, w = operands(dev, M, N, K, seed=K + N)
@@ -135,6 +136,18 @@ def test_bf16_kernel_within_one_bf16_ulp_of_the_rounded_product(dev, M, N, K):
     bad = ((got - want).abs() > tol).sum().item()
     assert bad == 0, f'{bad} of {got.numel()} beyond one bf16 ulp'
     assert ((got - want).abs() <= want.abs() / 128.0).float().mean().item() > 0.999
+
+
+@pytest.mark.parametrize('N,K', [(2048, 1536), (1536, 8960), (17920, 1536)])
+def test_bf16_64_and_128_row_kernels_agree_bitwise(dev, N, K):
+    """Above 64 rows the bf16 GEMM runs 128-row CTAs; up to 128 rows they take
+    the 64-row kernel's split plan and promotion order, so the rows agree bit
+    for bit with a 50-row call (a two-user decode batch equals batch 1)."""
+    from rapidtinyrec_b200 import _native
+    x, w = operands(dev, 100, N, K, seed=N + 7)
+    both = _native.gemm(x, w, 3)
+    assert torch.equal(both[:50], _native.gemm(x[:50].contiguous(), w, 3))
+    assert torch.equal(both[50:], _native.gemm(x[50:].contiguous(), w, 3))
 
 
 @pytest.mark.parametrize('M,N,K', [(50, 2048, 1536), (50, 1536, 8960), (237, 1536, 1536)])
