@@ -4,7 +4,8 @@
 //   C[m, n] (+ epilogue) = sum_k X[m, k] * W[n, k]        X: bf16 activations, W: bf16 weight
 //
 // A CTA owns 128 weight rows (MMA M) x 64 activation rows (MMA N) for a range
-// of K, walked in 64-element chunks (one 128-byte row of bf16):
+// of K, walked in 64-element chunks (one 128-byte row of bf16); above 64 rows
+// gemm_bf16_wide_kernel (further down) owns 128 activation rows:
 //   warp 0     TMA of the packed W tiles [128 x 64] (128B swizzle)
 //   warp 2     TMA of the activation tiles [64 x 64]
 //              both into a 4-deep ring of stages of two chunks; a stage has one
