@@ -123,7 +123,7 @@ def test_64_and_128_row_kernels_agree_bitwise_up_to_64_rows(dev):
 
 @pytest.mark.parametrize('M,N,K', [(50, 256, 64), (50, 256, 192), (50, 256, 1536), (50, 256, 8960),
                                    (50, 17920, 1536), (50, 1536, 8960), (237, 2048, 1536), (100, 1536, 8960),
-                                   (300, 17920, 1536), (766, 3584, 3584)])
+                                   (300, 17920, 1536), (766, 3584, 3584), (766, 3584, 18944)])
 def test_bf16_kernel_within_one_bf16_ulp_of_the_rounded_product(dev, M, N, K):
     from rapidtinyrec_b200 import _native
     x, w = operands(dev, M, N, K, seed=K + N)
