@@ -294,6 +294,10 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   constexpr int VEC = HD / 32, QLD = HD + DQLD_PAD, E = 16 / (int)sizeof(T);
   constexpr int AD4 = HD / 4 / AWARPS;  // float4 columns per warp in phase A
   static_assert(DBEAMS == 8 && AWARPS == 8 && AK == 64, "tiling assumes 8 beams, 8 warps, 64-key chunks");
+  // batched decode: user u owns rows u * beams .. (its own prefix, length and ancestry)
+  const int gpu = (beams + DBEAMS - 1) / DBEAMS, u = blockIdx.y / gpu;
+  // the prompt length is copied in before the request's first kernel: read before the wait
+  int L = L_dev[u];
   pdl_launch_dependents();
   pdl_wait();
   extern __shared__ __align__(16) unsigned char asmem[];
@@ -306,12 +310,9 @@ __global__ void __launch_bounds__(ATHREADS) decode_attn_kernel(
   float* pr = part + AWARPS * DBEAMS * DSLD;                     // [DBEAMS][AK] probabilities
   float* corr_s = pr + DBEAMS * AK;                              // [DBEAMS]
   const int h = blockIdx.x, g = h / (heads / kv_heads);
-  // batched decode: user u owns rows u * beams .. (its own prefix, length and ancestry)
-  const int gpu = (beams + DBEAMS - 1) / DBEAMS, u = blockIdx.y / gpu;
   const int b0 = (blockIdx.y % gpu) * DBEAMS, r0 = u * beams, rows = users * beams;
   anc += (long)u * anc_user_stride;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int L = L_dev[u];
   if (L < 1 || L > cap) {  // the prefill recorded no valid prefix: attend to the suffix only
     if (threadIdx.x == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
     L = 0;

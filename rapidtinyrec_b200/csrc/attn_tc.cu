@@ -200,10 +200,10 @@ __global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS,
   const uint32_t tmem = *tmem_slot;
   const uint32_t s_tmem = tmem, o_tmem = tmem + C::S_COLS;
   const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+  int L = L_dev[u];  // copied in before the request's first kernel: read before the wait
   pdl_launch_dependents();
   pdl_wait();  // q, the suffix rows and the pair copies come from earlier kernels
 
-  int L = L_dev[u];
   if (L < 1 || L > cap || L > AT_MAX_PREFIX) {  // no valid prefix: attend to the suffix only
     if (tid == 0 && rank == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
     L = 0;
@@ -1171,10 +1171,10 @@ __global__ void __cluster_dims__(AT_CLUSTER, 1, 1) __launch_bounds__(AT_THREADS,
   const uint32_t tmem = *tmem_slot;
   const uint32_t o_tmem = tmem + 2 * C::S_COLS;
   const uint32_t lane_base = (uint32_t)(lq * 32) << 16;
+  int L = L_dev[u];  // copied in before the request's first kernel: read before the wait
   pdl_launch_dependents();
   pdl_wait();  // q, the suffix rows and the prefix copies come from earlier kernels
 
-  int L = L_dev[u];
   if (L < 1 || L > cap) {  // no valid prefix: attend to the suffix only
     if (tid == 0 && rank == 0) atomicOr(status, RTR_DEV_BAD_LENGTH);
     L = 0;
