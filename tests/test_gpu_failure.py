@@ -72,3 +72,27 @@ def test_bounded_wait_expires_in_a_clustered_split_k_gemm():
     assert err.value.code == _native.RTR_ERR_DEVICE
     got = _native.gemm(x, w, kernel=5)
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize('M,N,K', [(50, 1536, 1536), (100, 1536, 1536), (237, 17920, 1536)])
+def test_bounded_wait_expires_in_the_bf16_gemm(M, N, K):
+    """The bf16 GEMM's waits are bounded the same way: 64-row CTAs in split-K
+    clusters (50 rows), 128-row CTAs in split-K clusters (100 rows) and without
+    split-K (237 rows, 2 x 140 tiles).  The aborted launch reports a device
+    error and the next one is exact again."""
+    if not torch.cuda.is_available():
+        pytest.fail('CUDA device required for -m gpu tests')
+    from rapidtinyrec_b200 import _native
+    g = torch.Generator().manual_seed(M + N)
+    x = (torch.rand((M, K), generator=g) - 0.5).cuda()
+    w = ((torch.rand((N, K), generator=g) - 0.5) * 0.04).cuda()
+    want = _native.gemm(x, w, kernel=3)
+    _native.wait_control(0, SHORT_WAIT, withhold_activation_copies=True)
+    try:
+        with pytest.raises(_native.NativeError) as err:
+            _native.gemm(x, w, kernel=3)
+    finally:
+        _native.wait_control(0)
+    assert err.value.code == _native.RTR_ERR_DEVICE
+    got = _native.gemm(x, w, kernel=3)
+    assert torch.equal(got, want)
