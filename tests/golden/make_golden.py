@@ -28,8 +28,8 @@ Models: the two CPU models of the reference's own tests
 grammar, FP32 and BF16) and the tiny synthetic workload (all 8 users).
 
 ``--cohort WORKLOAD`` runs the same reference ``generate`` on the full-size
-synthetic workloads (the 1.5B-shaped FP32 and BF16 cohorts, the 7B-shaped BF16
-model) and writes ``cohort_<workload>.npz``: per user the ranked token ids,
+synthetic workloads (the 1.5B-shaped FP32 and BF16 cohorts, the 0.5B-shaped FP32
+cohort, the 7B-shaped BF16 model) and writes ``cohort_<workload>.npz``: per user the ranked token ids,
 beam indices, sequence and transition log-probabilities, plus fingerprints of
 the weights and prompts the records were made from.  BF16 follows the
 reference's ``bf16-experimental`` opt-in on the CPU: the whole model cast to
