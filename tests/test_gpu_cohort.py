@@ -20,7 +20,7 @@ weights and prompts they were made from; both are checked first.
   (the reference's CPU top-k keeps either of two equal scores; this build keeps
   the lower flat index): then at most two SIDs are exchanged, the shared ones
   agree within the score tolerance, and such users are counted (at most 3).
-* qwen1.5b-bf16, all 500 users, and qwen7b-bf16 (the longest prompts, 4 KV
+* qwen1.5b-bf16, all 500 users, and qwen7b-bf16 (24 users; the longest prompts, 4 KV
   heads with 7 query heads each, an untied LM head, the 50,000-item trie): the
   reference's BF16 opt-in rounds differently on the CPU than any GPU kernel, so
   the report is the one the reference publishes for its BF16 run
@@ -284,7 +284,7 @@ def bf16_cohort(name):
                'mean_top50_overlap': float(np.mean(overlaps)), 'min_top50_overlap': int(min(overlaps)),
                'abs_delta_shared_sids': {'max': float(d.max()), 'p99': float(np.percentile(d, 99)),
                                          'median': float(np.median(d))},
-               'per_user': per_user if len(refs) <= 16 else None}
+               'per_user': per_user if len(refs) <= 32 else None}
     write_report(name, summary)
     return summary
 
@@ -302,11 +302,16 @@ def test_bf16_cohort_against_the_reference_bf16_run():
 
 
 def test_7b_bf16_long_prefix_against_the_reference_bf16_run():
-    """Five users including the longest prompt (1,024 tokens) and the shortest
-    (600).  Measured: the same top item for all five, overlap 47-48, |delta|
-    0.088 median / 0.45 max."""
+    """24 users including the longest prompt (1,024 tokens) and the shortest
+    (600).  Measured on B200: every rank list changes, 365 of 1,200 positions
+    match, the same top item for 21, top-50 overlap 46.5 mean / 43 min, |delta|
+    of shared SIDs 0.085 median / 0.38 max.  For scale: the reference's own
+    BF16 run, repeated on another host CPU for five of these users, changes
+    every rank list too (overlap 48-49, |delta| up to 0.21).  Bounds leave a
+    margin."""
     s = bf16_cohort('qwen7b-bf16')
+    assert s['users'] == 24
     assert max(u['prompt_tokens'] for u in s['per_user']) == 1024
-    assert s['min_top50_overlap'] >= 44
-    assert s['same_top1_users'] >= 4
+    assert s['min_top50_overlap'] >= 40 and s['mean_top50_overlap'] >= 45
+    assert s['same_top1_users'] >= 0.75 * s['users']
     assert s['abs_delta_shared_sids']['max'] <= 0.7
