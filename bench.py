@@ -263,6 +263,32 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def rank_users(all_users, rank, world):
+    """This rank's users: dealt round-robin (rank, rank + world, ...); the ranks
+    share nothing on the per-step path."""
+    return all_users[rank::world]
+
+
+def combine_ranks(total_ms, e2e_total, per_user, e2e_lat, world, device):
+    """The job's timing from every rank's own, outside the timed region: the max
+    of the ranks' timed spans (the job ends with its slowest rank) and every
+    rank's per-user latencies, rank after rank.  One rank returns its own."""
+    if world == 1:
+        return total_ms, e2e_total, per_user, e2e_lat
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([total_ms, e2e_total], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    lat = torch.tensor(per_user, dtype=torch.float64, device=device)
+    gathered = [torch.empty_like(lat) for _ in range(world)]
+    dist.all_gather(gathered, lat)
+    el = torch.tensor(e2e_lat, dtype=torch.float64, device=device)
+    g2 = [torch.empty_like(el) for _ in range(world)]
+    dist.all_gather(g2, el)
+    return (float(t[0]), float(t[1]), [float(x) for g in gathered for x in g.tolist()],
+            [float(x) for g in g2 for x in g.tolist()])
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -278,7 +304,7 @@ def run_ours(args):
 
     per_rank = args.warmup + args.steps
     wl, items, cons, all_users = build_workload(args.workload, per_rank * world)
-    users = all_users[rank::world]
+    users = rank_users(all_users, rank, world)
     cfg = wl.model
     max_prefix = max(wl.prompt_max, max(u.prompt_tokens for u in users))
     weights = wk.synth_weights(cfg, seed=wl.weight_seed, device=f'cuda:{local}')
@@ -426,18 +452,7 @@ def run_ours(args):
     gemm_bytes = gemm_weight_bytes(cfg)
     peak, peak_kind = measured_peaks()
 
-    if world > 1:
-        t = torch.tensor([total_ms, e2e_total], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms, e2e_total = float(t[0]), float(t[1])
-        lat = torch.tensor(per_user, dtype=torch.float64, device=dev)
-        gathered = [torch.empty_like(lat) for _ in range(world)]
-        dist.all_gather(gathered, lat)
-        per_user = [float(x) for g in gathered for x in g.tolist()]
-        el = torch.tensor(e2e_lat, dtype=torch.float64, device=dev)
-        g2 = [torch.empty_like(el) for _ in range(world)]
-        dist.all_gather(g2, el)
-        e2e_lat = [float(x) for g in g2 for x in g.tolist()]
+    total_ms, e2e_total, per_user, e2e_lat = combine_ranks(total_ms, e2e_total, per_user, e2e_lat, world, dev)
 
     cpu = None
     if weights_cpu is not None:
